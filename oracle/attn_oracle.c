@@ -1,0 +1,402 @@
+/*
+ * attn_oracle.c -- TEST INFRASTRUCTURE ONLY (see attn_oracle.h).
+ *
+ * CPU restatement of the reference engine's attention step, written from the
+ * reference's behaviour, in the reference's operation order, so that results
+ * are bit-identical to the reference compiled without FP contraction.  Built
+ * with -ffp-contract=off so that every a*b+c below is two rounded operations,
+ * as in the reference's scalar code.  Each function cites the reference
+ * file:line it follows.  Only tests/, __graft_entry__.smoke() and bench.py's
+ * cpu_baseline leg may load the library built from this file.
+ */
+#include "attn_oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ------------------------------------------------------------------------ */
+/* fp16 <-> fp32, cpp/quant.hpp:73-135 (= picolm/quant.c:11-78)             */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * The reference rounds the magnitude half-up (adds half an ulp, then
+ * truncates), not round-to-nearest-even, and flushes f32 subnormals to a
+ * signed zero (cpp/quant.hpp:110-134).  Adding half an ulp to the rebiased
+ * (exponent|fraction) word lets the carry bump the exponent, which is the same
+ * as the reference's explicit overflow branch, including overflow to inf.
+ */
+uint16_t ora_f32_to_f16(float f) {
+    uint32_t u;
+    memcpy(&u, &f, sizeof u);
+    const uint16_t sgn = (uint16_t)((u >> 16) & 0x8000u);
+    const uint32_t be = (u >> 23) & 0xFFu;
+    const uint32_t frac = u & 0x7FFFFFu;
+    if (be == 0) return sgn;                                   /* quant.hpp:110-112 */
+    if (be == 0xFF) return (uint16_t)(sgn | 0x7C00u | (frac ? 0x200u : 0u)); /* :113-115 */
+    const int e = (int)be - 112;                               /* 127 -> 15 rebias */
+    if (e >= 31) return (uint16_t)(sgn | 0x7C00u);             /* :116-118 */
+    if (e <= 0) {                                              /* :119-126 */
+        if (e < -10) return sgn;
+        const uint32_t sig = frac | 0x800000u;
+        const uint32_t sh = (uint32_t)(14 - e);
+        return (uint16_t)(sgn | ((sig + (1u << (sh - 1))) >> sh));
+    }
+    const uint32_t word = (((uint32_t)e << 23) | frac) + 0x1000u; /* :128-134 */
+    return (uint16_t)(sgn | (word >> 13));
+}
+
+/* Exact widening; subnormals are mant * 2^-24 (cpp/quant.hpp:73-100). */
+float ora_f16_to_f32(uint16_t h) {
+    const uint32_t sgn = (uint32_t)(h & 0x8000u) << 16;
+    const uint32_t e = (h >> 10) & 0x1Fu;
+    const uint32_t m = h & 0x3FFu;
+    uint32_t u;
+    if (e == 0) {
+        float mag = (float)m * 5.9604644775390625e-8f;        /* 2^-24, exact */
+        memcpy(&u, &mag, sizeof u);
+        u |= sgn;
+    } else if (e == 31) {
+        u = sgn | 0x7F800000u | (m << 13);
+    } else {
+        u = sgn | ((e + 112u) << 23) | (m << 13);
+    }
+    float f;
+    memcpy(&f, &u, sizeof f);
+    return f;
+}
+
+void ora_f32_to_f16_n(const float* in, uint16_t* out, size_t n) {
+    for (size_t i = 0; i < n; i++) out[i] = ora_f32_to_f16(in[i]);
+}
+
+void ora_f16_to_f32_n(const uint16_t* in, float* out, size_t n) {
+    for (size_t i = 0; i < n; i++) out[i] = ora_f16_to_f32(in[i]);
+}
+
+/* ------------------------------------------------------------------------ */
+/* RMSNorm, cpp/tensor.hpp:146-176 (SSE2 path, the one x86 builds take)     */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Sum of squares in four interleaved lanes (element i goes to lane i%4), the
+ * lanes folded as (l0+l2)+(l1+l3) (hsum_sse, cpp/quant.hpp:296-302), then any
+ * tail elements added one by one.  scale = 1/sqrtf(ss/n + eps); out = x*scale*w.
+ */
+void ora_rmsnorm_inplace(float* x, const float* w, int n, float eps) {
+    float lane[4] = {0.f, 0.f, 0.f, 0.f};
+    int i = 0;
+    for (; i + 3 < n; i += 4)
+        for (int j = 0; j < 4; j++) {
+            const float sq = x[i + j] * x[i + j];
+            lane[j] = lane[j] + sq;
+        }
+    float ss = (lane[0] + lane[2]) + (lane[1] + lane[3]);
+    for (; i < n; i++) {
+        const float sq = x[i] * x[i];
+        ss = ss + sq;
+    }
+    const float scale = 1.0f / sqrtf(ss / (float)n + eps);
+    for (int d = 0; d < n; d++) {
+        const float t = x[d] * scale;
+        x[d] = t * w[d];
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* RoPE                                                                     */
+/* ------------------------------------------------------------------------ */
+
+static void rot_pair(float* a, float* b, float c, float s) {
+    const float x0 = *a, x1 = *b;
+    const float p0 = x0 * c, p1 = x1 * s, p2 = x0 * s, p3 = x1 * c;
+    *a = p0 - p1;
+    *b = p2 + p3;
+}
+
+/* NeoX: element i pairs with i + hd/2 (cpp/tensor.hpp:201-283). */
+void ora_rope_neox(float* q, float* k, int hd, int hq, int hkv,
+                   const float* c, const float* s) {
+    const int half = hd / 2;
+    for (int h = 0; h < hq; h++)
+        for (int i = 0; i < half; i++) rot_pair(q + h * hd + i, q + h * hd + i + half, c[i], s[i]);
+    for (int h = 0; h < hkv; h++)
+        for (int i = 0; i < half; i++) rot_pair(k + h * hd + i, k + h * hd + i + half, c[i], s[i]);
+}
+
+/* Interleaved: element 2i pairs with 2i+1 (picolm/tensor.c:247-293). */
+void ora_rope_interleaved(float* q, float* k, int hd, int hq, int hkv,
+                          const float* c, const float* s) {
+    const int half = hd / 2;
+    for (int h = 0; h < hq; h++)
+        for (int i = 0; i < half; i++) rot_pair(q + h * hd + 2 * i, q + h * hd + 2 * i + 1, c[i], s[i]);
+    for (int h = 0; h < hkv; h++)
+        for (int i = 0; i < half; i++) rot_pair(k + h * hd + 2 * i, k + h * hd + 2 * i + 1, c[i], s[i]);
+}
+
+/* theta = (float)pos / powf(base, (float)(2i)/(float)hd) (cpp/model.hpp:1008-1017). */
+void ora_rope_table(float* cos_t, float* sin_t, int max_seq, int hd, float base) {
+    const int half = hd / 2;
+    for (int p = 0; p < max_seq; p++)
+        for (int i = 0; i < half; i++) {
+            const float theta = (float)p / powf(base, (float)(2 * i) / (float)hd);
+            cos_t[(size_t)p * half + i] = cosf(theta);
+            sin_t[(size_t)p * half + i] = sinf(theta);
+        }
+}
+
+/* ------------------------------------------------------------------------ */
+/* Attention                                                                */
+/* ------------------------------------------------------------------------ */
+
+/* Online-softmax scan of one q head over cache rows [b, e), C++ engine order
+ * (cpp/model.hpp:378-413).  State (m, l, acc) is updated in place. */
+static void scan_rows_cpp(const float* qh, const uint16_t* kc, const uint16_t* vc,
+                          int kvd, int kvh, int hd, int b, int e,
+                          float* m, float* l, float* acc) {
+    const float rs = sqrtf((float)hd);
+    for (int t = b; t < e; t++) {
+        const uint16_t* kt = kc + (size_t)t * kvd + (size_t)kvh * hd;
+        const uint16_t* vt = vc + (size_t)t * kvd + (size_t)kvh * hd;
+        float score = 0.0f;
+        for (int d = 0; d < hd; d++) {
+            const float p = qh[d] * ora_f16_to_f32(kt[d]);
+            score = score + p;
+        }
+        score = score / rs;
+        if (score > *m) {
+            const float corr = expf(*m - score);
+            *l = *l * corr;
+            for (int d = 0; d < hd; d++) acc[d] = acc[d] * corr;
+            *l = *l + 1.0f;
+            for (int d = 0; d < hd; d++) acc[d] = acc[d] + ora_f16_to_f32(vt[d]);
+            *m = score;
+        } else {
+            const float w = expf(score - *m);
+            *l = *l + w;
+            for (int d = 0; d < hd; d++) {
+                const float p = w * ora_f16_to_f32(vt[d]);
+                acc[d] = acc[d] + p;
+            }
+        }
+    }
+}
+
+/* Same scan in the C engine's fused order (picolm/model.c:790-817). */
+static void scan_rows_c(const float* qh, const uint16_t* kc, const uint16_t* vc,
+                        int kvd, int kvh, int hd, int b, int e,
+                        float* m, float* l, float* acc) {
+    const float rs = sqrtf((float)hd);
+    for (int t = b; t < e; t++) {
+        const uint16_t* kt = kc + (size_t)t * kvd + (size_t)kvh * hd;
+        const uint16_t* vt = vc + (size_t)t * kvd + (size_t)kvh * hd;
+        float score = 0.0f;
+        for (int d = 0; d < hd; d++) {
+            const float p = qh[d] * ora_f16_to_f32(kt[d]);
+            score = score + p;
+        }
+        score = score / rs;
+        if (score > *m) {
+            const float corr = expf(*m - score);
+            *l = *l * corr + 1.0f;
+            for (int d = 0; d < hd; d++) {
+                const float p = acc[d] * corr;
+                acc[d] = p + ora_f16_to_f32(vt[d]);
+            }
+            *m = score;
+        } else {
+            const float w = expf(score - *m);
+            *l = *l + w;
+            for (int d = 0; d < hd; d++) {
+                const float p = w * ora_f16_to_f32(vt[d]);
+                acc[d] = acc[d] + p;
+            }
+        }
+    }
+}
+
+void ora_attend_rows(int hq, int hkv, int hd, const float* q_rot,
+                     const uint16_t* kc, const uint16_t* vc,
+                     int row_begin, int row_end,
+                     float* m, float* l, float* acc) {
+    const int g = hq / hkv, kvd = hkv * hd;
+    for (int h = 0; h < hq; h++) {
+        m[h] = -1e30f;
+        l[h] = 0.0f;
+        memset(acc + (size_t)h * hd, 0, sizeof(float) * (size_t)hd);
+        scan_rows_cpp(q_rot + (size_t)h * hd, kc, vc, kvd, h / g, hd, row_begin, row_end,
+                      &m[h], &l[h], acc + (size_t)h * hd);
+    }
+}
+
+static int bad_shape(int hq, int hkv, int hd) {
+    return hq <= 0 || hkv <= 0 || hq % hkv != 0 || hd <= 0 || hd % 2 != 0 || hd > 512;
+}
+
+/* Norm + RoPE + cache store for one token (cpp/model.hpp:326-373). */
+static void prep_token(int hq, int hkv, int hd, int rope_mode, float eps,
+                       float* q, float* k, const float* v,
+                       const float* qn_w, const float* kn_w,
+                       const float* c, const float* s,
+                       uint16_t* kc, uint16_t* vc, int pos) {
+    const int kvd = hkv * hd;
+    if (qn_w)
+        for (int h = 0; h < hq; h++) ora_rmsnorm_inplace(q + (size_t)h * hd, qn_w, hd, eps);
+    if (kn_w)
+        for (int h = 0; h < hkv; h++) ora_rmsnorm_inplace(k + (size_t)h * hd, kn_w, hd, eps);
+    if (rope_mode == 0) ora_rope_neox(q, k, hd, hq, hkv, c, s);
+    else ora_rope_interleaved(q, k, hd, hq, hkv, c, s);
+    ora_f32_to_f16_n(k, kc + (size_t)pos * kvd, (size_t)kvd);
+    ora_f32_to_f16_n(v, vc + (size_t)pos * kvd, (size_t)kvd);
+}
+
+/* Attention of one token over rows [0, pos] (cpp/model.hpp:375-418). */
+static void attend_token(int hq, int hkv, int hd, const float* q,
+                         const uint16_t* kc, const uint16_t* vc, int pos,
+                         float* out, int variant, int h_begin, int h_end) {
+    const int g = hq / hkv, kvd = hkv * hd;
+    float* acc = (float*)malloc(sizeof(float) * (size_t)hd);
+    for (int h = h_begin; h < h_end; h++) {
+        float m = -1e30f, l = 0.0f;
+        memset(acc, 0, sizeof(float) * (size_t)hd);
+        if (variant == 0) {
+            scan_rows_cpp(q + (size_t)h * hd, kc, vc, kvd, h / g, hd, 0, pos + 1, &m, &l, acc);
+            for (int d = 0; d < hd; d++) out[(size_t)h * hd + d] = acc[d] / l;
+        } else {
+            scan_rows_c(q + (size_t)h * hd, kc, vc, kvd, h / g, hd, 0, pos + 1, &m, &l, acc);
+            const float inv = 1.0f / l;
+            for (int d = 0; d < hd; d++) out[(size_t)h * hd + d] = acc[d] * inv;
+        }
+    }
+    free(acc);
+}
+
+int ora_decode_step(int hq, int hkv, int hd, int rope_mode, float eps,
+                    float* q, float* k, const float* v,
+                    const float* qn_w, const float* kn_w,
+                    const float* cos_row, const float* sin_row,
+                    uint16_t* kc, uint16_t* vc, int pos, float* out, int variant) {
+    if (bad_shape(hq, hkv, hd) || pos < 0 || !q || !k || !v || !kc || !vc || !out) return -1;
+    prep_token(hq, hkv, hd, rope_mode, eps, q, k, v, qn_w, kn_w, cos_row, sin_row, kc, vc, pos);
+    attend_token(hq, hkv, hd, q, kc, vc, pos, out, variant, 0, hq);
+    return 0;
+}
+
+/* ------------------------------------------------------------------------ */
+/* Threaded drivers (same arithmetic per head; tasks are independent)       */
+/* ------------------------------------------------------------------------ */
+
+typedef struct {
+    int (*fn)(void* ctx, int task);
+    void* ctx;
+    int n_tasks;
+    int next;
+    pthread_mutex_t mu;
+} pool_t;
+
+static void* pool_worker(void* arg) {
+    pool_t* p = (pool_t*)arg;
+    for (;;) {
+        pthread_mutex_lock(&p->mu);
+        const int t = p->next++;
+        pthread_mutex_unlock(&p->mu);
+        if (t >= p->n_tasks) break;
+        p->fn(p->ctx, t);
+    }
+    return NULL;
+}
+
+static void run_tasks(int (*fn)(void*, int), void* ctx, int n_tasks, int n_threads) {
+    if (n_threads < 1) n_threads = 1;
+    if (n_threads > n_tasks) n_threads = n_tasks;
+    pool_t p = {fn, ctx, n_tasks, 0, PTHREAD_MUTEX_INITIALIZER};
+    if (n_threads <= 1) {
+        pool_worker(&p);
+        return;
+    }
+    pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * (size_t)n_threads);
+    for (int i = 0; i < n_threads; i++) pthread_create(&th[i], NULL, pool_worker, &p);
+    for (int i = 0; i < n_threads; i++) pthread_join(th[i], NULL);
+    free(th);
+}
+
+typedef struct {
+    int hq, hkv, hd;
+    const float* qrot;       /* [n_tok][hq*hd] rotated */
+    const uint16_t *kc, *vc;
+    int start_pos;
+    float* out;
+} prefill_ctx_t;
+
+static int prefill_task(void* vctx, int task) {
+    prefill_ctx_t* c = (prefill_ctx_t*)vctx;
+    const int qd = c->hq * c->hd;
+    attend_token(c->hq, c->hkv, c->hd, c->qrot + (size_t)task * qd, c->kc, c->vc,
+                 c->start_pos + task, c->out + (size_t)task * qd, 0, 0, c->hq);
+    return 0;
+}
+
+int ora_prefill(int hq, int hkv, int hd, int rope_mode, float eps,
+                const float* q, const float* k, const float* v,
+                const float* qn_w, const float* kn_w,
+                const float* cos_t, const float* sin_t,
+                uint16_t* kc, uint16_t* vc, int start_pos, int n_tok,
+                float* out, int n_threads) {
+    if (bad_shape(hq, hkv, hd) || start_pos < 0 || n_tok < 0) return -1;
+    const int qd = hq * hd, kvd = hkv * hd, half = hd / 2;
+    float* qrot = (float*)malloc(sizeof(float) * (size_t)n_tok * qd + 1);
+    float* kt = (float*)malloc(sizeof(float) * (size_t)kvd);
+    /* Every token's k/v row is stored before any token reads rows beyond its
+     * own position, so storing all rows first and then attending (in parallel)
+     * reads exactly what the reference's token-by-token loop reads. */
+    for (int i = 0; i < n_tok; i++) {
+        const int pos = start_pos + i;
+        memcpy(qrot + (size_t)i * qd, q + (size_t)i * qd, sizeof(float) * (size_t)qd);
+        memcpy(kt, k + (size_t)i * kvd, sizeof(float) * (size_t)kvd);
+        prep_token(hq, hkv, hd, rope_mode, eps, qrot + (size_t)i * qd, kt, v + (size_t)i * kvd,
+                   qn_w, kn_w, cos_t + (size_t)pos * half, sin_t + (size_t)pos * half, kc, vc, pos);
+    }
+    prefill_ctx_t ctx = {hq, hkv, hd, qrot, kc, vc, start_pos, out};
+    run_tasks(prefill_task, &ctx, n_tok, n_threads);
+    free(kt);
+    free(qrot);
+    return 0;
+}
+
+typedef struct {
+    int hq, hkv, hd, rope_mode;
+    float eps;
+    const float *q, *k, *v, *qn_w, *kn_w, *cos_t, *sin_t;
+    uint16_t* const* kc;
+    uint16_t* const* vc;
+    const int* pos;
+    float* out;
+} batch_ctx_t;
+
+static int batch_task(void* vctx, int b) {
+    batch_ctx_t* c = (batch_ctx_t*)vctx;
+    const int qd = c->hq * c->hd, kvd = c->hkv * c->hd, half = c->hd / 2;
+    float* qb = (float*)malloc(sizeof(float) * (size_t)(qd + kvd));
+    float* kb = qb + qd;
+    memcpy(qb, c->q + (size_t)b * qd, sizeof(float) * (size_t)qd);
+    memcpy(kb, c->k + (size_t)b * kvd, sizeof(float) * (size_t)kvd);
+    const int p = c->pos[b];
+    ora_decode_step(c->hq, c->hkv, c->hd, c->rope_mode, c->eps, qb, kb, c->v + (size_t)b * kvd,
+                    c->qn_w, c->kn_w, c->cos_t + (size_t)p * half, c->sin_t + (size_t)p * half,
+                    c->kc[b], c->vc[b], p, c->out + (size_t)b * qd, 0);
+    free(qb);
+    return 0;
+}
+
+int ora_decode_batch(int B, int hq, int hkv, int hd, int rope_mode, float eps,
+                     const float* q, const float* k, const float* v,
+                     const float* qn_w, const float* kn_w,
+                     const float* cos_t, const float* sin_t,
+                     uint16_t* const* kc, uint16_t* const* vc,
+                     const int* pos, float* out, int n_threads) {
+    if (bad_shape(hq, hkv, hd) || B < 0) return -1;
+    batch_ctx_t ctx = {hq, hkv, hd, rope_mode, eps, q, k, v, qn_w, kn_w, cos_t, sin_t, kc, vc, pos, out};
+    run_tasks(batch_task, &ctx, B, n_threads);
+    return 0;
+}

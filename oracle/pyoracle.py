@@ -1,0 +1,279 @@
+"""TEST INFRASTRUCTURE ONLY: numpy wrappers over the CPU oracle libraries.
+
+* ``Oracle`` wraps ``oracle/_build/libpicooracle.so``, the plain-C restatement
+  of the reference's attention step (``oracle/attn_oracle.c``).
+* ``RefHarness`` wraps ``oracle/_ref/libpicoref.so``, the reference's own
+  sources (cpp/model.hpp, cpp/tensor.hpp, cpp/quant.hpp, picolm/tensor.c)
+  compiled in place and driven by ``oracle/ref_harness.cpp``.
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg may
+import this module; the product path never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "_build", "libpicooracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libpicoref.so")
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+
+
+def build(ref: bool = False) -> None:
+    """Build the oracle (and, when asked and the reference tree exists, _ref)."""
+    targets = ["oracle"]
+    if ref:
+        targets.append("ref")
+    subprocess.run(["make", "-s", "-C", HERE] + targets, check=True)
+
+
+def _opt(a):
+    return None if a is None else np.ascontiguousarray(a, np.float32).ctypes.data_as(C.c_void_p)
+
+
+class Oracle:
+    def __init__(self, path: str = ORACLE_SO):
+        if not os.path.exists(path):
+            build()
+        L = C.CDLL(path)
+        L.ora_f32_to_f16.restype = C.c_uint16
+        L.ora_f32_to_f16.argtypes = [C.c_float]
+        L.ora_f16_to_f32.restype = C.c_float
+        L.ora_f16_to_f32.argtypes = [C.c_uint16]
+        L.ora_f32_to_f16_n.argtypes = [_f32p, _u16p, C.c_size_t]
+        L.ora_f16_to_f32_n.argtypes = [_u16p, _f32p, C.c_size_t]
+        L.ora_rmsnorm_inplace.argtypes = [_f32p, _f32p, C.c_int, C.c_float]
+        for n in ("ora_rope_neox", "ora_rope_interleaved"):
+            getattr(L, n).argtypes = [_f32p, _f32p, C.c_int, C.c_int, C.c_int, _f32p, _f32p]
+        L.ora_rope_table.argtypes = [_f32p, _f32p, C.c_int, C.c_int, C.c_float]
+        L.ora_decode_step.restype = C.c_int
+        L.ora_decode_step.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
+                                      _f32p, _f32p, _f32p, C.c_void_p, C.c_void_p,
+                                      _f32p, _f32p, _u16p, _u16p, C.c_int, _f32p, C.c_int]
+        L.ora_attend_rows.argtypes = [C.c_int, C.c_int, C.c_int, _f32p, _u16p, _u16p,
+                                      C.c_int, C.c_int, _f32p, _f32p, _f32p]
+        L.ora_prefill.restype = C.c_int
+        L.ora_prefill.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
+                                  _f32p, _f32p, _f32p, C.c_void_p, C.c_void_p,
+                                  _f32p, _f32p, _u16p, _u16p, C.c_int, C.c_int, _f32p, C.c_int]
+        L.ora_decode_batch.restype = C.c_int
+        L.ora_decode_batch.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
+                                       _f32p, _f32p, _f32p, C.c_void_p, C.c_void_p,
+                                       _f32p, _f32p, C.c_void_p, C.c_void_p, _i32p, _f32p, C.c_int]
+        self.L = L
+
+    def f32_to_f16(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32).ravel()
+        out = np.empty(x.size, np.uint16)
+        self.L.ora_f32_to_f16_n(x, out, x.size)
+        return out
+
+    def f16_to_f32(self, h: np.ndarray) -> np.ndarray:
+        h = np.ascontiguousarray(h, np.uint16).ravel()
+        out = np.empty(h.size, np.float32)
+        self.L.ora_f16_to_f32_n(h, out, h.size)
+        return out
+
+    def rmsnorm(self, x: np.ndarray, w: np.ndarray, eps: float = 1e-6) -> np.ndarray:
+        x = np.array(x, np.float32)
+        self.L.ora_rmsnorm_inplace(x, np.ascontiguousarray(w, np.float32), x.size, eps)
+        return x
+
+    def rope(self, mode: int, q, k, hd, hq, hkv, c, s):
+        q = np.array(q, np.float32)
+        k = np.array(k, np.float32)
+        fn = self.L.ora_rope_neox if mode == 0 else self.L.ora_rope_interleaved
+        fn(q, k, hd, hq, hkv, np.ascontiguousarray(c, np.float32), np.ascontiguousarray(s, np.float32))
+        return q, k
+
+    def rope_table(self, max_seq: int, hd: int, base: float):
+        c = np.empty((max_seq, hd // 2), np.float32)
+        s = np.empty((max_seq, hd // 2), np.float32)
+        self.L.ora_rope_table(c, s, max_seq, hd, base)
+        return c, s
+
+    def decode_step(self, hq, hkv, hd, rope_mode, q, k, v, qn_w, kn_w, cos_t, sin_t,
+                    kc, vc, pos, variant=0, eps=1e-6):
+        """kc/vc: this layer's slabs [S][kvd] uint16, row pos written in place."""
+        q = np.array(q, np.float32)
+        k = np.array(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        out = np.empty(hq * hd, np.float32)
+        half = hd // 2
+        c = np.ascontiguousarray(cos_t[pos], np.float32).reshape(half)
+        s = np.ascontiguousarray(sin_t[pos], np.float32).reshape(half)
+        qn = None if qn_w is None else np.ascontiguousarray(qn_w, np.float32)
+        kn = None if kn_w is None else np.ascontiguousarray(kn_w, np.float32)
+        rc = self.L.ora_decode_step(hq, hkv, hd, rope_mode, eps, q, k, v, _opt(qn), _opt(kn),
+                                    c, s, kc, vc, pos, out, variant)
+        assert rc == 0
+        return out, q, k
+
+    def attend_rows(self, hq, hkv, hd, q_rot, kc, vc, b, e):
+        m = np.empty(hq, np.float32)
+        l = np.empty(hq, np.float32)
+        acc = np.empty(hq * hd, np.float32)
+        self.L.ora_attend_rows(hq, hkv, hd, np.ascontiguousarray(q_rot, np.float32), kc, vc,
+                               b, e, m, l, acc)
+        return m, l, acc
+
+    def prefill(self, hq, hkv, hd, rope_mode, q, k, v, qn_w, kn_w, cos_t, sin_t, kc, vc,
+                start_pos, n_threads=1, eps=1e-6):
+        n_tok = q.shape[0]
+        out = np.empty((n_tok, hq * hd), np.float32)
+        qn = None if qn_w is None else np.ascontiguousarray(qn_w, np.float32)
+        kn = None if kn_w is None else np.ascontiguousarray(kn_w, np.float32)
+        rc = self.L.ora_prefill(hq, hkv, hd, rope_mode, eps,
+                                np.ascontiguousarray(q, np.float32),
+                                np.ascontiguousarray(k, np.float32),
+                                np.ascontiguousarray(v, np.float32), _opt(qn), _opt(kn),
+                                np.ascontiguousarray(cos_t, np.float32),
+                                np.ascontiguousarray(sin_t, np.float32),
+                                kc, vc, start_pos, n_tok, out, n_threads)
+        assert rc == 0
+        return out
+
+    def decode_batch(self, hq, hkv, hd, rope_mode, q, k, v, qn_w, kn_w, cos_t, sin_t,
+                     kcs, vcs, pos, n_threads=1, eps=1e-6):
+        """kcs/vcs: lists of per-sequence layer slabs [S][kvd] uint16 (modified)."""
+        B = len(kcs)
+        out = np.empty((B, hq * hd), np.float32)
+        kp = (C.c_void_p * B)(*[a.ctypes.data for a in kcs])
+        vp = (C.c_void_p * B)(*[a.ctypes.data for a in vcs])
+        qn = None if qn_w is None else np.ascontiguousarray(qn_w, np.float32)
+        kn = None if kn_w is None else np.ascontiguousarray(kn_w, np.float32)
+        rc = self.L.ora_decode_batch(B, hq, hkv, hd, rope_mode, eps,
+                                     np.ascontiguousarray(q, np.float32),
+                                     np.ascontiguousarray(k, np.float32),
+                                     np.ascontiguousarray(v, np.float32), _opt(qn), _opt(kn),
+                                     np.ascontiguousarray(cos_t, np.float32),
+                                     np.ascontiguousarray(sin_t, np.float32),
+                                     C.cast(kp, C.c_void_p), C.cast(vp, C.c_void_p),
+                                     np.ascontiguousarray(pos, np.int32), out, n_threads)
+        assert rc == 0
+        return out
+
+
+class RefHarness:
+    """The reference's own code, compiled from its sources (oracle/_ref)."""
+
+    def __init__(self, path: str = REF_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} not built (make -C oracle ref)")
+        L = C.CDLL(path)
+        L.pref_model_create.restype = C.c_void_p
+        L.pref_model_create.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, C.c_int, C.c_int]
+        L.pref_model_destroy.argtypes = [C.c_void_p]
+        for n in ("pref_model_kcache", "pref_model_vcache"):
+            getattr(L, n).restype = C.POINTER(C.c_uint16)
+            getattr(L, n).argtypes = [C.c_void_p]
+        for n in ("pref_model_rope_cos", "pref_model_rope_sin"):
+            getattr(L, n).restype = C.POINTER(C.c_float)
+            getattr(L, n).argtypes = [C.c_void_p]
+        L.pref_model_set_norm.argtypes = [C.c_void_p, _f32p, _f32p]
+        L.pref_model_decode.restype = C.c_int
+        L.pref_model_decode.argtypes = [C.c_void_p, _f32p, _f32p, _f32p, C.c_int, _f32p]
+        L.pref_fp32_to_fp16.restype = C.c_uint16
+        L.pref_fp32_to_fp16.argtypes = [C.c_float]
+        L.pref_fp16_to_fp32.restype = C.c_float
+        L.pref_fp16_to_fp32.argtypes = [C.c_uint16]
+        L.pref_fp32_to_fp16_n.argtypes = [_f32p, _u16p, C.c_size_t]
+        L.pref_fp16_to_fp32_n.argtypes = [_u16p, _f32p, C.c_size_t]
+        L.pref_rmsnorm.argtypes = [_f32p, _f32p, _f32p, C.c_int]
+        L.pref_rope.argtypes = [C.c_int, _f32p, _f32p, C.c_int, C.c_int, C.c_int, _f32p, _f32p]
+        L.pref_attn_decode_batch.restype = C.c_int
+        L.pref_attn_decode_batch.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                             _f32p, _f32p, _f32p, C.c_void_p, C.c_void_p,
+                                             _f32p, _f32p, C.c_void_p, C.c_void_p, _i32p, _f32p,
+                                             C.c_int]
+        self.L = L
+
+    def f32_to_f16(self, x):
+        x = np.ascontiguousarray(x, np.float32).ravel()
+        out = np.empty(x.size, np.uint16)
+        self.L.pref_fp32_to_fp16_n(x, out, x.size)
+        return out
+
+    def f16_to_f32(self, h):
+        h = np.ascontiguousarray(h, np.uint16).ravel()
+        out = np.empty(h.size, np.float32)
+        self.L.pref_fp16_to_fp32_n(h, out, h.size)
+        return out
+
+    def rmsnorm(self, x, w):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty_like(x)
+        self.L.pref_rmsnorm(out, x, np.ascontiguousarray(w, np.float32), x.size)
+        return out
+
+    def rope(self, mode, q, k, hd, hq, hkv, c, s):
+        q = np.array(q, np.float32)
+        k = np.array(k, np.float32)
+        self.L.pref_rope(mode, q, k, hd, hq, hkv, np.ascontiguousarray(c, np.float32),
+                         np.ascontiguousarray(s, np.float32))
+        return q, k
+
+    def attn_decode_batch(self, hq, hkv, hd, rope_mode, q, k, v, qn_w, kn_w, cos_t, sin_t,
+                          kcs, vcs, pos, n_threads=1):
+        B = len(kcs)
+        out = np.empty((B, hq * hd), np.float32)
+        kp = (C.c_void_p * B)(*[a.ctypes.data for a in kcs])
+        vp = (C.c_void_p * B)(*[a.ctypes.data for a in vcs])
+        qn = None if qn_w is None else np.ascontiguousarray(qn_w, np.float32)
+        kn = None if kn_w is None else np.ascontiguousarray(kn_w, np.float32)
+        rc = self.L.pref_attn_decode_batch(B, hq, hkv, hd, rope_mode,
+                                           np.ascontiguousarray(q, np.float32),
+                                           np.ascontiguousarray(k, np.float32),
+                                           np.ascontiguousarray(v, np.float32), _opt(qn), _opt(kn),
+                                           np.ascontiguousarray(cos_t, np.float32),
+                                           np.ascontiguousarray(sin_t, np.float32),
+                                           C.cast(kp, C.c_void_p), C.cast(vp, C.c_void_p),
+                                           np.ascontiguousarray(pos, np.int32), out, n_threads)
+        assert rc == 0
+        return out
+
+
+class RefModel:
+    """One-layer synthetic reference Model driven through Model::forward."""
+
+    def __init__(self, ref: RefHarness, hq, hkv, hd, max_seq, rope_base, rope_mode, qk_norm):
+        self.ref, self.L = ref, ref.L
+        self.hq, self.hkv, self.hd, self.S = hq, hkv, hd, max_seq
+        self.h = self.L.pref_model_create(hq, hkv, hd, max_seq, rope_base, rope_mode, int(qk_norm))
+        if not self.h:
+            raise RuntimeError("pref_model_create failed")
+        kvd = hkv * hd
+        self.kcache = np.ctypeslib.as_array(self.L.pref_model_kcache(self.h), shape=(max_seq, kvd))
+        self.vcache = np.ctypeslib.as_array(self.L.pref_model_vcache(self.h), shape=(max_seq, kvd))
+        self.rope_cos = np.ctypeslib.as_array(self.L.pref_model_rope_cos(self.h), shape=(max_seq, hd // 2))
+        self.rope_sin = np.ctypeslib.as_array(self.L.pref_model_rope_sin(self.h), shape=(max_seq, hd // 2))
+
+    def set_norm(self, qn_w, kn_w):
+        self.L.pref_model_set_norm(self.h, np.ascontiguousarray(qn_w, np.float32),
+                                   np.ascontiguousarray(kn_w, np.float32))
+
+    def decode(self, q, k, v, pos):
+        out = np.empty(self.hq * self.hd, np.float32)
+        rc = self.L.pref_model_decode(self.h, np.ascontiguousarray(q, np.float32),
+                                      np.ascontiguousarray(k, np.float32),
+                                      np.ascontiguousarray(v, np.float32), pos, out)
+        assert rc == 0
+        return out
+
+    def close(self):
+        if self.h:
+            self.L.pref_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
