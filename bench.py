@@ -1,0 +1,423 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 attention step (decode attention HBM GB/s).
+
+Workload ("Qwen2.5-7B-shape batched decode"):
+28 layers, 28 q heads, 4 KV heads, head_dim 128, RoPE theta 1e6 (NeoX),
+64 sequences with cached lengths uniform in [1024, 8192] (seeded), one new token
+per sequence per step.  A step is one decode attention pass over all 28 layers
+for all 64 sequences: per layer, the new k/v row is appended to each sequence's
+FP16 cache and every q head attends over rows 0..pos.  The cache (15.8 GiB of
+visited K/V per step, 30 GB allocated) is far larger than L2, so no flush is
+needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun (N > 1) every rank runs its own 64 sequences (weak scaling; no
+collective on the data path) and rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOAD = dict(name="qwen2.5-7b-batched-decode", n_layers=28, n_heads=28, n_kv_heads=4, head_dim=128,
+                rope_base=1e6, n_seqs=64, len_lo=1024, len_hi=8192, seed=0)
+METRIC = "decode attn HBM GB/s"
+
+
+def seq_lengths(rank: int) -> np.ndarray:
+    """Cached lengths per sequence; the new token sits at pos = length."""
+    rng = np.random.default_rng(WORKLOAD["seed"] + rank)
+    return rng.integers(WORKLOAD["len_lo"], WORKLOAD["len_hi"] + 1, WORKLOAD["n_seqs"]).astype(np.int32)
+
+
+def step_bytes(lens: np.ndarray, n_layers: int, kv_dim: int) -> int:
+    """Algorithmic bytes of one step: K and V rows 0..pos of every sequence, every layer."""
+    return int(n_layers * np.sum(2 * (lens.astype(np.int64) + 1) * kv_dim * 2))
+
+
+def measured_peaks() -> tuple[float, str]:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profiled_traffic() -> float | None:
+    """DRAM bytes per attention launch from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "decode_attn_traffic.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["dram_bytes_per_launch"])
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region (NVML reads only; nothing is changed)
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting"}
+
+    def __init__(self, device_index: int, pci_bus_id: str | None):
+        self.samples: list[int] = []
+        self.reasons: set[str] = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            h = None
+            if pci_bus_id:
+                try:
+                    h = pynvml.nvmlDeviceGetHandleByPciBusId(pci_bus_id)
+                except Exception:
+                    h = None
+            self.h = h if h is not None else pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.005)
+
+    def __enter__(self):
+        if self.nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the reference's attention loop (oracle/_ref) or the oracle port
+# ---------------------------------------------------------------------------
+
+def cpu_attention_runner():
+    """Returns (run(B-seq sample) -> seconds, kind).  Test/baseline use only."""
+    from oracle import pyoracle
+    if os.path.exists(pyoracle.REF_SO):
+        return pyoracle.RefHarness(), "reference"
+    pyoracle.build()
+    return pyoracle.Oracle(), "port"
+
+
+def make_host_sample(lens: np.ndarray, kv_dim: int, rng: np.random.Generator):
+    S = int(lens.max()) + 1
+    kcs, vcs = [], []
+    for n in lens:
+        kc = np.zeros((S, kv_dim), np.uint16)
+        vc = np.zeros((S, kv_dim), np.uint16)
+        kc[:n] = (rng.standard_normal((int(n), kv_dim), dtype=np.float32) * 0.5).astype(np.float16).view(np.uint16)
+        vc[:n] = (rng.standard_normal((int(n), kv_dim), dtype=np.float32) * 0.5).astype(np.float16).view(np.uint16)
+        kcs.append(kc)
+        vcs.append(vc)
+    return S, kcs, vcs
+
+
+_ROPE_CACHE: dict = {}
+
+
+def run_cpu_sample(runner, lens, S, kcs, vcs, n_threads, rng):
+    """One decode attention pass of one layer over len(lens) sequences on the host."""
+    from oracle.pyoracle import Oracle
+    w = WORKLOAD
+    hq, hkv, hd = w["n_heads"], w["n_kv_heads"], w["head_dim"]
+    B = len(lens)
+    if S not in _ROPE_CACHE:  # the table is bit-identical to the reference's (tests pin it)
+        _ROPE_CACHE[S] = Oracle().rope_table(S, hd, w["rope_base"])
+    cos_t, sin_t = _ROPE_CACHE[S]
+    q = rng.standard_normal((B, hq * hd), dtype=np.float32)
+    k = rng.standard_normal((B, hkv * hd), dtype=np.float32)
+    v = rng.standard_normal((B, hkv * hd), dtype=np.float32)
+    pos = lens.astype(np.int32)
+    t0 = time.perf_counter()
+    if isinstance(runner, Oracle):
+        runner.decode_batch(hq, hkv, hd, 0, q, k, v, None, None, cos_t, sin_t, kcs, vcs, pos, n_threads)
+    else:
+        runner.attn_decode_batch(hq, hkv, hd, 0, q, k, v, None, None, cos_t, sin_t, kcs, vcs, pos, n_threads)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(lens: np.ndarray) -> dict:
+    """All host threads over a bounded sample: the 64 sequences of one layer."""
+    w = WORKLOAD
+    kvd = w["n_kv_heads"] * w["head_dim"]
+    rng = np.random.default_rng(1234)
+    runner, kind = cpu_attention_runner()
+    S, kcs, vcs = make_host_sample(lens, kvd, rng)
+    cores = os.cpu_count() or 1
+    secs = run_cpu_sample(runner, lens, S, kcs, vcs, cores, rng)
+    gbs = step_bytes(lens, 1, kvd) / secs / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+            "sample": f"1 of 28 layers x {len(lens)} sequences (same lengths), {secs:.2f} s wall, "
+                      f"one host thread per sequence; the reference's attention loop (cpp/model.hpp:326-418) "
+                      f"compiled from its sources"}
+
+
+def run_reference_arm(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    w = WORKLOAD
+    kvd = w["n_kv_heads"] * w["head_dim"]
+    lens = seq_lengths(0)
+    runner, kind = cpu_attention_runner()
+    rng = np.random.default_rng(1234)
+    cores = os.cpu_count() or 1
+    # size each step so that warmup+steps end within ~2 minutes
+    n_sample = len(lens)
+    S, kcs, vcs = make_host_sample(lens[:n_sample], kvd, rng)
+    probe = run_cpu_sample(runner, lens[:8], S, kcs[:8], vcs[:8], cores, rng)
+    per_seq = probe / 8 * min(8, cores) / max(1, min(n_sample, cores))
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    n_sample = int(max(1, min(len(lens), budget / max(per_seq, 1e-6))))
+    sample_lens = lens[:n_sample]
+    for _ in range(args.warmup):
+        run_cpu_sample(runner, sample_lens, S, kcs[:n_sample], vcs[:n_sample], cores, rng)
+    total = 0.0
+    for _ in range(args.steps):
+        total += run_cpu_sample(runner, sample_lens, S, kcs[:n_sample], vcs[:n_sample], cores, rng)
+    nbytes = step_bytes(sample_lens, 1, kvd) * args.steps
+    gbs = nbytes / total / 1e9
+    line = {"metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32 (fp16 cache)", "data": "synthetic",
+            "config": {"workload": w["name"] + " (CPU sample)", "layers_per_step": 1, "sequences": n_sample,
+                       "heads": [w["n_heads"], w["n_kv_heads"], w["head_dim"]]},
+            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+                             "sample": f"{n_sample} sequences x 1 layer per step"},
+            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+
+    from picolm_qwen_b200 import abi
+    from picolm_qwen_b200.runtime import AttnState, stream_handle
+
+    w = WORKLOAD
+    L, hq, hkv, hd = w["n_layers"], w["n_heads"], w["n_kv_heads"], w["head_dim"]
+    kvd, qd = hkv * hd, hq * hd
+    lens = seq_lengths(rank)
+    B = len(lens)
+    S = int(lens.max()) + 1
+    max_ctx = S
+    cfg = abi.Config.make(L, hq, hkv, hd, S, w["rope_base"], abi.ROPE_NEOX)
+    st = AttnState(cfg, n_seqs=B, device=dev, max_ctx=max_ctx)
+    # synthetic cache rows 0..len-1, N(0, 0.5^2) in fp16
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    for b in range(B):
+        n = int(lens[b])
+        for cache in (st.k_cache, st.v_cache):
+            cache[b, :, :n].copy_((torch.randn((L, n, kvd), generator=g, device=dev) * 0.5)
+                                  .to(torch.float16).view(torch.int16))
+    q = torch.randn((L, B, qd), generator=g, device=dev)
+    k = torch.randn((L, B, kvd), generator=g, device=dev)
+    v = torch.randn((L, B, kvd), generator=g, device=dev)
+    out = torch.empty((L, B, qd), device=dev)
+    pos = torch.from_numpy(lens).to(dev)
+    stream = torch.cuda.current_stream(dev)
+    sh = stream_handle(stream)
+    lib = abi.lib()
+    cfgp = C.byref(cfg)
+    common = (st.rope_cos.data_ptr(), st.rope_sin.data_ptr(), st.k_ptrs.data_ptr(), st.v_ptrs.data_ptr(),
+              pos.data_ptr())
+
+    def call(l, stages, qq=None, kk=None, vv=None, oo=None):
+        qq = q[l] if qq is None else qq
+        kk = k[l] if kk is None else kk
+        vv = v[l] if vv is None else vv
+        oo = out[l] if oo is None else oo
+        s = lib.picoattn_decode_staged(cfgp, l, B, max_ctx, qq.data_ptr(), kk.data_ptr(), vv.data_ptr(), None, None,
+                                       *common, oo.data_ptr(), st.workspace.data_ptr(), st.workspace.numel(), sh,
+                                       stages)
+        if s != 0:
+            raise abi.PicoAttnError(s, "picoattn_decode_staged")
+
+    def one_step(ev_pairs=None):
+        for l in range(L):
+            if ev_pairs is None:
+                call(l, abi.STAGE_ALL)
+            else:
+                a, b_ = ev_pairs[l]
+                call(l, abi.STAGE_PREPARE)
+                a.record(stream)
+                call(l, abi.STAGE_ATTEND)
+                b_.record(stream)
+                call(l, abi.STAGE_COMBINE)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        one_step()
+    barrier()
+    assert st.status() == 0
+    props = torch.cuda.get_device_properties(dev)
+    pci = getattr(props, "pci_bus_id", None)
+    if pci is not None and not isinstance(pci, str):
+        pci = None
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+          for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with ClockSampler(local, pci) as clk:
+        t_start.record(stream)
+        for i in range(args.steps):
+            one_step(ev[i])
+        t_end.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    elapsed_ms = t_start.elapsed_time(t_end)
+    attn_ms = [a.elapsed_time(b_) for step in ev for (a, b_) in step]
+    status = st.status()
+    if status != 0:
+        raise RuntimeError(f"device status {status:#x} after the timed region")
+
+    # e2e through the C ABI with pinned host buffers
+    hq_host = q.cpu().pin_memory()
+    hk_host = k.cpu().pin_memory()
+    hv_host = v.cpu().pin_memory()
+    hout = torch.empty((L, B, qd), dtype=torch.float32).pin_memory()
+    dq, dk, dv, dout = torch.empty_like(q[0]), torch.empty_like(k[0]), torch.empty_like(v[0]), torch.empty_like(out[0])
+
+    def e2e_step():
+        for l in range(L):
+            dq.copy_(hq_host[l], non_blocking=True)
+            dk.copy_(hk_host[l], non_blocking=True)
+            dv.copy_(hv_host[l], non_blocking=True)
+            call(l, abi.STAGE_ALL, dq, dk, dv, dout)
+            hout[l].copy_(dout, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+    barrier()
+
+    nbytes = step_bytes(lens, L, kvd)
+    times = torch.tensor([elapsed_ms, e2e_ms, float(nbytes)], dtype=torch.float64, device=dev)
+    if world > 1:
+        tmax = times.clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        tsum = times.clone()
+        dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
+        elapsed_ms, e2e_ms = float(tmax[0]), float(tmax[1])
+        total_bytes = float(tsum[2])
+    else:
+        total_bytes = float(nbytes)
+
+    if rank == 0:
+        value = total_bytes * args.steps / (elapsed_ms / 1e3) / 1e9
+        e2e_value = total_bytes * args.steps / (e2e_ms / 1e3) / 1e9
+        per_launch = nbytes / L
+        mean_attn_ms = float(np.mean(attn_ms))
+        achieved = per_launch / (mean_attn_ms / 1e3) / 1e9
+        peak, peak_kind = measured_peaks()
+        clocks = clk.summary()
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16 cache, f32 accumulate", "data": "synthetic",
+            "config": {"workload": w["name"], "layers": L, "sequences_per_gpu": B,
+                       "heads_q_kv_dim": [hq, hkv, hd], "cached_len_range": [w["len_lo"], w["len_hi"]],
+                       "bytes_per_step_per_gpu": nbytes, "l2": "inputs (15.8 GiB/step) larger than L2, no flush",
+                       "parallelism": f"sequence-sharded x{world}" if world > 1 else "single GPU"},
+            "roofline": {"bound": "hbm", "kernel": "decode_attn_kernel<128>", "achieved": round(achieved, 1),
+                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": profiled_traffic(), "algorithmic_bytes_per_launch": per_launch,
+                         "mean_launch_ms": round(mean_attn_ms, 5)},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": int(L * (hq_host[0].numel() + 2 * hk_host[0].numel()) * 4),
+                    "d2h_bytes_per_step": int(L * hout[0].numel() * 4)},
+            "gpu_launches": 3 * L * args.steps,
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu:
+            try:
+                line["cpu_baseline"] = cpu_baseline(lens)
+            except Exception as e:  # the CPU leg never hides a GPU number
+                line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,187 @@
+/*
+ * picoattn.h -- C ABI of the B200 (sm_100a) attention step.
+ *
+ * The reference engine (rain1201/picolm_qwen) runs its attention step inline in
+ * the forward functions; it has no callable seam besides the RoPE function
+ * pointer (RopeFn, cpp/model.hpp:176).  This ABI is the seam: the block
+ *
+ *     QK-RMSNorm  (cpp/model.hpp:326-333, 342-349)
+ *     RoPE        (cpp/model.hpp:351-352 -> cpp/tensor.hpp:201-369)
+ *     fp16 K/V store at row pos   (cpp/model.hpp:354-373)
+ *     online-softmax GQA attention over rows 0..pos (cpp/model.hpp:375-418)
+ *
+ * of Model::forward (decode) and of Model::forward_batch (prefill,
+ * cpp/model.hpp:507-593) becomes one call.  The caller keeps the reference's
+ * data: q/k/v as produced by the projections, the per-layer FP16 KV cache in the
+ * reference layout (uint16 [n_layers][max_seq_len][n_kv_heads*head_dim],
+ * cpp/model.hpp:1003-1006), the host-built RoPE table ([max_seq_len][head_dim/2],
+ * cpp/model.hpp:1008-1017) and the attention output xb [n_heads*head_dim].
+ *
+ * Conventions
+ *   - Every pointer argument is device memory unless its comment says "host".
+ *   - The caller owns every buffer (as RunState owns them in the reference,
+ *     cpp/model.hpp:158-174); the library allocates nothing on these paths.
+ *   - Every entry point returns PICOATTN_OK (0) or a negative status; none
+ *     exits, throws or traps.  Errors that only the device can see (a position
+ *     read from device memory that is out of range, a misaligned cache
+ *     pointer) set a sticky bit in the workspace header, read back with
+ *     picoattn_workspace_status().
+ *   - Calls are asynchronous on `stream` and re-entrant per stream.
+ *   - Kernels are built for sm_100a only; on any other device calls return
+ *     PICOATTN_EDEVICE.
+ */
+#ifndef PICOATTN_H
+#define PICOATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* A cudaStream_t; NULL is the legacy default stream. */
+typedef struct CUstream_st* picoattn_stream_t;
+
+/* Status codes. */
+#define PICOATTN_OK            0
+#define PICOATTN_EINVAL       -1  /* null pointer, bad count, inconsistent shape */
+#define PICOATTN_EUNSUPPORTED -2  /* shape the kernels do not implement */
+#define PICOATTN_ERANGE       -3  /* a position outside [0, max_seq_len) */
+#define PICOATTN_ENOSPACE     -4  /* workspace smaller than the *_workspace_size() */
+#define PICOATTN_ECUDA        -5  /* CUDA runtime error */
+#define PICOATTN_ENCCL        -6  /* NCCL error */
+#define PICOATTN_ETIMEOUT     -7  /* a bounded wait ran out */
+#define PICOATTN_EDEVICE      -8  /* current device is not sm_100 */
+#define PICOATTN_EDEVSTATUS   -9  /* a kernel flagged bad input (see workspace status) */
+
+/* Device-side sticky status bits (picoattn_workspace_status). */
+#define PICOATTN_DEV_BAD_POS      0x1u  /* pos[b] < 0, >= max_seq_len or >= max_ctx */
+#define PICOATTN_DEV_MISALIGNED   0x2u  /* a cache pointer not 16-byte aligned */
+#define PICOATTN_DEV_TIMEOUT      0x4u  /* a bounded barrier wait gave up */
+
+/* RoPE pairing.  NEOX = TensorOps::rope_qwen (cpp/tensor.hpp:201-283, element i
+ * with i+hd/2).  INTERLEAVED = rope_llama's scalar definition (element 2i with
+ * 2i+1, picolm/tensor.c:247-293).  The reference picks one from the model file
+ * name (cpp/picolm.cpp:181-186); here it is explicit. */
+#define PICOATTN_ROPE_NEOX        0
+#define PICOATTN_ROPE_INTERLEAVED 1
+
+/* Element type of q/k/v inputs. */
+#define PICOATTN_DTYPE_F32 0
+#define PICOATTN_DTYPE_F16 1
+
+/* Model shape as the reference's config map holds it (cpp/model.hpp:33-47). */
+typedef struct {
+    int32_t n_layers;        /* cfg::N_LAYERS  */
+    int32_t n_heads;         /* cfg::N_HEADS   */
+    int32_t n_kv_heads;      /* cfg::N_KV_HEADS; n_heads % n_kv_heads == 0 */
+    int32_t head_dim;        /* cfg::HEAD_DIM; 64 or 128 */
+    int32_t max_seq_len;     /* cfg::MAX_SEQ_LEN: cache rows per layer */
+    float   rope_freq_base;  /* cfg::ROPE_FREQ_BASE */
+    int32_t rope_mode;       /* PICOATTN_ROPE_* */
+    float   qk_norm_eps;     /* 1e-6 in the reference (cpp/tensor.hpp:162) */
+} picoattn_config_t;
+
+/* ---------------------------------------------------------------------- */
+/* Host helpers                                                            */
+/* ---------------------------------------------------------------------- */
+
+/* Library version, major*10000 + minor*100 + patch. */
+int32_t picoattn_version(void);
+
+/* Text for a status code. */
+const char* picoattn_strerror(int32_t status);
+
+/* Validates a config; PICOATTN_OK, EINVAL or EUNSUPPORTED. */
+int32_t picoattn_config_check(const picoattn_config_t* cfg);
+
+/* Fills HOST arrays cos_out/sin_out [max_seq_len][head_dim/2] exactly as
+ * Model::allocate_run_state does (cpp/model.hpp:1008-1017):
+ *   theta = (float)pos / powf(base, (float)(2i)/(float)head_dim); cosf/sinf.
+ * The kernels read this table instead of evaluating sin/cos on the device so
+ * that positions up to 131071 rotate exactly as the reference rotates them. */
+int32_t picoattn_rope_table(const picoattn_config_t* cfg, float* cos_out, float* sin_out);
+
+/* Returns PICOATTN_OK when the current CUDA device is sm_100. */
+int32_t picoattn_device_check(void);
+
+/* Workspace header: zero the sticky device-status word.  Call once after
+ * allocating a workspace (cudaMemset of the first 256 bytes also does). */
+int32_t picoattn_workspace_init(void* workspace, size_t workspace_bytes, picoattn_stream_t stream);
+
+/* Synchronises `stream`, reads the sticky device-status bits into *status_out
+ * (host) and clears them. */
+int32_t picoattn_workspace_status(void* workspace, picoattn_stream_t stream, uint32_t* status_out);
+
+/* ---------------------------------------------------------------------- */
+/* Decode (Model::forward, cpp/model.hpp:326-418)                          */
+/* ---------------------------------------------------------------------- */
+
+/* Workspace bytes for picoattn_decode with n_seqs sequences whose longest
+ * attended length (pos+1) is at most max_ctx. */
+size_t picoattn_decode_workspace_size(const picoattn_config_t* cfg, int32_t n_seqs, int32_t max_ctx);
+
+/*
+ * One decode step of layer `layer` for n_seqs independent sequences (n_seqs = 1
+ * is the reference's single-sequence forward(token, pos)).
+ *   q        [n_seqs][n_heads*head_dim]    fp32, projection output (state.q)
+ *   k, v     [n_seqs][n_kv_heads*head_dim] fp32 (state.xb2 before each store)
+ *   q_norm_w, k_norm_w  [head_dim] fp32 per-layer QK-RMSNorm weights, or both
+ *            NULL when the layer has none (cpp/model.hpp:326-349)
+ *   rope_cos, rope_sin  [max_seq_len][head_dim/2] fp32 (picoattn_rope_table)
+ *   k_cache, v_cache    device array of n_seqs device pointers; entry b is
+ *            sequence b's cache base, uint16 [n_layers][max_seq_len][kv_dim],
+ *            16-byte aligned
+ *   pos      [n_seqs] int32 device: the position of the new token; row pos of
+ *            this layer is written and rows 0..pos are attended
+ *   max_ctx  host upper bound on pos[b]+1 over the batch (sizes the launch)
+ *   out      [n_seqs][n_heads*head_dim] fp32 attention output (state.xb)
+ * Replaces cpp/model.hpp:326-418 (C engine: picolm/model.c:725-825).
+ */
+int32_t picoattn_decode(const picoattn_config_t* cfg, int32_t layer, int32_t n_seqs, int32_t max_ctx,
+                        const float* q, const float* k, const float* v,
+                        const float* q_norm_w, const float* k_norm_w,
+                        const float* rope_cos, const float* rope_sin,
+                        uint16_t* const* k_cache, uint16_t* const* v_cache,
+                        const int32_t* pos, float* out,
+                        void* workspace, size_t workspace_bytes, picoattn_stream_t stream);
+
+/* Stage bits for picoattn_decode_staged. */
+#define PICOATTN_STAGE_PREPARE 0x1u  /* QK-norm, RoPE, fp16 append of row pos, rotated q to workspace */
+#define PICOATTN_STAGE_ATTEND  0x2u  /* split-KV attention partials into the workspace */
+#define PICOATTN_STAGE_COMBINE 0x4u  /* log-sum-exp merge of the partials into out */
+#define PICOATTN_STAGE_ALL     0x7u
+
+/*
+ * picoattn_decode split into its three kernels; `stages` selects which run
+ * (in the order above).  Stages communicate through the workspace, so a call
+ * with ATTEND must follow one with PREPARE on the same workspace and stream,
+ * with the same arguments.  Lets a caller put events between the kernels or
+ * overlap other work with them.  picoattn_decode == stages PICOATTN_STAGE_ALL.
+ */
+int32_t picoattn_decode_staged(const picoattn_config_t* cfg, int32_t layer, int32_t n_seqs, int32_t max_ctx,
+                               const float* q, const float* k, const float* v,
+                               const float* q_norm_w, const float* k_norm_w,
+                               const float* rope_cos, const float* rope_sin,
+                               uint16_t* const* k_cache, uint16_t* const* v_cache,
+                               const int32_t* pos, float* out,
+                               void* workspace, size_t workspace_bytes, picoattn_stream_t stream,
+                               uint32_t stages);
+
+/*
+ * Single-sequence decode with a host position, the shape of the reference's
+ * Model::forward(token, pos) call site (cpp/model.hpp:288): k_cache/v_cache are
+ * the sequence's cache bases (device), pos is a host int.
+ */
+int32_t picoattn_decode_one(const picoattn_config_t* cfg, int32_t layer, int32_t pos,
+                            const float* q, const float* k, const float* v,
+                            const float* q_norm_w, const float* k_norm_w,
+                            const float* rope_cos, const float* rope_sin,
+                            uint16_t* k_cache, uint16_t* v_cache, float* out,
+                            void* workspace, size_t workspace_bytes, picoattn_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PICOATTN_H */

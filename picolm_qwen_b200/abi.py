@@ -1,0 +1,132 @@
+"""ctypes binding of the C ABI in include/picoattn.h.
+
+This is the reference-side binding a Python host would add: plain pointers and
+sizes, no framework types.  ``lib()`` loads the in-tree ``libpicoattn.so`` and
+raises if it is missing; nothing here computes anything itself.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "libpicoattn.so")
+HEADER = os.path.join(os.path.dirname(PKG), "include", "picoattn.h")
+
+PICOATTN_OK = 0
+PICOATTN_EINVAL = -1
+PICOATTN_EUNSUPPORTED = -2
+PICOATTN_ERANGE = -3
+PICOATTN_ENOSPACE = -4
+PICOATTN_ECUDA = -5
+PICOATTN_ENCCL = -6
+PICOATTN_ETIMEOUT = -7
+PICOATTN_EDEVICE = -8
+PICOATTN_EDEVSTATUS = -9
+
+DEV_BAD_POS = 0x1
+DEV_MISALIGNED = 0x2
+DEV_TIMEOUT = 0x4
+
+STAGE_PREPARE = 0x1
+STAGE_ATTEND = 0x2
+STAGE_COMBINE = 0x4
+STAGE_ALL = 0x7
+
+ROPE_NEOX = 0
+ROPE_INTERLEAVED = 1
+DTYPE_F32 = 0
+DTYPE_F16 = 1
+
+
+class Config(C.Structure):
+    """picoattn_config_t."""
+    _fields_ = [
+        ("n_layers", C.c_int32),
+        ("n_heads", C.c_int32),
+        ("n_kv_heads", C.c_int32),
+        ("head_dim", C.c_int32),
+        ("max_seq_len", C.c_int32),
+        ("rope_freq_base", C.c_float),
+        ("rope_mode", C.c_int32),
+        ("qk_norm_eps", C.c_float),
+    ]
+
+    @classmethod
+    def make(cls, n_layers, n_heads, n_kv_heads, head_dim, max_seq_len, rope_freq_base,
+             rope_mode=ROPE_NEOX, qk_norm_eps=1e-6):
+        return cls(n_layers, n_heads, n_kv_heads, head_dim, max_seq_len, rope_freq_base,
+                   rope_mode, qk_norm_eps)
+
+    @property
+    def kv_dim(self) -> int:
+        return self.n_kv_heads * self.head_dim
+
+    @property
+    def q_dim(self) -> int:
+        return self.n_heads * self.head_dim
+
+
+_P = C.c_void_p
+_I = C.c_int32
+_Z = C.c_size_t
+_CFG = C.POINTER(Config)
+
+# name -> (restype, argtypes); every function declared in include/picoattn.h
+PROTOTYPES = {
+    "picoattn_version": (_I, []),
+    "picoattn_strerror": (C.c_char_p, [_I]),
+    "picoattn_config_check": (_I, [_CFG]),
+    "picoattn_rope_table": (_I, [_CFG, _P, _P]),
+    "picoattn_device_check": (_I, []),
+    "picoattn_workspace_init": (_I, [_P, _Z, _P]),
+    "picoattn_workspace_status": (_I, [_P, _P, C.POINTER(C.c_uint32)]),
+    "picoattn_decode_workspace_size": (_Z, [_CFG, _I, _I]),
+    "picoattn_decode": (_I, [_CFG, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P]),
+    "picoattn_decode_staged": (_I, [_CFG, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P,
+                                   C.c_uint32]),
+    "picoattn_decode_one": (_I, [_CFG, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P]),
+}
+
+_lib = None
+
+
+class PicoAttnError(RuntimeError):
+    def __init__(self, status: int, what: str = ""):
+        msg = lib().picoattn_strerror(status).decode()
+        super().__init__(f"{what}: {msg} ({status})" if what else f"{msg} ({status})")
+        self.status = status
+
+
+def lib() -> C.CDLL:
+    """The loaded libpicoattn.so.  Raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(
+                f"{LIB_PATH} is missing: build it with `python -m picolm_qwen_b200.build`")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in PROTOTYPES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(status: int, what: str = "") -> None:
+    if status != PICOATTN_OK:
+        raise PicoAttnError(status, what)
+
+
+def declared_functions() -> list[str]:
+    """Function names declared in include/picoattn.h."""
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[A-Za-z_][A-Za-z0-9_]*\s*\*?\s*(picoattn_[a-z0-9_]+)\s*\(",
+                                 text, re.M)))
+
+
+def ptr(t) -> int | None:
+    """Device/host address of a torch tensor (or None)."""
+    return None if t is None else t.data_ptr()

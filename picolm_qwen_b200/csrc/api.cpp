@@ -1,0 +1,197 @@
+// api.cpp -- the extern "C" boundary declared in include/picoattn.h.
+//
+// Host-side argument checking, workspace carving, the RoPE table builder and
+// dispatch to the CUDA launchers.  No allocation happens on the call paths.
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+
+#include <cuda_runtime.h>
+
+#include "picoattn.h"
+#include "picoattn_internal.h"
+
+using namespace picoattn;
+
+namespace {
+
+int32_t cuda_status(cudaError_t e) { return e == cudaSuccess ? PICOATTN_OK : PICOATTN_ECUDA; }
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+// Cached per process: the sm_100 check runs once per device.
+int32_t device_ok() {
+    static int checked_dev = -1;
+    static int32_t verdict = PICOATTN_EDEVICE;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return PICOATTN_ECUDA;
+    if (dev == checked_dev) return verdict;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return PICOATTN_ECUDA;
+    verdict = prop.major == 10 && prop.minor == 0 ? PICOATTN_OK : PICOATTN_EDEVICE;
+    checked_dev = dev;
+    return verdict;
+}
+
+int32_t decode_common(const picoattn_config_t* cfg, int32_t layer, int32_t n_seqs, int32_t max_ctx,
+                      const float* q, const float* k, const float* v, const float* qn, const float* kn,
+                      const float* rc, const float* rs, uint16_t* const* kcp, uint16_t* const* vcp,
+                      uint16_t* kc1, uint16_t* vc1, const int32_t* pos_dev, int32_t pos_host, float* out,
+                      void* ws, size_t ws_bytes, cudaStream_t stream, uint32_t stages) {
+    int32_t st = picoattn_config_check(cfg);
+    if (stages == 0 || (stages & ~PICOATTN_STAGE_ALL)) return PICOATTN_EINVAL;
+    if (st != PICOATTN_OK) return st;
+    if (layer < 0 || layer >= cfg->n_layers || n_seqs <= 0) return PICOATTN_EINVAL;
+    if (!q || !k || !v || !rc || !rs || !out || !ws) return PICOATTN_EINVAL;
+    if ((qn == nullptr) != (kn == nullptr)) return PICOATTN_EINVAL;
+    if (kcp == nullptr && (kc1 == nullptr || vc1 == nullptr)) return PICOATTN_EINVAL;
+    if (kcp != nullptr && vcp == nullptr) return PICOATTN_EINVAL;
+    if (kc1 && (!aligned16(kc1) || !aligned16(vc1))) return PICOATTN_EINVAL;
+    if (max_ctx <= 0 || max_ctx > cfg->max_seq_len) return PICOATTN_ERANGE;
+    if (!pos_dev && (pos_host < 0 || pos_host >= cfg->max_seq_len)) return PICOATTN_ERANGE;
+    DecodePlan plan;
+    if (!make_decode_plan(*cfg, n_seqs, max_ctx, &plan)) return PICOATTN_EUNSUPPORTED;
+    if (ws_bytes < plan.ws_total || !aligned16(ws)) return PICOATTN_ENOSPACE;
+    st = device_ok();
+    if (st != PICOATTN_OK) return st;
+
+    uint8_t* w = static_cast<uint8_t*>(ws);
+    DecodeArgs a{};
+    a.hq = cfg->n_heads;
+    a.hkv = cfg->n_kv_heads;
+    a.g = a.hq / a.hkv;
+    a.hd = cfg->head_dim;
+    a.kvd = a.hkv * a.hd;
+    a.max_seq = cfg->max_seq_len;
+    a.layer = layer;
+    a.n_seqs = n_seqs;
+    a.max_ctx = max_ctx;
+    a.rope_mode = cfg->rope_mode;
+    a.eps = cfg->qk_norm_eps;
+    a.q = q, a.k = k, a.v = v, a.qn_w = qn, a.kn_w = kn, a.rope_cos = rc, a.rope_sin = rs;
+    a.kc_ptrs = kcp, a.vc_ptrs = vcp, a.kc_one = kc1, a.vc_one = vc1;
+    a.pos_dev = pos_dev, a.pos_host = pos_host, a.out = out;
+    a.status = reinterpret_cast<unsigned int*>(w);
+    a.q_rot = reinterpret_cast<float*>(w + plan.ws_qrot);
+    a.part_ml = reinterpret_cast<float*>(w + plan.ws_ml);
+    a.part_o = reinterpret_cast<float*>(w + plan.ws_o);
+    a.chunk_rows = plan.chunk_rows;
+    a.tile_rows = plan.tile_rows;
+    a.stages = plan.stages;
+    a.warps_per_head = plan.warps_per_head;
+    a.compute_warps = plan.compute_warps;
+    a.max_parts = plan.max_parts;
+    return cuda_status(launch_decode(a, plan, stream, stages));
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t picoattn_version(void) { return 100; }
+
+const char* picoattn_strerror(int32_t s) {
+    switch (s) {
+        case PICOATTN_OK: return "ok";
+        case PICOATTN_EINVAL: return "invalid argument";
+        case PICOATTN_EUNSUPPORTED: return "unsupported shape";
+        case PICOATTN_ERANGE: return "position out of range";
+        case PICOATTN_ENOSPACE: return "workspace too small or misaligned";
+        case PICOATTN_ECUDA: return "CUDA error";
+        case PICOATTN_ENCCL: return "NCCL error";
+        case PICOATTN_ETIMEOUT: return "timed out";
+        case PICOATTN_EDEVICE: return "device is not sm_100";
+        case PICOATTN_EDEVSTATUS: return "a kernel flagged bad input";
+        default: return "unknown status";
+    }
+}
+
+int32_t picoattn_config_check(const picoattn_config_t* c) {
+    if (!c) return PICOATTN_EINVAL;
+    if (c->n_layers <= 0 || c->n_heads <= 0 || c->n_kv_heads <= 0 || c->max_seq_len <= 0) return PICOATTN_EINVAL;
+    if (c->n_heads % c->n_kv_heads != 0) return PICOATTN_EINVAL;
+    if (c->head_dim <= 0 || c->head_dim % 2 != 0) return PICOATTN_EINVAL;
+    if (c->rope_mode != PICOATTN_ROPE_NEOX && c->rope_mode != PICOATTN_ROPE_INTERLEAVED) return PICOATTN_EINVAL;
+    if (!(c->qk_norm_eps >= 0.f) || !(c->rope_freq_base > 0.f)) return PICOATTN_EINVAL;
+    if (c->head_dim != 64 && c->head_dim != 128) return PICOATTN_EUNSUPPORTED;
+    const int hkv = c->n_kv_heads;
+    if (!(hkv == 1 || hkv == 2 || hkv == 4 || hkv == 8)) return PICOATTN_EUNSUPPORTED;
+    if (c->n_heads / hkv > 16) return PICOATTN_EUNSUPPORTED;
+    return PICOATTN_OK;
+}
+
+int32_t picoattn_rope_table(const picoattn_config_t* c, float* cos_out, float* sin_out) {
+    if (!c || !cos_out || !sin_out || c->max_seq_len <= 0 || c->head_dim <= 0 || c->head_dim % 2) return PICOATTN_EINVAL;
+    const int half = c->head_dim / 2;
+    const float base = c->rope_freq_base;
+    // Same float expression as Model::allocate_run_state (cpp/model.hpp:1013):
+    // powf, a float division and cosf/sinf from the C library.
+    for (int p = 0; p < c->max_seq_len; p++) {
+        for (int i = 0; i < half; i++) {
+            const float theta = (float)p / powf(base, (float)(2 * i) / (float)c->head_dim);
+            cos_out[(size_t)p * half + i] = cosf(theta);
+            sin_out[(size_t)p * half + i] = sinf(theta);
+        }
+    }
+    return PICOATTN_OK;
+}
+
+int32_t picoattn_device_check(void) { return device_ok(); }
+
+int32_t picoattn_workspace_init(void* ws, size_t ws_bytes, picoattn_stream_t stream) {
+    if (!ws || ws_bytes < kWsHeaderBytes) return PICOATTN_EINVAL;
+    return cuda_status(cudaMemsetAsync(ws, 0, kWsHeaderBytes, (cudaStream_t)stream));
+}
+
+int32_t picoattn_workspace_status(void* ws, picoattn_stream_t stream, uint32_t* status_out) {
+    if (!ws || !status_out) return PICOATTN_EINVAL;
+    unsigned int v = 0;
+    cudaError_t e = cudaMemcpyAsync(&v, ws, sizeof v, cudaMemcpyDeviceToHost, (cudaStream_t)stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(ws, 0, sizeof v, (cudaStream_t)stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+    *status_out = v;
+    return cuda_status(e);
+}
+
+size_t picoattn_decode_workspace_size(const picoattn_config_t* cfg, int32_t n_seqs, int32_t max_ctx) {
+    if (picoattn_config_check(cfg) != PICOATTN_OK || n_seqs <= 0 || max_ctx <= 0) return 0;
+    DecodePlan plan;
+    if (!make_decode_plan(*cfg, n_seqs, max_ctx, &plan)) return 0;
+    return plan.ws_total;
+}
+
+int32_t picoattn_decode(const picoattn_config_t* cfg, int32_t layer, int32_t n_seqs, int32_t max_ctx,
+                        const float* q, const float* k, const float* v, const float* q_norm_w,
+                        const float* k_norm_w, const float* rope_cos, const float* rope_sin,
+                        uint16_t* const* k_cache, uint16_t* const* v_cache, const int32_t* pos, float* out,
+                        void* workspace, size_t workspace_bytes, picoattn_stream_t stream) {
+    return picoattn_decode_staged(cfg, layer, n_seqs, max_ctx, q, k, v, q_norm_w, k_norm_w, rope_cos, rope_sin,
+                                  k_cache, v_cache, pos, out, workspace, workspace_bytes, stream,
+                                  PICOATTN_STAGE_ALL);
+}
+
+int32_t picoattn_decode_staged(const picoattn_config_t* cfg, int32_t layer, int32_t n_seqs, int32_t max_ctx,
+                               const float* q, const float* k, const float* v, const float* q_norm_w,
+                               const float* k_norm_w, const float* rope_cos, const float* rope_sin,
+                               uint16_t* const* k_cache, uint16_t* const* v_cache, const int32_t* pos,
+                               float* out, void* workspace, size_t workspace_bytes, picoattn_stream_t stream,
+                               uint32_t stages) {
+    if (!k_cache || !v_cache || !pos) return PICOATTN_EINVAL;
+    return decode_common(cfg, layer, n_seqs, max_ctx, q, k, v, q_norm_w, k_norm_w, rope_cos, rope_sin, k_cache,
+                         v_cache, nullptr, nullptr, pos, 0, out, workspace, workspace_bytes,
+                         (cudaStream_t)stream, stages);
+}
+
+int32_t picoattn_decode_one(const picoattn_config_t* cfg, int32_t layer, int32_t pos, const float* q,
+                            const float* k, const float* v, const float* q_norm_w, const float* k_norm_w,
+                            const float* rope_cos, const float* rope_sin, uint16_t* k_cache, uint16_t* v_cache,
+                            float* out, void* workspace, size_t workspace_bytes, picoattn_stream_t stream) {
+    if (!k_cache || !v_cache) return PICOATTN_EINVAL;
+    if (cfg && (pos < 0 || pos >= cfg->max_seq_len)) return PICOATTN_ERANGE;
+    return decode_common(cfg, layer, 1, pos + 1, q, k, v, q_norm_w, k_norm_w, rope_cos, rope_sin, nullptr,
+                         nullptr, k_cache, v_cache, nullptr, pos, out, workspace, workspace_bytes,
+                         (cudaStream_t)stream, PICOATTN_STAGE_ALL);
+}
+
+}  // extern "C"

@@ -1,0 +1,65 @@
+// picoattn_internal.h -- launch descriptors shared by the ABI layer and the kernels.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+#include "picoattn.h"
+
+namespace picoattn {
+
+// Workspace header: the first 256 bytes of every workspace.
+struct WsHeader {
+    unsigned int status;  // sticky PICOATTN_DEV_* bits
+    unsigned int pad[63];
+};
+constexpr size_t kWsHeaderBytes = 256;
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Decode launch plan: how the cache rows of a sequence are cut into chunks
+// (one CTA each), tiles (one pipeline stage each) and row groups (16 rows, one
+// warp-level MMA step each).
+struct DecodePlan {
+    int compute_warps;    // 4 or 8
+    int warps_per_head;   // compute_warps / n_kv_heads
+    int tile_rows;        // rows per pipeline stage (multiple of 16*warps_per_head)
+    int stages;           // pipeline depth
+    int chunk_rows;       // rows per CTA (multiple of tile_rows)
+    int max_chunks;       // ceil(max_ctx / chunk_rows): grid x
+    int max_parts;        // partial slots per sequence in the workspace (>= max_chunks*warps_per_head)
+    int smem_bytes;       // dynamic shared memory per CTA
+    size_t ws_qrot, ws_ml, ws_o, ws_total;  // workspace offsets and size
+};
+
+struct DecodeArgs {
+    int hq, hkv, g, hd, kvd, max_seq, layer, n_seqs, max_ctx;
+    int rope_mode;
+    float eps;
+    const float* q;
+    const float* k;
+    const float* v;
+    const float* qn_w;
+    const float* kn_w;
+    const float* rope_cos;
+    const float* rope_sin;
+    uint16_t* const* kc_ptrs;  // per-sequence cache bases (device array), or null
+    uint16_t* const* vc_ptrs;
+    uint16_t* kc_one;          // single-sequence base when kc_ptrs is null
+    uint16_t* vc_one;
+    const int* pos_dev;        // per-sequence positions (device), or null
+    int pos_host;              // position when pos_dev is null
+    float* out;
+    unsigned int* status;
+    float* q_rot;              // [n_seqs][hq][hd]
+    float* part_ml;            // [n_seqs][max_parts][hq][2]  (max, sum) in log2 units
+    float* part_o;             // [n_seqs][max_parts][hq][hd]
+    int chunk_rows, tile_rows, stages, warps_per_head, compute_warps, max_parts;
+};
+
+bool make_decode_plan(const picoattn_config_t& cfg, int n_seqs, int max_ctx, DecodePlan* plan);
+cudaError_t launch_decode(const DecodeArgs& a, const DecodePlan& plan, cudaStream_t stream, unsigned stages);
+
+}  // namespace picoattn

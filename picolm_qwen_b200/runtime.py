@@ -1,0 +1,89 @@
+"""Device-side attention state: the B200 counterpart of the reference's RunState
+attention buffers (key_cache/val_cache, rope_cos/rope_sin, cpp/model.hpp:158-174,
+allocated in cpp/model.hpp:1003-1017), plus the call that replaces the inline
+attention block of Model::forward (cpp/model.hpp:326-418).
+
+PyTorch is used only to own device memory and streams; every computation is a
+call into libpicoattn.so through the C ABI.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+from . import abi
+
+
+def rope_table(cfg: abi.Config) -> tuple[np.ndarray, np.ndarray]:
+    """Host RoPE table built by the library exactly as the reference builds it."""
+    half = cfg.head_dim // 2
+    cos = np.empty((cfg.max_seq_len, half), np.float32)
+    sin = np.empty((cfg.max_seq_len, half), np.float32)
+    abi.check(abi.lib().picoattn_rope_table(C.byref(cfg), cos.ctypes.data, sin.ctypes.data), "rope_table")
+    return cos, sin
+
+
+def stream_handle(stream: torch.cuda.Stream | None = None) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+class AttnState:
+    """KV caches of n_seqs sequences in the reference layout plus RoPE tables.
+
+    k_cache/v_cache: int16 tensors [n_seqs, n_layers, max_seq_len, kv_dim]
+    (fp16 bit patterns; int16 is only the container type).
+    """
+
+    def __init__(self, cfg: abi.Config, n_seqs: int = 1, device: str | torch.device = "cuda",
+                 max_ctx: int | None = None, rope: tuple[np.ndarray, np.ndarray] | None = None):
+        self.cfg = cfg
+        self.n_seqs = n_seqs
+        self.device = torch.device(device)
+        shape = (n_seqs, cfg.n_layers, cfg.max_seq_len, cfg.kv_dim)
+        self.k_cache = torch.zeros(shape, dtype=torch.int16, device=self.device)
+        self.v_cache = torch.zeros(shape, dtype=torch.int16, device=self.device)
+        cos, sin = rope if rope is not None else rope_table(cfg)
+        self.rope_cos = torch.from_numpy(cos).to(self.device)
+        self.rope_sin = torch.from_numpy(sin).to(self.device)
+        per = cfg.n_layers * cfg.max_seq_len * cfg.kv_dim * 2
+        kb, vb = self.k_cache.data_ptr(), self.v_cache.data_ptr()
+        self.k_ptrs = torch.tensor([kb + i * per for i in range(n_seqs)], dtype=torch.int64, device=self.device)
+        self.v_ptrs = torch.tensor([vb + i * per for i in range(n_seqs)], dtype=torch.int64, device=self.device)
+        self.max_ctx = max_ctx if max_ctx is not None else cfg.max_seq_len
+        ws = abi.lib().picoattn_decode_workspace_size(C.byref(cfg), n_seqs, self.max_ctx)
+        if ws == 0:
+            raise abi.PicoAttnError(abi.PICOATTN_EUNSUPPORTED, "decode_workspace_size")
+        self.workspace = torch.zeros(ws, dtype=torch.uint8, device=self.device)
+        abi.check(abi.lib().picoattn_workspace_init(self.workspace.data_ptr(), ws, stream_handle()), "ws init")
+
+    # -- the call that replaces cpp/model.hpp:326-418 ---------------------------
+    def decode(self, layer: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pos: torch.Tensor,
+               out: torch.Tensor, q_norm_w: torch.Tensor | None = None, k_norm_w: torch.Tensor | None = None,
+               max_ctx: int | None = None, stream: torch.cuda.Stream | None = None) -> None:
+        """q [B, Hq*hd], k/v [B, kvd] fp32, pos [B] int32 (device), out [B, Hq*hd] fp32."""
+        B = q.shape[0]
+        st = abi.lib().picoattn_decode(
+            C.byref(self.cfg), layer, B, max_ctx if max_ctx is not None else self.max_ctx,
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), abi.ptr(q_norm_w), abi.ptr(k_norm_w),
+            self.rope_cos.data_ptr(), self.rope_sin.data_ptr(), self.k_ptrs.data_ptr(), self.v_ptrs.data_ptr(),
+            pos.data_ptr(), out.data_ptr(), self.workspace.data_ptr(), self.workspace.numel(),
+            stream_handle(stream))
+        abi.check(st, "picoattn_decode")
+
+    def decode_one(self, layer: int, pos: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                   out: torch.Tensor, q_norm_w: torch.Tensor | None = None, k_norm_w: torch.Tensor | None = None,
+                   seq: int = 0, stream: torch.cuda.Stream | None = None) -> int:
+        """Model::forward-shaped call: one sequence, host position.  Returns the status."""
+        return abi.lib().picoattn_decode_one(
+            C.byref(self.cfg), layer, pos, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+            abi.ptr(q_norm_w), abi.ptr(k_norm_w), self.rope_cos.data_ptr(), self.rope_sin.data_ptr(),
+            self.k_cache[seq].data_ptr(), self.v_cache[seq].data_ptr(), out.data_ptr(),
+            self.workspace.data_ptr(), self.workspace.numel(), stream_handle(stream))
+
+    def status(self) -> int:
+        v = C.c_uint32(0)
+        abi.check(abi.lib().picoattn_workspace_status(self.workspace.data_ptr(), stream_handle(), C.byref(v)))
+        return v.value
