@@ -410,7 +410,10 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--seqs", type=int, default=WORKLOAD["n_seqs"],
+                    help="sequences per GPU (default 64 = the benchmark; smaller only for profiling)")
     args = ap.parse_args()
+    WORKLOAD["n_seqs"] = args.seqs
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -181,6 +181,46 @@ int32_t picoattn_decode_one(const picoattn_config_t* cfg, int32_t layer, int32_t
                             uint16_t* k_cache, uint16_t* v_cache, float* out,
                             void* workspace, size_t workspace_bytes, picoattn_stream_t stream);
 
+/* ---------------------------------------------------------------------- */
+/* Prefill (Model::forward_batch, cpp/model.hpp:462-593)                   */
+/* ---------------------------------------------------------------------- */
+
+/* Workspace bytes for picoattn_prefill of up to n_tok tokens. */
+size_t picoattn_prefill_workspace_size(const picoattn_config_t* cfg, int32_t n_tok);
+
+/*
+ * Attention step of one layer for a prompt of n_tok tokens at positions
+ * start_pos .. start_pos+n_tok-1 of one sequence.  Token i runs the decode step
+ * at pos = start_pos+i (cpp/model.hpp:493-593): its k/v row is stored and it
+ * attends over rows 0..pos, i.e. causal attention over the cache.
+ *   in_dtype  PICOATTN_DTYPE_F32 or PICOATTN_DTYPE_F16 for q, k, v
+ *   q         [n_tok][n_heads*head_dim]    (pre-norm, pre-RoPE projection output)
+ *   k, v      [n_tok][n_kv_heads*head_dim]
+ *   q_norm_w, k_norm_w, rope_cos, rope_sin   as for picoattn_decode
+ *   k_cache, v_cache   the sequence's cache bases (device, 16-byte aligned);
+ *             rows 0..start_pos-1 of this layer must already hold the earlier
+ *             tokens, rows start_pos..start_pos+n_tok-1 are written
+ *   out       [n_tok][n_heads*head_dim] fp32
+ * Requires start_pos + n_tok <= max_seq_len.
+ */
+int32_t picoattn_prefill(const picoattn_config_t* cfg, int32_t layer, int32_t n_tok, int32_t start_pos,
+                         int32_t in_dtype, const void* q, const void* k, const void* v,
+                         const float* q_norm_w, const float* k_norm_w,
+                         const float* rope_cos, const float* rope_sin,
+                         uint16_t* k_cache, uint16_t* v_cache, float* out,
+                         void* workspace, size_t workspace_bytes, picoattn_stream_t stream);
+
+/* picoattn_prefill split into its kernels (PICOATTN_STAGE_PREPARE: norm, RoPE,
+ * cache append and fp16 q; PICOATTN_STAGE_ATTEND: causal attention into out).
+ * Same contract as picoattn_decode_staged. */
+int32_t picoattn_prefill_staged(const picoattn_config_t* cfg, int32_t layer, int32_t n_tok, int32_t start_pos,
+                                int32_t in_dtype, const void* q, const void* k, const void* v,
+                                const float* q_norm_w, const float* k_norm_w,
+                                const float* rope_cos, const float* rope_sin,
+                                uint16_t* k_cache, uint16_t* v_cache, float* out,
+                                void* workspace, size_t workspace_bytes, picoattn_stream_t stream,
+                                uint32_t stages);
+
 #ifdef __cplusplus
 }
 #endif

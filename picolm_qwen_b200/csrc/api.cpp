@@ -194,4 +194,59 @@ int32_t picoattn_decode_one(const picoattn_config_t* cfg, int32_t layer, int32_t
                          (cudaStream_t)stream, PICOATTN_STAGE_ALL);
 }
 
+size_t picoattn_prefill_workspace_size(const picoattn_config_t* cfg, int32_t n_tok) {
+    if (picoattn_config_check(cfg) != PICOATTN_OK || n_tok <= 0) return 0;
+    return prefill_workspace_bytes(*cfg, n_tok);
+}
+
+int32_t picoattn_prefill_staged(const picoattn_config_t* cfg, int32_t layer, int32_t n_tok, int32_t start_pos,
+                                int32_t in_dtype, const void* q, const void* k, const void* v,
+                                const float* q_norm_w, const float* k_norm_w, const float* rope_cos,
+                                const float* rope_sin, uint16_t* k_cache, uint16_t* v_cache, float* out,
+                                void* workspace, size_t workspace_bytes, picoattn_stream_t stream, uint32_t stages) {
+    int32_t st = picoattn_config_check(cfg);
+    if (st != PICOATTN_OK) return st;
+    if (stages == 0 || (stages & ~(PICOATTN_STAGE_PREPARE | PICOATTN_STAGE_ATTEND))) return PICOATTN_EINVAL;
+    if (layer < 0 || layer >= cfg->n_layers || n_tok <= 0) return PICOATTN_EINVAL;
+    if (in_dtype != PICOATTN_DTYPE_F32 && in_dtype != PICOATTN_DTYPE_F16) return PICOATTN_EINVAL;
+    if (!q || !k || !v || !rope_cos || !rope_sin || !k_cache || !v_cache || !out || !workspace)
+        return PICOATTN_EINVAL;
+    if ((q_norm_w == nullptr) != (k_norm_w == nullptr)) return PICOATTN_EINVAL;
+    if (!aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out)) return PICOATTN_EINVAL;
+    if (start_pos < 0 || (int64_t)start_pos + n_tok > cfg->max_seq_len) return PICOATTN_ERANGE;
+    if (workspace_bytes < prefill_workspace_bytes(*cfg, n_tok) || !aligned16(workspace)) return PICOATTN_ENOSPACE;
+    st = device_ok();
+    if (st != PICOATTN_OK) return st;
+    uint8_t* w = static_cast<uint8_t*>(workspace);
+    PrefillArgs a{};
+    a.hq = cfg->n_heads;
+    a.hkv = cfg->n_kv_heads;
+    a.g = a.hq / a.hkv;
+    a.hd = cfg->head_dim;
+    a.kvd = a.hkv * a.hd;
+    a.max_seq = cfg->max_seq_len;
+    a.layer = layer;
+    a.n_tok = n_tok;
+    a.start = start_pos;
+    a.n_qtiles = (n_tok + 127) / 128;
+    a.rope_mode = cfg->rope_mode;
+    a.in_dtype = in_dtype;
+    a.eps = cfg->qk_norm_eps;
+    a.q = q, a.k = k, a.v = v, a.qn_w = q_norm_w, a.kn_w = k_norm_w, a.rope_cos = rope_cos, a.rope_sin = rope_sin;
+    a.k_cache = k_cache, a.v_cache = v_cache, a.out = out;
+    a.status = reinterpret_cast<unsigned int*>(w);
+    a.q16 = reinterpret_cast<__half*>(w + kWsHeaderBytes);
+    return cuda_status(launch_prefill(a, (cudaStream_t)stream, stages));
+}
+
+int32_t picoattn_prefill(const picoattn_config_t* cfg, int32_t layer, int32_t n_tok, int32_t start_pos,
+                         int32_t in_dtype, const void* q, const void* k, const void* v, const float* q_norm_w,
+                         const float* k_norm_w, const float* rope_cos, const float* rope_sin, uint16_t* k_cache,
+                         uint16_t* v_cache, float* out, void* workspace, size_t workspace_bytes,
+                         picoattn_stream_t stream) {
+    return picoattn_prefill_staged(cfg, layer, n_tok, start_pos, in_dtype, q, k, v, q_norm_w, k_norm_w, rope_cos,
+                                   rope_sin, k_cache, v_cache, out, workspace, workspace_bytes, stream,
+                                   PICOATTN_STAGE_PREPARE | PICOATTN_STAGE_ATTEND);
+}
+
 }  // extern "C"

@@ -72,7 +72,9 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 // Bounded wait for the phase with the given parity to complete.  A legitimate
 // wait here lasts microseconds; after ~2 s the wait gives up, sets
 // PICOATTN_DEV_TIMEOUT in the sticky status word and returns false so that the
-// kernel finishes instead of hanging the device.
+// kernel finishes instead of hanging the device.  Once that bit is set (by any
+// CTA of any kernel sharing the workspace) every other wait gives up at its
+// next check, so a broken pipeline costs one timeout, not one per wait.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* status) {
     const uint32_t a = smem_u32(bar);
     uint64_t t0 = 0;
@@ -87,6 +89,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
             : "memory");
         if (done) return true;
         if ((it & 1023u) == 0u) {
+            if (*reinterpret_cast<volatile unsigned int*>(status) & PICOATTN_DEV_TIMEOUT) return false;
             const uint64_t now = global_timer_ns();
             if (it == 0u) t0 = now;
             else if (now - t0 > 2000000000ull) {

@@ -4,6 +4,7 @@
 #include <cstddef>
 #include <cstdint>
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "picoattn.h"
@@ -61,5 +62,26 @@ struct DecodeArgs {
 
 bool make_decode_plan(const picoattn_config_t& cfg, int n_seqs, int max_ctx, DecodePlan* plan);
 cudaError_t launch_decode(const DecodeArgs& a, const DecodePlan& plan, cudaStream_t stream, unsigned stages);
+
+struct PrefillArgs {
+    int hq, hkv, g, hd, kvd, max_seq, layer, n_tok, start, n_qtiles;
+    int rope_mode, in_dtype;
+    float eps;
+    const void* q;   // [n_tok][hq*hd]  fp32 or fp16
+    const void* k;   // [n_tok][kvd]
+    const void* v;
+    const float* qn_w;
+    const float* kn_w;
+    const float* rope_cos;
+    const float* rope_sin;
+    uint16_t* k_cache;  // sequence cache base [n_layers][max_seq][kvd]
+    uint16_t* v_cache;
+    float* out;         // [n_tok][hq*hd]
+    unsigned int* status;
+    __half* q16;        // workspace: rotated, scaled q [n_tok][hq][hd]
+};
+
+cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream, unsigned stages);
+size_t prefill_workspace_bytes(const picoattn_config_t& cfg, int n_tok);
 
 }  // namespace picoattn

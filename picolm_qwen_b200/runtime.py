@@ -83,6 +83,32 @@ class AttnState:
             self.k_cache[seq].data_ptr(), self.v_cache[seq].data_ptr(), out.data_ptr(),
             self.workspace.data_ptr(), self.workspace.numel(), stream_handle(stream))
 
+    # -- the call that replaces cpp/model.hpp:493-593 (forward_batch) ------------
+    def prefill(self, layer: int, start_pos: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                out: torch.Tensor, q_norm_w: torch.Tensor | None = None, k_norm_w: torch.Tensor | None = None,
+                seq: int = 0, workspace: torch.Tensor | None = None, stages: int = 0x3,
+                stream: torch.cuda.Stream | None = None) -> int:
+        """q [n, Hq*hd], k/v [n, kvd] fp32 or fp16 (device); out [n, Hq*hd] fp32.  Returns the status."""
+        n = q.shape[0]
+        dtype = abi.DTYPE_F16 if q.dtype == torch.float16 else abi.DTYPE_F32
+        if workspace is None:
+            workspace = self.prefill_workspace(n)
+        return abi.lib().picoattn_prefill_staged(
+            C.byref(self.cfg), layer, n, start_pos, dtype, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+            abi.ptr(q_norm_w), abi.ptr(k_norm_w), self.rope_cos.data_ptr(), self.rope_sin.data_ptr(),
+            self.k_cache[seq].data_ptr(), self.v_cache[seq].data_ptr(), out.data_ptr(),
+            workspace.data_ptr(), workspace.numel(), stream_handle(stream), stages)
+
+    def prefill_workspace(self, n_tok: int) -> torch.Tensor:
+        n = abi.lib().picoattn_prefill_workspace_size(C.byref(self.cfg), n_tok)
+        if n == 0:
+            raise abi.PicoAttnError(abi.PICOATTN_EUNSUPPORTED, "prefill_workspace_size")
+        ws = getattr(self, "_pf_ws", None)
+        if ws is None or ws.numel() < n:
+            ws = torch.zeros(n, dtype=torch.uint8, device=self.device)
+            self._pf_ws = ws
+        return ws
+
     def status(self) -> int:
         v = C.c_uint32(0)
         abi.check(abi.lib().picoattn_workspace_status(self.workspace.data_ptr(), stream_handle(), C.byref(v)))
