@@ -355,6 +355,12 @@ def run_ours(args) -> None:
     e2e_ms = e0.elapsed_time(e1)
     barrier()
 
+    del st  # free the decode caches before the prefill leg
+    prefill_line = None
+    if not args.no_prefill:
+        torch.cuda.empty_cache()
+        prefill_line = run_prefill(args, dev, world, rank, local)
+
     nbytes = step_bytes(lens, L, kvd)
     times = torch.tensor([elapsed_ms, e2e_ms, float(nbytes)], dtype=torch.float64, device=dev)
     if world > 1:
@@ -393,6 +399,8 @@ def run_ours(args) -> None:
             "gpu_launches": 3 * L * args.steps,
             "clocks": clocks,
         }
+        if prefill_line is not None:
+            line["prefill"] = prefill_line
         if world == 1 and not args.no_cpu:
             try:
                 line["cpu_baseline"] = cpu_baseline(lens)
@@ -403,6 +411,97 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+PREFILL = dict(name="qwen3-8b-prefill", n_layers=36, n_heads=32, n_kv_heads=8, head_dim=128, rope_base=1e6,
+               n_tok=2048, seed=0)
+
+
+def prefill_flops(n_tok: int, n_heads: int, head_dim: int) -> float:
+    """QK^T + PV over causally visible (query, key) pairs only: 4*H*hd*S(S+1)/2."""
+    return 4.0 * n_heads * head_dim * n_tok * (n_tok + 1) / 2
+
+
+def run_prefill(args, dev, world, rank, local) -> dict:
+    """36 layers x 2048-token prompt, QK-norm, fp16 q/k/v in."""
+    import torch
+    import torch.distributed as dist
+    from picolm_qwen_b200 import abi
+    from picolm_qwen_b200.runtime import AttnState, stream_handle
+
+    p = PREFILL
+    L, hq, hkv, hd, n = p["n_layers"], p["n_heads"], p["n_kv_heads"], p["head_dim"], p["n_tok"]
+    kvd = hkv * hd
+    cfg = abi.Config.make(L, hq, hkv, hd, n, p["rope_base"], abi.ROPE_NEOX)
+    st = AttnState(cfg, n_seqs=1, device=dev, max_ctx=1)
+    g = torch.Generator(device=dev)
+    g.manual_seed(2000 + rank)
+    q = torch.randn((L, n, hq * hd), generator=g, device=dev).half()
+    k = torch.randn((L, n, kvd), generator=g, device=dev).half()
+    v = torch.randn((L, n, kvd), generator=g, device=dev).half()
+    qn = 1 + 0.1 * torch.randn((L, hd), generator=g, device=dev)
+    kn = 1 + 0.1 * torch.randn((L, hd), generator=g, device=dev)
+    out = torch.empty((n, hq * hd), device=dev)
+    ws = st.prefill_workspace(n)
+    stream = torch.cuda.current_stream(dev)
+
+    def layer_call(l, stages):
+        s = st.prefill(l, 0, q[l], k[l], v[l], out, qn[l], kn[l], workspace=ws, stages=stages, stream=stream)
+        if s != 0:
+            raise abi.PicoAttnError(s, "picoattn_prefill_staged")
+
+    def step(evs=None):
+        for l in range(L):
+            if evs is None:
+                layer_call(l, abi.STAGE_PREPARE | abi.STAGE_ATTEND)
+            else:
+                layer_call(l, abi.STAGE_PREPARE)
+                evs[l][0].record(stream)
+                layer_call(l, abi.STAGE_ATTEND)
+                evs[l][1].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    steps = max(3, args.steps // 10)
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+           for _ in range(steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    torch.cuda.synchronize(dev)
+    t0.record(stream)
+    for i in range(steps):
+        step(evs[i])
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = t0.elapsed_time(t1)
+    attn_ms = float(np.mean([a.elapsed_time(b) for e in evs for (a, b) in e]))
+    if st.status() != 0:
+        raise RuntimeError("prefill device status set")
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+    flops_layer = prefill_flops(n, hq, hd)
+    total = flops_layer * L * steps * world
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    achieved = flops_layer / (attn_ms / 1e3) / 1e12
+    return {"metric": "prefill attn TFLOP/s", "value": round(total / (ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+            "steps": steps, "ms_per_step": round(ms / steps, 4), "dtype": "f16 operands, f32 accumulate",
+            "config": {"workload": p["name"], "layers": L, "heads_q_kv_dim": [hq, hkv, hd], "prompt_tokens": n,
+                       "qk_norm": True, "flops_per_step": flops_layer * L,
+                       "flops_note": "causally visible pairs only, QK^T + PV"},
+            "roofline": {"bound": "tensor", "kernel": "prefill_attn_kernel<128>", "achieved": round(achieved, 1),
+                         "peak": peak, "peak_kind": "measured" if peaks else "fallback", "unit": "TFLOP/s",
+                         "frac": round(achieved / peak, 4), "mean_launch_ms": round(attn_ms, 5),
+                         "algorithmic_flops_per_launch": flops_layer}}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -410,6 +509,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill (Qwen3-8B) leg")
     ap.add_argument("--seqs", type=int, default=WORKLOAD["n_seqs"],
                     help="sequences per GPU (default 64 = the benchmark; smaller only for profiling)")
     args = ap.parse_args()
