@@ -75,12 +75,11 @@ int32_t decode_common(const picoattn_config_t* cfg, int32_t layer, int32_t n_seq
     a.q_rot = reinterpret_cast<float*>(w + plan.ws_qrot);
     a.part_ml = reinterpret_cast<float*>(w + plan.ws_ml);
     a.part_o = reinterpret_cast<float*>(w + plan.ws_o);
-    a.chunk_rows = plan.chunk_rows;
+    a.prefix = reinterpret_cast<long long*>(w + plan.ws_prefix);
     a.tile_rows = plan.tile_rows;
     a.stages = plan.stages;
     a.warps_per_head = plan.warps_per_head;
     a.compute_warps = plan.compute_warps;
-    a.max_parts = plan.max_parts;
     return cuda_status(launch_decode(a, plan, stream, stages));
 }
 

@@ -28,11 +28,10 @@ struct DecodePlan {
     int warps_per_head;   // compute_warps / n_kv_heads
     int tile_rows;        // rows per pipeline stage (multiple of 16*warps_per_head)
     int stages;           // pipeline depth
-    int chunk_rows;       // rows per CTA (multiple of tile_rows)
-    int max_chunks;       // ceil(max_ctx / chunk_rows): grid x
-    int max_parts;        // partial slots per sequence in the workspace (>= max_chunks*warps_per_head)
+    int grid_ctas;        // persistent CTAs of the attention kernel
+    int max_grid;         // upper bound on grid_ctas (sizes the partial slots)
     int smem_bytes;       // dynamic shared memory per CTA
-    size_t ws_qrot, ws_ml, ws_o, ws_total;  // workspace offsets and size
+    size_t ws_prefix, ws_qrot, ws_ml, ws_o, ws_total;  // workspace offsets and size
 };
 
 struct DecodeArgs {
@@ -55,9 +54,10 @@ struct DecodeArgs {
     float* out;
     unsigned int* status;
     float* q_rot;              // [n_seqs][hq][hd]
-    float* part_ml;            // [n_seqs][max_parts][hq][2]  (max, sum) in log2 units
-    float* part_o;             // [n_seqs][max_parts][hq][hd]
-    int chunk_rows, tile_rows, stages, warps_per_head, compute_warps, max_parts;
+    long long* prefix;         // [n_seqs+1] exclusive prefix sums of attended lengths
+    float* part_ml;            // [slot][warp][hq][2]  (max, sum) in log2 units; slot = cta + seq
+    float* part_o;             // [slot][warp][hq][hd]
+    int tile_rows, stages, warps_per_head, compute_warps;
 };
 
 bool make_decode_plan(const picoattn_config_t& cfg, int n_seqs, int max_ctx, DecodePlan* plan);

@@ -81,7 +81,7 @@ __device__ __forceinline__ float load_in(const void* p, size_t i, int dtype) {
 template <int HD>
 __global__ void __launch_bounds__(256) prefill_prep_kernel(PrefillArgs a) {
     __shared__ float buf[8][HD];
-    const int i = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int i = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pos = a.start + i;
     const size_t row = ((size_t)a.layer * a.max_seq + pos) * a.kvd;
     const float* crow = a.rope_cos + (size_t)pos * (HD / 2);
@@ -89,7 +89,9 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(PrefillArgs a) {
     const float qscale = 1.4426950408889634f / sqrtf((float)HD);
     float* x = buf[warp];
     const int n_slots = a.hq + 2 * a.hkv;
-    for (int slot = warp; slot < n_slots; slot += 8) {
+    {
+        const int slot = blockIdx.x * 8 + warp;  // one warp per head vector
+        if (slot >= n_slots) return;
         int kind, h;
         const void* src;
         size_t off;
@@ -382,7 +384,10 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, u
 
 template <int HD>
 cudaError_t launch_prefill_hd(const PrefillArgs& a, cudaStream_t stream, unsigned stages) {
-    if (stages & PICOATTN_STAGE_PREPARE) prefill_prep_kernel<HD><<<a.n_tok, 256, 0, stream>>>(a);
+    if (stages & PICOATTN_STAGE_PREPARE) {
+        const unsigned slot_blocks = (unsigned)((a.hq + 2 * a.hkv + 7) / 8);
+        prefill_prep_kernel<HD><<<dim3(slot_blocks, (unsigned)a.n_tok), 256, 0, stream>>>(a);
+    }
     if (stages & PICOATTN_STAGE_ATTEND) {
         static bool attr_done = false;
         if (!attr_done) {
