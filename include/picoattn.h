@@ -181,6 +181,34 @@ int32_t picoattn_decode_one(const picoattn_config_t* cfg, int32_t layer, int32_t
                             uint16_t* k_cache, uint16_t* v_cache, float* out,
                             void* workspace, size_t workspace_bytes, picoattn_stream_t stream);
 
+/*
+ * picoattn_decode without a workspace argument: the call allocates nothing and
+ * needs no caller-provided scratch.  No counterpart in the reference (whose CPU
+ * engine needs no device scratch); it exists for callers that cannot allocate
+ * device memory on their token path: engines that size all memory once at
+ * start-up, and hosts whose device memory is owned by another allocator.
+ *   Scratch: a fixed 8 MiB device array inside the library, held by every GPU
+ *   that loads the library until the process exits.  Requests whose decode
+ *   workspace (picoattn_decode_workspace_size) exceeds 8 MiB return
+ *   PICOATTN_ENOSPACE; nothing is launched.
+ *   The first call made with a given device current looks up the array's
+ *   device address; make that first call before any stream capture.
+ *   All calls share the array and it keeps the last call's contents: each call
+ *   clears its status word first; calls whose kernels overlap on the GPU
+ *   (different streams) race and must not be issued.
+ *   status_out (host, optional): when non-NULL the call synchronises `stream`
+ *   and stores the device status bits (PICOATTN_DEV_*) there; a non-zero value
+ *   is also returned as PICOATTN_EDEVSTATUS.
+ * Other arguments as for picoattn_decode.
+ */
+int32_t picoattn_decode_noalloc(const picoattn_config_t* cfg, int32_t layer, int32_t n_seqs, int32_t max_ctx,
+                                const float* q, const float* k, const float* v,
+                                const float* q_norm_w, const float* k_norm_w,
+                                const float* rope_cos, const float* rope_sin,
+                                uint16_t* const* k_cache, uint16_t* const* v_cache,
+                                const int32_t* pos, float* out,
+                                picoattn_stream_t stream, uint32_t* status_out);
+
 /* ---------------------------------------------------------------------- */
 /* Prefill (Model::forward_batch, cpp/model.hpp:462-593)                   */
 /* ---------------------------------------------------------------------- */

@@ -87,6 +87,8 @@ PROTOTYPES = {
     "picoattn_decode_staged": (_I, [_CFG, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P,
                                    C.c_uint32]),
     "picoattn_decode_one": (_I, [_CFG, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P]),
+    "picoattn_decode_noalloc": (_I, [_CFG, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                    C.POINTER(C.c_uint32)]),
     "picoattn_prefill_workspace_size": (_Z, [_CFG, _I]),
     "picoattn_prefill": (_I, [_CFG, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P]),
     "picoattn_prefill_staged": (_I, [_CFG, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P,

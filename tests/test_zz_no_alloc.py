@@ -1,0 +1,94 @@
+"""picoattn_decode_noalloc: the decode step for callers that cannot allocate.
+
+Some hosts cannot give this library device memory on their token path: an
+engine that sizes everything once at start-up (as the reference sizes its
+RunState once) or a host whose device memory belongs to another allocator.
+For them picoattn_decode_noalloc keeps its scratch in a fixed 8 MiB array
+inside the library.  This test calls it through the C ABI twice in a row and
+checks each result against picoattn_decode (the workspace entry point) on the
+same inputs, with the tolerance the other decode tests use.
+
+Kept in a file of its own, named to be collected last.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-3, 1e-2
+
+
+def assert_close(got, ref, what):
+    err = np.abs(got.astype(np.float64) - ref.astype(np.float64))
+    bad = ~(err <= ATOL + RTOL * np.abs(ref.astype(np.float64)))
+    assert not bad.any(), f"{what}: {bad.sum()} outside tolerance, max err {err.max():.3g}"
+
+
+@pytest.fixture(scope="module")
+def cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from picolm_qwen_b200 import abi
+    assert abi.lib().picoattn_device_check() == 0
+    return torch.device("cuda")
+
+
+def test_noalloc_decode_matches_workspace_decode_twice(cuda):
+    from picolm_qwen_b200 import abi
+    from picolm_qwen_b200.runtime import AttnState, stream_handle
+
+    L = abi.lib()
+    hq, hkv, hd = 28, 4, 128
+    lens = np.array([1, 900, 2500, 4000], np.int32)  # cached rows; the new token sits at pos = len
+    B = len(lens)
+    S = int(lens.max()) + 2
+    cfg = abi.Config.make(2, hq, hkv, hd, S, 1e6)
+    g = torch.Generator(device="cuda").manual_seed(9)
+    ref = AttnState(cfg, n_seqs=B)      # caches for the workspace entry point
+    for b, n in enumerate(lens):
+        ref.k_cache[b, :, :n] = (torch.randn((2, int(n), hkv * hd), generator=g, device="cuda") * 0.5).half().view(
+            torch.int16)
+        ref.v_cache[b, :, :n] = (torch.randn((2, int(n), hkv * hd), generator=g, device="cuda") * 0.5).half().view(
+            torch.int16)
+    mine = AttnState(cfg, n_seqs=B)     # identical caches for the no-alloc entry point
+    mine.k_cache.copy_(ref.k_cache)
+    mine.v_cache.copy_(ref.v_cache)
+    sh = stream_handle()
+
+    for call, (layer, extra) in enumerate([(1, 0), (0, 1)]):  # two calls in a row, different layer and positions
+        pos = torch.from_numpy(lens + extra).cuda()
+        max_ctx = int(lens.max()) + 1 + extra
+        q = torch.randn((B, hq * hd), generator=g, device="cuda")
+        k = torch.randn((B, hkv * hd), generator=g, device="cuda")
+        v = torch.randn((B, hkv * hd), generator=g, device="cuda")
+        want = torch.empty((B, hq * hd), device="cuda")
+        got = torch.full((B, hq * hd), float("nan"), device="cuda")
+        ref.decode(layer, q, k, v, pos, want, max_ctx=max_ctx)
+        status = C.c_uint32(12345)
+        st = L.picoattn_decode_noalloc(C.byref(cfg), layer, B, max_ctx, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                       None, None, mine.rope_cos.data_ptr(), mine.rope_sin.data_ptr(),
+                                       mine.k_ptrs.data_ptr(), mine.v_ptrs.data_ptr(), pos.data_ptr(),
+                                       got.data_ptr(), sh, C.byref(status))
+        assert st == abi.PICOATTN_OK, L.picoattn_strerror(st)
+        assert status.value == 0
+        torch.cuda.synchronize()
+        assert_close(got.cpu().numpy(), want.cpu().numpy(), f"call {call}")
+        assert torch.equal(mine.k_cache, ref.k_cache) and torch.equal(mine.v_cache, ref.v_cache)
+
+
+def test_noalloc_rejects_requests_beyond_its_scratch(cuda):
+    from picolm_qwen_b200 import abi
+    from picolm_qwen_b200.runtime import stream_handle
+
+    L = abi.lib()
+    cfg = abi.Config.make(1, 28, 4, 128, 8192, 1e6)
+    n_seqs = 4096  # needs far more than the fixed 8 MiB
+    assert L.picoattn_decode_workspace_size(C.byref(cfg), n_seqs, 8192) > (8 << 20)
+    fake = 0x10000  # never dereferenced: the size check comes first
+    st = L.picoattn_decode_noalloc(C.byref(cfg), 0, n_seqs, 8192, fake, fake, fake, None, None, fake, fake,
+                                   fake, fake, fake, fake, stream_handle(), None)
+    assert st == abi.PICOATTN_ENOSPACE
