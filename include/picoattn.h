@@ -93,6 +93,10 @@ int32_t picoattn_version(void);
 /* Text for a status code. */
 const char* picoattn_strerror(int32_t status);
 
+/* Text of the last CUDA runtime error behind a PICOATTN_ECUDA status on the
+ * calling thread. */
+const char* picoattn_last_cuda_error(void);
+
 /* Validates a config; PICOATTN_OK, EINVAL or EUNSUPPORTED. */
 int32_t picoattn_config_check(const picoattn_config_t* cfg);
 
@@ -208,6 +212,64 @@ int32_t picoattn_decode_noalloc(const picoattn_config_t* cfg, int32_t layer, int
                                 uint16_t* const* k_cache, uint16_t* const* v_cache,
                                 const int32_t* pos, float* out,
                                 picoattn_stream_t stream, uint32_t* status_out);
+
+/* ---------------------------------------------------------------------- */
+/* Split-KV decode across GPUs (long context)                             */
+/* ---------------------------------------------------------------------- */
+/* The reference attends rows 0..pos in one loop (cpp/model.hpp:378-413); it
+ * has no multi-device path.  Split across G devices, device g holds absolute
+ * positions [row_offset, row_offset + local_rows) of every layer and of every
+ * sequence, computes a per-head shard result (acc/sum over its rows and the
+ * log2-sum-exp of its scores), and any device recovers the single-loop result
+ * by a log-sum-exp combination. */
+
+/* Bytes of one shard result: [n_seqs][n_heads][head_dim + 2] fp32. */
+size_t picoattn_shard_partial_bytes(const picoattn_config_t* cfg, int32_t n_seqs);
+
+/*
+ * Decode step over this device's shard.  k_cache/v_cache entries are the local
+ * slab bases, uint16 [n_layers][local_rows][kv_dim]; pos[] are absolute
+ * positions (< max_seq_len; RoPE uses them); the new token's row is stored only
+ * by the device whose shard holds pos.  max_ctx bounds the local rows attended
+ * (<= local_rows).  partial receives [n_seqs][n_heads][head_dim+2]: the
+ * normalised shard output and, at index head_dim, its log2-sum-exp (-inf when
+ * the shard holds no row <= pos).  Workspace: picoattn_decode_workspace_size
+ * (cfg, n_seqs, max_ctx).
+ */
+int32_t picoattn_decode_shard(const picoattn_config_t* cfg, int32_t layer, int32_t n_seqs, int32_t max_ctx,
+                              int32_t row_offset, int32_t local_rows,
+                              const float* q, const float* k, const float* v,
+                              const float* q_norm_w, const float* k_norm_w,
+                              const float* rope_cos, const float* rope_sin,
+                              uint16_t* const* k_cache, uint16_t* const* v_cache,
+                              const int32_t* pos, float* partial,
+                              void* workspace, size_t workspace_bytes, picoattn_stream_t stream);
+
+/* out[n_seqs][n_heads*head_dim] = log-sum-exp combination of n_shards shard
+ * results laid out [n_shards][n_seqs][n_heads][head_dim+2] (device). */
+int32_t picoattn_combine_shards(const picoattn_config_t* cfg, int32_t n_seqs, int32_t n_shards,
+                                const float* partials, float* out, picoattn_stream_t stream);
+
+/* NCCL: 128-byte unique id (host buffer) for picoattn_nccl_comm_create. */
+int32_t picoattn_nccl_unique_id(void* id_out);
+/* Non-blocking communicator creation; returns PICOATTN_ETIMEOUT (and aborts the
+ * communicator) if the other ranks do not join within timeout_s seconds. */
+int32_t picoattn_nccl_comm_create(int32_t n_ranks, const void* id, int32_t rank, double timeout_s, void** comm_out);
+int32_t picoattn_nccl_comm_destroy(void* comm);
+/* Bytes of the all-gather buffer of picoattn_decode_splitkv_nccl. */
+size_t picoattn_splitkv_gather_bytes(const picoattn_config_t* cfg, int32_t n_seqs, int32_t n_ranks);
+/* picoattn_decode_shard into this rank's slice of `gather`, an in-place NCCL
+ * all-gather of the shard results, then picoattn_combine_shards into out
+ * (every rank gets the full output, as the next layer's projections need). */
+int32_t picoattn_decode_splitkv_nccl(const picoattn_config_t* cfg, int32_t layer, int32_t n_seqs, int32_t max_ctx,
+                                     int32_t row_offset, int32_t local_rows,
+                                     const float* q, const float* k, const float* v,
+                                     const float* q_norm_w, const float* k_norm_w,
+                                     const float* rope_cos, const float* rope_sin,
+                                     uint16_t* const* k_cache, uint16_t* const* v_cache,
+                                     const int32_t* pos, float* gather, float* out,
+                                     void* workspace, size_t workspace_bytes, void* comm,
+                                     picoattn_stream_t stream);
 
 /* ---------------------------------------------------------------------- */
 /* Prefill (Model::forward_batch, cpp/model.hpp:462-593)                   */

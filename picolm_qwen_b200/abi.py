@@ -77,6 +77,7 @@ _CFG = C.POINTER(Config)
 PROTOTYPES = {
     "picoattn_version": (_I, []),
     "picoattn_strerror": (C.c_char_p, [_I]),
+    "picoattn_last_cuda_error": (C.c_char_p, []),
     "picoattn_config_check": (_I, [_CFG]),
     "picoattn_rope_table": (_I, [_CFG, _P, _P]),
     "picoattn_device_check": (_I, []),
@@ -89,6 +90,16 @@ PROTOTYPES = {
     "picoattn_decode_one": (_I, [_CFG, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P]),
     "picoattn_decode_noalloc": (_I, [_CFG, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                     C.POINTER(C.c_uint32)]),
+    "picoattn_shard_partial_bytes": (_Z, [_CFG, _I]),
+    "picoattn_decode_shard": (_I, [_CFG, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _Z,
+                                  _P]),
+    "picoattn_combine_shards": (_I, [_CFG, _I, _I, _P, _P, _P]),
+    "picoattn_nccl_unique_id": (_I, [_P]),
+    "picoattn_nccl_comm_create": (_I, [_I, _P, _I, C.c_double, C.POINTER(C.c_void_p)]),
+    "picoattn_nccl_comm_destroy": (_I, [_P]),
+    "picoattn_splitkv_gather_bytes": (_Z, [_CFG, _I, _I]),
+    "picoattn_decode_splitkv_nccl": (_I, [_CFG, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                         _P, _Z, _P, _P]),
     "picoattn_prefill_workspace_size": (_Z, [_CFG, _I]),
     "picoattn_prefill": (_I, [_CFG, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P]),
     "picoattn_prefill_staged": (_I, [_CFG, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P,
@@ -101,6 +112,8 @@ _lib = None
 class PicoAttnError(RuntimeError):
     def __init__(self, status: int, what: str = ""):
         msg = lib().picoattn_strerror(status).decode()
+        if status == PICOATTN_ECUDA:
+            msg += " (" + lib().picoattn_last_cuda_error().decode() + ")"
         super().__init__(f"{what}: {msg} ({status})" if what else f"{msg} ({status})")
         self.status = status
 

@@ -88,7 +88,7 @@ def build(force: bool = False, ptxas_v: bool = False, verbose: bool = False) -> 
                 if ptxas_v or verbose:
                     sys.stderr.write(r.stderr)
     if force or jobs or _stale(LIB, objs):
-        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs
+        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lnccl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             sys.stderr.write(r.stdout + r.stderr)

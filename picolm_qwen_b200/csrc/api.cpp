@@ -15,7 +15,13 @@ using namespace picoattn;
 
 namespace {
 
-int32_t cuda_status(cudaError_t e) { return e == cudaSuccess ? PICOATTN_OK : PICOATTN_ECUDA; }
+thread_local cudaError_t g_last_cuda_error = cudaSuccess;
+
+int32_t cuda_status(cudaError_t e) {
+    if (e == cudaSuccess) return PICOATTN_OK;
+    g_last_cuda_error = e;
+    return PICOATTN_ECUDA;
+}
 
 bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
@@ -43,6 +49,7 @@ int32_t decode_common(const picoattn_config_t* cfg, int32_t layer, int32_t n_seq
     if (st != PICOATTN_OK) return st;
     if (layer < 0 || layer >= cfg->n_layers || n_seqs <= 0) return PICOATTN_EINVAL;
     if (!q || !k || !v || !rc || !rs || !out || !ws) return PICOATTN_EINVAL;
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return PICOATTN_EINVAL;
     if ((qn == nullptr) != (kn == nullptr)) return PICOATTN_EINVAL;
     if (kcp == nullptr && (kc1 == nullptr || vc1 == nullptr)) return PICOATTN_EINVAL;
     if (kcp != nullptr && vcp == nullptr) return PICOATTN_EINVAL;
@@ -76,6 +83,9 @@ int32_t decode_common(const picoattn_config_t* cfg, int32_t layer, int32_t n_seq
     a.part_ml = reinterpret_cast<float*>(w + plan.ws_ml);
     a.part_o = reinterpret_cast<float*>(w + plan.ws_o);
     a.prefix = reinterpret_cast<long long*>(w + plan.ws_prefix);
+    a.row_offset = 0;
+    a.local_rows = cfg->max_seq_len;
+    a.shard_out = nullptr;
     a.tile_rows = plan.tile_rows;
     a.stages = plan.stages;
     a.warps_per_head = plan.warps_per_head;
@@ -103,6 +113,10 @@ const char* picoattn_strerror(int32_t s) {
         case PICOATTN_EDEVSTATUS: return "a kernel flagged bad input";
         default: return "unknown status";
     }
+}
+
+const char* picoattn_last_cuda_error(void) {
+    return g_last_cuda_error == cudaSuccess ? "no CUDA error" : cudaGetErrorString(g_last_cuda_error);
 }
 
 int32_t picoattn_config_check(const picoattn_config_t* c) {
@@ -212,6 +226,7 @@ int32_t picoattn_prefill_staged(const picoattn_config_t* cfg, int32_t layer, int
         return PICOATTN_EINVAL;
     if ((q_norm_w == nullptr) != (k_norm_w == nullptr)) return PICOATTN_EINVAL;
     if (!aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out)) return PICOATTN_EINVAL;
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v)) return PICOATTN_EINVAL;
     if (start_pos < 0 || (int64_t)start_pos + n_tok > cfg->max_seq_len) return PICOATTN_ERANGE;
     if (workspace_bytes < prefill_workspace_bytes(*cfg, n_tok) || !aligned16(workspace)) return PICOATTN_ENOSPACE;
     st = device_ok();
@@ -234,6 +249,7 @@ int32_t picoattn_prefill_staged(const picoattn_config_t* cfg, int32_t layer, int
     a.q = q, a.k = k, a.v = v, a.qn_w = q_norm_w, a.kn_w = k_norm_w, a.rope_cos = rope_cos, a.rope_sin = rope_sin;
     a.k_cache = k_cache, a.v_cache = v_cache, a.out = out;
     a.status = reinterpret_cast<unsigned int*>(w);
+    a.work_counter = reinterpret_cast<int*>(w + 64);
     a.q16 = reinterpret_cast<__half*>(w + kWsHeaderBytes);
     return cuda_status(launch_prefill(a, (cudaStream_t)stream, stages));
 }

@@ -28,6 +28,7 @@
 
 #include "device_common.cuh"
 #include "picoattn_internal.h"
+#include "prep_common.cuh"
 
 namespace picoattn {
 
@@ -42,8 +43,13 @@ __device__ __forceinline__ uint16_t* seq_kcache(const DecodeArgs& a, int b) {
 __device__ __forceinline__ uint16_t* seq_vcache(const DecodeArgs& a, int b) {
     return a.vc_ptrs ? a.vc_ptrs[b] : a.vc_one;
 }
+// Rows of this sequence held in the local slab that the token at `pos` attends:
+// the slab holds absolute positions [row_offset, row_offset + local_rows).
+__device__ __forceinline__ int local_len(const DecodeArgs& a, int pos) {
+    return max(0, min(pos + 1 - a.row_offset, a.local_rows));
+}
 __device__ __forceinline__ bool pos_ok(const DecodeArgs& a, int pos) {
-    return pos >= 0 && pos < a.max_seq && pos < a.max_ctx;
+    return pos >= 0 && pos < a.max_seq && local_len(a, pos) <= a.max_ctx;
 }
 
 // CTA i streams concatenated rows [slice_start(i), slice_start(i+1)).
@@ -61,43 +67,6 @@ __device__ __forceinline__ int cta_of_row(long long x, long long R, int G) {
 // prep
 // ---------------------------------------------------------------------------
 
-// Per-head RMSNorm in the reference's order (cpp/tensor.hpp:146-176): element
-// i is squared into lane i%4 of a 4-wide accumulator, lanes folded as
-// (l0+l2)+(l1+l3), scale = 1/sqrt(ss/n + eps), out = (x*scale)*w.  Explicit
-// _rn intrinsics keep every operation a single IEEE rounding (no FMA fusion).
-template <int HD>
-__device__ __forceinline__ void rmsnorm_ref(float* x, const float* w, float eps, int lane) {
-    float part = 0.f;
-    if (lane < 4) {
-#pragma unroll 8
-        for (int i = lane; i < HD; i += 4) part = __fadd_rn(part, __fmul_rn(x[i], x[i]));
-    }
-    const float l0 = __shfl_sync(0xffffffffu, part, 0);
-    const float l1 = __shfl_sync(0xffffffffu, part, 1);
-    const float l2 = __shfl_sync(0xffffffffu, part, 2);
-    const float l3 = __shfl_sync(0xffffffffu, part, 3);
-    const float ss = __fadd_rn(__fadd_rn(l0, l2), __fadd_rn(l1, l3));
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)HD), eps)));
-    for (int i = lane; i < HD; i += 32) x[i] = __fmul_rn(__fmul_rn(x[i], scale), w[i]);
-    __syncwarp();
-}
-
-// RoPE of one head (cpp/tensor.hpp:201-283 NeoX; picolm/tensor.c:247-293
-// interleaved): (x0, x1) -> (x0*c - x1*s, x0*s + x1*c), each product and the
-// sum rounded separately as in the reference's scalar/SSE code.
-template <int HD>
-__device__ __forceinline__ void rope_ref(float* x, const float* c, const float* s, int mode, int lane) {
-    constexpr int half = HD / 2;
-    for (int i = lane; i < half; i += 32) {
-        const int i0 = mode == PICOATTN_ROPE_NEOX ? i : 2 * i;
-        const int i1 = mode == PICOATTN_ROPE_NEOX ? i + half : 2 * i + 1;
-        const float x0 = x[i0], x1 = x[i1], ci = c[i], si = s[i];
-        x[i0] = __fsub_rn(__fmul_rn(x0, ci), __fmul_rn(x1, si));
-        x[i1] = __fadd_rn(__fmul_rn(x0, si), __fmul_rn(x1, ci));
-    }
-    __syncwarp();
-}
-
 // Exclusive scan of the attended lengths (pos+1, or 0 for a rejected position)
 // into prefix[0..n_seqs]; one block of 256 threads.
 __device__ void scan_lengths(const DecodeArgs& a) {
@@ -108,7 +77,7 @@ __device__ void scan_lengths(const DecodeArgs& a) {
     long long mine = 0;
     for (int b = b0; b < b1; b++) {
         const int p = seq_pos(a, b);
-        mine += pos_ok(a, p) ? p + 1 : 0;
+        mine += pos_ok(a, p) ? local_len(a, p) : 0;
     }
     long long incl = mine;
     for (int o = 1; o < 32; o <<= 1) {
@@ -123,7 +92,7 @@ __device__ void scan_lengths(const DecodeArgs& a) {
     for (int b = b0; b < b1; b++) {
         a.prefix[b] = run;
         const int p = seq_pos(a, b);
-        run += pos_ok(a, p) ? p + 1 : 0;
+        run += pos_ok(a, p) ? local_len(a, p) : 0;
     }
     if (tid == 255) a.prefix[a.n_seqs] = base + incl;
 }
@@ -134,41 +103,53 @@ __global__ void __launch_bounds__(256) decode_prep_kernel(DecodeArgs a) {
         if (blockIdx.x == 0) scan_lengths(a);
         return;
     }
-    __shared__ float buf[8][HD];
+    // 8 warps x 4 head vectors of one sequence per block (helpers: prep_common.cuh)
+    constexpr int V = HD / 32;
+    __shared__ float sq[8][HD];
     const int b = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int slot = blockIdx.x * 8 + warp;
-    const int n_slots = a.hq + 2 * a.hkv;
     const int pos = seq_pos(a, b);
     if (!pos_ok(a, pos)) {
         if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(a.status, PICOATTN_DEV_BAD_POS);
         return;
     }
-    if (slot >= n_slots) return;
-    int kind, h;  // 0 = q head, 1 = k head, 2 = v head
-    const float* src;
-    if (slot < a.hq) {
-        kind = 0, h = slot, src = a.q + ((size_t)b * a.hq + h) * HD;
-    } else if (slot < a.hq + a.hkv) {
-        kind = 1, h = slot - a.hq, src = a.k + ((size_t)b * a.hkv + h) * HD;
-    } else {
-        kind = 2, h = slot - a.hq - a.hkv, src = a.v + ((size_t)b * a.hkv + h) * HD;
+    const int n_slots = a.hq + 2 * a.hkv;
+    const int slot0 = (blockIdx.x * 8 + warp) * 4;
+    if (slot0 >= n_slots) return;
+    RopeLane<HD> rl;
+    rope_lane_load<HD>(rl, a.rope_cos + (size_t)pos * (HD / 2), a.rope_sin + (size_t)pos * (HD / 2), a.rope_mode,
+                       lane);
+    float qw[V], kw[V];
+    if (a.qn_w) {
+#pragma unroll
+        for (int j = 0; j < V; j++) qw[j] = a.qn_w[V * lane + j], kw[j] = a.kn_w[V * lane + j];
     }
-    float* x = buf[warp];
-    for (int i = lane; i < HD; i += 32) x[i] = src[i];
-    __syncwarp();
-    if (kind != 2) {
-        const float* w = kind == 0 ? a.qn_w : a.kn_w;
-        if (w) rmsnorm_ref<HD>(x, w, a.eps, lane);
-        rope_ref<HD>(x, a.rope_cos + (size_t)pos * (HD / 2), a.rope_sin + (size_t)pos * (HD / 2), a.rope_mode,
-                     lane);
+    Vec<HD> x[4];
+    int kind[4], head[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+        const int slot = slot0 + u;
+        kind[u] = slot < a.hq ? 0 : (slot < a.hq + a.hkv ? 1 : (slot < n_slots ? 2 : 3));
+        head[u] = kind[u] == 0 ? slot : (kind[u] == 1 ? slot - a.hq : slot - a.hq - a.hkv);
+        if (kind[u] == 0) vec_load<HD>(x[u], a.q, ((size_t)b * a.hq + head[u]) * HD, PICOATTN_DTYPE_F32, lane);
+        else if (kind[u] == 1) vec_load<HD>(x[u], a.k, ((size_t)b * a.hkv + head[u]) * HD, PICOATTN_DTYPE_F32, lane);
+        else if (kind[u] == 2) vec_load<HD>(x[u], a.v, ((size_t)b * a.hkv + head[u]) * HD, PICOATTN_DTYPE_F32, lane);
     }
-    if (kind == 0) {
-        float* dst = a.q_rot + ((size_t)b * a.hq + h) * HD;
-        for (int i = lane; i < HD; i += 32) dst[i] = x[i];
-    } else {
-        const size_t row = ((size_t)a.layer * a.max_seq + pos) * a.kvd;
-        uint16_t* dst = (kind == 1 ? seq_kcache(a, b) : seq_vcache(a, b)) + row + (size_t)h * HD;
-        for (int i = lane; i < HD; i += 32) dst[i] = f32_to_f16_ref(x[i]);
+    const int lrow = pos - a.row_offset;  // the new row lives in this slab only if 0 <= lrow < local_rows
+    const bool row_here = lrow >= 0 && lrow < a.local_rows;
+    const size_t row = ((size_t)a.layer * a.local_rows + (row_here ? lrow : 0)) * a.kvd;
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+        if (kind[u] == 3) break;
+        if (kind[u] != 0 && !row_here) continue;
+        if (kind[u] != 2) {
+            if (a.qn_w) vec_rmsnorm<HD>(x[u], kind[u] == 0 ? qw : kw, a.eps, sq[warp], lane);
+            vec_rope<HD>(x[u], rl, a.rope_mode, lane);
+        }
+        if (kind[u] == 0)
+            vec_store_f32<HD>(x[u], a.q_rot + ((size_t)b * a.hq + head[u]) * HD, lane);
+        else
+            vec_store_ref16<HD>(x[u], (kind[u] == 1 ? seq_kcache(a, b) : seq_vcache(a, b)) + row +
+                                          (size_t)head[u] * HD, lane);
     }
 }
 
@@ -211,7 +192,7 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + a.stages;
     uint8_t* tiles = smem + 128;
-    const size_t slab = (size_t)a.layer * a.max_seq * a.kvd;
+    const size_t slab = (size_t)a.layer * a.local_rows * a.kvd;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < a.stages; s++) {
@@ -380,11 +361,14 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
                 const int h = kvh * G_q + r;
                 if (direct) {
                     const float inv = 1.0f / l[half];
-                    float* od = a.out + ((size_t)b * a.hq + h) * HD + 2 * tig;
+                    float* od = a.shard_out ? a.shard_out + ((size_t)b * a.hq + h) * (HD + 2) + 2 * tig
+                                            : a.out + ((size_t)b * a.hq + h) * HD + 2 * tig;
 #pragma unroll
                     for (int i = 0; i < HD / 8; i++)
                         *reinterpret_cast<float2*>(od + i * 8) =
                             make_float2(o[i][2 * half] * inv, o[i][2 * half + 1] * inv);
+                    if (a.shard_out && tig == 0)  // log2-sum-exp of this shard's scores
+                        a.shard_out[((size_t)b * a.hq + h) * (HD + 2) + HD] = m[half] + __log2f(l[half]);
                 } else {
                     float* od = a.part_o + (pbase + h) * HD + 2 * tig;
 #pragma unroll
@@ -403,50 +387,65 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
 // ---------------------------------------------------------------------------
 
 template <int HD>
-__global__ void __launch_bounds__(HD) decode_merge_kernel(DecodeArgs a, int G) {
+__global__ void __launch_bounds__(256) decode_merge_kernel(DecodeArgs a, int G) {
+    // 256 threads: head dim d = tid % HD, piece group = tid / HD; every group sums
+    // its pieces with 4 independent accumulators so many loads are in flight
+    constexpr int NT = 256, NG = NT / HD;
     __shared__ float w_s[2048];
-    __shared__ float red[HD / 32];
+    __shared__ float red[NT / 32];
     __shared__ float bc[2];
-    const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x, lane = d & 31, warp = d >> 5;
-    float* dst = a.out + ((size_t)b * a.hq + h) * HD + d;
+    __shared__ float part[NG][HD];
+    const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int d = tid % HD, grp = tid / HD;
+    const size_t row_stride = a.shard_out ? (size_t)(HD + 2) : (size_t)HD;
+    float* dst = (a.shard_out ? a.shard_out : a.out) + ((size_t)b * a.hq + h) * row_stride + d;
     const int pos = seq_pos(a, b);
     if (!pos_ok(a, pos)) {
-        *dst = __int_as_float(0x7fc00000);
+        if (grp == 0) {
+            *dst = __int_as_float(0x7fc00000);
+            if (a.shard_out && d == 0) dst[HD - d] = __int_as_float(0x7fc00000);
+        }
         return;
     }
     const long long R = a.prefix[a.n_seqs];
     const long long p0 = a.prefix[b], p1 = a.prefix[b + 1];
+    if (p0 == p1) {  // no rows of this sequence in this shard: empty partial
+        if (grp == 0) {
+            *dst = 0.f;
+            if (d == 0) dst[HD] = -INFINITY;
+        }
+        return;
+    }
     const int i_lo = cta_of_row(p0, R, G), i_hi = cta_of_row(p1 - 1, R, G);
     const int W = a.warps_per_head;
     if (i_lo == i_hi && W == 1) return;  // written directly by the attention kernel
     const int n_pieces = (i_hi - i_lo + 1) * W;  // <= 2048 (checked on the host)
     // piece k -> (cta i_lo + k/W, warp k%W); skipped if that CTA's slice is empty
+    auto piece = [&](int k) -> size_t { return ((size_t)(i_lo + k / W + b) * W + k % W) * a.hq + h; };
     float mloc = -INFINITY;
-    for (int k = d; k < n_pieces; k += HD) {
+    for (int k = tid; k < n_pieces; k += NT) {
         const int i = i_lo + k / W;
         float m = -INFINITY;
-        if (slice_start(i, R, G) < slice_start(i + 1, R, G))
-            m = a.part_ml[((((size_t)(i + b) * W + k % W) * a.hq) + h) * 2];
+        if (slice_start(i, R, G) < slice_start(i + 1, R, G)) m = a.part_ml[piece(k) * 2];
         w_s[k] = m;
         mloc = fmaxf(mloc, m);
     }
     for (int o = 16; o; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
     if (lane == 0) red[warp] = mloc;
     __syncthreads();
-    if (d == 0) {
+    if (tid == 0) {
         float M = red[0];
-        for (int w = 1; w < HD / 32; w++) M = fmaxf(M, red[w]);
+        for (int w = 1; w < NT / 32; w++) M = fmaxf(M, red[w]);
         bc[0] = M;
     }
     __syncthreads();
     const float M = bc[0];
     float lloc = 0.f;
-    for (int k = d; k < n_pieces; k += HD) {
-        const int i = i_lo + k / W;
+    for (int k = tid; k < n_pieces; k += NT) {
         float wgt = 0.f;
         if (w_s[k] != -INFINITY) {
             wgt = ex2(w_s[k] - M);
-            lloc += wgt * a.part_ml[((((size_t)(i + b) * W + k % W) * a.hq) + h) * 2 + 1];
+            lloc += wgt * a.part_ml[piece(k) * 2 + 1];
         }
         w_s[k] = wgt;
     }
@@ -454,19 +453,34 @@ __global__ void __launch_bounds__(HD) decode_merge_kernel(DecodeArgs a, int G) {
     __syncthreads();
     if (lane == 0) red[warp] = lloc;
     __syncthreads();
-    if (d == 0) {
+    if (tid == 0) {
         float L = 0.f;
-        for (int w = 0; w < HD / 32; w++) L += red[w];
+        for (int w = 0; w < NT / 32; w++) L += red[w];
         bc[1] = L;
     }
     __syncthreads();
-    float acc = 0.f;
-#pragma unroll 4
-    for (int k = 0; k < n_pieces; k++) {
-        const float wgt = w_s[k];
-        if (wgt != 0.f) acc += wgt * a.part_o[((((size_t)(i_lo + k / W + b) * W + k % W) * a.hq) + h) * HD + d];
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    int k = grp;
+    for (; k + 3 * NG < n_pieces; k += 4 * NG) {
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const float wgt = w_s[k + u * NG];
+            if (wgt != 0.f) acc[u] += wgt * a.part_o[piece(k + u * NG) * HD + d];
+        }
     }
-    *dst = acc / bc[1];
+    for (; k < n_pieces; k += NG) {
+        const float wgt = w_s[k];
+        if (wgt != 0.f) acc[0] += wgt * a.part_o[piece(k) * HD + d];
+    }
+    part[grp][d] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    __syncthreads();
+    if (grp == 0) {
+        float o = part[0][d];
+#pragma unroll
+        for (int g2 = 1; g2 < NG; g2++) o += part[g2][d];
+        *dst = o / bc[1];
+        if (a.shard_out && d == 0) dst[HD] = M + __log2f(bc[1]);
+    }
 }
 
 template <int HD>
@@ -480,11 +494,11 @@ cudaError_t launch_decode_hd(const DecodeArgs& a, const DecodePlan& plan, cudaSt
     }
     const int n_slots = a.hq + 2 * a.hkv;
     if (stages & PICOATTN_STAGE_PREPARE)
-        decode_prep_kernel<HD><<<dim3((unsigned)((n_slots + 7) / 8), (unsigned)a.n_seqs + 1), 256, 0, stream>>>(a);
+        decode_prep_kernel<HD><<<dim3((unsigned)((n_slots + 31) / 32), (unsigned)a.n_seqs + 1), 256, 0, stream>>>(a);
     if (stages & PICOATTN_STAGE_ATTEND)
         decode_attn_kernel<HD><<<plan.grid_ctas, (plan.compute_warps + 1) * 32, plan.smem_bytes, stream>>>(a);
     if (stages & PICOATTN_STAGE_COMBINE)
-        decode_merge_kernel<HD><<<dim3((unsigned)a.hq, (unsigned)a.n_seqs), HD, 0, stream>>>(a, plan.grid_ctas);
+        decode_merge_kernel<HD><<<dim3((unsigned)a.hq, (unsigned)a.n_seqs), 256, 0, stream>>>(a, plan.grid_ctas);
     return cudaGetLastError();
 }
 

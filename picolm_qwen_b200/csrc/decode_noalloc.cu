@@ -69,6 +69,7 @@ extern "C" int32_t picoattn_decode_noalloc(const picoattn_config_t* cfg, int32_t
     if (st != PICOATTN_OK) return st;
     if (layer < 0 || layer >= cfg->n_layers || n_seqs <= 0) return PICOATTN_EINVAL;
     if (!q || !k || !v || !rope_cos || !rope_sin || !k_cache || !v_cache || !pos || !out) return PICOATTN_EINVAL;
+    if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15u) return PICOATTN_EINVAL;
     if ((q_norm_w == nullptr) != (k_norm_w == nullptr)) return PICOATTN_EINVAL;
     if (max_ctx <= 0 || max_ctx > cfg->max_seq_len) return PICOATTN_ERANGE;
     DecodePlan plan;
@@ -104,6 +105,9 @@ extern "C" int32_t picoattn_decode_noalloc(const picoattn_config_t* cfg, int32_t
     a.part_ml = reinterpret_cast<float*>(w + plan.ws_ml);
     a.part_o = reinterpret_cast<float*>(w + plan.ws_o);
     a.prefix = reinterpret_cast<long long*>(w + plan.ws_prefix);
+    a.row_offset = 0;
+    a.local_rows = cfg->max_seq_len;
+    a.shard_out = nullptr;
     a.tile_rows = plan.tile_rows;
     a.stages = plan.stages;
     a.warps_per_head = plan.warps_per_head;

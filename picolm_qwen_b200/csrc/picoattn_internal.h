@@ -55,6 +55,9 @@ struct DecodeArgs {
     unsigned int* status;
     float* q_rot;              // [n_seqs][hq][hd]
     long long* prefix;         // [n_seqs+1] exclusive prefix sums of attended lengths
+    int row_offset;            // absolute position of local cache row 0 (0 unless the rows are sharded)
+    int local_rows;            // cache rows per layer in the local slab (max_seq unless sharded)
+    float* shard_out;          // non-null: write [n_seqs][hq][hd+2] = (acc/sum, log2-sum-exp) instead of out
     float* part_ml;            // [slot][warp][hq][2]  (max, sum) in log2 units; slot = cta + seq
     float* part_o;             // [slot][warp][hq][hd]
     int tile_rows, stages, warps_per_head, compute_warps;
@@ -78,6 +81,7 @@ struct PrefillArgs {
     uint16_t* v_cache;
     float* out;         // [n_tok][hq*hd]
     unsigned int* status;
+    int* work_counter;  // workspace header: next work item of the persistent attention kernel
     __half* q16;        // workspace: rotated, scaled q [n_tok][hq][hd]
 };
 

@@ -29,6 +29,7 @@
 
 #include "device_common.cuh"
 #include "picoattn_internal.h"
+#include "prep_common.cuh"
 #include "tcgen05.cuh"
 
 namespace picoattn {
@@ -40,83 +41,53 @@ constexpr int BN = 128;  // keys per tile
 constexpr float kRescaleThreshold = 8.0f;
 
 // ---------------------------------------------------------------------------
-// prep
+// prep (head-vector helpers in prep_common.cuh)
 // ---------------------------------------------------------------------------
 
 template <int HD>
-__device__ __forceinline__ void rmsnorm_ref_p(float* x, const float* w, float eps, int lane) {
-    float part = 0.f;
-    if (lane < 4) {
-#pragma unroll 8
-        for (int i = lane; i < HD; i += 4) part = __fadd_rn(part, __fmul_rn(x[i], x[i]));
-    }
-    const float l0 = __shfl_sync(0xffffffffu, part, 0);
-    const float l1 = __shfl_sync(0xffffffffu, part, 1);
-    const float l2 = __shfl_sync(0xffffffffu, part, 2);
-    const float l3 = __shfl_sync(0xffffffffu, part, 3);
-    const float ss = __fadd_rn(__fadd_rn(l0, l2), __fadd_rn(l1, l3));
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)HD), eps)));
-    for (int i = lane; i < HD; i += 32) x[i] = __fmul_rn(__fmul_rn(x[i], scale), w[i]);
-    __syncwarp();
-}
-
-template <int HD>
-__device__ __forceinline__ void rope_ref_p(float* x, const float* c, const float* s, int mode, int lane) {
-    constexpr int half = HD / 2;
-    for (int i = lane; i < half; i += 32) {
-        const int i0 = mode == PICOATTN_ROPE_NEOX ? i : 2 * i;
-        const int i1 = mode == PICOATTN_ROPE_NEOX ? i + half : 2 * i + 1;
-        const float x0 = x[i0], x1 = x[i1], ci = c[i], si = s[i];
-        x[i0] = __fsub_rn(__fmul_rn(x0, ci), __fmul_rn(x1, si));
-        x[i1] = __fadd_rn(__fmul_rn(x0, si), __fmul_rn(x1, ci));
-    }
-    __syncwarp();
-}
-
-__device__ __forceinline__ float load_in(const void* p, size_t i, int dtype) {
-    return dtype == PICOATTN_DTYPE_F16 ? __half2float(reinterpret_cast<const __half*>(p)[i])
-                                       : reinterpret_cast<const float*>(p)[i];
-}
-
-template <int HD>
 __global__ void __launch_bounds__(256) prefill_prep_kernel(PrefillArgs a) {
-    __shared__ float buf[8][HD];
-    const int i = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int pos = a.start + i;
-    const size_t row = ((size_t)a.layer * a.max_seq + pos) * a.kvd;
-    const float* crow = a.rope_cos + (size_t)pos * (HD / 2);
-    const float* srow = a.rope_sin + (size_t)pos * (HD / 2);
-    const float qscale = 1.4426950408889634f / sqrtf((float)HD);
-    float* x = buf[warp];
+    // 8 warps x 4 head vectors of one token per block; all of a warp's global
+    // loads are issued before any of them is used
+    constexpr int V = HD / 32;
+    __shared__ float sq[8][HD];
+    const int tok = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *a.work_counter = 0;  // attention work queue
     const int n_slots = a.hq + 2 * a.hkv;
-    {
-        const int slot = blockIdx.x * 8 + warp;  // one warp per head vector
-        if (slot >= n_slots) return;
-        int kind, h;
-        const void* src;
-        size_t off;
-        if (slot < a.hq) {
-            kind = 0, h = slot, src = a.q, off = ((size_t)i * a.hq + h) * HD;
-        } else if (slot < a.hq + a.hkv) {
-            kind = 1, h = slot - a.hq, src = a.k, off = ((size_t)i * a.hkv + h) * HD;
-        } else {
-            kind = 2, h = slot - a.hq - a.hkv, src = a.v, off = ((size_t)i * a.hkv + h) * HD;
+    const int slot0 = (blockIdx.x * 8 + warp) * 4;
+    if (slot0 >= n_slots) return;
+    const int pos = a.start + tok;
+    RopeLane<HD> rl;
+    rope_lane_load<HD>(rl, a.rope_cos + (size_t)pos * (HD / 2), a.rope_sin + (size_t)pos * (HD / 2), a.rope_mode,
+                       lane);
+    float qw[V], kw[V];
+    if (a.qn_w) {
+#pragma unroll
+        for (int j = 0; j < V; j++) qw[j] = a.qn_w[V * lane + j], kw[j] = a.kn_w[V * lane + j];
+    }
+    Vec<HD> x[4];
+    int kind[4], head[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+        const int slot = slot0 + u;
+        kind[u] = slot < a.hq ? 0 : (slot < a.hq + a.hkv ? 1 : (slot < n_slots ? 2 : 3));
+        head[u] = kind[u] == 0 ? slot : (kind[u] == 1 ? slot - a.hq : slot - a.hq - a.hkv);
+        if (kind[u] == 0) vec_load<HD>(x[u], a.q, ((size_t)tok * a.hq + head[u]) * HD, a.in_dtype, lane);
+        else if (kind[u] == 1) vec_load<HD>(x[u], a.k, ((size_t)tok * a.hkv + head[u]) * HD, a.in_dtype, lane);
+        else if (kind[u] == 2) vec_load<HD>(x[u], a.v, ((size_t)tok * a.hkv + head[u]) * HD, a.in_dtype, lane);
+    }
+    const float qscale = 1.4426950408889634f / sqrtf((float)HD);
+    const size_t row = ((size_t)a.layer * a.max_seq + pos) * a.kvd;
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+        if (kind[u] == 3) break;
+        if (kind[u] != 2) {
+            if (a.qn_w) vec_rmsnorm<HD>(x[u], kind[u] == 0 ? qw : kw, a.eps, sq[warp], lane);
+            vec_rope<HD>(x[u], rl, a.rope_mode, lane);
         }
-        for (int d = lane; d < HD; d += 32) x[d] = load_in(src, off + d, a.in_dtype);
-        __syncwarp();
-        if (kind != 2) {
-            const float* w = kind == 0 ? a.qn_w : a.kn_w;
-            if (w) rmsnorm_ref_p<HD>(x, w, a.eps, lane);
-            rope_ref_p<HD>(x, crow, srow, a.rope_mode, lane);
-        }
-        if (kind == 0) {
-            __half* dst = a.q16 + ((size_t)i * a.hq + h) * HD;
-            for (int d = lane; d < HD; d += 32) dst[d] = __float2half_rn(x[d] * qscale);
-        } else {
-            uint16_t* dst = (kind == 1 ? a.k_cache : a.v_cache) + row + (size_t)h * HD;
-            for (int d = lane; d < HD; d += 32) dst[d] = f32_to_f16_ref(x[d]);
-        }
-        __syncwarp();
+        if (kind[u] == 0)
+            vec_store_h16_scaled<HD>(x[u], a.q16 + ((size_t)tok * a.hq + head[u]) * HD, qscale, lane);
+        else
+            vec_store_ref16<HD>(x[u], (kind[u] == 1 ? a.k_cache : a.v_cache) + row + (size_t)head[u] * HD, lane);
     }
 }
 
@@ -261,24 +232,30 @@ __global__ void __launch_bounds__(192, 1)
             const int b = j & 1;
             mbar_wait(&s_full[b], (uint32_t)((j >> 1) & 1), a.status);
             tc_fence_after();
-            float s[BN];
-#pragma unroll
-            for (int c = 0; c < BN / 32; c++) {
-                uint32_t t[32];
-                tmem_ld32(tS0 + b * 128 + c * 32 + lane_off, t);
-                tmem_ld_wait();
-#pragma unroll
-                for (int e = 0; e < 32; e++) s[c * 32 + e] = __uint_as_float(t[e]);
-            }
+            uint32_t sr[BN];
+            // four loads in flight, one wait
+            tmem_ld32(tS0 + b * 128 + 0 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+            tmem_ld32(tS0 + b * 128 + 32 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+            tmem_ld32(tS0 + b * 128 + 64 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
+            tmem_ld32(tS0 + b * 128 + 96 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
+            tmem_ld_wait();
+            float* s = reinterpret_cast<float*>(sr);
             const int kbase = j * BN;
             if (kbase + BN - 1 > a.start + q0) {  // tile crosses the diagonal of this q tile
 #pragma unroll
                 for (int c = 0; c < BN; c++)
                     if (kbase + c > qpos) s[c] = -INFINITY;
             }
-            float mx = s[0];
+            // row max with 8 independent chains
+            float mx8[8];
 #pragma unroll
-            for (int c = 1; c < BN; c++) mx = fmaxf(mx, s[c]);
+            for (int e = 0; e < 8; e++) mx8[e] = s[e];
+#pragma unroll
+            for (int c = 8; c < BN; c += 8)
+#pragma unroll
+                for (int e = 0; e < 8; e++) mx8[e] = fmaxf(mx8[e], s[c + e]);
+            const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
             if (j == 0) {
                 m_run = mx;
             } else if (__any_sync(0xffffffffu, mx > m_run + kRescaleThreshold)) {
@@ -300,7 +277,7 @@ __global__ void __launch_bounds__(192, 1)
                 l_run *= corr;
                 m_run = m_new;
             }
-            float lsum = 0.f;
+            float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int c = 0; c < BN / 64; c++) {
                 uint32_t t[32];
@@ -308,12 +285,12 @@ __global__ void __launch_bounds__(192, 1)
                 for (int e = 0; e < 32; e++) {
                     const float p0 = ex2(s[c * 64 + 2 * e] - m_run);
                     const float p1 = ex2(s[c * 64 + 2 * e + 1] - m_run);
-                    lsum += p0 + p1;
+                    ls8[e & 7] += p0 + p1;
                     t[e] = pack_half2(p0, p1);
                 }
                 tmem_st32(tS0 + b * 128 + c * 32 + lane_off, t);
             }
-            l_run += lsum;
+            l_run += ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
@@ -342,6 +319,350 @@ __global__ void __launch_bounds__(192, 1)
     }
     __syncthreads();
     if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// attention, head-pair persistent variant (even GQA group size)
+// ---------------------------------------------------------------------------
+//
+// Work item = (128-token q tile, two q heads h0, h0+1 of the same KV group);
+// items are handed out longest-first by an atomic counter, so a persistent
+// grid of one CTA per SM balances the causal triangle.  Both heads read the
+// same K/V tiles: one TMA stream feeds two softmax warpgroups, each with its own
+// S (128 TMEM columns, P written back over it) and O (128 columns):
+//   TMEM  [0,128) S0   [128,256) O0   [256,384) S1   [384,512) O1
+// Warps 0-3 / 4-7 softmax for head 0 / 1 (thread = q row = TMEM lane), warp 8
+// TMA and work-queue fetch, warp 9 MMA issue.  Per KV tile t the MMA warp issues
+// PV0(t), QK0(t+1), PV1(t), QK1(t+1), so each warpgroup's softmax overlaps the
+// other head's tensor work.
+
+template <int HD>
+struct Attn2Smem {
+    static constexpr int kBoxBytes = BM * 128;
+    static constexpr int kTileBytes = (HD / 64) * kBoxBytes;
+    static constexpr int NK = 2, NV = 2;
+    static constexpr int kQ = 0;  // Q0, Q1
+    static constexpr int kK = kQ + 2 * kTileBytes;
+    static constexpr int kV = kK + NK * kTileBytes;
+    static constexpr int kBars = kV + NV * kTileBytes;
+    static constexpr int kEnd = kBars + 512;
+    static constexpr int kDynBytes = kEnd + 1024;
+};
+
+template <int HD>
+__global__ void __maxnreg__(184)
+    prefill_attn2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV, PrefillArgs a) {
+    using L = Attn2Smem<HD>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_pairs = a.hq / 2;
+    const int n_items = a.n_qtiles * n_pairs;
+
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBars);
+    uint64_t* item_full = bars + 0;     // [2]
+    uint64_t* item_empty = bars + 2;    // [2]
+    uint64_t* q_full = bars + 4;
+    uint64_t* q_empty = bars + 5;
+    uint64_t* k_full = bars + 6;        // [NK]
+    uint64_t* k_empty = k_full + L::NK;
+    uint64_t* v_full = k_empty + L::NK;
+    uint64_t* v_empty = v_full + L::NV;
+    uint64_t* s_full = v_empty + L::NV;  // [2] per head
+    uint64_t* p_full = s_full + 2;       // [2]
+    uint64_t* pv_done = p_full + 2;      // [2]
+    uint64_t* o_free = pv_done + 2;      // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 2);
+    int* item_slot = reinterpret_cast<int*>(tmem_slot + 1);  // [2]
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 2; i++) mbar_init(&item_full[i], 1), mbar_init(&item_empty[i], 3);
+        mbar_init(q_full, 1);
+        mbar_init(q_empty, 1);
+        for (int s = 0; s < L::NK; s++) mbar_init(&k_full[s], 1), mbar_init(&k_empty[s], 1);
+        for (int s = 0; s < L::NV; s++) mbar_init(&v_full[s], 1), mbar_init(&v_empty[s], 1);
+        for (int w = 0; w < 2; w++)
+            mbar_init(&s_full[w], 1), mbar_init(&p_full[w], 4), mbar_init(&pv_done[w], 1), mbar_init(&o_free[w], 4);
+        fence_mbar_init();
+    }
+    if (warp == 9) tmem_alloc(tmem_slot, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t sQ = smem_u32(smem + L::kQ);
+    const uint32_t sK = smem_u32(smem + L::kK);
+    const uint32_t sV = smem_u32(smem + L::kV);
+
+    auto n_kv_of = [&](int qt) {
+        const int q_last = min(qt * BM + BM, a.n_tok) - 1;
+        return (a.start + q_last) / BN + 1;
+    };
+    auto decode_item = [&](int it, int& qt, int& h0) {
+        qt = a.n_qtiles - 1 - it / n_pairs;  // longest rows of the causal triangle first
+        h0 = 2 * (it % n_pairs);
+    };
+
+    if (warp == 8) {
+        // ---------------- work queue + TMA producer ----------------
+        if (lane == 0) {
+            prefetch_tmap(&tmQ);
+            prefetch_tmap(&tmK);
+            prefetch_tmap(&tmV);
+            int t = 0;  // KV tile counter across items
+            for (int k = 0;; k++) {
+                const int slot = k & 1;
+                if (k >= 2) mbar_wait(&item_empty[slot], (uint32_t)(((k >> 1) - 1) & 1), a.status);
+                int it = atomicAdd(a.work_counter, 1);
+                if (it >= n_items) it = -1;
+                *reinterpret_cast<volatile int*>(&item_slot[slot]) = it;
+                mbar_arrive(&item_full[slot]);  // release: the slot write is visible to waiters
+                if (it < 0) break;
+                int qt, h0;
+                decode_item(it, qt, h0);
+                const int kvh = h0 / a.g;
+                if (k >= 1) mbar_wait(q_empty, (uint32_t)((k - 1) & 1), a.status);
+                mbar_arrive_expect_tx(q_full, 2 * L::kTileBytes);
+                for (int w = 0; w < 2; w++)
+                    for (int c = 0; c < HD / 64; c++)
+                        tma_load_2d(smem + L::kQ + w * L::kTileBytes + c * L::kBoxBytes, &tmQ, (h0 + w) * HD + 64 * c,
+                                    qt * BM, q_full);
+                const int n_kv = n_kv_of(qt);
+                for (int j = 0; j < n_kv; j++, t++) {
+                    const int sk = t % L::NK, uk = t / L::NK;
+                    if (uk > 0) mbar_wait(&k_empty[sk], (uint32_t)((uk - 1) & 1), a.status);
+                    mbar_arrive_expect_tx(&k_full[sk], L::kTileBytes);
+                    for (int c = 0; c < HD / 64; c++)
+                        tma_load_2d(smem + L::kK + sk * L::kTileBytes + c * L::kBoxBytes, &tmK, kvh * HD + 64 * c,
+                                    j * BN, &k_full[sk]);
+                    const int sv = t % L::NV, uv = t / L::NV;
+                    if (uv > 0) mbar_wait(&v_empty[sv], (uint32_t)((uv - 1) & 1), a.status);
+                    mbar_arrive_expect_tx(&v_full[sv], L::kTileBytes);
+                    for (int c = 0; c < HD / 64; c++)
+                        tma_load_2d(smem + L::kV + sv * L::kTileBytes + c * L::kBoxBytes, &tmV, kvh * HD + 64 * c,
+                                    j * BN, &v_full[sv]);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 9) {
+        // ---------------- MMA issuer ----------------
+        constexpr uint32_t idesc_qk = idesc_f16_f32(BM, BN, false, false);
+        constexpr uint32_t idesc_pv = idesc_f16_f32(BM, HD, false, true);
+        int t = 0;  // KV tile counter across items
+        auto issue_qk = [&](int w, int tt, uint32_t kbase) {
+            if (tt >= 1) mbar_wait(&pv_done[w], (uint32_t)((tt - 1) & 1), a.status);  // S_w holds P_w(tt-1)
+            tc_fence_after();
+            if (lane == 0) {
+                const uint32_t qbase = sQ + w * L::kTileBytes;
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; kk++) {
+                    const uint32_t koff = (kk >> 2) * L::kBoxBytes + (kk & 3) * 32;
+                    umma_ss(tmem + w * 256, smem_desc_sw128(qbase + koff, 16, 1024),
+                            smem_desc_sw128(kbase + koff, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
+                }
+                umma_commit(&s_full[w]);
+            }
+            __syncwarp();
+        };
+        auto issue_pv = [&](int w, int tt, bool first, int k, uint32_t vbase) {
+            mbar_wait(&p_full[w], (uint32_t)(tt & 1), a.status);
+            if (first && k >= 1) mbar_wait(&o_free[w], (uint32_t)((k - 1) & 1), a.status);
+            tc_fence_after();
+            if (lane == 0) {
+#pragma unroll
+                for (int kk = 0; kk < BN / 16; kk++)
+                    umma_ts(tmem + w * 256 + 128, tmem + w * 256 + kk * 8,
+                            smem_desc_sw128(vbase + kk * 16 * 128, L::kBoxBytes, 1024), idesc_pv,
+                            (!first || kk > 0) ? 1u : 0u);
+                umma_commit(&pv_done[w]);
+            }
+            __syncwarp();
+        };
+        for (int k = 0;; k++) {
+            const int slot = k & 1;
+            mbar_wait(&item_full[slot], (uint32_t)((k >> 1) & 1), a.status);
+            const int it = *reinterpret_cast<volatile int*>(&item_slot[slot]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&item_empty[slot]);
+            if (it < 0) break;
+            int qt, h0;
+            decode_item(it, qt, h0);
+            const int n_kv = n_kv_of(qt);
+            mbar_wait(q_full, (uint32_t)(k & 1), a.status);
+            // prologue: QK of the first tile for both heads
+            {
+                const int sk = t % L::NK;
+                mbar_wait(&k_full[sk], (uint32_t)((t / L::NK) & 1), a.status);
+                const uint32_t kb = sK + sk * L::kTileBytes;
+                issue_qk(0, t, kb);
+                issue_qk(1, t, kb);
+                if (lane == 0) {
+                    umma_commit(&k_empty[sk]);
+                    if (n_kv == 1) umma_commit(q_empty);
+                }
+                __syncwarp();
+            }
+            for (int j = 0; j < n_kv; j++, t++) {
+                const int sv = t % L::NV;
+                mbar_wait(&v_full[sv], (uint32_t)((t / L::NV) & 1), a.status);
+                const uint32_t vb = sV + sv * L::kTileBytes;
+                const bool more = j + 1 < n_kv;
+                uint32_t kb_next = 0;
+                int sk_next = 0;
+                if (more) {
+                    sk_next = (t + 1) % L::NK;
+                    mbar_wait(&k_full[sk_next], (uint32_t)(((t + 1) / L::NK) & 1), a.status);
+                    kb_next = sK + sk_next * L::kTileBytes;
+                }
+                issue_pv(0, t, j == 0, k, vb);
+                if (more) issue_qk(0, t + 1, kb_next);
+                issue_pv(1, t, j == 0, k, vb);
+                if (lane == 0) umma_commit(&v_empty[sv]);
+                __syncwarp();
+                if (more) {
+                    issue_qk(1, t + 1, kb_next);
+                    if (lane == 0) {
+                        umma_commit(&k_empty[sk_next]);
+                        if (j + 2 == n_kv) umma_commit(q_empty);
+                    }
+                    __syncwarp();
+                }
+            }
+        }
+    } else {
+        // ---------------- softmax warpgroups ----------------
+        const int w = warp >> 2;           // head of the pair
+        const int r = threadIdx.x & 127;   // q row == TMEM lane
+        const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+        const uint32_t tS = tmem + w * 256, tO = tS + 128;
+        int t = 0;
+        for (int k = 0;; k++) {
+            const int slot = k & 1;
+            mbar_wait(&item_full[slot], (uint32_t)((k >> 1) & 1), a.status);
+            const int it = *reinterpret_cast<volatile int*>(&item_slot[slot]);
+            // one arrival per warpgroup, after all of its warps have read the slot
+            asm volatile("bar.sync %0, 128;" ::"r"(1 + w) : "memory");
+            if ((threadIdx.x & 127) == 0) mbar_arrive(&item_empty[slot]);
+            if (it < 0) break;
+            int qt, h0;
+            decode_item(it, qt, h0);
+            const int h = h0 + w;
+            const int q0 = qt * BM;
+            const int qpos = a.start + q0 + r;
+            const int n_kv = n_kv_of(qt);
+            float m_run = -INFINITY, l_run = 0.f;
+            for (int j = 0; j < n_kv; j++, t++) {
+                mbar_wait(&s_full[w], (uint32_t)(t & 1), a.status);
+                tc_fence_after();
+                const int kbase = j * BN;
+                const bool diag = kbase + BN - 1 > a.start + q0;  // tile crosses this q tile's diagonal
+                // pass 1: row max (scores are read again in pass 2, so none stay live)
+                float mx;
+                {
+                    uint32_t sr[BN];
+                    tmem_ld32(tS + 0 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+                    tmem_ld32(tS + 32 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+                    tmem_ld32(tS + 64 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
+                    tmem_ld32(tS + 96 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
+                    tmem_ld_wait();
+                    float* s = reinterpret_cast<float*>(sr);
+                    if (diag) {
+#pragma unroll
+                        for (int c = 0; c < BN; c++)
+                            if (kbase + c > qpos) s[c] = -INFINITY;
+                    }
+                    float mx8[8];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) mx8[e] = s[e];
+#pragma unroll
+                    for (int c = 8; c < BN; c += 8)
+#pragma unroll
+                        for (int e = 0; e < 8; e++) mx8[e] = fmaxf(mx8[e], s[c + e]);
+                    mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+                }
+                if (j == 0) {
+                    m_run = mx;
+                } else if (__any_sync(0xffffffffu, mx > m_run + kRescaleThreshold)) {
+                    const float m_new = fmaxf(m_run, mx);
+                    const float corr = ex2(m_run - m_new);
+                    mbar_wait(&pv_done[w], (uint32_t)((t - 1) & 1), a.status);
+                    tc_fence_after();
+#pragma unroll
+                    for (int c = 0; c < HD / 32; c++) {
+                        uint32_t o[32];
+                        tmem_ld32(tO + c * 32 + lane_off, o);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int e = 0; e < 32; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
+                        tmem_st32(tO + c * 32 + lane_off, o);
+                    }
+                    tmem_st_wait();
+                    l_run *= corr;
+                    m_run = m_new;
+                }
+                // pass 2: 32 scores at a time -> p (fp16) over the S columns already
+                // read: chunk c's P lands in columns [16c, 16c+16) < 32(c+1)
+                float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                uint32_t sbuf[2][32];
+                tmem_ld32(tS + lane_off, sbuf[0]);
+#pragma unroll
+                for (int c = 0; c < BN / 32; c++) {
+                    tmem_ld_wait();
+                    uint32_t (&sr)[32] = sbuf[c & 1];
+                    if (c + 1 < BN / 32) tmem_ld32(tS + (c + 1) * 32 + lane_off, sbuf[(c + 1) & 1]);  // next chunk in flight
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int e = 0; e < 16; e++) {
+                        float s0 = __uint_as_float(sr[2 * e]), s1 = __uint_as_float(sr[2 * e + 1]);
+                        if (diag) {
+                            if (kbase + c * 32 + 2 * e > qpos) s0 = -INFINITY;
+                            if (kbase + c * 32 + 2 * e + 1 > qpos) s1 = -INFINITY;
+                        }
+                        const float p0 = ex2(s0 - m_run);
+                        const float p1 = ex2(s1 - m_run);
+                        ls8[e & 7] += p0 + p1;
+                        pk[e] = pack_half2(p0, p1);
+                    }
+                    tmem_st16(tS + c * 16 + lane_off, pk);
+                }
+                l_run += ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_full[w]);
+            }
+            // epilogue: O / l -> out[token][h][:], then hand O back to the MMA warp
+            mbar_wait(&pv_done[w], (uint32_t)((t - 1) & 1), a.status);
+            tc_fence_after();
+            const int tok = q0 + r;
+            const float inv = 1.0f / l_run;
+            float* dst = a.out + ((size_t)tok * a.hq + h) * HD;
+#pragma unroll
+            for (int c = 0; c < HD / 32; c++) {
+                uint32_t o[32];
+                tmem_ld32(tO + c * 32 + lane_off, o);
+                tmem_ld_wait();
+                if (tok < a.n_tok) {
+#pragma unroll
+                    for (int e = 0; e < 32; e += 4)
+                        *reinterpret_cast<float4*>(dst + c * 32 + e) =
+                            make_float4(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv,
+                                        __uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&o_free[w]);
+        }
+    }
+    __syncthreads();
+    if (warp == 9) {
         tc_fence_after();
         tmem_dealloc(tmem, 512);
     }
@@ -385,7 +706,7 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, u
 template <int HD>
 cudaError_t launch_prefill_hd(const PrefillArgs& a, cudaStream_t stream, unsigned stages) {
     if (stages & PICOATTN_STAGE_PREPARE) {
-        const unsigned slot_blocks = (unsigned)((a.hq + 2 * a.hkv + 7) / 8);
+        const unsigned slot_blocks = (unsigned)((a.hq + 2 * a.hkv + 31) / 32);  // 32 head vectors per block
         prefill_prep_kernel<HD><<<dim3(slot_blocks, (unsigned)a.n_tok), 256, 0, stream>>>(a);
     }
     if (stages & PICOATTN_STAGE_ATTEND) {
@@ -393,6 +714,9 @@ cudaError_t launch_prefill_hd(const PrefillArgs& a, cudaStream_t stream, unsigne
         if (!attr_done) {
             cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  AttnSmem<HD>::kDynBytes);
+            if (e != cudaSuccess) return e;
+            e = cudaFuncSetAttribute(prefill_attn2_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Attn2Smem<HD>::kDynBytes);
             if (e != cudaSuccess) return e;
             attr_done = true;
         }
@@ -403,8 +727,18 @@ cudaError_t launch_prefill_hd(const PrefillArgs& a, cudaStream_t stream, unsigne
             !make_map(&mk, a.k_cache + slab, kvd, (uint64_t)(a.start + a.n_tok), kvd * 2) ||
             !make_map(&mv, a.v_cache + slab, kvd, (uint64_t)(a.start + a.n_tok), kvd * 2))
             return cudaErrorInvalidValue;
-        dim3 grid((unsigned)a.n_qtiles, (unsigned)a.hq);
-        prefill_attn_kernel<HD><<<grid, 192, AttnSmem<HD>::kDynBytes, stream>>>(mq, mk, mv, a);
+        if (a.g % 2 == 0) {
+            // head pairs share a KV head: persistent grid, one CTA per SM
+            const int n_items = a.n_qtiles * (a.hq / 2);
+            int dev = 0, sms = 148;
+            cudaGetDevice(&dev);
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+            const int grid = n_items < sms ? n_items : sms;
+            prefill_attn2_kernel<HD><<<grid, 320, Attn2Smem<HD>::kDynBytes, stream>>>(mq, mk, mv, a);
+        } else {
+            dim3 grid((unsigned)a.n_qtiles, (unsigned)a.hq);
+            prefill_attn_kernel<HD><<<grid, 192, AttnSmem<HD>::kDynBytes, stream>>>(mq, mk, mv, a);
+        }
     }
     return cudaGetLastError();
 }

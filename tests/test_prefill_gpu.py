@@ -59,7 +59,7 @@ def test_prefill_matches_reference_golden(cuda, golden_dir):
     v = dev(g["v"].astype(np.float16))
     assert np.array_equal(g["q"].astype(np.float16).astype(np.float32), g["q"])
     s = st.prefill(1, 0, q, k, v, out, dev(g["q_norm_w"]), dev(g["k_norm_w"]))
-    assert s == 0, abi.lib().picoattn_strerror(s)
+    assert s == 0, (abi.lib().picoattn_strerror(s), abi.lib().picoattn_last_cuda_error())
     torch.cuda.synchronize()
     assert_close(out.cpu().numpy(), g["out"], "prefill")
     assert np.array_equal(st.k_cache[0, 1, :n].cpu().numpy(), g["kcache"].view(np.int16))
