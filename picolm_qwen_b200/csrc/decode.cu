@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(256) decode_prep_kernel(DecodeArgs a) {
     }
     // 8 warps x 4 head vectors of one sequence per block (helpers: prep_common.cuh)
     constexpr int V = HD / 32;
-    __shared__ float sq[8][HD];
+    __shared__ float sq[8][4 * HD];
     const int b = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pos = seq_pos(a, b);
     if (!pos_ok(a, pos)) {
@@ -137,12 +137,22 @@ __global__ void __launch_bounds__(256) decode_prep_kernel(DecodeArgs a) {
     const int lrow = pos - a.row_offset;  // the new row lives in this slab only if 0 <= lrow < local_rows
     const bool row_here = lrow >= 0 && lrow < a.local_rows;
     const size_t row = ((size_t)a.layer * a.local_rows + (row_here ? lrow : 0)) * a.kvd;
+    if (a.qn_w) {  // QK-RMSNorm of the q and k vectors, four at a time
+        float wsel[4][V];
+        bool nrm[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            nrm[u] = kind[u] == 0 || kind[u] == 1;
+#pragma unroll
+            for (int j = 0; j < V; j++) wsel[u][j] = kind[u] == 0 ? qw[j] : kw[j];
+        }
+        vec_rmsnorm4<HD>(x, wsel, nrm, a.eps, sq[warp], lane);
+    }
 #pragma unroll
     for (int u = 0; u < 4; u++) {
         if (kind[u] == 3) break;
         if (kind[u] != 0 && !row_here) continue;
         if (kind[u] != 2) {
-            if (a.qn_w) vec_rmsnorm<HD>(x[u], kind[u] == 0 ? qw : kw, a.eps, sq[warp], lane);
             vec_rope<HD>(x[u], rl, a.rope_mode, lane);
         }
         if (kind[u] == 0)

@@ -137,6 +137,15 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// Two exponentials in one MUFU operation: 2^x for a pair of arguments rounded
+// to fp16, result as a packed fp16 pair (low half = first argument).
+__device__ __forceinline__ uint32_t ex2_h2(float x0, float x1) {
+    uint32_t in, out;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(in) : "f"(x1), "f"(x0));
+    asm("ex2.approx.f16x2 %0, %1;" : "=r"(out) : "r"(in));
+    return out;
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     const __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<const uint32_t*>(&h);

@@ -39,6 +39,8 @@ namespace {
 constexpr int BM = 128;  // q rows per tile
 constexpr int BN = 128;  // keys per tile
 constexpr float kRescaleThreshold = 8.0f;
+// stale-max margin of the single-pass softmax: p <= 2^15 < 65504 stays finite and exact in fp16
+constexpr float kStaleMaxMargin = 15.0f;
 
 // ---------------------------------------------------------------------------
 // prep (head-vector helpers in prep_common.cuh)
@@ -49,7 +51,7 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(PrefillArgs a) {
     // 8 warps x 4 head vectors of one token per block; all of a warp's global
     // loads are issued before any of them is used
     constexpr int V = HD / 32;
-    __shared__ float sq[8][HD];
+    __shared__ float sq[8][4 * HD];
     const int tok = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *a.work_counter = 0;  // attention work queue
     const int n_slots = a.hq + 2 * a.hkv;
@@ -77,11 +79,21 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(PrefillArgs a) {
     }
     const float qscale = 1.4426950408889634f / sqrtf((float)HD);
     const size_t row = ((size_t)a.layer * a.max_seq + pos) * a.kvd;
+    if (a.qn_w) {  // QK-RMSNorm of the q and k vectors, four at a time
+        float wsel[4][V];
+        bool nrm[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            nrm[u] = kind[u] == 0 || kind[u] == 1;
+#pragma unroll
+            for (int j = 0; j < V; j++) wsel[u][j] = kind[u] == 0 ? qw[j] : kw[j];
+        }
+        vec_rmsnorm4<HD>(x, wsel, nrm, a.eps, sq[warp], lane);
+    }
 #pragma unroll
     for (int u = 0; u < 4; u++) {
         if (kind[u] == 3) break;
         if (kind[u] != 2) {
-            if (a.qn_w) vec_rmsnorm<HD>(x[u], kind[u] == 0 ? qw : kw, a.eps, sq[warp], lane);
             vec_rope<HD>(x[u], rl, a.rope_mode, lane);
         }
         if (kind[u] == 0)
@@ -343,7 +355,9 @@ template <int HD>
 struct Attn2Smem {
     static constexpr int kBoxBytes = BM * 128;
     static constexpr int kTileBytes = (HD / 64) * kBoxBytes;
-    static constexpr int NK = 2, NV = 2;
+    // V(t) may only load once PV(t-NV) has finished; a tile takes ~1.5k cycles
+    // to land, so a third V stage keeps the load off the critical path
+    static constexpr int NK = 2, NV = 3;
     static constexpr int kQ = 0;  // Q0, Q1
     static constexpr int kK = kQ + 2 * kTileBytes;
     static constexpr int kV = kK + NK * kTileBytes;
@@ -353,7 +367,7 @@ struct Attn2Smem {
 };
 
 template <int HD>
-__global__ void __maxnreg__(184)
+__global__ void __maxnreg__(168)
     prefill_attn2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, PrefillArgs a) {
     using L = Attn2Smem<HD>;
@@ -514,13 +528,13 @@ __global__ void __maxnreg__(184)
                 const bool more = j + 1 < n_kv;
                 uint32_t kb_next = 0;
                 int sk_next = 0;
-                if (more) {
+                issue_pv(0, t, j == 0, k, vb);
+                if (more) {  // K(t+1) is needed only from here on
                     sk_next = (t + 1) % L::NK;
                     mbar_wait(&k_full[sk_next], (uint32_t)(((t + 1) / L::NK) & 1), a.status);
                     kb_next = sK + sk_next * L::kTileBytes;
+                    issue_qk(0, t + 1, kb_next);
                 }
-                issue_pv(0, t, j == 0, k, vb);
-                if (more) issue_qk(0, t + 1, kb_next);
                 issue_pv(1, t, j == 0, k, vb);
                 if (lane == 0) umma_commit(&v_empty[sv]);
                 __syncwarp();
@@ -561,77 +575,117 @@ __global__ void __maxnreg__(184)
                 tc_fence_after();
                 const int kbase = j * BN;
                 const bool diag = kbase + BN - 1 > a.start + q0;  // tile crosses this q tile's diagonal
-                // pass 1: row max (scores are read again in pass 2, so none stay live)
-                float mx;
-                {
-                    uint32_t sr[BN];
-                    tmem_ld32(tS + 0 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-                    tmem_ld32(tS + 32 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-                    tmem_ld32(tS + 64 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
-                    tmem_ld32(tS + 96 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
-                    tmem_ld_wait();
-                    float* s = reinterpret_cast<float*>(sr);
-                    if (diag) {
+                // Optimistic single pass (every tile after the first): p = 2^(s - m_run)
+                // with the running max, kept in registers while the tile max is
+                // tracked.  p <= 2^15 is exact in fp16 and safe in the fp32 sums, so
+                // unless a row max exceeds m_run by more than that, P is stored as is.
+                bool done = false;
+                float mx = -INFINITY;
+                if (j > 0) {
+                    uint32_t pk[BN / 2];
+                    float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                    float mx8[8] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY,
+                                    -INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                    uint32_t sbuf[2][32];
+                    tmem_ld32(tS + lane_off, sbuf[0]);
 #pragma unroll
-                        for (int c = 0; c < BN; c++)
-                            if (kbase + c > qpos) s[c] = -INFINITY;
+                    for (int c = 0; c < BN / 32; c++) {
+                        tmem_ld_wait();
+                        uint32_t (&sr)[32] = sbuf[c & 1];
+                        if (c + 1 < BN / 32) tmem_ld32(tS + (c + 1) * 32 + lane_off, sbuf[(c + 1) & 1]);
+#pragma unroll
+                        for (int e = 0; e < 16; e++) {
+                            float s0 = __uint_as_float(sr[2 * e]), s1 = __uint_as_float(sr[2 * e + 1]);
+                            if (diag) {
+                                if (kbase + c * 32 + 2 * e > qpos) s0 = -INFINITY;
+                                if (kbase + c * 32 + 2 * e + 1 > qpos) s1 = -INFINITY;
+                            }
+                            mx8[e & 7] = fmaxf(mx8[e & 7], fmaxf(s0, s1));
+                            const float p0 = ex2(s0 - m_run);
+                            const float p1 = ex2(s1 - m_run);
+                            ls8[e & 7] += p0 + p1;
+                            pk[c * 16 + e] = pack_half2(p0, p1);
+                        }
                     }
-                    float mx8[8];
-#pragma unroll
-                    for (int e = 0; e < 8; e++) mx8[e] = s[e];
-#pragma unroll
-                    for (int c = 8; c < BN; c += 8)
-#pragma unroll
-                        for (int e = 0; e < 8; e++) mx8[e] = fmaxf(mx8[e], s[c + e]);
                     mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+                    if (!__any_sync(0xffffffffu, mx > m_run + kStaleMaxMargin)) {
+                        tmem_st32(tS + 0 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
+                        tmem_st32(tS + 32 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
+                        l_run += ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
+                        done = true;
+                    }
                 }
-                if (j == 0) {
-                    m_run = mx;
-                } else if (__any_sync(0xffffffffu, mx > m_run + kRescaleThreshold)) {
-                    const float m_new = fmaxf(m_run, mx);
-                    const float corr = ex2(m_run - m_new);
-                    mbar_wait(&pv_done[w], (uint32_t)((t - 1) & 1), a.status);
-                    tc_fence_after();
-#pragma unroll
-                    for (int c = 0; c < HD / 32; c++) {
-                        uint32_t o[32];
-                        tmem_ld32(tO + c * 32 + lane_off, o);
+                if (!done) {
+                    if (j == 0) {
+                        // first tile of the item: row max first (scores read twice)
+                        uint32_t sr[BN];
+                        tmem_ld32(tS + 0 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+                        tmem_ld32(tS + 32 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+                        tmem_ld32(tS + 64 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
+                        tmem_ld32(tS + 96 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
                         tmem_ld_wait();
-#pragma unroll
-                        for (int e = 0; e < 32; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
-                        tmem_st32(tO + c * 32 + lane_off, o);
-                    }
-                    tmem_st_wait();
-                    l_run *= corr;
-                    m_run = m_new;
-                }
-                // pass 2: 32 scores at a time -> p (fp16) over the S columns already
-                // read: chunk c's P lands in columns [16c, 16c+16) < 32(c+1)
-                float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-                uint32_t sbuf[2][32];
-                tmem_ld32(tS + lane_off, sbuf[0]);
-#pragma unroll
-                for (int c = 0; c < BN / 32; c++) {
-                    tmem_ld_wait();
-                    uint32_t (&sr)[32] = sbuf[c & 1];
-                    if (c + 1 < BN / 32) tmem_ld32(tS + (c + 1) * 32 + lane_off, sbuf[(c + 1) & 1]);  // next chunk in flight
-                    uint32_t pk[16];
-#pragma unroll
-                    for (int e = 0; e < 16; e++) {
-                        float s0 = __uint_as_float(sr[2 * e]), s1 = __uint_as_float(sr[2 * e + 1]);
+                        float* sv = reinterpret_cast<float*>(sr);
                         if (diag) {
-                            if (kbase + c * 32 + 2 * e > qpos) s0 = -INFINITY;
-                            if (kbase + c * 32 + 2 * e + 1 > qpos) s1 = -INFINITY;
+#pragma unroll
+                            for (int c = 0; c < BN; c++)
+                                if (kbase + c > qpos) sv[c] = -INFINITY;
                         }
-                        const float p0 = ex2(s0 - m_run);
-                        const float p1 = ex2(s1 - m_run);
-                        ls8[e & 7] += p0 + p1;
-                        pk[e] = pack_half2(p0, p1);
+                        float mx8[8];
+#pragma unroll
+                        for (int e = 0; e < 8; e++) mx8[e] = sv[e];
+#pragma unroll
+                        for (int c = 8; c < BN; c += 8)
+#pragma unroll
+                            for (int e = 0; e < 8; e++) mx8[e] = fmaxf(mx8[e], sv[c + e]);
+                        m_run = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                      fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+                    } else {
+                        // a row max jumped: rescale O (sum through tile j-1) to the new max
+                        const float m_new = fmaxf(m_run, mx);
+                        const float corr = ex2(m_run - m_new);
+                        mbar_wait(&pv_done[w], (uint32_t)((t - 1) & 1), a.status);
+                        tc_fence_after();
+#pragma unroll
+                        for (int c = 0; c < HD / 32; c++) {
+                            uint32_t o[32];
+                            tmem_ld32(tO + c * 32 + lane_off, o);
+                            tmem_ld_wait();
+#pragma unroll
+                            for (int e = 0; e < 32; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
+                            tmem_st32(tO + c * 32 + lane_off, o);
+                        }
+                        tmem_st_wait();
+                        l_run *= corr;
+                        m_run = m_new;
                     }
-                    tmem_st16(tS + c * 16 + lane_off, pk);
+                    // exact pass: 32 scores at a time -> p (fp16) over the S columns
+                    // already read: chunk c's P lands in columns [16c, 16c+16) < 32(c+1)
+                    float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                    uint32_t sbuf[2][32];
+                    tmem_ld32(tS + lane_off, sbuf[0]);
+#pragma unroll
+                    for (int c = 0; c < BN / 32; c++) {
+                        tmem_ld_wait();
+                        uint32_t (&sr)[32] = sbuf[c & 1];
+                        if (c + 1 < BN / 32) tmem_ld32(tS + (c + 1) * 32 + lane_off, sbuf[(c + 1) & 1]);
+                        uint32_t pk[16];
+#pragma unroll
+                        for (int e = 0; e < 16; e++) {
+                            float s0 = __uint_as_float(sr[2 * e]), s1 = __uint_as_float(sr[2 * e + 1]);
+                            if (diag) {
+                                if (kbase + c * 32 + 2 * e > qpos) s0 = -INFINITY;
+                                if (kbase + c * 32 + 2 * e + 1 > qpos) s1 = -INFINITY;
+                            }
+                            const float p0 = ex2(s0 - m_run);
+                            const float p1 = ex2(s1 - m_run);
+                            ls8[e & 7] += p0 + p1;
+                            pk[e] = pack_half2(p0, p1);
+                        }
+                        tmem_st16(tS + c * 16 + lane_off, pk);
+                    }
+                    l_run += ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
                 }
-                l_run += ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
                 tmem_st_wait();
                 tc_fence_before();
                 __syncwarp();
@@ -727,7 +781,15 @@ cudaError_t launch_prefill_hd(const PrefillArgs& a, cudaStream_t stream, unsigne
             !make_map(&mk, a.k_cache + slab, kvd, (uint64_t)(a.start + a.n_tok), kvd * 2) ||
             !make_map(&mv, a.v_cache + slab, kvd, (uint64_t)(a.start + a.n_tok), kvd * 2))
             return cudaErrorInvalidValue;
-        if (a.g % 2 == 0) {
+        // the head-pair kernel needs one resident CTA of 320 threads per SM
+        static int pair_ok = -1;
+        if (pair_ok < 0) {
+            int nb = 0;
+            pair_ok = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, prefill_attn2_kernel<HD>, 320,
+                                                                    Attn2Smem<HD>::kDynBytes) == cudaSuccess &&
+                      nb > 0;
+        }
+        if (a.g % 2 == 0 && pair_ok) {
             // head pairs share a KV head: persistent grid, one CTA per SM
             const int n_items = a.n_qtiles * (a.hq / 2);
             int dev = 0, sms = 148;

@@ -93,6 +93,43 @@ __device__ __forceinline__ void vec_rmsnorm(Vec<HD>& v, const float (&w)[HD / 32
     __syncwarp();  // sq is reused by the next vector
 }
 
+// RMSNorm of up to four vectors at once (norm[u] selects them; w[u] are this
+// lane's weights for vector u).  Same arithmetic as vec_rmsnorm: lanes 4u..4u+3
+// run the reference's four interleaved lane sums of vector u side by side, lane
+// u folds them and computes vector u's scale, so one summation loop and one
+// divide/sqrt sequence serve four vectors.  sq: 4*HD floats of shared memory.
+template <int HD>
+__device__ __forceinline__ void vec_rmsnorm4(Vec<HD> (&v)[4], const float (&w)[4][HD / 32], const bool (&norm)[4],
+                                             float eps, float* sq, int lane) {
+    constexpr int V = HD / 32;
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+#pragma unroll
+        for (int j = 0; j < V; j++) sq[u * HD + V * lane + j] = __fmul_rn(v[u].x[j], v[u].x[j]);
+    __syncwarp();
+    float part = 0.f;
+    if (lane < 16) {
+        const float* s = sq + (lane >> 2) * HD;
+#pragma unroll 8
+        for (int d = lane & 3; d < HD; d += 4) part = __fadd_rn(part, s[d]);
+    }
+    // lane u < 4 gathers the four lane sums of vector u
+    const int src = (lane & 3) * 4;
+    const float l0 = __shfl_sync(0xffffffffu, part, src + 0), l1 = __shfl_sync(0xffffffffu, part, src + 1);
+    const float l2 = __shfl_sync(0xffffffffu, part, src + 2), l3 = __shfl_sync(0xffffffffu, part, src + 3);
+    const float ss = __fadd_rn(__fadd_rn(l0, l2), __fadd_rn(l1, l3));
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)HD), eps)));
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+        const float su = __shfl_sync(0xffffffffu, scale, u);
+        if (norm[u]) {
+#pragma unroll
+            for (int j = 0; j < V; j++) v[u].x[j] = __fmul_rn(__fmul_rn(v[u].x[j], su), w[u][j]);
+        }
+    }
+    __syncwarp();  // sq is reused
+}
+
 template <int HD>
 __device__ __forceinline__ void vec_rope(Vec<HD>& v, const RopeLane<HD>& r, int mode, int lane) {
     constexpr int V = HD / 32;
