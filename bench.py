@@ -73,7 +73,7 @@ class ClockSampler:
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting"}
 
-    def __init__(self, device_index: int, pci_bus_id: str | None):
+    def __init__(self, device_index: int, props=None):
         self.samples: list[int] = []
         self.reasons: set[str] = set()
         self.max_mhz = None
@@ -84,11 +84,19 @@ class ClockSampler:
             pynvml.nvmlInit()
             self.nv = pynvml
             h = None
-            if pci_bus_id:
+            # the CUDA device under CUDA_VISIBLE_DEVICES: match by UUID, then PCI address
+            if props is not None:
                 try:
-                    h = pynvml.nvmlDeviceGetHandleByPciBusId(pci_bus_id)
+                    u = str(props.uuid)
+                    h = pynvml.nvmlDeviceGetHandleByUUID(u if u.startswith("GPU-") else "GPU-" + u)
                 except Exception:
                     h = None
+                if h is None:
+                    try:
+                        bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+                        h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+                    except Exception:
+                        h = None
             self.h = h if h is not None else pynvml.nvmlDeviceGetHandleByIndex(device_index)
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
         except Exception:
@@ -310,9 +318,6 @@ def run_ours(args) -> None:
     barrier()
     assert st.status() == 0
     props = torch.cuda.get_device_properties(dev)
-    pci = getattr(props, "pci_bus_id", None)
-    if pci is not None and not isinstance(pci, str):
-        pci = None
     # The step (28 layers x one ABI call) is captured once into a CUDA graph and
     # replayed: per-kernel host launch cost leaves the timed region, the work
     # does not (the library's calls are stream-ordered, allocate nothing and do
@@ -325,7 +330,7 @@ def run_ours(args) -> None:
     graph.replay()
     barrier()
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local, pci) as clk:
+    with ClockSampler(local, props) as clk:
         t_start.record(stream)
         for i in range(args.steps):
             graph.replay()

@@ -1,0 +1,118 @@
+"""Split-KV decode across two GPUs through NCCL (picoattn_decode_splitkv_nccl).
+
+Two processes, one per GPU.  Rank r holds half of the cache rows (its shard
+slab); each rank runs the shard decode, the shard results are all-gathered by
+NCCL and combined on every rank.  Both ranks must produce the reference's
+single-loop result (oracle), within |gpu - ref| <= 2e-3 + 1e-2 |ref|.
+Skipped unless two GPUs are visible.
+"""
+import multiprocessing as mp
+import os
+import socket
+import traceback
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank(rank, world, port, q_ret):
+    try:
+        import ctypes as C
+        from datetime import timedelta
+        import torch.distributed as dist
+        from oracle.pyoracle import Oracle, build
+        from picolm_qwen_b200 import abi, sharding
+        from picolm_qwen_b200.runtime import rope_table, stream_handle
+        torch.cuda.set_device(rank)
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+        L = abi.lib()
+        uid = torch.zeros(128, dtype=torch.uint8)
+        if rank == 0:
+            assert L.picoattn_nccl_unique_id(uid.data_ptr()) == 0
+        dist.broadcast(uid, 0)
+        comm = C.c_void_p()
+        st = L.picoattn_nccl_comm_create(world, uid.data_ptr(), rank, 60.0, C.byref(comm))
+        assert st == 0, L.picoattn_strerror(st)
+
+        build()
+        ora = Oracle()
+        hq, hkv, hd, total = 40, 8, 128, 6000
+        kvd = hkv * hd
+        lens = np.array([5999, 2000], np.int32)  # positions of the new tokens
+        B = len(lens)
+        rng = np.random.default_rng(11)  # identical data on both ranks
+        full_k = [np.zeros((total, kvd), np.uint16) for _ in range(B)]
+        full_v = [np.zeros((total, kvd), np.uint16) for _ in range(B)]
+        for b in range(B):
+            n = int(lens[b])
+            full_k[b][:n] = ora.f32_to_f16(rng.standard_normal(n * kvd).astype(np.float32) * 0.5).reshape(n, kvd)
+            full_v[b][:n] = ora.f32_to_f16(rng.standard_normal(n * kvd).astype(np.float32) * 0.5).reshape(n, kvd)
+        q = rng.standard_normal((B, hq * hd)).astype(np.float32)
+        k = rng.standard_normal((B, kvd)).astype(np.float32)
+        v = rng.standard_normal((B, kvd)).astype(np.float32)
+        cos_t, sin_t = ora.rope_table(total, hd, 1e6)
+        ref = ora.decode_batch(hq, hkv, hd, 0, q, k, v, None, None, cos_t, sin_t,
+                               [a.copy() for a in full_k], [a.copy() for a in full_v], lens, n_threads=8)
+
+        cfg = abi.Config.make(1, hq, hkv, hd, total, 1e6)
+        off, rows = sharding.shard_rows(total, world, rank)
+        kc = torch.zeros((B, 1, rows, kvd), dtype=torch.int16, device="cuda")
+        vc = torch.zeros_like(kc)
+        for b in range(B):
+            kc[b, 0] = torch.from_numpy(full_k[b][off:off + rows].view(np.int16)).cuda()
+            vc[b, 0] = torch.from_numpy(full_v[b][off:off + rows].view(np.int16)).cuda()
+        kp = torch.tensor([kc[b].data_ptr() for b in range(B)], dtype=torch.int64, device="cuda")
+        vp = torch.tensor([vc[b].data_ptr() for b in range(B)], dtype=torch.int64, device="cuda")
+        cos, sin = rope_table(cfg)
+        d_cos, d_sin = torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda()
+        dq, dk, dv = (torch.from_numpy(a).cuda() for a in (q, k, v))
+        dpos = torch.from_numpy(lens).cuda()
+        ws_n = L.picoattn_decode_workspace_size(C.byref(cfg), B, rows)
+        ws = torch.zeros(ws_n, dtype=torch.uint8, device="cuda")
+        gather = torch.empty(L.picoattn_splitkv_gather_bytes(C.byref(cfg), B, world) // 4, device="cuda")
+        out = torch.empty((B, hq * hd), device="cuda")
+        st = L.picoattn_decode_splitkv_nccl(C.byref(cfg), 0, B, rows, off, rows, dq.data_ptr(), dk.data_ptr(),
+                                            dv.data_ptr(), None, None, d_cos.data_ptr(), d_sin.data_ptr(),
+                                            kp.data_ptr(), vp.data_ptr(), dpos.data_ptr(), gather.data_ptr(),
+                                            out.data_ptr(), ws.data_ptr(), ws_n, comm, stream_handle())
+        assert st == 0, L.picoattn_strerror(st)
+        torch.cuda.synchronize()
+        got = out.cpu().numpy()
+        err = np.abs(got - ref)
+        ok = bool(np.all(err <= 2e-3 + 1e-2 * np.abs(ref)))
+        assert L.picoattn_nccl_comm_destroy(comm) == 0
+        dist.destroy_process_group()
+        q_ret.put((rank, ok, float(err.max())))
+    except Exception:
+        q_ret.put((rank, False, traceback.format_exc()))
+
+
+def test_splitkv_nccl_two_gpus():
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    for rank, ok, info in res:
+        assert ok, f"rank {rank}: {info}"
