@@ -8,7 +8,7 @@ Skipped unless two GPUs are visible.
 """
 import multiprocessing as mp
 import os
-import socket
+import tempfile
 import traceback
 
 import numpy as np
@@ -19,15 +19,12 @@ torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
 
-def _free_port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
+def store_path() -> str:
+    """Rendezvous through a file store: no TCP port to race for."""
+    return os.path.join(tempfile.mkdtemp(prefix="picoattn_pg_"), "store")
 
 
-def _rank(rank, world, port, q_ret):
+def _rank(rank, world, store_file, q_ret):
     try:
         import ctypes as C
         from datetime import timedelta
@@ -36,8 +33,8 @@ def _rank(rank, world, port, q_ret):
         from picolm_qwen_b200 import abi, sharding
         from picolm_qwen_b200.runtime import rope_table, stream_handle
         torch.cuda.set_device(rank)
-        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+        dist.init_process_group("gloo", store=dist.FileStore(store_file, world), rank=rank, world_size=world,
+                                timeout=timedelta(seconds=60))
         L = abi.lib()
         uid = torch.zeros(128, dtype=torch.uint8)
         if rank == 0:
@@ -105,8 +102,8 @@ def test_splitkv_nccl_two_gpus():
         pytest.skip("needs two GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    store_file = store_path()
+    procs = [ctx.Process(target=_rank, args=(r, 2, store_file, q)) for r in range(2)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda r: r[0])

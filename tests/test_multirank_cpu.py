@@ -10,7 +10,7 @@
 """
 import multiprocessing as mp
 import os
-import socket
+import tempfile
 import traceback
 
 import numpy as np
@@ -19,22 +19,19 @@ import pytest
 from picolm_qwen_b200 import sharding
 
 
-def free_port() -> int:
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
+def store_path() -> str:
+    """Rendezvous through a file store: no TCP port to race for."""
+    return os.path.join(tempfile.mkdtemp(prefix="picoattn_pg_"), "store")
 
 
-def _splitkv_rank(rank, world, port, q_ret):
+def _splitkv_rank(rank, world, store_file, q_ret):
     try:
         import torch
         import torch.distributed as dist
         from datetime import timedelta
         from oracle.pyoracle import Oracle
-        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
+        dist.init_process_group("gloo", store=dist.FileStore(store_file, world), rank=rank, world_size=world,
+                                timeout=timedelta(seconds=20))
         ora = Oracle()
         hq, hkv, hd, n = 40, 8, 128, 3000  # Qwen2.5-32B heads; rows 0..n-1 attended
         rng = np.random.default_rng(17)
@@ -64,8 +61,8 @@ def _splitkv_rank(rank, world, port, q_ret):
 def _run(target, world, extra=()):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = free_port()
-    procs = [ctx.Process(target=target, args=(r, world, port, q) + tuple(extra)) for r in range(world)]
+    store_file = store_path()
+    procs = [ctx.Process(target=target, args=(r, world, store_file, q) + tuple(extra)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=120) for _ in range(world)]
@@ -82,13 +79,13 @@ def test_splitkv_two_ranks_gloo_matches_single_loop():
         assert ok, f"rank {rank}: {info}"
 
 
-def _dead_peer_rank(rank, world, port, q_ret):
+def _dead_peer_rank(rank, world, store_file, q_ret):
     try:
         import torch
         import torch.distributed as dist
         from datetime import timedelta
-        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=3))
+        dist.init_process_group("gloo", store=dist.FileStore(store_file, world), rank=rank, world_size=world,
+                                timeout=timedelta(seconds=3))
         if rank == 1:
             q_ret.put((rank, True, "left before the collective"))
             q_ret.close()
