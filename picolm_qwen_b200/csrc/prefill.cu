@@ -107,6 +107,34 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(PrefillArgs a) {
 // attention (tcgen05 / TMEM)
 // ---------------------------------------------------------------------------
 
+// Writes a 32 x 32 block of a head's output, rows y..y+31 (lane i holds row y+i:
+// the TMEM lane layout) and columns x..x+31, scaled by `inv`.  Stored from that
+// layout, each lane's row sits hq*hd*4 bytes from its neighbour's and every warp
+// store touches 32 lines; the SM's store path then limits the epilogue.  Instead
+// the block goes into a 4 KB shared stage in the 128-byte-swizzled layout (16-byte
+// unit g of row r at unit g ^ (r & 7): conflict-free for these row-wise writes)
+// and leaves as one tiled TMA store; rows past the map's extent are not written.
+// The stage is reused once the previous store has read it.  A block whose rows
+// all lie past the map (y >= rows) is not stored at all.
+__device__ __forceinline__ void stage_store_32x32(const uint32_t (&o)[32], float inv, float* stage,
+                                                  const CUtensorMap* map, int x, int y, int rows, int lane) {
+    if (y >= rows) return;
+    if (lane == 0) bulk_wait_read_all();
+    __syncwarp();
+#pragma unroll
+    for (int g = 0; g < 8; g++) {
+        const float4 val = make_float4(__uint_as_float(o[4 * g]) * inv, __uint_as_float(o[4 * g + 1]) * inv,
+                                       __uint_as_float(o[4 * g + 2]) * inv, __uint_as_float(o[4 * g + 3]) * inv);
+        *reinterpret_cast<float4*>(stage + lane * 32 + ((g ^ (lane & 7)) * 4)) = val;
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_2d(map, stage, x, y);
+        bulk_commit_group();
+    }
+}
+
 template <int HD>
 struct AttnSmem {
     static constexpr int kBoxBytes = BM * 128;              // one 128-row x 64-column fp16 box
@@ -115,7 +143,8 @@ struct AttnSmem {
     static constexpr int kQ = 0;
     static constexpr int kK = kQ + kTileBytes;
     static constexpr int kV = kK + NK * kTileBytes;
-    static constexpr int kBars = kV + NV * kTileBytes;
+    static constexpr int kStage = kV + NV * kTileBytes;  // epilogue: 32 x 32 fp32 per softmax warp
+    static constexpr int kBars = kStage + 4 * 4096;
     static constexpr int kEnd = kBars + 256;
     static constexpr int kDynBytes = kEnd + 1024;  // slack to align the base to 1024
 };
@@ -123,7 +152,8 @@ struct AttnSmem {
 template <int HD>
 __global__ void __launch_bounds__(192, 1)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                        const __grid_constant__ CUtensorMap tmV, PrefillArgs a) {
+                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                        PrefillArgs a) {
     using L = AttnSmem<HD>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -311,22 +341,17 @@ __global__ void __launch_bounds__(192, 1)
         // epilogue: O / l -> out[token][h][:]
         mbar_wait(&pv_done[(n_kv - 1) & 1], (uint32_t)(((n_kv - 1) >> 1) & 1), a.status);
         tc_fence_after();
-        const int tok = q0 + r;
         const float inv = 1.0f / l_run;
-        float* dst = a.out + ((size_t)tok * a.hq + h) * HD;
-#pragma unroll
+        const int row0 = q0 + warp * 32;
+        float* stage = reinterpret_cast<float*>(smem + L::kStage + warp * 4096);
+#pragma unroll 1
         for (int c = 0; c < HD / 32; c++) {
             uint32_t t[32];
             tmem_ld32(tO + c * 32 + lane_off, t);
             tmem_ld_wait();
-            if (tok < a.n_tok) {
-#pragma unroll
-                for (int e = 0; e < 32; e += 4)
-                    *reinterpret_cast<float4*>(dst + c * 32 + e) =
-                        make_float4(__uint_as_float(t[e]) * inv, __uint_as_float(t[e + 1]) * inv,
-                                    __uint_as_float(t[e + 2]) * inv, __uint_as_float(t[e + 3]) * inv);
-            }
+            stage_store_32x32(t, inv, stage, &tmO, h * HD + c * 32, row0, a.n_tok, lane);
         }
+        if (lane == 0) bulk_wait_all();
         tc_fence_before();
     }
     __syncthreads();
@@ -355,13 +380,13 @@ template <int HD>
 struct Attn2Smem {
     static constexpr int kBoxBytes = BM * 128;
     static constexpr int kTileBytes = (HD / 64) * kBoxBytes;
-    // V(t) may only load once PV(t-NV) has finished; a tile takes ~1.5k cycles
-    // to land, so a third V stage keeps the load off the critical path
-    static constexpr int NK = 2, NV = 3;
+    static constexpr int NK = 2, NV = 2;
     static constexpr int kQ = 0;  // Q0, Q1
     static constexpr int kK = kQ + 2 * kTileBytes;
     static constexpr int kV = kK + NK * kTileBytes;
-    static constexpr int kBars = kV + NV * kTileBytes;
+    // epilogue staging: one 32 x 32 fp32 block per softmax warp
+    static constexpr int kStage = kV + NV * kTileBytes;
+    static constexpr int kBars = kStage + 8 * 4096;
     static constexpr int kEnd = kBars + 512;
     static constexpr int kDynBytes = kEnd + 1024;
 };
@@ -369,7 +394,8 @@ struct Attn2Smem {
 template <int HD>
 __global__ void __maxnreg__(168)
     prefill_attn2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                         const __grid_constant__ CUtensorMap tmV, PrefillArgs a) {
+                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                         PrefillArgs a) {
     using L = Attn2Smem<HD>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -575,19 +601,29 @@ __global__ void __maxnreg__(168)
                 tc_fence_after();
                 const int kbase = j * BN;
                 const bool diag = kbase + BN - 1 > a.start + q0;  // tile crosses this q tile's diagonal
-                // Optimistic single pass (every tile after the first): p = 2^(s - m_run)
-                // with the running max, kept in registers while the tile max is
-                // tracked.  p <= 2^15 is exact in fp16 and safe in the fp32 sums, so
-                // unless a row max exceeds m_run by more than that, P is stored as is.
+                // Optimistic single pass: p = 2^(s - m_run) with the running max, kept
+                // in registers while the tile max is tracked.  p <= 2^15 is exact in
+                // fp16 and safe in the fp32 sums, so unless a row max exceeds m_run by
+                // more than that, P is stored as is.  On the first tile of an item the
+                // running max starts as the max of the first 32 columns (column 0 is
+                // visible to every row).
                 bool done = false;
                 float mx = -INFINITY;
-                if (j > 0) {
+                {
                     uint32_t pk[BN / 2];
                     float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
                     float mx8[8] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY,
                                     -INFINITY, -INFINITY, -INFINITY, -INFINITY};
                     uint32_t sbuf[2][32];
                     tmem_ld32(tS + lane_off, sbuf[0]);
+                    if (j == 0) {
+                        tmem_ld_wait();
+                        float m0 = -INFINITY;
+#pragma unroll
+                        for (int e = 0; e < 32; e++)
+                            if (!diag || kbase + e <= qpos) m0 = fmaxf(m0, __uint_as_float(sbuf[0][e]));
+                        m_run = m0;
+                    }
 #pragma unroll
                     for (int c = 0; c < BN / 32; c++) {
                         tmem_ld_wait();
@@ -694,26 +730,23 @@ __global__ void __maxnreg__(168)
             // epilogue: O / l -> out[token][h][:], then hand O back to the MMA warp
             mbar_wait(&pv_done[w], (uint32_t)((t - 1) & 1), a.status);
             tc_fence_after();
-            const int tok = q0 + r;
             const float inv = 1.0f / l_run;
-            float* dst = a.out + ((size_t)tok * a.hq + h) * HD;
-#pragma unroll
+            const int row0 = q0 + (warp & 3) * 32;
+            float* stage = reinterpret_cast<float*>(smem + L::kStage + warp * 4096);
+#pragma unroll 1
             for (int c = 0; c < HD / 32; c++) {
                 uint32_t o[32];
                 tmem_ld32(tO + c * 32 + lane_off, o);
                 tmem_ld_wait();
-                if (tok < a.n_tok) {
-#pragma unroll
-                    for (int e = 0; e < 32; e += 4)
-                        *reinterpret_cast<float4*>(dst + c * 32 + e) =
-                            make_float4(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv,
-                                        __uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
+                if (c == HD / 32 - 1) {  // O is in registers: the MMA warp may overwrite it
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&o_free[w]);
                 }
+                stage_store_32x32(o, inv, stage, &tmO, h * HD + c * 32, row0, a.n_tok, lane);
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&o_free[w]);
         }
+        if (lane == 0) bulk_wait_all();  // the stage must outlive the stores reading it
     }
     __syncthreads();
     if (warp == 9) {
@@ -757,6 +790,20 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, u
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D map over the fp32 output [n_tok][hq*hd] for the epilogue's stores: 32 x 32
+// boxes (128-byte rows, 128-byte swizzle, matching stage_store_32x32's stage).
+bool make_out_map(CUtensorMap* m, float* base, uint64_t inner, uint64_t rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {inner, rows};
+    const cuuint64_t strides[1] = {inner * 4};
+    const cuuint32_t box[2] = {32, 32};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int HD>
 cudaError_t launch_prefill_hd(const PrefillArgs& a, cudaStream_t stream, unsigned stages) {
     if (stages & PICOATTN_STAGE_PREPARE) {
@@ -774,12 +821,13 @@ cudaError_t launch_prefill_hd(const PrefillArgs& a, cudaStream_t stream, unsigne
             if (e != cudaSuccess) return e;
             attr_done = true;
         }
-        CUtensorMap mq, mk, mv;
+        CUtensorMap mq, mk, mv, mo;
         const uint64_t kvd = (uint64_t)a.kvd;
         const size_t slab = (size_t)a.layer * a.max_seq * a.kvd;
         if (!make_map(&mq, a.q16, (uint64_t)a.hq * HD, (uint64_t)a.n_tok, (uint64_t)a.hq * HD * 2) ||
             !make_map(&mk, a.k_cache + slab, kvd, (uint64_t)(a.start + a.n_tok), kvd * 2) ||
-            !make_map(&mv, a.v_cache + slab, kvd, (uint64_t)(a.start + a.n_tok), kvd * 2))
+            !make_map(&mv, a.v_cache + slab, kvd, (uint64_t)(a.start + a.n_tok), kvd * 2) ||
+            !make_out_map(&mo, a.out, (uint64_t)a.hq * HD, (uint64_t)a.n_tok))
             return cudaErrorInvalidValue;
         // the head-pair kernel needs one resident CTA of 320 threads per SM
         static int pair_ok = -1;
@@ -796,10 +844,10 @@ cudaError_t launch_prefill_hd(const PrefillArgs& a, cudaStream_t stream, unsigne
             cudaGetDevice(&dev);
             cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
             const int grid = n_items < sms ? n_items : sms;
-            prefill_attn2_kernel<HD><<<grid, 320, Attn2Smem<HD>::kDynBytes, stream>>>(mq, mk, mv, a);
+            prefill_attn2_kernel<HD><<<grid, 320, Attn2Smem<HD>::kDynBytes, stream>>>(mq, mk, mv, mo, a);
         } else {
             dim3 grid((unsigned)a.n_qtiles, (unsigned)a.hq);
-            prefill_attn_kernel<HD><<<grid, 192, AttnSmem<HD>::kDynBytes, stream>>>(mq, mk, mv, a);
+            prefill_attn_kernel<HD><<<grid, 192, AttnSmem<HD>::kDynBytes, stream>>>(mq, mk, mv, mo, a);
         }
     }
     return cudaGetLastError();
