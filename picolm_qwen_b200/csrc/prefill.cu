@@ -46,60 +46,150 @@ constexpr float kStaleMaxMargin = 15.0f;
 // prep (head-vector helpers in prep_common.cuh)
 // ---------------------------------------------------------------------------
 
+// fp16 input bits -> the reference's fp16 rounding of their fp32 value: the
+// identity on every fp16 value except NaN, whose payload becomes the quiet bit
+// (f32_to_f16_ref of the widened value); two halves per word.
+__device__ __forceinline__ uint32_t h2_ref16(uint32_t w) {
+    uint32_t r = 0;
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+        uint32_t h = (w >> (16 * k)) & 0xFFFFu;
+        if ((h & 0x7C00u) == 0x7C00u && (h & 0x3FFu)) h = (h & 0x8000u) | 0x7E00u;
+        r |= h << (16 * k);
+    }
+    return r;
+}
+
+// One warp = up to 8 head vectors of ONE kind (q, k or v) of one token, so the
+// three paths never run predicated inside each other; lane l owns elements
+// [V*l, V*l+V) of each vector.
+// RMSNorm: the reference accumulates the squares of elements i = c, c+4, c+8, ...
+// into lane c = i % 4 in index order (cpp/tensor.hpp:146-176).  The squares are
+// written to shared memory transposed, chain c of vector u as one contiguous
+// row, and lane 4u+c runs that chain with 128-bit loads: 8 vectors x 4 chains
+// keep all 32 lanes busy.  Lane u then folds vector u's chains as
+// (c0+c2)+(c1+c3) and computes its scale, as in vec_rmsnorm.
 template <int HD>
 __global__ void __launch_bounds__(256) prefill_prep_kernel(PrefillArgs a) {
-    // 8 warps x 4 head vectors of one token per block; all of a warp's global
-    // loads are issued before any of them is used
-    constexpr int V = HD / 32;
-    __shared__ float sq[8][4 * HD];
-    const int tok = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *a.work_counter = 0;  // attention work queue
-    const int n_slots = a.hq + 2 * a.hkv;
-    const int slot0 = (blockIdx.x * 8 + warp) * 4;
-    if (slot0 >= n_slots) return;
+    constexpr int V = HD / 32;  // elements per lane
+    constexpr int U = 8;        // vectors per warp
+    constexpr int CH = HD / 4;  // terms per chain
+    constexpr int RS = CH + 4;  // chain row stride (floats): 16-byte rows, conflict-free 128-bit reads
+    __shared__ __align__(16) float sq_all[8][U * 4 * RS];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (blockIdx.x == 0 && threadIdx.x == 0) *a.work_counter = 0;  // attention work queue
+    const int qg = (a.hq + U - 1) / U, kg = (a.hkv + U - 1) / U;
+    const int wpt = qg + 2 * kg;  // warps per token
+    const int gw = blockIdx.x * 8 + warp;
+    const int tok = gw / wpt;
+    if (tok >= a.n_tok) return;
+    const int r = gw - tok * wpt;
+    const int kind = r < qg ? 0 : (r < qg + kg ? 1 : 2);
+    const int h0 = (kind == 0 ? r : (kind == 1 ? r - qg : r - qg - kg)) * U;
+    const int nheads = kind == 0 ? a.hq : a.hkv;
+    const int nh = min(U, nheads - h0);
     const int pos = a.start + tok;
+    const size_t crow = ((size_t)a.layer * a.max_seq + pos) * a.kvd;
+
+    if (kind == 2) {  // v: stored as the reference's fp16 of the input
+        uint16_t* dst = a.v_cache + crow + (size_t)h0 * HD;
+        if (a.in_dtype == PICOATTN_DTYPE_F16) {
+            const __half* src = reinterpret_cast<const __half*>(a.v) + ((size_t)tok * a.hkv + h0) * HD;
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                if (u < nh) {
+                    if constexpr (V == 4) {
+                        uint2 w = *reinterpret_cast<const uint2*>(src + u * HD + V * lane);
+                        w.x = h2_ref16(w.x), w.y = h2_ref16(w.y);
+                        *reinterpret_cast<uint2*>(dst + u * HD + V * lane) = w;
+                    } else {
+                        const uint32_t w = *reinterpret_cast<const uint32_t*>(src + u * HD + V * lane);
+                        *reinterpret_cast<uint32_t*>(dst + u * HD + V * lane) = h2_ref16(w);
+                    }
+                }
+            }
+        } else {
+            Vec<HD> x[U];
+#pragma unroll
+            for (int u = 0; u < U; u++)
+                if (u < nh) vec_load<HD>(x[u], a.v, ((size_t)tok * a.hkv + h0 + u) * HD, a.in_dtype, lane);
+#pragma unroll
+            for (int u = 0; u < U; u++)
+                if (u < nh) vec_store_ref16<HD>(x[u], dst + u * HD, lane);
+        }
+        return;
+    }
+
+    const void* src = kind == 0 ? a.q : a.k;
+    Vec<HD> x[U];
+#pragma unroll
+    for (int u = 0; u < U; u++)
+        if (u < nh) vec_load<HD>(x[u], src, ((size_t)tok * nheads + h0 + u) * HD, a.in_dtype, lane);
     RopeLane<HD> rl;
     rope_lane_load<HD>(rl, a.rope_cos + (size_t)pos * (HD / 2), a.rope_sin + (size_t)pos * (HD / 2), a.rope_mode,
                        lane);
-    float qw[V], kw[V];
     if (a.qn_w) {
+        const float* wsrc = kind == 0 ? a.qn_w : a.kn_w;
+        float w[V];
 #pragma unroll
-        for (int j = 0; j < V; j++) qw[j] = a.qn_w[V * lane + j], kw[j] = a.kn_w[V * lane + j];
-    }
-    Vec<HD> x[4];
-    int kind[4], head[4];
+        for (int j = 0; j < V; j++) w[j] = wsrc[V * lane + j];
+        float* sq = sq_all[warp];
 #pragma unroll
-    for (int u = 0; u < 4; u++) {
-        const int slot = slot0 + u;
-        kind[u] = slot < a.hq ? 0 : (slot < a.hq + a.hkv ? 1 : (slot < n_slots ? 2 : 3));
-        head[u] = kind[u] == 0 ? slot : (kind[u] == 1 ? slot - a.hq : slot - a.hq - a.hkv);
-        if (kind[u] == 0) vec_load<HD>(x[u], a.q, ((size_t)tok * a.hq + head[u]) * HD, a.in_dtype, lane);
-        else if (kind[u] == 1) vec_load<HD>(x[u], a.k, ((size_t)tok * a.hkv + head[u]) * HD, a.in_dtype, lane);
-        else if (kind[u] == 2) vec_load<HD>(x[u], a.v, ((size_t)tok * a.hkv + head[u]) * HD, a.in_dtype, lane);
-    }
-    const float qscale = 1.4426950408889634f / sqrtf((float)HD);
-    const size_t row = ((size_t)a.layer * a.max_seq + pos) * a.kvd;
-    if (a.qn_w) {  // QK-RMSNorm of the q and k vectors, four at a time
-        float wsel[4][V];
-        bool nrm[4];
+        for (int u = 0; u < U; u++) {
+            if (u < nh) {
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
-            nrm[u] = kind[u] == 0 || kind[u] == 1;
-#pragma unroll
-            for (int j = 0; j < V; j++) wsel[u][j] = kind[u] == 0 ? qw[j] : kw[j];
+                for (int j = 0; j < V; j++) {
+                    const int i = V * lane + j;
+                    sq[(u * 4 + (i & 3)) * RS + (i >> 2)] = __fmul_rn(x[u].x[j], x[u].x[j]);
+                }
+            }
         }
-        vec_rmsnorm4<HD>(x, wsel, nrm, a.eps, sq[warp], lane);
-    }
+        __syncwarp();
+        float part = 0.f;
+        if ((lane >> 2) < nh) {
+            const float4* row = reinterpret_cast<const float4*>(sq + lane * RS);  // (u*4 + c) == lane
 #pragma unroll
-    for (int u = 0; u < 4; u++) {
-        if (kind[u] == 3) break;
-        if (kind[u] != 2) {
-            vec_rope<HD>(x[u], rl, a.rope_mode, lane);
+            for (int k4 = 0; k4 < CH / 4; k4++) {
+                const float4 t = row[k4];
+                part = __fadd_rn(part, t.x);
+                part = __fadd_rn(part, t.y);
+                part = __fadd_rn(part, t.z);
+                part = __fadd_rn(part, t.w);
+            }
         }
-        if (kind[u] == 0)
-            vec_store_h16_scaled<HD>(x[u], a.q16 + ((size_t)tok * a.hq + head[u]) * HD, qscale, lane);
-        else
-            vec_store_ref16<HD>(x[u], (kind[u] == 1 ? a.k_cache : a.v_cache) + row + (size_t)head[u] * HD, lane);
+        const int s4 = (lane & 7) * 4;
+        const float c0 = __shfl_sync(0xffffffffu, part, s4 + 0), c1 = __shfl_sync(0xffffffffu, part, s4 + 1);
+        const float c2 = __shfl_sync(0xffffffffu, part, s4 + 2), c3 = __shfl_sync(0xffffffffu, part, s4 + 3);
+        const float ss = __fadd_rn(__fadd_rn(c0, c2), __fadd_rn(c1, c3));
+        const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)HD), a.eps)));
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const float su = __shfl_sync(0xffffffffu, scale, u);
+            if (u < nh) {
+#pragma unroll
+                for (int j = 0; j < V; j++) x[u].x[j] = __fmul_rn(__fmul_rn(x[u].x[j], su), w[j]);
+            }
+        }
+    }
+    if (kind == 0) {
+        const float qscale = 1.4426950408889634f / sqrtf((float)HD);
+        __half* dst = a.q16 + ((size_t)tok * a.hq + h0) * HD;
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            if (u < nh) {
+                vec_rope<HD>(x[u], rl, a.rope_mode, lane);
+                vec_store_h16_scaled<HD>(x[u], dst + u * HD, qscale, lane);
+            }
+        }
+    } else {
+        uint16_t* dst = a.k_cache + crow + (size_t)h0 * HD;
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            if (u < nh) {
+                vec_rope<HD>(x[u], rl, a.rope_mode, lane);
+                vec_store_ref16<HD>(x[u], dst + u * HD, lane);
+            }
+        }
     }
 }
 
@@ -807,8 +897,9 @@ bool make_out_map(CUtensorMap* m, float* base, uint64_t inner, uint64_t rows) {
 template <int HD>
 cudaError_t launch_prefill_hd(const PrefillArgs& a, cudaStream_t stream, unsigned stages) {
     if (stages & PICOATTN_STAGE_PREPARE) {
-        const unsigned slot_blocks = (unsigned)((a.hq + 2 * a.hkv + 31) / 32);  // 32 head vectors per block
-        prefill_prep_kernel<HD><<<dim3(slot_blocks, (unsigned)a.n_tok), 256, 0, stream>>>(a);
+        // one warp per (token, kind, group of 8 heads), 8 warps per block
+        const long warps = (long)a.n_tok * ((a.hq + 7) / 8 + 2 * ((a.hkv + 7) / 8));
+        prefill_prep_kernel<HD><<<(unsigned)((warps + 7) / 8), 256, 0, stream>>>(a);
     }
     if (stages & PICOATTN_STAGE_ATTEND) {
         static bool attr_done = false;

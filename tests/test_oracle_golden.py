@@ -29,6 +29,18 @@ def test_fp16_widening_matches_reference_for_all_65536_patterns(oracle, golden_d
     assert np.array_equal(got.view(np.uint32), g["f16_all_f32"].view(np.uint32))
 
 
+def test_fp16_round_trip_is_identity_except_nan(oracle, golden_dir):
+    # The prefill prep stores fp16 v inputs by bits (h2_ref16): rounding the
+    # widened value of any fp16 pattern gives the pattern back, NaNs becoming
+    # sign | 0x7E00.  Checked over all 65536 patterns with the reference's widening.
+    g = _load(golden_dir, "numerics.npz")
+    bits = g["f16_all_bits"].astype(np.uint16)
+    got = oracle.f32_to_f16(g["f16_all_f32"])
+    nan = ((bits & 0x7C00) == 0x7C00) & ((bits & 0x3FF) != 0)
+    want = np.where(nan, (bits & 0x8000) | 0x7E00, bits).astype(np.uint16)
+    assert np.array_equal(got, want)
+
+
 def test_fp16_rounding_is_half_up_not_even(oracle):
     # 1 + 2^-11 lies half way between 1.0 and 1 + 2^-10: the reference rounds
     # the magnitude up (0x3C01) where round-to-nearest-even gives 0x3C00.
