@@ -100,6 +100,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
     }
 }
 
+// Non-blocking probe: has the phase with the given parity completed?  A thread
+// that issues tcgen05.mma stalls for the latency of any load it makes, and the
+// tensor pipe idles meanwhile (~180 cycles for a try_wait, ~100 for this probe),
+// so such a thread probes all the phases it needs at once and falls back to
+// mbar_wait only when one is not complete yet.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
 // One-dimensional bulk copy global -> shared (TMA engine), completion counted
 // in bytes on `bar`.  dst, src 16-byte aligned; bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -135,15 +152,6 @@ __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
-}
-
-// Two exponentials in one MUFU operation: 2^x for a pair of arguments rounded
-// to fp16, result as a packed fp16 pair (low half = first argument).
-__device__ __forceinline__ uint32_t ex2_h2(float x0, float x1) {
-    uint32_t in, out;
-    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(in) : "f"(x1), "f"(x0));
-    asm("ex2.approx.f16x2 %0, %1;" : "=r"(out) : "r"(in));
-    return out;
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {

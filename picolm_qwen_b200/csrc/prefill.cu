@@ -314,19 +314,21 @@ __global__ void __launch_bounds__(192, 1)
         // ---------------- MMA issuer ----------------
         constexpr uint32_t idesc_qk = idesc_f16_f32(BM, BN, false, false);
         constexpr uint32_t idesc_pv = idesc_f16_f32(BM, HD, false, true);
+        const uint64_t dq = smem_desc_sw128(sQ, 16, 1024);
+        const uint64_t dk = smem_desc_sw128(sK, 16, 1024);
+        // B = V tile, MN-major: 64-column boxes LBO apart, 8-key groups SBO apart
+        const uint64_t dv = smem_desc_sw128(sV, L::kBoxBytes, 1024);
         auto issue_pv = [&](int i) {
             const int b = i & 1, sv = i % L::NV;
             mbar_wait(&p_full[b], (uint32_t)((i >> 1) & 1), a.status);
             mbar_wait(&v_full[sv], (uint32_t)((i / L::NV) & 1), a.status);
             tc_fence_after();
             if (lane == 0) {
-                const uint32_t vbase = sV + sv * L::kTileBytes;
+                const uint64_t vd = desc_advance(dv, sv * L::kTileBytes);
 #pragma unroll
-                for (int kk = 0; kk < BN / 16; kk++) {
-                    // B = V tile, MN-major: 64-column boxes LBO apart, 8-key groups SBO apart
-                    const uint64_t bdesc = smem_desc_sw128(vbase + kk * 16 * 128, L::kBoxBytes, 1024);
-                    umma_ts(tO, tS0 + b * 128 + kk * 8, bdesc, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
-                }
+                for (int kk = 0; kk < BN / 16; kk++)
+                    umma_ts(tO, tS0 + b * 128 + kk * 8, desc_advance(vd, kk * 16 * 128), idesc_pv,
+                            (i > 0 || kk > 0) ? 1u : 0u);
                 umma_commit(&v_empty[sv]);
                 umma_commit(&pv_done[b]);
             }
@@ -339,13 +341,11 @@ __global__ void __launch_bounds__(192, 1)
             if (j >= 2) mbar_wait(&pv_done[b], (uint32_t)(((j - 2) >> 1) & 1), a.status);
             tc_fence_after();
             if (lane == 0) {
-                const uint32_t kbase = sK + sk * L::kTileBytes;
+                const uint64_t kd = desc_advance(dk, sk * L::kTileBytes);
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; kk++) {
                     const uint32_t koff = (kk >> 2) * L::kBoxBytes + (kk & 3) * 32;
-                    const uint64_t adesc = smem_desc_sw128(sQ + koff, 16, 1024);
-                    const uint64_t bdesc = smem_desc_sw128(kbase + koff, 16, 1024);
-                    umma_ss(tS0 + b * 128, adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+                    umma_ss(tS0 + b * 128, desc_advance(dq, koff), desc_advance(kd, koff), idesc_qk, kk > 0 ? 1u : 0u);
                 }
                 umma_commit(&s_full[b]);
                 umma_commit(&k_empty[sk]);
@@ -460,7 +460,7 @@ __global__ void __launch_bounds__(192, 1)
 // grid of one CTA per SM balances the causal triangle.  Both heads read the
 // same K/V tiles: one TMA stream feeds two softmax warpgroups, each with its own
 // S (128 TMEM columns, P written back over it) and O (128 columns):
-//   TMEM  [0,128) S0   [128,256) O0   [256,384) S1   [384,512) O1
+//   TMEM  [0,128) S0   [128,256) S1   [256,384) O0   [384,512) O1
 // Warps 0-3 / 4-7 softmax for head 0 / 1 (thread = q row = TMEM lane), warp 8
 // TMA and work-queue fetch, warp 9 MMA issue.  Per KV tile t the MMA warp issues
 // PV0(t), QK0(t+1), PV1(t), QK1(t+1), so each warpgroup's softmax overlaps the
@@ -580,96 +580,105 @@ __global__ void __maxnreg__(168)
         }
         __syncwarp();
     } else if (warp == 9) {
-        // ---------------- MMA issuer ----------------
-        constexpr uint32_t idesc_qk = idesc_f16_f32(BM, BN, false, false);
-        constexpr uint32_t idesc_pv = idesc_f16_f32(BM, HD, false, true);
-        int t = 0;  // KV tile counter across items
-        auto issue_qk = [&](int w, int tt, uint32_t kbase) {
-            if (tt >= 1) mbar_wait(&pv_done[w], (uint32_t)((tt - 1) & 1), a.status);  // S_w holds P_w(tt-1)
-            tc_fence_after();
-            if (lane == 0) {
-                const uint32_t qbase = sQ + w * L::kTileBytes;
+        // ---------------- MMA issuer (lane 0) ----------------
+        // Per KV tile t two issue points of 16 MMAs each: [PV0(t), QK0(t+1)] and
+        // [PV1(t), QK1(t+1)], each preceded by ONE batch of barrier probes.  S_w(t+1)
+        // overwrites P_w(t), the A operand of the PV issued just before it:
+        // tcgen05.mma operations of one thread execute in issue order, so no
+        // completion wait is needed between the two.
+        if (lane == 0) {
+            constexpr uint32_t idesc_qk = idesc_f16_f32(BM, BN, false, false);
+            constexpr uint32_t idesc_pv = idesc_f16_f32(BM, HD, false, true);
+            const uint64_t dq = smem_desc_sw128(sQ, 16, 1024);            // Q0; Q1 one tile later
+            const uint64_t dk = smem_desc_sw128(sK, 16, 1024);            // K stage 0
+            const uint64_t dv = smem_desc_sw128(sV, L::kBoxBytes, 1024);  // V stage 0, MN-major
+            auto mma_qk = [&](int w, int sk) {
+                const uint64_t qd = desc_advance(dq, w * L::kTileBytes);
+                const uint64_t kd = desc_advance(dk, sk * L::kTileBytes);
+                const uint32_t dS = tmem + w * 128;
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; kk++) {
                     const uint32_t koff = (kk >> 2) * L::kBoxBytes + (kk & 3) * 32;
-                    umma_ss(tmem + w * 256, smem_desc_sw128(qbase + koff, 16, 1024),
-                            smem_desc_sw128(kbase + koff, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
+                    umma_ss(dS, desc_advance(qd, koff), desc_advance(kd, koff), idesc_qk, kk > 0 ? 1u : 0u);
                 }
                 umma_commit(&s_full[w]);
-            }
-            __syncwarp();
-        };
-        auto issue_pv = [&](int w, int tt, bool first, int k, uint32_t vbase) {
-            mbar_wait(&p_full[w], (uint32_t)(tt & 1), a.status);
-            if (first && k >= 1) mbar_wait(&o_free[w], (uint32_t)((k - 1) & 1), a.status);
-            tc_fence_after();
-            if (lane == 0) {
+            };
+            auto mma_pv = [&](int w, int sv, bool first) {
+                const uint64_t vd = desc_advance(dv, sv * L::kTileBytes);
+                const uint32_t dS = tmem + w * 128, dO = tmem + 256 + w * 128;
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; kk++)
-                    umma_ts(tmem + w * 256 + 128, tmem + w * 256 + kk * 8,
-                            smem_desc_sw128(vbase + kk * 16 * 128, L::kBoxBytes, 1024), idesc_pv,
+                    umma_ts(dO, dS + kk * 8, desc_advance(vd, kk * 16 * 128), idesc_pv,
                             (!first || kk > 0) ? 1u : 0u);
                 umma_commit(&pv_done[w]);
-            }
-            __syncwarp();
-        };
-        for (int k = 0;; k++) {
-            const int slot = k & 1;
-            mbar_wait(&item_full[slot], (uint32_t)((k >> 1) & 1), a.status);
-            const int it = *reinterpret_cast<volatile int*>(&item_slot[slot]);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&item_empty[slot]);
-            if (it < 0) break;
-            int qt, h0;
-            decode_item(it, qt, h0);
-            const int n_kv = n_kv_of(qt);
-            mbar_wait(q_full, (uint32_t)(k & 1), a.status);
-            // prologue: QK of the first tile for both heads
-            {
-                const int sk = t % L::NK;
-                mbar_wait(&k_full[sk], (uint32_t)((t / L::NK) & 1), a.status);
-                const uint32_t kb = sK + sk * L::kTileBytes;
-                issue_qk(0, t, kb);
-                issue_qk(1, t, kb);
-                if (lane == 0) {
+            };
+            int t = 0;  // KV tile counter across items
+            for (int k = 0;; k++) {
+                const int slot = k & 1;
+                mbar_wait(&item_full[slot], (uint32_t)((k >> 1) & 1), a.status);
+                const int it = *reinterpret_cast<volatile int*>(&item_slot[slot]);
+                mbar_arrive(&item_empty[slot]);
+                if (it < 0) break;
+                int qt, h0;
+                decode_item(it, qt, h0);
+                const int n_kv = n_kv_of(qt);
+                const uint32_t po = (uint32_t)((k - 1) & 1);  // o_free phase of the previous item
+                {   // prologue: QK of the first tile for both heads
+                    const int sk = t % L::NK;
+                    const uint32_t pk = (uint32_t)((t / L::NK) & 1);
+                    if (!(mbar_test(q_full, (uint32_t)(k & 1)) & mbar_test(&k_full[sk], pk))) {
+                        mbar_wait(q_full, (uint32_t)(k & 1), a.status);
+                        mbar_wait(&k_full[sk], pk, a.status);
+                    }
+                    tc_fence_after();
+                    mma_qk(0, sk);
+                    mma_qk(1, sk);
                     umma_commit(&k_empty[sk]);
                     if (n_kv == 1) umma_commit(q_empty);
                 }
-                __syncwarp();
-            }
-            for (int j = 0; j < n_kv; j++, t++) {
-                const int sv = t % L::NV;
-                mbar_wait(&v_full[sv], (uint32_t)((t / L::NV) & 1), a.status);
-                const uint32_t vb = sV + sv * L::kTileBytes;
-                const bool more = j + 1 < n_kv;
-                uint32_t kb_next = 0;
-                int sk_next = 0;
-                issue_pv(0, t, j == 0, k, vb);
-                if (more) {  // K(t+1) is needed only from here on
-                    sk_next = (t + 1) % L::NK;
-                    mbar_wait(&k_full[sk_next], (uint32_t)(((t + 1) / L::NK) & 1), a.status);
-                    kb_next = sK + sk_next * L::kTileBytes;
-                    issue_qk(0, t + 1, kb_next);
-                }
-                issue_pv(1, t, j == 0, k, vb);
-                if (lane == 0) umma_commit(&v_empty[sv]);
-                __syncwarp();
-                if (more) {
-                    issue_qk(1, t + 1, kb_next);
-                    if (lane == 0) {
-                        umma_commit(&k_empty[sk_next]);
+                for (int j = 0; j < n_kv; j++, t++) {
+                    const int sv = t % L::NV, skn = (t + 1) % L::NK;
+                    const uint32_t pv = (uint32_t)((t / L::NV) & 1), pp = (uint32_t)(t & 1);
+                    const uint32_t pkn = (uint32_t)(((t + 1) / L::NK) & 1);
+                    const bool more = j + 1 < n_kv, first = j == 0, need_o = first && k >= 1;
+                    // issue point 1: V(t), P0(t), O0 free (first tile), K(t+1)
+                    bool ok = mbar_test(&v_full[sv], pv) & mbar_test(&p_full[0], pp);
+                    if (need_o) ok &= mbar_test(&o_free[0], po);
+                    if (more) ok &= mbar_test(&k_full[skn], pkn);
+                    if (!ok) {
+                        mbar_wait(&v_full[sv], pv, a.status);
+                        mbar_wait(&p_full[0], pp, a.status);
+                        if (need_o) mbar_wait(&o_free[0], po, a.status);
+                        if (more) mbar_wait(&k_full[skn], pkn, a.status);
+                    }
+                    tc_fence_after();
+                    mma_pv(0, sv, first);
+                    if (more) mma_qk(0, skn);
+                    // issue point 2: P1(t), O1 free (first tile)
+                    ok = mbar_test(&p_full[1], pp);
+                    if (need_o) ok &= mbar_test(&o_free[1], po);
+                    if (!ok) {
+                        mbar_wait(&p_full[1], pp, a.status);
+                        if (need_o) mbar_wait(&o_free[1], po, a.status);
+                    }
+                    tc_fence_after();
+                    mma_pv(1, sv, first);
+                    umma_commit(&v_empty[sv]);
+                    if (more) {
+                        mma_qk(1, skn);
+                        umma_commit(&k_empty[skn]);
                         if (j + 2 == n_kv) umma_commit(q_empty);
                     }
-                    __syncwarp();
                 }
             }
         }
+        __syncwarp();
     } else {
         // ---------------- softmax warpgroups ----------------
         const int w = warp >> 2;           // head of the pair
         const int r = threadIdx.x & 127;   // q row == TMEM lane
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-        const uint32_t tS = tmem + w * 256, tO = tS + 128;
+        const uint32_t tS = tmem + w * 128, tO = tmem + 256 + w * 128;
         int t = 0;
         for (int k = 0;; k++) {
             const int slot = k & 1;
@@ -692,18 +701,17 @@ __global__ void __maxnreg__(168)
                 const int kbase = j * BN;
                 const bool diag = kbase + BN - 1 > a.start + q0;  // tile crosses this q tile's diagonal
                 // Optimistic single pass: p = 2^(s - m_run) with the running max, kept
-                // in registers while the tile max is tracked.  p <= 2^15 is exact in
-                // fp16 and safe in the fp32 sums, so unless a row max exceeds m_run by
-                // more than that, P is stored as is.  On the first tile of an item the
-                // running max starts as the max of the first 32 columns (column 0 is
-                // visible to every row).
+                // in registers.  p <= 2^15 is exact in fp16 and safe in the fp32 sums,
+                // so unless some p of the tile exceeds 2^15 (a row max above m_run + 15;
+                // checked on the packed fp16 values) P is stored as is.  On the first
+                // tile of an item the running max starts as the max of the first 32
+                // columns (column 0 is visible to every row).
                 bool done = false;
-                float mx = -INFINITY;
                 {
                     uint32_t pk[BN / 2];
                     float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-                    float mx8[8] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY,
-                                    -INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                    __half2 hm[4] = {__float2half2_rn(0.f), __float2half2_rn(0.f), __float2half2_rn(0.f),
+                                     __float2half2_rn(0.f)};
                     uint32_t sbuf[2][32];
                     tmem_ld32(tS + lane_off, sbuf[0]);
                     if (j == 0) {
@@ -726,16 +734,17 @@ __global__ void __maxnreg__(168)
                                 if (kbase + c * 32 + 2 * e > qpos) s0 = -INFINITY;
                                 if (kbase + c * 32 + 2 * e + 1 > qpos) s1 = -INFINITY;
                             }
-                            mx8[e & 7] = fmaxf(mx8[e & 7], fmaxf(s0, s1));
                             const float p0 = ex2(s0 - m_run);
                             const float p1 = ex2(s1 - m_run);
                             ls8[e & 7] += p0 + p1;
-                            pk[c * 16 + e] = pack_half2(p0, p1);
+                            const __half2 h = __floats2half2_rn(p0, p1);
+                            hm[e & 3] = __hmax2(hm[e & 3], h);
+                            pk[c * 16 + e] = *reinterpret_cast<const uint32_t*>(&h);
                         }
                     }
-                    mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-                    if (!__any_sync(0xffffffffu, mx > m_run + kStaleMaxMargin)) {
+                    const float2 hmax = __half22float2(__hmax2(__hmax2(hm[0], hm[1]), __hmax2(hm[2], hm[3])));
+                    const float pmax = fmaxf(hmax.x, hmax.y);
+                    if (!__any_sync(0xffffffffu, !(pmax <= 32768.0f))) {
                         tmem_st32(tS + 0 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
                         tmem_st32(tS + 32 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
                         l_run += ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
@@ -768,6 +777,16 @@ __global__ void __maxnreg__(168)
                                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
                     } else {
                         // a row max jumped: rescale O (sum through tile j-1) to the new max
+                        float mx = -INFINITY;
+#pragma unroll 1
+                        for (int c = 0; c < BN / 32; c++) {
+                            uint32_t sr[32];
+                            tmem_ld32(tS + c * 32 + lane_off, sr);
+                            tmem_ld_wait();
+#pragma unroll
+                            for (int e = 0; e < 32; e++)
+                                if (!diag || kbase + c * 32 + e <= qpos) mx = fmaxf(mx, __uint_as_float(sr[e]));
+                        }
                         const float m_new = fmaxf(m_run, mx);
                         const float corr = ex2(m_run - m_new);
                         mbar_wait(&pv_done[w], (uint32_t)((t - 1) & 1), a.status);

@@ -64,6 +64,15 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
     return d;
 }
 
+// Descriptor of the operand `off_bytes` past the one described by `d`, same
+// layout: only the 14-bit start-address field moves, and shared-memory operands
+// lie below 256 KB, so it never carries into the next field.  Issue loops build
+// their descriptors this way (one add) so that the single issuing thread keeps
+// up with the tensor core (~64 cycles per M128 N128 K16 instruction).
+__device__ __forceinline__ uint64_t desc_advance(uint64_t d, uint32_t off_bytes) {
+    return d + (uint64_t)(off_bytes >> 4);
+}
+
 // kind::f16 instruction descriptor: f16 x f16 -> f32.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool a_mn_major, bool b_mn_major) {
     return (1u << 4) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
