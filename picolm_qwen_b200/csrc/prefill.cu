@@ -466,6 +466,153 @@ __global__ void __launch_bounds__(192, 1)
 // PV0(t), QK0(t+1), PV1(t), QK1(t+1), so each warpgroup's softmax overlaps the
 // other head's tensor work.
 
+// One KV tile of the online softmax for the q row of this thread (TMEM lane):
+// reads S (128 fp32 columns at tS), writes P (fp16, over the first 64 columns
+// of S), updates the running max m_run and sum l_run, and rescales O (at tO)
+// when a row max grows past the stale-max margin.  wait_prev_pv() must return
+// once the PV of the previous tile has completed (called only before O is
+// rescaled).  Returns with the P stores complete (tcgen05.wait::st).
+template <int HD, class WaitPrevPV>
+__device__ __forceinline__ void softmax_tile(uint32_t tS, uint32_t tO, uint32_t lane_off, int j, int kbase, int qpos,
+                                             bool diag, float& m_run, float& l_run, WaitPrevPV wait_prev_pv) {
+    // Optimistic single pass: p = 2^(s - m_run) with the running max, kept
+    // in registers.  p <= 2^15 is exact in fp16 and safe in the fp32 sums,
+    // so unless some p of the tile exceeds 2^15 (a row max above m_run + 15;
+    // checked on the packed fp16 values) P is stored as is.  On the first
+    // tile of an item the running max starts as the max of the first 32
+    // columns (column 0 is visible to every row).
+    bool done = false;
+    {
+        uint32_t pk[BN / 2];
+        uint64_t ls2[4] = {0ull, 0ull, 0ull, 0ull};  // packed (even, odd) column sums
+        __half2 hm[4] = {__float2half2_rn(0.f), __float2half2_rn(0.f), __float2half2_rn(0.f),
+                         __float2half2_rn(0.f)};
+        uint32_t sbuf[2][32];
+        tmem_ld32(tS + lane_off, sbuf[0]);
+        if (j == 0) {
+            tmem_ld_wait();
+            float m0 = -INFINITY;
+#pragma unroll
+            for (int e = 0; e < 32; e++)
+                if (!diag || kbase + e <= qpos) m0 = fmaxf(m0, __uint_as_float(sbuf[0][e]));
+            m_run = m0;
+        }
+        const uint64_t mm2 = f2_pack(m_run, m_run);
+#pragma unroll
+        for (int c = 0; c < BN / 32; c++) {
+            tmem_ld_wait();
+            uint32_t (&sr)[32] = sbuf[c & 1];
+            if (c + 1 < BN / 32) tmem_ld32(tS + (c + 1) * 32 + lane_off, sbuf[(c + 1) & 1]);
+#pragma unroll
+            for (int e = 0; e < 16; e++) {
+                float s0 = __uint_as_float(sr[2 * e]), s1 = __uint_as_float(sr[2 * e + 1]);
+                if (diag) {
+                    if (kbase + c * 32 + 2 * e > qpos) s0 = -INFINITY;
+                    if (kbase + c * 32 + 2 * e + 1 > qpos) s1 = -INFINITY;
+                }
+                float d0, d1;
+                f2_unpack(f2_sub(f2_pack(s0, s1), mm2), d0, d1);
+                const float p0 = ex2(d0), p1 = ex2(d1);
+                ls2[e & 3] = f2_add(ls2[e & 3], f2_pack(p0, p1));
+                const __half2 h = __floats2half2_rn(p0, p1);
+                hm[e & 3] = __hmax2(hm[e & 3], h);
+                pk[c * 16 + e] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+        }
+        const float2 hmax = __half22float2(__hmax2(__hmax2(hm[0], hm[1]), __hmax2(hm[2], hm[3])));
+        const float pmax = fmaxf(hmax.x, hmax.y);
+        if (!__any_sync(0xffffffffu, !(pmax <= 32768.0f))) {
+            tmem_st32(tS + 0 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
+            tmem_st32(tS + 32 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
+            float a0, a1, b0, b1;
+            f2_unpack(f2_add(f2_add(ls2[0], ls2[1]), f2_add(ls2[2], ls2[3])), a0, a1);
+            l_run += a0 + a1;
+            done = true;
+        }
+    }
+    if (!done) {
+        if (j == 0) {
+            // first tile of the item: row max first (scores read twice)
+            uint32_t sr[BN];
+            tmem_ld32(tS + 0 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+            tmem_ld32(tS + 32 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+            tmem_ld32(tS + 64 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
+            tmem_ld32(tS + 96 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
+            tmem_ld_wait();
+            float* sv = reinterpret_cast<float*>(sr);
+            if (diag) {
+#pragma unroll
+                for (int c = 0; c < BN; c++)
+                    if (kbase + c > qpos) sv[c] = -INFINITY;
+            }
+            float mx8[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) mx8[e] = sv[e];
+#pragma unroll
+            for (int c = 8; c < BN; c += 8)
+#pragma unroll
+                for (int e = 0; e < 8; e++) mx8[e] = fmaxf(mx8[e], sv[c + e]);
+            m_run = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                          fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        } else {
+            // a row max jumped: rescale O (sum through tile j-1) to the new max
+            float mx = -INFINITY;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; c++) {
+                uint32_t sr[32];
+                tmem_ld32(tS + c * 32 + lane_off, sr);
+                tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < 32; e++)
+                    if (!diag || kbase + c * 32 + e <= qpos) mx = fmaxf(mx, __uint_as_float(sr[e]));
+            }
+            const float m_new = fmaxf(m_run, mx);
+            const float corr = ex2(m_run - m_new);
+            wait_prev_pv();
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < HD / 32; c++) {
+                uint32_t o[32];
+                tmem_ld32(tO + c * 32 + lane_off, o);
+                tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < 32; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
+                tmem_st32(tO + c * 32 + lane_off, o);
+            }
+            tmem_st_wait();
+            l_run *= corr;
+            m_run = m_new;
+        }
+        // exact pass: 32 scores at a time -> p (fp16) over the S columns
+        // already read: chunk c's P lands in columns [16c, 16c+16) < 32(c+1)
+        float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        uint32_t sbuf[2][32];
+        tmem_ld32(tS + lane_off, sbuf[0]);
+#pragma unroll
+        for (int c = 0; c < BN / 32; c++) {
+            tmem_ld_wait();
+            uint32_t (&sr)[32] = sbuf[c & 1];
+            if (c + 1 < BN / 32) tmem_ld32(tS + (c + 1) * 32 + lane_off, sbuf[(c + 1) & 1]);
+            uint32_t pk[16];
+#pragma unroll
+            for (int e = 0; e < 16; e++) {
+                float s0 = __uint_as_float(sr[2 * e]), s1 = __uint_as_float(sr[2 * e + 1]);
+                if (diag) {
+                    if (kbase + c * 32 + 2 * e > qpos) s0 = -INFINITY;
+                    if (kbase + c * 32 + 2 * e + 1 > qpos) s1 = -INFINITY;
+                }
+                const float p0 = ex2(s0 - m_run);
+                const float p1 = ex2(s1 - m_run);
+                ls8[e & 7] += p0 + p1;
+                pk[e] = pack_half2(p0, p1);
+            }
+            tmem_st16(tS + c * 16 + lane_off, pk);
+        }
+        l_run += ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
+    }
+    tmem_st_wait();
+}
+
 template <int HD>
 struct Attn2Smem {
     static constexpr int kBoxBytes = BM * 128;
@@ -700,138 +847,8 @@ __global__ void __maxnreg__(168)
                 tc_fence_after();
                 const int kbase = j * BN;
                 const bool diag = kbase + BN - 1 > a.start + q0;  // tile crosses this q tile's diagonal
-                // Optimistic single pass: p = 2^(s - m_run) with the running max, kept
-                // in registers.  p <= 2^15 is exact in fp16 and safe in the fp32 sums,
-                // so unless some p of the tile exceeds 2^15 (a row max above m_run + 15;
-                // checked on the packed fp16 values) P is stored as is.  On the first
-                // tile of an item the running max starts as the max of the first 32
-                // columns (column 0 is visible to every row).
-                bool done = false;
-                {
-                    uint32_t pk[BN / 2];
-                    float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-                    __half2 hm[4] = {__float2half2_rn(0.f), __float2half2_rn(0.f), __float2half2_rn(0.f),
-                                     __float2half2_rn(0.f)};
-                    uint32_t sbuf[2][32];
-                    tmem_ld32(tS + lane_off, sbuf[0]);
-                    if (j == 0) {
-                        tmem_ld_wait();
-                        float m0 = -INFINITY;
-#pragma unroll
-                        for (int e = 0; e < 32; e++)
-                            if (!diag || kbase + e <= qpos) m0 = fmaxf(m0, __uint_as_float(sbuf[0][e]));
-                        m_run = m0;
-                    }
-#pragma unroll
-                    for (int c = 0; c < BN / 32; c++) {
-                        tmem_ld_wait();
-                        uint32_t (&sr)[32] = sbuf[c & 1];
-                        if (c + 1 < BN / 32) tmem_ld32(tS + (c + 1) * 32 + lane_off, sbuf[(c + 1) & 1]);
-#pragma unroll
-                        for (int e = 0; e < 16; e++) {
-                            float s0 = __uint_as_float(sr[2 * e]), s1 = __uint_as_float(sr[2 * e + 1]);
-                            if (diag) {
-                                if (kbase + c * 32 + 2 * e > qpos) s0 = -INFINITY;
-                                if (kbase + c * 32 + 2 * e + 1 > qpos) s1 = -INFINITY;
-                            }
-                            const float p0 = ex2(s0 - m_run);
-                            const float p1 = ex2(s1 - m_run);
-                            ls8[e & 7] += p0 + p1;
-                            const __half2 h = __floats2half2_rn(p0, p1);
-                            hm[e & 3] = __hmax2(hm[e & 3], h);
-                            pk[c * 16 + e] = *reinterpret_cast<const uint32_t*>(&h);
-                        }
-                    }
-                    const float2 hmax = __half22float2(__hmax2(__hmax2(hm[0], hm[1]), __hmax2(hm[2], hm[3])));
-                    const float pmax = fmaxf(hmax.x, hmax.y);
-                    if (!__any_sync(0xffffffffu, !(pmax <= 32768.0f))) {
-                        tmem_st32(tS + 0 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
-                        tmem_st32(tS + 32 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
-                        l_run += ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
-                        done = true;
-                    }
-                }
-                if (!done) {
-                    if (j == 0) {
-                        // first tile of the item: row max first (scores read twice)
-                        uint32_t sr[BN];
-                        tmem_ld32(tS + 0 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-                        tmem_ld32(tS + 32 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-                        tmem_ld32(tS + 64 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
-                        tmem_ld32(tS + 96 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
-                        tmem_ld_wait();
-                        float* sv = reinterpret_cast<float*>(sr);
-                        if (diag) {
-#pragma unroll
-                            for (int c = 0; c < BN; c++)
-                                if (kbase + c > qpos) sv[c] = -INFINITY;
-                        }
-                        float mx8[8];
-#pragma unroll
-                        for (int e = 0; e < 8; e++) mx8[e] = sv[e];
-#pragma unroll
-                        for (int c = 8; c < BN; c += 8)
-#pragma unroll
-                            for (int e = 0; e < 8; e++) mx8[e] = fmaxf(mx8[e], sv[c + e]);
-                        m_run = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                      fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-                    } else {
-                        // a row max jumped: rescale O (sum through tile j-1) to the new max
-                        float mx = -INFINITY;
-#pragma unroll 1
-                        for (int c = 0; c < BN / 32; c++) {
-                            uint32_t sr[32];
-                            tmem_ld32(tS + c * 32 + lane_off, sr);
-                            tmem_ld_wait();
-#pragma unroll
-                            for (int e = 0; e < 32; e++)
-                                if (!diag || kbase + c * 32 + e <= qpos) mx = fmaxf(mx, __uint_as_float(sr[e]));
-                        }
-                        const float m_new = fmaxf(m_run, mx);
-                        const float corr = ex2(m_run - m_new);
-                        mbar_wait(&pv_done[w], (uint32_t)((t - 1) & 1), a.status);
-                        tc_fence_after();
-#pragma unroll
-                        for (int c = 0; c < HD / 32; c++) {
-                            uint32_t o[32];
-                            tmem_ld32(tO + c * 32 + lane_off, o);
-                            tmem_ld_wait();
-#pragma unroll
-                            for (int e = 0; e < 32; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
-                            tmem_st32(tO + c * 32 + lane_off, o);
-                        }
-                        tmem_st_wait();
-                        l_run *= corr;
-                        m_run = m_new;
-                    }
-                    // exact pass: 32 scores at a time -> p (fp16) over the S columns
-                    // already read: chunk c's P lands in columns [16c, 16c+16) < 32(c+1)
-                    float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-                    uint32_t sbuf[2][32];
-                    tmem_ld32(tS + lane_off, sbuf[0]);
-#pragma unroll
-                    for (int c = 0; c < BN / 32; c++) {
-                        tmem_ld_wait();
-                        uint32_t (&sr)[32] = sbuf[c & 1];
-                        if (c + 1 < BN / 32) tmem_ld32(tS + (c + 1) * 32 + lane_off, sbuf[(c + 1) & 1]);
-                        uint32_t pk[16];
-#pragma unroll
-                        for (int e = 0; e < 16; e++) {
-                            float s0 = __uint_as_float(sr[2 * e]), s1 = __uint_as_float(sr[2 * e + 1]);
-                            if (diag) {
-                                if (kbase + c * 32 + 2 * e > qpos) s0 = -INFINITY;
-                                if (kbase + c * 32 + 2 * e + 1 > qpos) s1 = -INFINITY;
-                            }
-                            const float p0 = ex2(s0 - m_run);
-                            const float p1 = ex2(s1 - m_run);
-                            ls8[e & 7] += p0 + p1;
-                            pk[e] = pack_half2(p0, p1);
-                        }
-                        tmem_st16(tS + c * 16 + lane_off, pk);
-                    }
-                    l_run += ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
-                }
-                tmem_st_wait();
+                softmax_tile<HD>(tS, tO, lane_off, j, kbase, qpos, diag, m_run, l_run,
+                                 [&] { mbar_wait(&pv_done[w], (uint32_t)((t - 1) & 1), a.status); });
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&p_full[w]);
@@ -865,6 +882,304 @@ __global__ void __maxnreg__(168)
 }
 
 // ---------------------------------------------------------------------------
+// attention, CTA-pair variant (even GQA group size, head_dim 128)
+// ---------------------------------------------------------------------------
+//
+// A cluster of two CTAs on two SMs takes a work item (128-token q tile, heads
+// h0, h0+1 of one KV group): CTA r holds head h0+r.  The leader CTA (rank 0)
+// issues 2-CTA tensor-core instructions (M = 256: each CTA's 128 q rows) for
+// both:
+//   S = Q K^T   B = K tile split by keys: CTA r loads keys [64r, 64r+64)
+//   O += P V    B = V tile split by columns: CTA r loads hd columns [64r, 64r+64)
+// so each SM loads half of every K/V tile, and one thread issues the MMAs of
+// two SMs.  TMEM: S_a, S_b, O_0, O_1 (4 x 128 columns).  S is double-buffered,
+// so QK of tile t+1 runs while the softmax of tile t does and the softmax never
+// waits for a PV; O alternates between items, so an item's output drains while
+// the next item runs.  Per CTA: warps 0-3 softmax (one q row per thread),
+// warp 4 TMA, warp 5 MMA issue (leader only) and TMEM allocation, warps 6-9
+// epilogue (O / l -> out by TMA stores).
+// Cross-CTA signalling: the peer's TMA bytes complete on the leader's full
+// barriers; MMA completions are committed to the same barrier in both CTAs; the
+// peer's softmax and epilogue arrive on the leader's barriers through cluster
+// addresses.  Items go to clusters statically, longest first, in serpentine
+// order.
+struct PairSmem {
+    static constexpr int kQBytes = 2 * BM * 128;    // 128 rows x 128 hd columns (two 64-column boxes)
+    static constexpr int kKBytes = 2 * 64 * 128;    // 64 keys x 128 hd columns (two boxes)
+    static constexpr int kVBytes = 128 * 128;       // 128 keys x 64 hd columns (one box)
+    static constexpr int NK = 3, NV = 3;
+    static constexpr int kQ = 0;  // two Q slots: item k uses slot k % 2
+    static constexpr int kK = kQ + 2 * kQBytes;
+    static constexpr int kV = kK + NK * kKBytes;
+    static constexpr int kStage = kV + NV * kVBytes;  // epilogue: 32 x 32 fp32 per epilogue warp
+    static constexpr int kLsum = kStage + 4 * 4096;   // row sums handed to the epilogue [2][128]
+    static constexpr int kBars = kLsum + 2 * 128 * 4;
+    static constexpr int kEnd = kBars + 512;
+    static constexpr int kDynBytes = kEnd + 1024;
+};
+
+__global__ void __launch_bounds__(320, 1)
+    prefill_attn_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKh,
+                             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                             PrefillArgs a) {
+    constexpr int HD = 128;
+    using L = PairSmem;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int cluster = blockIdx.x >> 1, n_clusters = gridDim.x >> 1;
+    const int n_pairs = a.hq / 2;
+    const int n_items = a.n_qtiles * n_pairs;
+
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBars);
+    uint64_t* q_full = bars + 0;          // [2] leader: both Q tiles of the slot landed
+    uint64_t* q_empty = bars + 2;         // [2] both: last QK reading the slot done
+    uint64_t* k_full = bars + 4;          // [NK] leader
+    uint64_t* k_empty = k_full + L::NK;   // [NK] both
+    uint64_t* v_full = k_empty + L::NK;   // [NV] leader
+    uint64_t* v_empty = v_full + L::NV;   // [NV] both
+    uint64_t* s_full = v_empty + L::NV;   // [2] both, per S buffer
+    uint64_t* p_full = s_full + 2;        // [2] leader, 8 arrivals (4 softmax warps x 2 CTAs)
+    // PV(t) completes pv_done[t % 2]: with QK(t+1) issued before PV(t) a single
+    // barrier could run two phases behind a waiter, which a parity wait cannot tell
+    uint64_t* pv_done = p_full + 2;       // [2] both
+    uint64_t* o_full = pv_done + 2;       // [2] both, per O buffer: the item's last PV done
+    uint64_t* l_full = o_full + 2;        // [2] own, 4 arrivals: row sums written
+    uint64_t* o_free = l_full + 2;        // [2] leader, 8 arrivals (4 epilogue warps x 2 CTAs)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 2);
+    float* lsum = reinterpret_cast<float*>(smem + L::kLsum);
+
+    if (threadIdx.x == 0) {
+        for (int b = 0; b < 2; b++) mbar_init(&q_full[b], 1), mbar_init(&q_empty[b], 1);
+        for (int s = 0; s < L::NK; s++) mbar_init(&k_full[s], 1), mbar_init(&k_empty[s], 1);
+        for (int s = 0; s < L::NV; s++) mbar_init(&v_full[s], 1), mbar_init(&v_empty[s], 1);
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&s_full[b], 1), mbar_init(&p_full[b], 8), mbar_init(&pv_done[b], 1);
+            mbar_init(&o_full[b], 1), mbar_init(&l_full[b], 4), mbar_init(&o_free[b], 8);
+        }
+        fence_mbar_init();
+    }
+    if (warp == 5) tmem_alloc_pair(tmem_slot, 512);
+    tc_fence_before();
+    cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated in both
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    // item r-th of this cluster: serpentine over the longest-first order
+    auto item_of = [&](int r) {
+        const int idx = r * n_clusters + ((r & 1) ? (n_clusters - 1 - cluster) : cluster);
+        return idx < n_items ? idx : -1;
+    };
+    auto n_kv_of = [&](int qt) {
+        const int q_last = min(qt * BM + BM, a.n_tok) - 1;
+        return (a.start + q_last) / BN + 1;
+    };
+
+    if (warp == 4) {
+        // ---------------- TMA producer (both CTAs) ----------------
+        if (lane == 0) {
+            prefetch_tmap(&tmQ);
+            prefetch_tmap(&tmKh);
+            prefetch_tmap(&tmV);
+            int t = 0, items = 0;
+            for (int k = 0;; k++) {
+                const int it = item_of(k);
+                if (it < 0) break;
+                const int qt = a.n_qtiles - 1 - it / n_pairs, h0 = 2 * (it % n_pairs);
+                const int h = h0 + (int)rank, kvh = h0 / a.g;
+                const int qs = k & 1;
+                if (k >= 2) mbar_wait(&q_empty[qs], (uint32_t)(((k >> 1) - 1) & 1), a.status);
+                if (rank == 0) mbar_arrive_expect_tx(&q_full[qs], 2 * L::kQBytes);
+                for (int c = 0; c < 2; c++)
+                    tma_load_2d_pair(smem + L::kQ + qs * L::kQBytes + c * BM * 128, &tmQ, h * HD + 64 * c, qt * BM,
+                                     mapa_shared(&q_full[qs], 0));
+                const int n_kv = n_kv_of(qt);
+                for (int j = 0; j < n_kv; j++, t++) {
+                    const int sk = t % L::NK, uk = t / L::NK;
+                    if (uk > 0) mbar_wait(&k_empty[sk], (uint32_t)((uk - 1) & 1), a.status);
+                    if (rank == 0) mbar_arrive_expect_tx(&k_full[sk], 2 * L::kKBytes);
+                    const uint32_t kf = mapa_shared(&k_full[sk], 0);
+                    for (int c = 0; c < 2; c++)
+                        tma_load_2d_pair(smem + L::kK + sk * L::kKBytes + c * 64 * 128, &tmKh, kvh * HD + 64 * c,
+                                         j * BN + 64 * (int)rank, kf);
+                    const int sv = t % L::NV, uv = t / L::NV;
+                    if (uv > 0) mbar_wait(&v_empty[sv], (uint32_t)((uv - 1) & 1), a.status);
+                    if (rank == 0) mbar_arrive_expect_tx(&v_full[sv], 2 * L::kVBytes);
+                    tma_load_2d_pair(smem + L::kV + sv * L::kVBytes, &tmV, kvh * HD + 64 * (int)rank, j * BN,
+                                     mapa_shared(&v_full[sv], 0));
+                }
+                items = k + 1;
+            }
+            // tail: the leader's last commits to this CTA's empty barriers must have
+            // landed before the CTA may exit
+            for (int s = 0; s < L::NK && s < t; s++) {
+                const int last = s + L::NK * ((t - 1 - s) / L::NK);
+                mbar_wait(&k_empty[s], (uint32_t)((last / L::NK) & 1), a.status);
+            }
+            for (int s = 0; s < L::NV && s < t; s++) {
+                const int last = s + L::NV * ((t - 1 - s) / L::NV);
+                mbar_wait(&v_empty[s], (uint32_t)((last / L::NV) & 1), a.status);
+            }
+            for (int qs = 0; qs < 2 && qs < items; qs++) {
+                const int last = qs + 2 * ((items - 1 - qs) / 2);
+                mbar_wait(&q_empty[qs], (uint32_t)((last >> 1) & 1), a.status);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 5) {
+        // ---------------- MMA issuer (leader lane 0) ----------------
+        if (rank == 0 && lane == 0) {
+            constexpr uint32_t idesc_qk = idesc_f16_f32(2 * BM, BN, false, false);
+            constexpr uint32_t idesc_pv = idesc_f16_f32(2 * BM, HD, false, true);
+            const uint64_t dq = smem_desc_sw128(smem_u32(smem + L::kQ), 16, 1024);
+            const uint64_t dk = smem_desc_sw128(smem_u32(smem + L::kK), 16, 1024);
+            const uint64_t dv = smem_desc_sw128(smem_u32(smem + L::kV), L::kVBytes, 1024);
+            auto mma_qk = [&](int tt, int qs) {  // S[tt % 2] = Q(slot qs) K(tt)^T
+                const int sk = tt % L::NK;
+                const uint64_t kd = desc_advance(dk, sk * L::kKBytes);
+                const uint64_t qd = desc_advance(dq, qs * L::kQBytes);
+                const uint32_t dS = tmem + (uint32_t)((tt & 1) * 128);
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; kk++) {
+                    const uint32_t qoff = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
+                    const uint32_t koff = (kk >> 2) * (64 * 128) + (kk & 3) * 32;
+                    umma2_ss(dS, desc_advance(qd, qoff), desc_advance(kd, koff), idesc_qk, kk > 0 ? 1u : 0u);
+                }
+                umma2_commit_both(&s_full[tt & 1]);
+                umma2_commit_both(&k_empty[sk]);
+            };
+            // QK of tile tt, the jj-th of item kk (n tiles): Q and K must have landed
+            auto issue_qk = [&](int tt, int kk, int jj, int n) {
+                const uint32_t pk = (uint32_t)((tt / L::NK) & 1);
+                bool ok = mbar_test(&k_full[tt % L::NK], pk);
+                if (jj == 0) ok &= mbar_test(&q_full[kk & 1], (uint32_t)((kk >> 1) & 1));
+                if (!ok) {
+                    if (jj == 0) mbar_wait(&q_full[kk & 1], (uint32_t)((kk >> 1) & 1), a.status);
+                    mbar_wait(&k_full[tt % L::NK], pk, a.status);
+                }
+                tc_fence_after();
+                mma_qk(tt, kk & 1);
+                if (jj + 1 == n) umma2_commit_both(&q_empty[kk & 1]);  // the item's last QK: Q slot free
+            };
+            int it = item_of(0);
+            int t = 0;
+            if (it >= 0) {
+                const int n0 = n_kv_of(a.n_qtiles - 1 - it / n_pairs);
+                issue_qk(0, 0, 0, n0);
+            }
+            for (int k = 0; it >= 0; k++) {
+                const int n_kv = n_kv_of(a.n_qtiles - 1 - it / n_pairs);
+                const int it_next = item_of(k + 1);
+                const int n_next = it_next >= 0 ? n_kv_of(a.n_qtiles - 1 - it_next / n_pairs) : 0;
+                const int ob = k & 1;
+                const uint32_t tO = tmem + 256 + (uint32_t)(ob * 128);
+                for (int j = 0; j < n_kv; j++, t++) {
+                    // S of the next tile into the other buffer, across the item boundary
+                    if (j + 1 < n_kv) issue_qk(t + 1, k, j + 1, n_kv);
+                    else if (n_next > 0) issue_qk(t + 1, k + 1, 0, n_next);
+                    const int sv = t % L::NV;
+                    const uint32_t pp = (uint32_t)((t >> 1) & 1), pv = (uint32_t)((t / L::NV) & 1);
+                    // the first PV of item k overwrites O_(k%2): item k-2's epilogue must have read it
+                    const bool first = j == 0, need_o = first && k >= 2;
+                    const uint32_t po = (uint32_t)(((k >> 1) - 1) & 1);
+                    bool ok = mbar_test(&p_full[t & 1], pp) & mbar_test(&v_full[sv], pv);
+                    if (need_o) ok &= mbar_test(&o_free[ob], po);
+                    if (!ok) {
+                        mbar_wait(&p_full[t & 1], pp, a.status);
+                        mbar_wait(&v_full[sv], pv, a.status);
+                        if (need_o) mbar_wait(&o_free[ob], po, a.status);
+                    }
+                    tc_fence_after();
+                    const uint64_t vd = desc_advance(dv, sv * L::kVBytes);
+                    const uint32_t dS = tmem + (uint32_t)((t & 1) * 128);
+#pragma unroll
+                    for (int kk = 0; kk < BN / 16; kk++)
+                        umma2_ts(tO, dS + kk * 8, desc_advance(vd, kk * 16 * 128), idesc_pv,
+                                 (!first || kk > 0) ? 1u : 0u);
+                    umma2_commit_both(&pv_done[t & 1]);
+                    umma2_commit_both(&v_empty[sv]);
+                    if (j + 1 == n_kv) umma2_commit_both(&o_full[ob]);
+                }
+                it = it_next;
+            }
+        }
+        __syncwarp();
+    } else if (warp < 4) {
+        // ---------------- softmax (both CTAs) ----------------
+        const int r = threadIdx.x;  // q row == TMEM lane
+        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+        const uint32_t p_full_l0 = mapa_shared(&p_full[0], 0), p_full_l1 = mapa_shared(&p_full[1], 0);
+        int t = 0;
+        for (int k = 0;; k++) {
+            const int it = item_of(k);
+            if (it < 0) break;
+            const int qt = a.n_qtiles - 1 - it / n_pairs;
+            const int q0 = qt * BM;
+            const int qpos = a.start + q0 + r;
+            const int n_kv = n_kv_of(qt);
+            const uint32_t tO = tmem + 256 + (uint32_t)((k & 1) * 128);
+            float m_run = -INFINITY, l_run = 0.f;
+            for (int j = 0; j < n_kv; j++, t++) {
+                mbar_wait(&s_full[t & 1], (uint32_t)((t >> 1) & 1), a.status);
+                tc_fence_after();
+                const int kbase = j * BN;
+                const bool diag = kbase + BN - 1 > a.start + q0;
+                const uint32_t tS = tmem + (uint32_t)((t & 1) * 128);
+                softmax_tile<HD>(tS, tO, lane_off, j, kbase, qpos, diag, m_run, l_run,
+                                 [&] { mbar_wait(&pv_done[(t - 1) & 1], (uint32_t)(((t - 1) >> 1) & 1), a.status); });
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_remote((t & 1) ? p_full_l1 : p_full_l0);
+            }
+            // hand the row sums to the epilogue warps.  lsum[k % 2] is free again:
+            // item k-2's epilogue read it before releasing O_(k%2), which this
+            // item's first PV waited for
+            lsum[(k & 1) * 128 + r] = l_run;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&l_full[k & 1]);
+        }
+    } else if (warp >= 6) {
+        // ---------------- epilogue (both CTAs) ----------------
+        const int sub = warp & 3;  // TMEM subpartition of this warp: rows 32*sub ..
+        const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
+        float* stage = reinterpret_cast<float*>(smem + L::kStage + (warp - 6) * 4096);
+        int k = 0;
+        for (;; k++) {
+            const int it = item_of(k);
+            if (it < 0) break;
+            const int qt = a.n_qtiles - 1 - it / n_pairs, h = 2 * (it % n_pairs) + (int)rank;
+            const int ob = k & 1;
+            const uint32_t tO = tmem + 256 + (uint32_t)(ob * 128);
+            mbar_wait(&o_full[ob], (uint32_t)((k >> 1) & 1), a.status);
+            mbar_wait(&l_full[ob], (uint32_t)((k >> 1) & 1), a.status);
+            tc_fence_after();
+            const float inv = 1.0f / lsum[ob * 128 + sub * 32 + lane];
+            const int row0 = qt * BM + sub * 32;
+#pragma unroll 1
+            for (int c = 0; c < HD / 32; c++) {
+                uint32_t o[32];
+                tmem_ld32(tO + c * 32 + lane_off, o);
+                tmem_ld_wait();
+                if (c == HD / 32 - 1) {  // O and l are in registers: release the buffer
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_remote(mapa_shared(&o_free[ob], 0));
+                }
+                stage_store_32x32(o, inv, stage, &tmO, h * HD + c * 32, row0, a.n_tok, lane);
+            }
+        }
+        if (lane == 0) bulk_wait_all();
+    }
+    tc_fence_before();
+    cluster_sync_all();  // no CTA leaves while its peer may still signal it
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // host: tensor maps and launch
 // ---------------------------------------------------------------------------
 
@@ -885,14 +1200,15 @@ EncodeTiledFn encode_fn() {
 }
 
 // 2-D map over a row-major fp16 matrix [rows][inner] with row stride `stride_bytes`;
-// 64 x 128 boxes with the 128-byte swizzle the UMMA descriptors above expect.
+// 64-column x box_rows boxes with the 128-byte swizzle the UMMA descriptors above expect.
 // Rows past `rows` read as zeros.
-bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t stride_bytes) {
+bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t stride_bytes,
+              uint32_t box_rows = 128) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     const cuuint64_t dims[2] = {inner, rows};
     const cuuint64_t strides[1] = {stride_bytes};
-    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t box[2] = {64, box_rows};
     const cuuint32_t estr[2] = {1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -939,6 +1255,46 @@ cudaError_t launch_prefill_hd(const PrefillArgs& a, cudaStream_t stream, unsigne
             !make_map(&mv, a.v_cache + slab, kvd, (uint64_t)(a.start + a.n_tok), kvd * 2) ||
             !make_out_map(&mo, a.out, (uint64_t)a.hq * HD, (uint64_t)a.n_tok))
             return cudaErrorInvalidValue;
+        // CTA pairs (head_dim 128, heads in pairs of one KV group): clusters of 2
+        static int pair2_clusters = -1;
+        if (HD == 128 && pair2_clusters < 0) {
+            pair2_clusters = 0;
+            if (cudaFuncSetAttribute(prefill_attn_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     PairSmem::kDynBytes) == cudaSuccess) {
+                cudaLaunchConfig_t cfg = {};
+                cudaLaunchAttribute attr[1];
+                attr[0].id = cudaLaunchAttributeClusterDimension;
+                attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
+                cfg.gridDim = dim3(2, 1, 1);
+                cfg.blockDim = dim3(320, 1, 1);
+                cfg.dynamicSmemBytes = PairSmem::kDynBytes;
+                cfg.attrs = attr;
+                cfg.numAttrs = 1;
+                int n = 0;
+                if (cudaOccupancyMaxActiveClusters(&n, prefill_attn_pair_kernel, &cfg) == cudaSuccess) pair2_clusters = n;
+            }
+            cudaGetLastError();
+        }
+        if (HD == 128 && a.g % 2 == 0 && pair2_clusters > 0) {
+            CUtensorMap mkh;
+            if (!make_map(&mkh, a.k_cache + slab, kvd, (uint64_t)(a.start + a.n_tok), kvd * 2, 64))
+                return cudaErrorInvalidValue;
+            const int n_items = a.n_qtiles * (a.hq / 2);
+            const int clusters = n_items < pair2_clusters ? n_items : pair2_clusters;
+            cudaLaunchConfig_t cfg = {};
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
+            cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
+            cfg.blockDim = dim3(320, 1, 1);
+            cfg.dynamicSmemBytes = PairSmem::kDynBytes;
+            cfg.stream = stream;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            cudaError_t e = cudaLaunchKernelEx(&cfg, prefill_attn_pair_kernel, mq, mkh, mv, mo, a);
+            if (e != cudaSuccess) return e;
+            return cudaGetLastError();
+        }
         // the head-pair kernel needs one resident CTA of 320 threads per SM
         static int pair_ok = -1;
         if (pair_ok < 0) {
