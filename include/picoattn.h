@@ -311,6 +311,17 @@ int32_t picoattn_prefill_staged(const picoattn_config_t* cfg, int32_t layer, int
                                 void* workspace, size_t workspace_bytes, picoattn_stream_t stream,
                                 uint32_t stages);
 
+/* Which attention kernel picoattn_prefill launches for this shape on the
+ * current device: PICOATTN_PREFILL_CTA_PAIR (head_dim 128, an even number of q
+ * heads per KV head: two SMs per head pair, 2-CTA tensor-core instructions),
+ * PICOATTN_PREFILL_HEAD_PAIR (one SM per head pair), PICOATTN_PREFILL_SINGLE
+ * (one CTA per q head and tile); a negative status on error.  No counterpart in
+ * the reference (diagnostic). */
+#define PICOATTN_PREFILL_SINGLE 0
+#define PICOATTN_PREFILL_HEAD_PAIR 1
+#define PICOATTN_PREFILL_CTA_PAIR 2
+int32_t picoattn_prefill_kernel(const picoattn_config_t* cfg);
+
 #ifdef __cplusplus
 }
 #endif

@@ -34,6 +34,10 @@ STAGE_ATTEND = 0x2
 STAGE_COMBINE = 0x4
 STAGE_ALL = 0x7
 
+PREFILL_SINGLE = 0
+PREFILL_HEAD_PAIR = 1
+PREFILL_CTA_PAIR = 2
+
 ROPE_NEOX = 0
 ROPE_INTERLEAVED = 1
 DTYPE_F32 = 0
@@ -101,6 +105,7 @@ PROTOTYPES = {
     "picoattn_decode_splitkv_nccl": (_I, [_CFG, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                          _P, _Z, _P, _P]),
     "picoattn_prefill_workspace_size": (_Z, [_CFG, _I]),
+    "picoattn_prefill_kernel": (_I, [_CFG]),
     "picoattn_prefill": (_I, [_CFG, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P]),
     "picoattn_prefill_staged": (_I, [_CFG, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P,
                                      C.c_uint32]),

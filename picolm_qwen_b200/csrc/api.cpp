@@ -207,6 +207,15 @@ int32_t picoattn_decode_one(const picoattn_config_t* cfg, int32_t layer, int32_t
                          (cudaStream_t)stream, PICOATTN_STAGE_ALL);
 }
 
+int32_t picoattn_prefill_kernel(const picoattn_config_t* cfg) {
+    const int32_t st = picoattn_config_check(cfg);
+    if (st != PICOATTN_OK) return st;
+    const int32_t d = device_ok();
+    if (d != PICOATTN_OK) return d;
+    const int v = prefill_kernel_variant(*cfg);
+    return v < 0 ? PICOATTN_ECUDA : v;
+}
+
 size_t picoattn_prefill_workspace_size(const picoattn_config_t* cfg, int32_t n_tok) {
     if (picoattn_config_check(cfg) != PICOATTN_OK || n_tok <= 0) return 0;
     return prefill_workspace_bytes(*cfg, n_tok);

@@ -87,5 +87,8 @@ struct PrefillArgs {
 
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream, unsigned stages);
 size_t prefill_workspace_bytes(const picoattn_config_t& cfg, int n_tok);
+// attention kernel picoattn_prefill launches for this shape on the current device:
+// 2 CTA pair, 1 head pair, 0 one head per CTA, -1 setup failed
+int prefill_kernel_variant(const picoattn_config_t& cfg);
 
 }  // namespace picoattn

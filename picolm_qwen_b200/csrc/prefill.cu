@@ -24,6 +24,7 @@
 //                  off the common path.
 #include <cmath>
 #include <cstdio>
+#include <mutex>
 
 #include <cuda.h>
 
@@ -895,14 +896,128 @@ __global__ void __maxnreg__(168)
 // two SMs.  TMEM: S_a, S_b, O_0, O_1 (4 x 128 columns).  S is double-buffered,
 // so QK of tile t+1 runs while the softmax of tile t does and the softmax never
 // waits for a PV; O alternates between items, so an item's output drains while
-// the next item runs.  Per CTA: warps 0-3 softmax (one q row per thread),
-// warp 4 TMA, warp 5 MMA issue (leader only) and TMEM allocation, warps 6-9
+// the next item runs.  Per CTA: warps 0-3 and 4-7 softmax over key columns
+// [0,64) and [64,128) of the same q rows (thread = q row, softmax_half), warp 8
+// TMA, warp 9 MMA issue (leader only) and TMEM allocation, warps 10-13
 // epilogue (O / l -> out by TMA stores).
 // Cross-CTA signalling: the peer's TMA bytes complete on the leader's full
 // barriers; MMA completions are committed to the same barrier in both CTAs; the
 // peer's softmax and epilogue arrive on the leader's barriers through cluster
 // addresses.  Items go to clusters statically, longest first, in serpentine
 // order.
+// Half of a KV tile (64 of its 128 key columns, half 0 or 1) of the online
+// softmax for the q row of this thread; the warp holding the other half of the
+// same 32 rows runs the same steps, and the two agree through named barrier
+// `bar` (the 64 threads of both warps) and the exchange area `xs` (128 floats):
+//   xs[0..31]   half 0's first-tile max estimate, per lane
+//   xs[32..95]  each half's tile max on the exact path [half][lane]
+//   xs[96..99]  per-tile flags [tile parity][half]
+// Both halves keep the same running max m_run; l_run is this half's partial
+// sum.  P (fp16) of the half's keys goes to TMEM columns [64*half, 64*half+32)
+// of the S buffer, which this half has already read.  On the first tile the
+// running max starts as the max of the tile's first 32 columns (half 0's, and
+// column 0 is visible to every row).  If any p of either half would exceed
+// 2^15 both take the exact path: shared new max, each rescales its half of O
+// and its partial sum, then recomputes P.
+template <int HD, class WaitPrevPV>
+__device__ __forceinline__ void softmax_half(uint32_t tS, uint32_t tO, uint32_t lane_off, int half, int j, int t,
+                                             int kbase, int qpos, bool diag, float& m_run, float& l_run, int bar,
+                                             float* xs, int lane, WaitPrevPV wait_prev_pv) {
+    const int col0 = half * 64;
+    // one 32-column chunk of this half's scores, masked beyond the diagonal
+    auto load_chunk = [&](int c, uint32_t (&sr)[32]) {
+        tmem_ld32(tS + col0 + c * 32 + lane_off, sr);
+        tmem_ld_wait();
+        if (diag) {
+#pragma unroll
+            for (int e = 0; e < 32; e++)
+                if (kbase + col0 + c * 32 + e > qpos) sr[e] = __float_as_uint(-INFINITY);
+        }
+    };
+    if (j == 0) {  // running max estimate from the tile's first 32 columns
+        if (half == 0) {
+            uint32_t sr[32];
+            load_chunk(0, sr);
+            float m0 = -INFINITY;
+#pragma unroll
+            for (int e = 0; e < 32; e++) m0 = fmaxf(m0, __uint_as_float(sr[e]));
+            xs[lane] = m0;
+        }
+        named_bar_sync(bar, 64);
+        m_run = xs[lane];
+    }
+    uint32_t pk[32];
+    // p = 2^(s - m_run) for the half's 64 scores into pk; partial sum and max p
+    auto p_pass = [&](float& psum, float& pmax) {
+        const uint64_t mm2 = f2_pack(m_run, m_run);
+        uint64_t ls2[4] = {0ull, 0ull, 0ull, 0ull};
+        __half2 hm[2] = {__float2half2_rn(0.f), __float2half2_rn(0.f)};
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            uint32_t sr[32];
+            load_chunk(c, sr);
+#pragma unroll
+            for (int e = 0; e < 16; e++) {
+                float d0, d1;
+                f2_unpack(f2_sub(f2_pack(__uint_as_float(sr[2 * e]), __uint_as_float(sr[2 * e + 1])), mm2), d0, d1);
+                const float p0 = ex2(d0), p1 = ex2(d1);
+                ls2[e & 3] = f2_add(ls2[e & 3], f2_pack(p0, p1));
+                const __half2 h = __floats2half2_rn(p0, p1);
+                hm[e & 1] = __hmax2(hm[e & 1], h);
+                pk[c * 16 + e] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+        }
+        float a0, a1;
+        f2_unpack(f2_add(f2_add(ls2[0], ls2[1]), f2_add(ls2[2], ls2[3])), a0, a1);
+        psum = a0 + a1;
+        const float2 hmax = __half22float2(__hmax2(hm[0], hm[1]));
+        pmax = fmaxf(hmax.x, hmax.y);
+    };
+    float psum, pmax;
+    p_pass(psum, pmax);
+    // both halves must accept the stale max for these rows
+    int* flags = reinterpret_cast<int*>(xs + 96);
+    const bool ok = __all_sync(0xffffffffu, pmax <= 32768.0f);
+    if (lane == 0) flags[(t & 1) * 2 + half] = ok ? 1 : 0;
+    named_bar_sync(bar, 64);
+    const bool ok_both = flags[(t & 1) * 2] != 0 && flags[(t & 1) * 2 + 1] != 0;
+    if (!ok_both) {
+        // exact path: the new row max over both halves
+        float mx = -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < 2; c++) {
+            uint32_t sr[32];
+            load_chunk(c, sr);
+#pragma unroll
+            for (int e = 0; e < 32; e++) mx = fmaxf(mx, __uint_as_float(sr[e]));
+        }
+        xs[32 + half * 32 + lane] = mx;
+        named_bar_sync(bar, 64);
+        const float m_new = fmaxf(j == 0 ? -INFINITY : m_run, fmaxf(mx, xs[32 + (1 - half) * 32 + lane]));
+        if (j > 0) {  // rescale this half's O columns (sum through tile j-1) and partial sum
+            const float corr = ex2(m_run - m_new);
+            wait_prev_pv();
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < 2; c++) {
+                uint32_t o[32];
+                tmem_ld32(tO + col0 + c * 32 + lane_off, o);
+                tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < 32; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
+                tmem_st32(tO + col0 + c * 32 + lane_off, o);
+            }
+            tmem_st_wait();
+            l_run *= corr;
+        }
+        m_run = m_new;
+        p_pass(psum, pmax);
+    }
+    tmem_st32(tS + col0 + lane_off, pk);
+    l_run += psum;
+    tmem_st_wait();
+}
+
 struct PairSmem {
     static constexpr int kQBytes = 2 * BM * 128;    // 128 rows x 128 hd columns (two 64-column boxes)
     static constexpr int kKBytes = 2 * 64 * 128;    // 64 keys x 128 hd columns (two boxes)
@@ -912,13 +1027,16 @@ struct PairSmem {
     static constexpr int kK = kQ + 2 * kQBytes;
     static constexpr int kV = kK + NK * kKBytes;
     static constexpr int kStage = kV + NV * kVBytes;  // epilogue: 32 x 32 fp32 per epilogue warp
-    static constexpr int kLsum = kStage + 4 * 4096;   // row sums handed to the epilogue [2][128]
-    static constexpr int kBars = kLsum + 2 * 128 * 4;
+    static constexpr int kLsum = kStage + 4 * 4096;   // row sums handed to the epilogue [O buffer][half][128]
+    static constexpr int kXch = kLsum + 2 * 2 * 128 * 4;  // softmax half exchange, 128 floats per warp pair
+    static constexpr int kBars = kXch + 4 * 128 * 4;
     static constexpr int kEnd = kBars + 512;
     static constexpr int kDynBytes = kEnd + 1024;
 };
 
-__global__ void __launch_bounds__(320, 1)
+// 448 threads: 14 warps, four of them on two of the SM's sub-partitions, whose
+// 16,384 registers then allow 128 per thread
+__global__ void __launch_bounds__(448, 1)
     prefill_attn_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKh,
                              const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                              PrefillArgs a) {
@@ -940,27 +1058,28 @@ __global__ void __launch_bounds__(320, 1)
     uint64_t* v_full = k_empty + L::NK;   // [NV] leader
     uint64_t* v_empty = v_full + L::NV;   // [NV] both
     uint64_t* s_full = v_empty + L::NV;   // [2] both, per S buffer
-    uint64_t* p_full = s_full + 2;        // [2] leader, 8 arrivals (4 softmax warps x 2 CTAs)
+    uint64_t* p_full = s_full + 2;        // [2] leader, 16 arrivals (8 softmax warps x 2 CTAs)
     // PV(t) completes pv_done[t % 2]: with QK(t+1) issued before PV(t) a single
     // barrier could run two phases behind a waiter, which a parity wait cannot tell
     uint64_t* pv_done = p_full + 2;       // [2] both
     uint64_t* o_full = pv_done + 2;       // [2] both, per O buffer: the item's last PV done
-    uint64_t* l_full = o_full + 2;        // [2] own, 4 arrivals: row sums written
+    uint64_t* l_full = o_full + 2;        // [2] own, 8 arrivals: row sums written
     uint64_t* o_free = l_full + 2;        // [2] leader, 8 arrivals (4 epilogue warps x 2 CTAs)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 2);
     float* lsum = reinterpret_cast<float*>(smem + L::kLsum);
+    float* xch = reinterpret_cast<float*>(smem + L::kXch);
 
     if (threadIdx.x == 0) {
         for (int b = 0; b < 2; b++) mbar_init(&q_full[b], 1), mbar_init(&q_empty[b], 1);
         for (int s = 0; s < L::NK; s++) mbar_init(&k_full[s], 1), mbar_init(&k_empty[s], 1);
         for (int s = 0; s < L::NV; s++) mbar_init(&v_full[s], 1), mbar_init(&v_empty[s], 1);
         for (int b = 0; b < 2; b++) {
-            mbar_init(&s_full[b], 1), mbar_init(&p_full[b], 8), mbar_init(&pv_done[b], 1);
-            mbar_init(&o_full[b], 1), mbar_init(&l_full[b], 4), mbar_init(&o_free[b], 8);
+            mbar_init(&s_full[b], 1), mbar_init(&p_full[b], 16), mbar_init(&pv_done[b], 1);
+            mbar_init(&o_full[b], 1), mbar_init(&l_full[b], 8), mbar_init(&o_free[b], 8);
         }
         fence_mbar_init();
     }
-    if (warp == 5) tmem_alloc_pair(tmem_slot, 512);
+    if (warp == 9) tmem_alloc_pair(tmem_slot, 512);
     tc_fence_before();
     cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated in both
     tc_fence_after();
@@ -976,7 +1095,7 @@ __global__ void __launch_bounds__(320, 1)
         return (a.start + q_last) / BN + 1;
     };
 
-    if (warp == 4) {
+    if (warp == 8) {
         // ---------------- TMA producer (both CTAs) ----------------
         if (lane == 0) {
             prefetch_tmap(&tmQ);
@@ -1027,7 +1146,7 @@ __global__ void __launch_bounds__(320, 1)
             }
         }
         __syncwarp();
-    } else if (warp == 5) {
+    } else if (warp == 9) {
         // ---------------- MMA issuer (leader lane 0) ----------------
         if (rank == 0 && lane == 0) {
             constexpr uint32_t idesc_qk = idesc_f16_f32(2 * BM, BN, false, false);
@@ -1093,10 +1212,11 @@ __global__ void __launch_bounds__(320, 1)
                     tc_fence_after();
                     const uint64_t vd = desc_advance(dv, sv * L::kVBytes);
                     const uint32_t dS = tmem + (uint32_t)((t & 1) * 128);
+                    // P of keys [0,64) in S columns [0,32), of keys [64,128) in [64,96)
 #pragma unroll
                     for (int kk = 0; kk < BN / 16; kk++)
-                        umma2_ts(tO, dS + kk * 8, desc_advance(vd, kk * 16 * 128), idesc_pv,
-                                 (!first || kk > 0) ? 1u : 0u);
+                        umma2_ts(tO, dS + (kk < 4 ? kk * 8 : 64 + (kk - 4) * 8), desc_advance(vd, kk * 16 * 128),
+                                 idesc_pv, (!first || kk > 0) ? 1u : 0u);
                     umma2_commit_both(&pv_done[t & 1]);
                     umma2_commit_both(&v_empty[sv]);
                     if (j + 1 == n_kv) umma2_commit_both(&o_full[ob]);
@@ -1105,10 +1225,13 @@ __global__ void __launch_bounds__(320, 1)
             }
         }
         __syncwarp();
-    } else if (warp < 4) {
-        // ---------------- softmax (both CTAs) ----------------
-        const int r = threadIdx.x;  // q row == TMEM lane
-        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    } else if (warp < 8) {
+        // ---------------- softmax (both CTAs): warps 0-3 keys [0,64), 4-7 keys [64,128) ----------------
+        const int half = warp >> 2;
+        const int r = threadIdx.x & 127;  // q row == TMEM lane
+        const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+        const int bar = 1 + (warp & 3);  // with the warp of the other half over the same rows
+        float* xs = xch + (warp & 3) * 128;
         const uint32_t p_full_l0 = mapa_shared(&p_full[0], 0), p_full_l1 = mapa_shared(&p_full[1], 0);
         int t = 0;
         for (int k = 0;; k++) {
@@ -1126,24 +1249,24 @@ __global__ void __launch_bounds__(320, 1)
                 const int kbase = j * BN;
                 const bool diag = kbase + BN - 1 > a.start + q0;
                 const uint32_t tS = tmem + (uint32_t)((t & 1) * 128);
-                softmax_tile<HD>(tS, tO, lane_off, j, kbase, qpos, diag, m_run, l_run,
+                softmax_half<HD>(tS, tO, lane_off, half, j, t, kbase, qpos, diag, m_run, l_run, bar, xs, lane,
                                  [&] { mbar_wait(&pv_done[(t - 1) & 1], (uint32_t)(((t - 1) >> 1) & 1), a.status); });
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive_remote((t & 1) ? p_full_l1 : p_full_l0);
             }
-            // hand the row sums to the epilogue warps.  lsum[k % 2] is free again:
-            // item k-2's epilogue read it before releasing O_(k%2), which this
-            // item's first PV waited for
-            lsum[(k & 1) * 128 + r] = l_run;
+            // hand the partial row sums to the epilogue warps.  lsum[k % 2] is free
+            // again: item k-2's epilogue read it before releasing O_(k%2), which
+            // this item's first PV waited for
+            lsum[((k & 1) * 2 + half) * 128 + r] = l_run;
             __syncwarp();
             if (lane == 0) mbar_arrive(&l_full[k & 1]);
         }
-    } else if (warp >= 6) {
+    } else if (warp >= 10) {
         // ---------------- epilogue (both CTAs) ----------------
         const int sub = warp & 3;  // TMEM subpartition of this warp: rows 32*sub ..
         const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
-        float* stage = reinterpret_cast<float*>(smem + L::kStage + (warp - 6) * 4096);
+        float* stage = reinterpret_cast<float*>(smem + L::kStage + (warp - 10) * 4096);
         int k = 0;
         for (;; k++) {
             const int it = item_of(k);
@@ -1154,7 +1277,8 @@ __global__ void __launch_bounds__(320, 1)
             mbar_wait(&o_full[ob], (uint32_t)((k >> 1) & 1), a.status);
             mbar_wait(&l_full[ob], (uint32_t)((k >> 1) & 1), a.status);
             tc_fence_after();
-            const float inv = 1.0f / lsum[ob * 128 + sub * 32 + lane];
+            const float inv =
+                1.0f / (lsum[(ob * 2 + 0) * 128 + sub * 32 + lane] + lsum[(ob * 2 + 1) * 128 + sub * 32 + lane]);
             const int row0 = qt * BM + sub * 32;
 #pragma unroll 1
             for (int c = 0; c < HD / 32; c++) {
@@ -1173,7 +1297,7 @@ __global__ void __launch_bounds__(320, 1)
     }
     tc_fence_before();
     cluster_sync_all();  // no CTA leaves while its peer may still signal it
-    if (warp == 5) {
+    if (warp == 9) {
         tc_fence_after();
         tmem_dealloc_pair(tmem, 512);
     }
@@ -1229,6 +1353,64 @@ bool make_out_map(CUtensorMap* m, float* base, uint64_t inner, uint64_t rows) {
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// One-time, per-device setup of the attention kernels for one head_dim: their
+// shared-memory limits, and whether the CTA-pair and head-pair kernels can be
+// resident (the CTA pair needs 448 threads x 128 registers and 2-CTA clusters).
+struct PrefillSetup {
+    bool done = false;
+    cudaError_t err = cudaSuccess;
+    int pair_clusters = 0;  // resident CTA-pair clusters, 0 if none
+    bool pair_ok = false;   // head-pair kernel resident
+    int sms = 148;
+};
+
+template <int HD>
+const PrefillSetup& prefill_setup() {
+    static std::mutex mu;
+    static PrefillSetup table[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    PrefillSetup& st = table[dev & 63];
+    if (st.done) return st;
+    st.done = true;
+    cudaDeviceGetAttribute(&st.sms, cudaDevAttrMultiProcessorCount, dev);
+    st.err = cudaFuncSetAttribute(prefill_attn_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  AttnSmem<HD>::kDynBytes);
+    if (st.err != cudaSuccess) return st;
+    st.err = cudaFuncSetAttribute(prefill_attn2_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  Attn2Smem<HD>::kDynBytes);
+    if (st.err != cudaSuccess) return st;
+    int nb = 0;
+    st.pair_ok = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, prefill_attn2_kernel<HD>, 320,
+                                                               Attn2Smem<HD>::kDynBytes) == cudaSuccess &&
+                 nb > 0;
+    if (HD == 128 && cudaFuncSetAttribute(prefill_attn_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          PairSmem::kDynBytes) == cudaSuccess) {
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(2, 1, 1);
+        cfg.blockDim = dim3(448, 1, 1);
+        cfg.dynamicSmemBytes = PairSmem::kDynBytes;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, prefill_attn_pair_kernel, &cfg) == cudaSuccess) st.pair_clusters = n;
+    }
+    cudaGetLastError();  // a refused query leaves the CTA pair off, not an error
+    return st;
+}
+
+// 2: CTA pair, 1: head pair on one SM, 0: one head per CTA
+template <int HD>
+int prefill_variant(const PrefillSetup& st, int g) {
+    if (HD == 128 && g % 2 == 0 && st.pair_clusters > 0) return 2;
+    if (g % 2 == 0 && st.pair_ok) return 1;
+    return 0;
+}
+
 template <int HD>
 cudaError_t launch_prefill_hd(const PrefillArgs& a, cudaStream_t stream, unsigned stages) {
     if (stages & PICOATTN_STAGE_PREPARE) {
@@ -1237,79 +1419,42 @@ cudaError_t launch_prefill_hd(const PrefillArgs& a, cudaStream_t stream, unsigne
         prefill_prep_kernel<HD><<<(unsigned)((warps + 7) / 8), 256, 0, stream>>>(a);
     }
     if (stages & PICOATTN_STAGE_ATTEND) {
-        static bool attr_done = false;
-        if (!attr_done) {
-            cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 AttnSmem<HD>::kDynBytes);
-            if (e != cudaSuccess) return e;
-            e = cudaFuncSetAttribute(prefill_attn2_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     Attn2Smem<HD>::kDynBytes);
-            if (e != cudaSuccess) return e;
-            attr_done = true;
-        }
+        const PrefillSetup& st = prefill_setup<HD>();
+        if (st.err != cudaSuccess) return st.err;
         CUtensorMap mq, mk, mv, mo;
         const uint64_t kvd = (uint64_t)a.kvd;
         const size_t slab = (size_t)a.layer * a.max_seq * a.kvd;
         if (!make_map(&mq, a.q16, (uint64_t)a.hq * HD, (uint64_t)a.n_tok, (uint64_t)a.hq * HD * 2) ||
-            !make_map(&mk, a.k_cache + slab, kvd, (uint64_t)(a.start + a.n_tok), kvd * 2) ||
             !make_map(&mv, a.v_cache + slab, kvd, (uint64_t)(a.start + a.n_tok), kvd * 2) ||
             !make_out_map(&mo, a.out, (uint64_t)a.hq * HD, (uint64_t)a.n_tok))
             return cudaErrorInvalidValue;
-        // CTA pairs (head_dim 128, heads in pairs of one KV group): clusters of 2
-        static int pair2_clusters = -1;
-        if (HD == 128 && pair2_clusters < 0) {
-            pair2_clusters = 0;
-            if (cudaFuncSetAttribute(prefill_attn_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     PairSmem::kDynBytes) == cudaSuccess) {
-                cudaLaunchConfig_t cfg = {};
-                cudaLaunchAttribute attr[1];
-                attr[0].id = cudaLaunchAttributeClusterDimension;
-                attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
-                cfg.gridDim = dim3(2, 1, 1);
-                cfg.blockDim = dim3(320, 1, 1);
-                cfg.dynamicSmemBytes = PairSmem::kDynBytes;
-                cfg.attrs = attr;
-                cfg.numAttrs = 1;
-                int n = 0;
-                if (cudaOccupancyMaxActiveClusters(&n, prefill_attn_pair_kernel, &cfg) == cudaSuccess) pair2_clusters = n;
-            }
-            cudaGetLastError();
-        }
-        if (HD == 128 && a.g % 2 == 0 && pair2_clusters > 0) {
-            CUtensorMap mkh;
-            if (!make_map(&mkh, a.k_cache + slab, kvd, (uint64_t)(a.start + a.n_tok), kvd * 2, 64))
+        const int variant = prefill_variant<HD>(st, a.g);
+        const int n_pair_items = a.n_qtiles * (a.hq / 2);
+        if (variant == 2) {
+            // CTA pairs (head_dim 128, heads in pairs of one KV group): clusters of 2;
+            // K tiles come in halves of 64 keys
+            if (!make_map(&mk, a.k_cache + slab, kvd, (uint64_t)(a.start + a.n_tok), kvd * 2, 64))
                 return cudaErrorInvalidValue;
-            const int n_items = a.n_qtiles * (a.hq / 2);
-            const int clusters = n_items < pair2_clusters ? n_items : pair2_clusters;
+            const int clusters = n_pair_items < st.pair_clusters ? n_pair_items : st.pair_clusters;
             cudaLaunchConfig_t cfg = {};
             cudaLaunchAttribute attr[1];
             attr[0].id = cudaLaunchAttributeClusterDimension;
             attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
             cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
-            cfg.blockDim = dim3(320, 1, 1);
+            cfg.blockDim = dim3(448, 1, 1);
             cfg.dynamicSmemBytes = PairSmem::kDynBytes;
             cfg.stream = stream;
             cfg.attrs = attr;
             cfg.numAttrs = 1;
-            cudaError_t e = cudaLaunchKernelEx(&cfg, prefill_attn_pair_kernel, mq, mkh, mv, mo, a);
+            cudaError_t e = cudaLaunchKernelEx(&cfg, prefill_attn_pair_kernel, mq, mk, mv, mo, a);
             if (e != cudaSuccess) return e;
             return cudaGetLastError();
         }
-        // the head-pair kernel needs one resident CTA of 320 threads per SM
-        static int pair_ok = -1;
-        if (pair_ok < 0) {
-            int nb = 0;
-            pair_ok = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, prefill_attn2_kernel<HD>, 320,
-                                                                    Attn2Smem<HD>::kDynBytes) == cudaSuccess &&
-                      nb > 0;
-        }
-        if (a.g % 2 == 0 && pair_ok) {
+        if (!make_map(&mk, a.k_cache + slab, kvd, (uint64_t)(a.start + a.n_tok), kvd * 2))
+            return cudaErrorInvalidValue;
+        if (variant == 1) {
             // head pairs share a KV head: persistent grid, one CTA per SM
-            const int n_items = a.n_qtiles * (a.hq / 2);
-            int dev = 0, sms = 148;
-            cudaGetDevice(&dev);
-            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-            const int grid = n_items < sms ? n_items : sms;
+            const int grid = n_pair_items < st.sms ? n_pair_items : st.sms;
             prefill_attn2_kernel<HD><<<grid, 320, Attn2Smem<HD>::kDynBytes, stream>>>(mq, mk, mv, mo, a);
         } else {
             dim3 grid((unsigned)a.n_qtiles, (unsigned)a.hq);
@@ -1323,6 +1468,16 @@ cudaError_t launch_prefill_hd(const PrefillArgs& a, cudaStream_t stream, unsigne
 
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream, unsigned stages) {
     return a.hd == 64 ? launch_prefill_hd<64>(a, stream, stages) : launch_prefill_hd<128>(a, stream, stages);
+}
+
+int prefill_kernel_variant(const picoattn_config_t& cfg) {
+    const int g = cfg.n_heads / cfg.n_kv_heads;
+    if (cfg.head_dim == 64) {
+        const PrefillSetup& st = prefill_setup<64>();
+        return st.err != cudaSuccess ? -1 : prefill_variant<64>(st, g);
+    }
+    const PrefillSetup& st = prefill_setup<128>();
+    return st.err != cudaSuccess ? -1 : prefill_variant<128>(st, g);
 }
 
 size_t prefill_workspace_bytes(const picoattn_config_t& cfg, int n_tok) {

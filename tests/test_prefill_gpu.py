@@ -178,3 +178,17 @@ def test_prefill_rejects_overflowing_prompt(cuda):
     k = torch.zeros((100, 256), device="cuda")
     out = torch.empty_like(q)
     assert st.prefill(0, 200, q, k, k, out) == abi.PICOATTN_ERANGE
+
+
+def test_prefill_kernel_selection(cuda):
+    """On a B200 the Qwen3-8B shape (32/8 heads, head_dim 128) runs the CTA-pair
+    kernel; odd group sizes and head_dim 64 fall back to the one-SM kernels.  A
+    CTA-pair kernel that could not be made resident would otherwise pass every
+    parity test on a slower fallback."""
+    from picolm_qwen_b200 import abi
+    L = abi.lib()
+    pick = lambda hq, hkv, hd: L.picoattn_prefill_kernel(abi.Config.make(1, hq, hkv, hd, 4096, 1e6))
+    assert pick(32, 8, 128) == abi.PREFILL_CTA_PAIR
+    assert pick(40, 8, 128) == abi.PREFILL_SINGLE          # Qwen2.5-32B: 5 q heads per KV head
+    assert pick(28, 4, 128) == abi.PREFILL_SINGLE          # Qwen2.5-7B: 7 per KV head
+    assert pick(32, 4, 64) == abi.PREFILL_HEAD_PAIR        # TinyLlama
