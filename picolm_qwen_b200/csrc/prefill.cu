@@ -947,15 +947,24 @@ __device__ __forceinline__ void softmax_half(uint32_t tS, uint32_t tO, uint32_t 
         m_run = xs[lane];
     }
     uint32_t pk[32];
-    // p = 2^(s - m_run) for the half's 64 scores into pk; partial sum and max p
+    // p = 2^(s - m_run) for the half's 64 scores into pk; partial sum and max p.
+    // The second chunk's TMEM load is in flight while the first is processed.
     auto p_pass = [&](float& psum, float& pmax) {
         const uint64_t mm2 = f2_pack(m_run, m_run);
         uint64_t ls2[4] = {0ull, 0ull, 0ull, 0ull};
         __half2 hm[2] = {__float2half2_rn(0.f), __float2half2_rn(0.f)};
+        uint32_t sb[2][32];
+        tmem_ld32(tS + col0 + lane_off, sb[0]);
 #pragma unroll
         for (int c = 0; c < 2; c++) {
-            uint32_t sr[32];
-            load_chunk(c, sr);
+            tmem_ld_wait();
+            if (c == 0) tmem_ld32(tS + col0 + 32 + lane_off, sb[1]);
+            uint32_t (&sr)[32] = sb[c];
+            if (diag) {
+#pragma unroll
+                for (int e = 0; e < 32; e++)
+                    if (kbase + col0 + c * 32 + e > qpos) sr[e] = __float_as_uint(-INFINITY);
+            }
 #pragma unroll
             for (int e = 0; e < 16; e++) {
                 float d0, d1;
@@ -1244,7 +1253,8 @@ __global__ void __launch_bounds__(448, 1)
             const uint32_t tO = tmem + 256 + (uint32_t)((k & 1) * 128);
             float m_run = -INFINITY, l_run = 0.f;
             for (int j = 0; j < n_kv; j++, t++) {
-                mbar_wait(&s_full[t & 1], (uint32_t)((t >> 1) & 1), a.status);
+                if (!mbar_test(&s_full[t & 1], (uint32_t)((t >> 1) & 1)))
+                    mbar_wait(&s_full[t & 1], (uint32_t)((t >> 1) & 1), a.status);
                 tc_fence_after();
                 const int kbase = j * BN;
                 const bool diag = kbase + BN - 1 > a.start + q0;
