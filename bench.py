@@ -535,15 +535,20 @@ def run_prefill(args, dev, world, rank, local) -> dict:
         pass
     peak = float(peaks.get("bf16_tflops", 1590.0))
     achieved = flops_layer / (attn_ms / 1e3) / 1e12
+    variant = lib.picoattn_prefill_kernel(cfgp)
+    kernel = {abi.PREFILL_CTA_PAIR: "prefill_attn_pair_kernel (2-SM CTA pair, tcgen05 cta_group::2)",
+              abi.PREFILL_HEAD_PAIR: "prefill_attn2_kernel<128> (head pair, 1 SM)",
+              abi.PREFILL_SINGLE: "prefill_attn_kernel<128> (single head)"}.get(variant, f"status {variant}")
     return {"metric": "prefill attn TFLOP/s", "value": round(total / (ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
             "steps": steps, "ms_per_step": round(ms / steps, 4), "dtype": "f16 operands, f32 accumulate",
             "config": {"workload": p["name"], "layers": L, "heads_q_kv_dim": [hq, hkv, hd], "prompt_tokens": n,
                        "qk_norm": True, "flops_per_step": flops_layer * L,
                        "flops_note": "causally visible pairs only, QK^T + PV"},
-            "roofline": {"bound": "tensor", "kernel": "prefill_attn_kernel<128>", "achieved": round(achieved, 1),
+            "roofline": {"bound": "tensor", "kernel": kernel, "achieved": round(achieved, 1),
                          "peak": peak, "peak_kind": "measured" if peaks else "fallback", "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4), "mean_launch_ms": round(attn_ms, 5),
-                         "algorithmic_flops_per_launch": flops_layer}}
+                         "algorithmic_flops_per_launch": flops_layer},
+            "prep_ms_per_layer": round(ms / steps / L - attn_ms, 5)}
 
 
 def main() -> None:
