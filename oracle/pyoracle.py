@@ -277,3 +277,93 @@ class RefModel:
             self.close()
         except Exception:
             pass
+
+
+class RefFullModel:
+    """Multi-layer reference Model with seeded random F32 weights (test only).
+
+    forward / forward_batch run the unmodified engine (cpp/model.hpp:288-636);
+    embed / pre_attn / post_attn / logits are its non-attention stages with the
+    reference's own functions, for a host loop whose attention block is swapped
+    for another implementation (the CPU loop here, or the GPU library)."""
+
+    def __init__(self, ref: RefHarness, n_layers, hq, hkv, hd, n_ffn, vocab, max_seq, rope_base,
+                 rope_mode, qk_norm, seed=0):
+        L = ref.L
+        if not hasattr(L, "_full_proto"):
+            L.pref_full_create.restype = C.c_void_p
+            L.pref_full_create.argtypes = [C.c_int] * 7 + [C.c_float, C.c_int, C.c_int, C.c_uint64]
+            L.pref_full_destroy.argtypes = [C.c_void_p]
+            L.pref_full_forward.restype = C.c_int
+            L.pref_full_forward.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p]
+            L.pref_full_forward_batch.restype = C.c_int
+            L.pref_full_forward_batch.argtypes = [C.c_void_p, _i32p, C.c_int, C.c_int, _f32p]
+            L.pref_full_embed.argtypes = [C.c_void_p, C.c_int, _f32p]
+            L.pref_full_pre_attn.argtypes = [C.c_void_p, C.c_int, _f32p, _f32p, _f32p, _f32p]
+            L.pref_full_post_attn.argtypes = [C.c_void_p, C.c_int, _f32p, _f32p]
+            L.pref_full_logits.argtypes = [C.c_void_p, _f32p, _f32p]
+            L.pref_full_norm_w.restype = C.POINTER(C.c_float)
+            L.pref_full_norm_w.argtypes = [C.c_void_p, C.c_int, C.c_int]
+            for n in ("pref_full_rope_cos", "pref_full_rope_sin"):
+                getattr(L, n).restype = C.POINTER(C.c_float)
+                getattr(L, n).argtypes = [C.c_void_p]
+            L._full_proto = True
+        self.ref, self.L = ref, L
+        self.nl, self.hq, self.hkv, self.hd, self.vocab, self.S = n_layers, hq, hkv, hd, vocab, max_seq
+        self.dim, self.kvd = hq * hd, hkv * hd
+        self.qk_norm = bool(qk_norm)
+        self.h = L.pref_full_create(n_layers, hq, hkv, hd, n_ffn, vocab, max_seq, rope_base, rope_mode,
+                                    int(qk_norm), seed)
+        if not self.h:
+            raise RuntimeError("pref_full_create failed")
+        self.rope_cos = np.ctypeslib.as_array(L.pref_full_rope_cos(self.h), shape=(max_seq, hd // 2)).copy()
+        self.rope_sin = np.ctypeslib.as_array(L.pref_full_rope_sin(self.h), shape=(max_seq, hd // 2)).copy()
+
+    def forward(self, token, pos):
+        out = np.empty(self.vocab, np.float32)
+        assert self.L.pref_full_forward(self.h, int(token), int(pos), out) == 0
+        return out
+
+    def forward_batch(self, tokens, start_pos):
+        out = np.empty(self.vocab, np.float32)
+        t = np.ascontiguousarray(tokens, np.int32)
+        assert self.L.pref_full_forward_batch(self.h, t, t.size, int(start_pos), out) == 0
+        return out
+
+    def embed(self, token):
+        x = np.empty(self.dim, np.float32)
+        self.L.pref_full_embed(self.h, int(token), x)
+        return x
+
+    def pre_attn(self, layer, x):
+        q = np.empty(self.dim, np.float32)
+        k = np.empty(self.kvd, np.float32)
+        v = np.empty(self.kvd, np.float32)
+        self.L.pref_full_pre_attn(self.h, layer, np.ascontiguousarray(x, np.float32), q, k, v)
+        return q, k, v
+
+    def post_attn(self, layer, x, attn):
+        x = np.array(x, np.float32)
+        self.L.pref_full_post_attn(self.h, layer, x, np.ascontiguousarray(attn, np.float32))
+        return x
+
+    def logits(self, x):
+        out = np.empty(self.vocab, np.float32)
+        self.L.pref_full_logits(self.h, np.ascontiguousarray(x, np.float32), out)
+        return out
+
+    def norm_w(self, layer, which):
+        if not self.qk_norm:
+            return None
+        return np.ctypeslib.as_array(self.L.pref_full_norm_w(self.h, layer, which), shape=(self.hd,)).copy()
+
+    def close(self):
+        if self.h:
+            self.L.pref_full_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

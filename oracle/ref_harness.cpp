@@ -19,6 +19,14 @@
 // (cpp/model.hpp:823-828) and the reference's own RoPE table
 // (cpp/model.hpp:1008-1017) are both available without a GGUF file.
 //
+// Full-forward parity (pref_full_*): a multi-layer model with seeded random F32
+// weights is run through the unmodified Model::forward / forward_batch for
+// reference logits, and its non-attention stages are exposed one by one
+// (embedding, attention norm + q/k/v projections, output projection + FFN,
+// final norm + logits; each the reference's own TensorOps calls in the order of
+// cpp/model.hpp:302-458) so that a host loop can run the same model with the
+// attention block replaced by the GPU library.
+//
 // The attention-only loop below (pref_attn_decode_batch) is the timed CPU
 // baseline: the inline block cpp/model.hpp:326-418 restated around the
 // reference's own functions (TensorOps::rmsnorm, rope_qwen, fp32_to_fp16,
@@ -260,5 +268,187 @@ int pref_attn_decode_batch(int B, int hq, int hkv, int hd, int rope_mode,
     for (auto& t : th) t.join();
     return 0;
 }
+
+// ---------------------------------------------------------------------------
+// full-model parity harness
+// ---------------------------------------------------------------------------
+
+namespace {
+
+struct FullHarness {
+    int L, hq, hkv, hd, dim, kvd, n_ffn, vocab, max_seq;
+    Model model;
+    std::vector<std::vector<float>> store;  // every weight array, owned here
+    std::vector<float> xb, q, k, v, xb2, hb, hb2;
+    const float* add(std::vector<float>&& w) {
+        store.push_back(std::move(w));
+        return store.back().data();
+    }
+};
+
+// splitmix64 -> uniform in [-a, a]
+struct Rng {
+    uint64_t s;
+    float next(float a) {
+        uint64_t z = (s += 0x9E3779B97F4A7C15ull);
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        z ^= z >> 31;
+        return a * (2.0f * (float)((z >> 40) * (1.0 / 16777216.0)) - 1.0f);
+    }
+    std::vector<float> vec(size_t n, float a, float center = 0.f) {
+        std::vector<float> w(n);
+        for (auto& x : w) x = center + next(a);
+        return w;
+    }
+};
+
+}  // namespace
+
+// Weights: embedding U(-1,1); projections U(-a,a) with a = sqrt(3/fan_in) (unit
+// variance per output); norms 1 + U(-0.1,0.1); biases U(-0.1,0.1).
+void* pref_full_create(int n_layers, int hq, int hkv, int hd, int n_ffn, int vocab, int max_seq,
+                       float rope_base, int rope_mode, int qk_norm, uint64_t seed) {
+    auto* h = new FullHarness();
+    h->L = n_layers; h->hq = hq; h->hkv = hkv; h->hd = hd; h->n_ffn = n_ffn; h->vocab = vocab;
+    h->max_seq = max_seq; h->dim = hq * hd; h->kvd = hkv * hd;
+    const int dim = h->dim, kvd = h->kvd;
+    h->store.reserve(8 + 16 * (size_t)n_layers);
+    Rng r{seed};
+    Model& m = h->model;
+    auto& ci = m.config.ints();
+    ci[cfg::N_EMBD] = dim;
+    ci[cfg::N_FFN] = n_ffn;
+    ci[cfg::N_HEADS] = hq;
+    ci[cfg::N_KV_HEADS] = hkv;
+    ci[cfg::N_LAYERS] = n_layers;
+    ci[cfg::VOCAB_SIZE] = vocab;
+    ci[cfg::MAX_SEQ_LEN] = max_seq;
+    ci[cfg::HEAD_DIM] = hd;
+    m.config.floats()[cfg::ROPE_FREQ_BASE] = rope_base;
+    const float a_d = std::sqrt(3.0f / (float)dim), a_f = std::sqrt(3.0f / (float)n_ffn);
+    m.weights.set(output::TOKEN_EMBD, h->add(r.vec((size_t)vocab * dim, 1.0f)), kF32);
+    m.weights.set(output::OUTPUT_NORM, h->add(r.vec((size_t)dim, 0.1f, 1.0f)), kF32);
+    m.weights.set(output::OUTPUT, h->add(r.vec((size_t)vocab * dim, a_d)), kF32);
+    for (int l = 0; l < n_layers; l++) {
+        LayerWeights& lw = m.weights.get_layer(l);
+        lw.set(layer::ATTN_NORM, h->add(r.vec((size_t)dim, 0.1f, 1.0f)), kF32);
+        lw.set(layer::FFN_NORM, h->add(r.vec((size_t)dim, 0.1f, 1.0f)), kF32);
+        lw.set(layer::ATTN_Q, h->add(r.vec((size_t)dim * dim, a_d)), kF32);
+        lw.set(layer::ATTN_K, h->add(r.vec((size_t)kvd * dim, a_d)), kF32);
+        lw.set(layer::ATTN_V, h->add(r.vec((size_t)kvd * dim, a_d)), kF32);
+        lw.set(layer::ATTN_OUTPUT, h->add(r.vec((size_t)dim * dim, a_d)), kF32);
+        lw.set(layer::ATTN_Q_B, h->add(r.vec((size_t)dim, 0.1f)), kF32);
+        lw.set(layer::ATTN_K_B, h->add(r.vec((size_t)kvd, 0.1f)), kF32);
+        lw.set(layer::ATTN_V_B, h->add(r.vec((size_t)kvd, 0.1f)), kF32);
+        if (qk_norm) {
+            lw.set(layer::ATTN_Q_NORM, h->add(r.vec((size_t)hd, 0.1f, 1.0f)), kF32);
+            lw.set(layer::ATTN_K_NORM, h->add(r.vec((size_t)hd, 0.1f, 1.0f)), kF32);
+        }
+        lw.set(layer::FFN_GATE, h->add(r.vec((size_t)n_ffn * dim, a_d)), kF32);
+        lw.set(layer::FFN_UP, h->add(r.vec((size_t)n_ffn * dim, a_d)), kF32);
+        lw.set(layer::FFN_DOWN, h->add(r.vec((size_t)dim * n_ffn, a_f)), kF32);
+    }
+    if (m.allocate_run_state() != 0) {
+        delete h;
+        return nullptr;
+    }
+    m.rope_fn = rope_for(rope_mode);
+    h->xb.resize((size_t)dim); h->xb2.resize((size_t)dim); h->q.resize((size_t)dim);
+    h->k.resize((size_t)kvd); h->v.resize((size_t)kvd);
+    h->hb.resize((size_t)n_ffn); h->hb2.resize((size_t)n_ffn);
+    return h;
+}
+
+void pref_full_destroy(void* hp) { delete (FullHarness*)hp; }
+
+// The unmodified engine: one token (cpp/model.hpp:288-460) ...
+int pref_full_forward(void* hp, int token, int pos, float* logits) {
+    auto* h = (FullHarness*)hp;
+    if (token < 0 || token >= h->vocab || pos < 0 || pos >= h->max_seq) return -1;
+    const float* lg = h->model.forward(token, pos);
+    std::memcpy(logits, lg, sizeof(float) * (size_t)h->vocab);
+    return 0;
+}
+
+// ... and a prompt chunk (cpp/model.hpp:462-636): logits of its last token.
+int pref_full_forward_batch(void* hp, const int* tokens, int n, int start_pos, float* logits) {
+    auto* h = (FullHarness*)hp;
+    if (n <= 0 || start_pos < 0 || start_pos + n > h->max_seq) return -1;
+    const float* lg = h->model.forward_batch(std::vector<int>(tokens, tokens + n), start_pos);
+    if (!lg) return -1;
+    std::memcpy(logits, lg, sizeof(float) * (size_t)h->vocab);
+    return 0;
+}
+
+// Stages around the attention block, with the reference's functions:
+// embedding row (cpp/model.hpp:302-308)
+void pref_full_embed(void* hp, int token, float* x) {
+    auto* h = (FullHarness*)hp;
+    auto e = h->model.weights.get(output::TOKEN_EMBD);
+    const size_t row = gguf_type_row_size((GGUFType)e.type, h->dim);
+    dequantize_row((const uint8_t*)e.ptr + (size_t)token * row, x, h->dim, (GGUFType)e.type);
+}
+
+// attention norm and the q, k, v projections with biases (cpp/model.hpp:315-367);
+// QK-norm, RoPE, the cache and the attention itself are the GPU's part
+void pref_full_pre_attn(void* hp, int l, const float* x, float* q, float* k, float* v) {
+    auto* h = (FullHarness*)hp;
+    auto& st = h->model.state;
+    LayerWeights& lw = h->model.weights.get_layer(l);
+    TensorOps::rmsnorm(h->xb.data(), x, st.attn_norm_w[l].data(), h->dim);
+    auto qe = lw.get(layer::ATTN_Q), qb = lw.get(layer::ATTN_Q_B);
+    TensorOps::matmul_bias(q, h->xb.data(), qe.ptr, st.attn_q_bias[l].data(), h->dim, h->dim,
+                           (GGUFType)qe.type, (GGUFType)qb.type, st.dequant_scratch.data());
+    auto ke = lw.get(layer::ATTN_K), kb = lw.get(layer::ATTN_K_B);
+    TensorOps::matmul_bias(k, h->xb.data(), ke.ptr, st.attn_k_bias[l].data(), h->dim, h->kvd,
+                           (GGUFType)ke.type, (GGUFType)kb.type, st.dequant_scratch.data());
+    auto ve = lw.get(layer::ATTN_V), vb = lw.get(layer::ATTN_V_B);
+    TensorOps::matmul_bias(v, h->xb.data(), ve.ptr, st.attn_v_bias[l].data(), h->dim, h->kvd,
+                           (GGUFType)ve.type, (GGUFType)vb.type, st.dequant_scratch.data());
+}
+
+// output projection, residual, FFN, residual (cpp/model.hpp:420-452); x in place
+void pref_full_post_attn(void* hp, int l, float* x, const float* attn) {
+    auto* h = (FullHarness*)hp;
+    auto& st = h->model.state;
+    LayerWeights& lw = h->model.weights.get_layer(l);
+    const int dim = h->dim, n_ffn = h->n_ffn;
+    auto oe = lw.get(layer::ATTN_OUTPUT), ob = lw.get(layer::ATTN_OUTPUT_B);
+    TensorOps::matmul_bias(h->xb2.data(), attn, oe.ptr, st.attn_output_bias[l].data(), dim, dim,
+                           (GGUFType)oe.type, (GGUFType)ob.type, st.dequant_scratch.data());
+    TensorOps::vec_add(x, h->xb2.data(), dim);
+    TensorOps::rmsnorm(h->xb.data(), x, st.ffn_norm_w[l].data(), dim);
+    auto ge = lw.get(layer::FFN_GATE), gb = lw.get(layer::FFN_GATE_B);
+    TensorOps::matmul_bias(h->hb.data(), h->xb.data(), ge.ptr, st.ffn_gate_bias[l].data(), dim, n_ffn,
+                           (GGUFType)ge.type, (GGUFType)gb.type, st.dequant_scratch.data());
+    TensorOps::silu(h->hb.data(), n_ffn);
+    auto ue = lw.get(layer::FFN_UP);
+    TensorOps::matmul(h->hb2.data(), h->xb.data(), ue.ptr, dim, n_ffn, (GGUFType)ue.type);
+    TensorOps::elemwise_mul(h->hb.data(), h->hb.data(), h->hb2.data(), n_ffn);
+    auto de = lw.get(layer::FFN_DOWN), db = lw.get(layer::FFN_DOWN_B);
+    TensorOps::matmul_bias(h->xb.data(), h->hb.data(), de.ptr, st.ffn_down_bias[l].data(), n_ffn, dim,
+                           (GGUFType)de.type, (GGUFType)db.type, st.dequant_scratch.data());
+    TensorOps::vec_add(x, h->xb.data(), dim);
+}
+
+// final norm and logits (cpp/model.hpp:454-458)
+void pref_full_logits(void* hp, const float* x, float* logits) {
+    auto* h = (FullHarness*)hp;
+    auto& st = h->model.state;
+    TensorOps::rmsnorm(h->xb.data(), x, st.output_norm_w.data(), h->dim);
+    auto oe = h->model.weights.get(output::OUTPUT);
+    TensorOps::matmul(logits, h->xb.data(), oe.ptr, h->dim, h->vocab, (GGUFType)oe.type);
+}
+
+// the per-layer QK-norm weights (which 0: q, 1: k) and the RoPE table, for the GPU side
+const float* pref_full_norm_w(void* hp, int l, int which) {
+    auto& st = ((FullHarness*)hp)->model.state;
+    return which == 0 ? st.attn_q_norm_w[l].data() : st.attn_k_norm_w[l].data();
+}
+const float* pref_full_rope_cos(void* hp) { return ((FullHarness*)hp)->model.state.rope_cos.data(); }
+const float* pref_full_rope_sin(void* hp) { return ((FullHarness*)hp)->model.state.rope_sin.data(); }
+uint16_t* pref_full_kcache(void* hp) { return ((FullHarness*)hp)->model.state.key_cache.data(); }
+uint16_t* pref_full_vcache(void* hp) { return ((FullHarness*)hp)->model.state.val_cache.data(); }
 
 }  // extern "C"

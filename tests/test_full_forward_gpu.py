@@ -1,0 +1,88 @@
+"""Full-forward parity on the GPU (SURVEY-style oracle c2): a 3-layer model with
+seeded random weights, run by the reference's unmodified Model::forward_batch
+(a 40-token prompt) and Model::forward (24 decode steps), against the same model
+run by a host loop whose attention block is this library through the C ABI
+(picoattn_prefill_staged for the prompt, picoattn_decode_one per step, the KV
+cache on the device) and whose other stages are the reference's own functions
+(pinned bit-exact by test_full_forward_cpu.py).  The next-token argmax must be
+identical at every step; the logits agree to the attention tolerance carried
+through three layers.  Both head_dim 128 shapes below run the tensor-core
+prefill kernels (G = 2: CTA pair; G = 3: one head per CTA).
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from oracle import pyoracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda")
+
+
+def _run(hq, hkv, hd, qk_norm, seed):
+    from picolm_qwen_b200 import abi
+    from picolm_qwen_b200.runtime import AttnState
+    if not __import__("os").path.exists(pyoracle.REF_SO):
+        pytest.skip("oracle/_ref not built")
+    ref = pyoracle.RefHarness()
+    L, S, vocab, n_prompt, n_gen = 3, 96, 211, 40, 24
+    kw = dict(n_layers=L, hq=hq, hkv=hkv, hd=hd, n_ffn=512, vocab=vocab, max_seq=S, rope_base=1e6,
+              rope_mode=0, qk_norm=qk_norm, seed=seed)
+    m_ref, m = pyoracle.RefFullModel(ref, **kw), pyoracle.RefFullModel(ref, **kw)
+    rng = np.random.default_rng(seed)
+    prompt = rng.integers(0, vocab, n_prompt).astype(np.int32)
+
+    cfg = abi.Config.make(L, hq, hkv, hd, S, 1e6, abi.ROPE_NEOX)
+    st = AttnState(cfg, n_seqs=1, max_ctx=S)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    norms = [(None, None) if not qk_norm else (dev(m.norm_w(l, 0)), dev(m.norm_w(l, 1))) for l in range(L)]
+
+    # prompt: every layer over all prompt tokens at once
+    xs = np.stack([m.embed(t) for t in prompt])
+    for l in range(L):
+        qkv = [m.pre_attn(l, x) for x in xs]
+        q = dev(np.stack([a[0] for a in qkv])); k = dev(np.stack([a[1] for a in qkv]))
+        v = dev(np.stack([a[2] for a in qkv]))
+        out = torch.empty((n_prompt, hq * hd), device="cuda")
+        assert st.prefill(l, 0, q, k, v, out, norms[l][0], norms[l][1]) == 0
+        attn = out.cpu().numpy()
+        xs = np.stack([m.post_attn(l, xs[i], attn[i]) for i in range(n_prompt)])
+    got = [m.logits(xs[-1])]
+    want = [m_ref.forward_batch(prompt, 0)]
+
+    # decode, teacher-forced on the reference's choice
+    tok = int(np.argmax(want[0]))
+    out1 = torch.empty(hq * hd, device="cuda")
+    for step in range(n_gen):
+        pos = n_prompt + step
+        want.append(m_ref.forward(tok, pos))
+        x = m.embed(tok)
+        for l in range(L):
+            q, k, v = (dev(a) for a in m.pre_attn(l, x))
+            assert st.decode_one(l, pos, q, k, v, out1, norms[l][0], norms[l][1]) == 0
+            x = m.post_attn(l, x, out1.cpu().numpy())
+        got.append(m.logits(x))
+        tok = int(np.argmax(want[-1]))
+    torch.cuda.synchronize()
+    assert st.status() == 0
+    got, want = np.stack(got), np.stack(want)
+    same = (np.argmax(got, 1) == np.argmax(want, 1))
+    assert same.all(), f"argmax differs at steps {np.nonzero(~same)[0].tolist()}"
+    scale = np.abs(want).max()
+    err = np.abs(got - want).max()
+    assert err <= 2e-2 * scale, f"max logit error {err:.3g} of scale {scale:.3g}"
+
+
+def test_full_forward_qwen3_like_cta_pair(cuda):
+    _run(hq=4, hkv=2, hd=128, qk_norm=1, seed=11)
+
+
+def test_full_forward_qwen2_like_no_qk_norm(cuda):
+    _run(hq=6, hkv=2, hd=128, qk_norm=0, seed=12)
