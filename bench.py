@@ -383,6 +383,10 @@ def run_ours(args) -> None:
     if not args.no_prefill:
         torch.cuda.empty_cache()
         prefill_line = run_prefill(args, dev, world, rank, local)
+    longctx_line = None
+    if not args.no_longctx:
+        torch.cuda.empty_cache()
+        longctx_line = run_longctx(args, dev, world, rank, local)
 
     nbytes = step_bytes(lens, L, kvd)
     times = torch.tensor([elapsed_ms, e2e_ms, float(nbytes)], dtype=torch.float64, device=dev)
@@ -424,6 +428,8 @@ def run_ours(args) -> None:
         }
         if prefill_line is not None:
             line["prefill"] = prefill_line
+        if longctx_line is not None:
+            line["long_context"] = longctx_line
         if world == 1 and not args.no_cpu:
             try:
                 line["cpu_baseline"] = cpu_baseline(lens)
@@ -551,6 +557,135 @@ def run_prefill(args, dev, world, rank, local) -> dict:
             "prep_ms_per_layer": round(ms / steps / L - attn_ms, 5)}
 
 
+LONGCTX = dict(name="qwen2.5-32b-128k-decode", n_layers=64, n_heads=40, n_kv_heads=8, head_dim=128,
+               rope_base=1e6, ctx=131072, seed=0)
+
+
+def run_longctx(args, dev, world, rank, local) -> dict:
+    """one sequence, 131071 cached rows + the new token
+    at position 131071, 64 layers.  Sequence-sharded: rank g holds the
+    contiguous rows [off_g, off_g + n_g) of every layer and attends only those;
+    for N > 1 each layer's shard results are all-gathered over NCCL and combined
+    by log-sum-exp on every rank (picoattn_decode_splitkv_nccl).  Total work is
+    fixed (strong scaling); value = the whole step's K/V bytes / step time."""
+    import torch
+    import torch.distributed as dist
+    from picolm_qwen_b200 import abi, sharding
+    from picolm_qwen_b200.runtime import stream_handle
+
+    p = LONGCTX
+    L, hq, hkv, hd, S = p["n_layers"], p["n_heads"], p["n_kv_heads"], p["head_dim"], p["ctx"]
+    kvd, qd = hkv * hd, hq * hd
+    pos_new = S - 1
+    off, rows = sharding.shard_rows(S, world, rank)
+    cfg = abi.Config.make(L, hq, hkv, hd, S, p["rope_base"], abi.ROPE_NEOX)
+    lib = abi.lib()
+    cfgp = C.byref(cfg)
+    g = torch.Generator(device=dev)
+    g.manual_seed(3000 + rank)
+    # this rank's rows of every layer, N(0, 0.5^2) in fp16 (the new row is written by its owner)
+    kc = torch.empty((L, rows, kvd), dtype=torch.int16, device=dev)
+    vc = torch.empty_like(kc)
+    for cache in (kc, vc):
+        for l in range(L):
+            cache[l].copy_((torch.randn((rows, kvd), generator=g, device=dev) * 0.5).half().view(torch.int16))
+    q = torch.randn((L, qd), generator=g, device=dev)
+    k = torch.randn((L, kvd), generator=g, device=dev)
+    v = torch.randn((L, kvd), generator=g, device=dev)
+    out = torch.empty((L, qd), device=dev)
+    cos = np.empty(S * hd // 2, np.float32)
+    sin = np.empty_like(cos)
+    assert lib.picoattn_rope_table(cfgp, cos.ctypes.data, sin.ctypes.data) == 0
+    d_cos, d_sin = torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev)
+    kp = torch.tensor([kc.data_ptr()], dtype=torch.int64, device=dev)
+    vp = torch.tensor([vc.data_ptr()], dtype=torch.int64, device=dev)
+    pos = torch.tensor([pos_new], dtype=torch.int32, device=dev)
+    ws_n = lib.picoattn_decode_workspace_size(cfgp, 1, rows)
+    ws = torch.zeros(ws_n, dtype=torch.uint8, device=dev)
+    assert lib.picoattn_workspace_init(ws.data_ptr(), ws_n, stream_handle()) == 0
+    comm = C.c_void_p()
+    gather = None
+    if world > 1:
+        uid = torch.zeros(128, dtype=torch.uint8)
+        if rank == 0:
+            assert lib.picoattn_nccl_unique_id(uid.data_ptr()) == 0
+        uid_d = uid.to(dev)
+        dist.broadcast(uid_d, 0)
+        uid = uid_d.cpu()
+        st = lib.picoattn_nccl_comm_create(world, uid.data_ptr(), rank, 60.0, C.byref(comm))
+        if st != 0:
+            raise abi.PicoAttnError(st, "picoattn_nccl_comm_create")
+        gather = torch.empty(lib.picoattn_splitkv_gather_bytes(cfgp, 1, world) // 4, device=dev)
+    common = (d_cos.data_ptr(), d_sin.data_ptr(), kp.data_ptr(), vp.data_ptr(), pos.data_ptr())
+
+    def layer(l, sh):
+        if world == 1:
+            st = lib.picoattn_decode_staged(cfgp, l, 1, S, q[l].data_ptr(), k[l].data_ptr(), v[l].data_ptr(),
+                                            None, None, *common, out[l].data_ptr(), ws.data_ptr(), ws_n, sh,
+                                            abi.STAGE_ALL)
+        else:
+            st = lib.picoattn_decode_splitkv_nccl(cfgp, l, 1, rows, off, rows, q[l].data_ptr(), k[l].data_ptr(),
+                                                  v[l].data_ptr(), None, None, *common, gather.data_ptr(),
+                                                  out[l].data_ptr(), ws.data_ptr(), ws_n, comm, sh)
+        if st != 0:
+            raise abi.PicoAttnError(st, "long-context decode")
+
+    stream = torch.cuda.current_stream(dev)
+    sh = stream_handle(stream)
+
+    def step(stream_h):
+        for l in range(L):
+            layer(l, stream_h)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    for _ in range(max(3, args.warmup)):
+        step(sh)
+    barrier()
+    steps = max(5, args.steps // 4)
+    timing = "graph"
+    graph = torch.cuda.CUDAGraph()
+    try:
+        with torch.cuda.graph(graph):
+            step(torch.cuda.current_stream(dev).cuda_stream)
+        graph.replay()
+        torch.cuda.synchronize(dev)
+    except Exception:
+        graph, timing = None, "eager"
+        torch.cuda.synchronize(dev)
+    barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        if graph is not None:
+            graph.replay()
+        else:
+            step(sh)
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = t0.elapsed_time(t1)
+    barrier()
+    if graph is not None:
+        del graph  # holds NCCL work: released before the communicator
+    status = np.zeros(1, np.uint32)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+        lib.picoattn_nccl_comm_destroy(comm)
+    total_bytes = float(L) * 2 * S * kvd * 2  # every layer's K and V rows 0..131071, all ranks together
+    return {"metric": "long-context decode attn HBM GB/s", "value": round(total_bytes * steps / (ms / 1e3) / 1e9, 2),
+            "unit": "GB/s", "ms_per_step": round(ms / steps, 4), "steps": steps, "scaling": "strong",
+            "timing": timing,
+            "config": {"workload": p["name"], "layers": L, "heads_q_kv_dim": [hq, hkv, hd], "cached_rows": S - 1,
+                       "rows_per_gpu": rows, "bytes_per_step": total_bytes,
+                       "parallelism": f"sequence-sharded x{world}, NCCL all-gather + LSE combine per layer"
+                       if world > 1 else "single GPU"}}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -559,6 +694,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill (Qwen3-8B) leg")
+    ap.add_argument("--no-longctx", action="store_true", help="skip the long-context (Qwen2.5-32B, 128K) leg")
     ap.add_argument("--seqs", type=int, default=WORKLOAD["n_seqs"],
                     help="sequences per GPU (default 64 = the benchmark; smaller only for profiling)")
     args = ap.parse_args()

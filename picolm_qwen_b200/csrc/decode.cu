@@ -396,24 +396,28 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
 // merge: out = sum_p 2^(m_p - M) acc_p / sum_p 2^(m_p - M) l_p over the pieces
 // ---------------------------------------------------------------------------
 
-template <int HD>
+// Merges the partial (max, sum, acc) pieces of one (head, sequence) into its
+// output; block z handles head-dim columns [z*DS, z*DS+DS), so that few long
+// sequences still spread over many blocks.
+template <int HD, int DS>
 __global__ void __launch_bounds__(256) decode_merge_kernel(DecodeArgs a, int G) {
-    // 256 threads: head dim d = tid % HD, piece group = tid / HD; every group sums
-    // its pieces with 4 independent accumulators so many loads are in flight
-    constexpr int NT = 256, NG = NT / HD;
+    // 256 threads: column d = z*DS + tid % DS, piece group = tid / DS; every group
+    // sums its pieces with 4 independent accumulators so many loads are in flight
+    constexpr int NT = 256, NG = NT / DS;
     __shared__ float w_s[2048];
     __shared__ float red[NT / 32];
     __shared__ float bc[2];
-    __shared__ float part[NG][HD];
+    __shared__ float part[NG][DS];
     const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int d = tid % HD, grp = tid / HD;
+    const int dl = tid % DS, grp = tid / DS, d = blockIdx.z * DS + dl;
+    const bool lse_writer = blockIdx.z == 0 && dl == 0;
     const size_t row_stride = a.shard_out ? (size_t)(HD + 2) : (size_t)HD;
     float* dst = (a.shard_out ? a.shard_out : a.out) + ((size_t)b * a.hq + h) * row_stride + d;
     const int pos = seq_pos(a, b);
     if (!pos_ok(a, pos)) {
         if (grp == 0) {
             *dst = __int_as_float(0x7fc00000);
-            if (a.shard_out && d == 0) dst[HD - d] = __int_as_float(0x7fc00000);
+            if (a.shard_out && lse_writer) dst[HD - d] = __int_as_float(0x7fc00000);
         }
         return;
     }
@@ -422,7 +426,7 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(DecodeArgs a, int G) 
     if (p0 == p1) {  // no rows of this sequence in this shard: empty partial
         if (grp == 0) {
             *dst = 0.f;
-            if (d == 0) dst[HD] = -INFINITY;
+            if (lse_writer) dst[HD] = -INFINITY;
         }
         return;
     }
@@ -482,14 +486,14 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(DecodeArgs a, int G) 
         const float wgt = w_s[k];
         if (wgt != 0.f) acc[0] += wgt * a.part_o[piece(k) * HD + d];
     }
-    part[grp][d] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    part[grp][dl] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
     __syncthreads();
     if (grp == 0) {
-        float o = part[0][d];
+        float o = part[0][dl];
 #pragma unroll
-        for (int g2 = 1; g2 < NG; g2++) o += part[g2][d];
+        for (int g2 = 1; g2 < NG; g2++) o += part[g2][dl];
         *dst = o / bc[1];
-        if (a.shard_out && d == 0) dst[HD] = M + __log2f(bc[1]);
+        if (a.shard_out && lse_writer) dst[HD] = M + __log2f(bc[1]);
     }
 }
 
@@ -507,8 +511,16 @@ cudaError_t launch_decode_hd(const DecodeArgs& a, const DecodePlan& plan, cudaSt
         decode_prep_kernel<HD><<<dim3((unsigned)((n_slots + 31) / 32), (unsigned)a.n_seqs + 1), 256, 0, stream>>>(a);
     if (stages & PICOATTN_STAGE_ATTEND)
         decode_attn_kernel<HD><<<plan.grid_ctas, (plan.compute_warps + 1) * 32, plan.smem_bytes, stream>>>(a);
-    if (stages & PICOATTN_STAGE_COMBINE)
-        decode_merge_kernel<HD><<<dim3((unsigned)a.hq, (unsigned)a.n_seqs), 256, 0, stream>>>(a, plan.grid_ctas);
+    if (stages & PICOATTN_STAGE_COMBINE) {
+        // one block per (head, sequence) when those fill the GPU twice over, else
+        // each also split into HD/32 column slices
+        if ((long)a.hq * a.n_seqs >= 2L * plan.max_grid)
+            decode_merge_kernel<HD, HD><<<dim3((unsigned)a.hq, (unsigned)a.n_seqs, 1), 256, 0, stream>>>(
+                a, plan.grid_ctas);
+        else
+            decode_merge_kernel<HD, 32><<<dim3((unsigned)a.hq, (unsigned)a.n_seqs, HD / 32), 256, 0, stream>>>(
+                a, plan.grid_ctas);
+    }
     return cudaGetLastError();
 }
 
