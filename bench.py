@@ -565,9 +565,11 @@ def run_longctx(args, dev, world, rank, local) -> dict:
     """one sequence, 131071 cached rows + the new token
     at position 131071, 64 layers.  Sequence-sharded: rank g holds the
     contiguous rows [off_g, off_g + n_g) of every layer and attends only those;
-    for N > 1 each layer's shard results are all-gathered over NCCL and combined
-    by log-sum-exp on every rank (picoattn_decode_splitkv_nccl).  Total work is
-    fixed (strong scaling); value = the whole step's K/V bytes / step time."""
+    for N > 1 each layer's shard results go to every rank over peer memory and
+    are combined by log-sum-exp on every rank, in one kernel
+    (picoattn_decode_splitkv_p2p; the IPC handles travel over the process
+    group).  Total work is fixed (strong scaling); value = the whole step's K/V
+    bytes / step time."""
     import torch
     import torch.distributed as dist
     from picolm_qwen_b200 import abi, sharding
@@ -604,18 +606,17 @@ def run_longctx(args, dev, world, rank, local) -> dict:
     ws = torch.zeros(ws_n, dtype=torch.uint8, device=dev)
     assert lib.picoattn_workspace_init(ws.data_ptr(), ws_n, stream_handle()) == 0
     comm = C.c_void_p()
-    gather = None
     if world > 1:
-        uid = torch.zeros(128, dtype=torch.uint8)
-        if rank == 0:
-            assert lib.picoattn_nccl_unique_id(uid.data_ptr()) == 0
-        uid_d = uid.to(dev)
-        dist.broadcast(uid_d, 0)
-        uid = uid_d.cpu()
-        st = lib.picoattn_nccl_comm_create(world, uid.data_ptr(), rank, 60.0, C.byref(comm))
+        handle = torch.zeros(abi.P2P_HANDLE_BYTES, dtype=torch.uint8)
+        st = lib.picoattn_p2p_create(cfgp, 1, world, rank, handle.data_ptr(), C.byref(comm))
         if st != 0:
-            raise abi.PicoAttnError(st, "picoattn_nccl_comm_create")
-        gather = torch.empty(lib.picoattn_splitkv_gather_bytes(cfgp, 1, world) // 4, device=dev)
+            raise abi.PicoAttnError(st, "picoattn_p2p_create")
+        hs = [torch.zeros(abi.P2P_HANDLE_BYTES, dtype=torch.uint8, device=dev) for _ in range(world)]
+        dist.all_gather(hs, handle.to(dev))
+        allh = torch.cat([h.cpu() for h in hs]).contiguous()
+        st = lib.picoattn_p2p_open(comm, allh.data_ptr())
+        if st != 0:
+            raise abi.PicoAttnError(st, "picoattn_p2p_open")
     common = (d_cos.data_ptr(), d_sin.data_ptr(), kp.data_ptr(), vp.data_ptr(), pos.data_ptr())
 
     def layer(l, sh):
@@ -624,9 +625,9 @@ def run_longctx(args, dev, world, rank, local) -> dict:
                                             None, None, *common, out[l].data_ptr(), ws.data_ptr(), ws_n, sh,
                                             abi.STAGE_ALL)
         else:
-            st = lib.picoattn_decode_splitkv_nccl(cfgp, l, 1, rows, off, rows, q[l].data_ptr(), k[l].data_ptr(),
-                                                  v[l].data_ptr(), None, None, *common, gather.data_ptr(),
-                                                  out[l].data_ptr(), ws.data_ptr(), ws_n, comm, sh)
+            st = lib.picoattn_decode_splitkv_p2p(cfgp, l, 1, rows, off, rows, q[l].data_ptr(), k[l].data_ptr(),
+                                                 v[l].data_ptr(), None, None, *common, out[l].data_ptr(),
+                                                 ws.data_ptr(), ws_n, comm, sh)
         if st != 0:
             raise abi.PicoAttnError(st, "long-context decode")
 
@@ -669,20 +670,25 @@ def run_longctx(args, dev, world, rank, local) -> dict:
     ms = t0.elapsed_time(t1)
     barrier()
     if graph is not None:
-        del graph  # holds NCCL work: released before the communicator
-    status = np.zeros(1, np.uint32)
+        del graph
+    dev_status = C.c_uint32(0)
+    lib.picoattn_workspace_status(ws.data_ptr(), sh, C.byref(dev_status))
+    if dev_status.value != 0:
+        raise RuntimeError(f"long-context device status {dev_status.value:#x}")
     if world > 1:
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t[0])
-        lib.picoattn_nccl_comm_destroy(comm)
+        dist.barrier(device_ids=[local])  # every rank's last exchange is done before the areas go
+        lib.picoattn_p2p_destroy(comm)
     total_bytes = float(L) * 2 * S * kvd * 2  # every layer's K and V rows 0..131071, all ranks together
     return {"metric": "long-context decode attn HBM GB/s", "value": round(total_bytes * steps / (ms / 1e3) / 1e9, 2),
             "unit": "GB/s", "ms_per_step": round(ms / steps, 4), "steps": steps, "scaling": "strong",
             "timing": timing,
             "config": {"workload": p["name"], "layers": L, "heads_q_kv_dim": [hq, hkv, hd], "cached_rows": S - 1,
                        "rows_per_gpu": rows, "bytes_per_step": total_bytes,
-                       "parallelism": f"sequence-sharded x{world}, NCCL all-gather + LSE combine per layer"
+                       "parallelism": f"sequence-sharded x{world}, per-layer exchange + LSE combine in one kernel "
+                                      "over NVLink peer memory"
                        if world > 1 else "single GPU"}}
 
 

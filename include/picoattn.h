@@ -311,6 +311,32 @@ int32_t picoattn_prefill_staged(const picoattn_config_t* cfg, int32_t layer, int
                                 void* workspace, size_t workspace_bytes, picoattn_stream_t stream,
                                 uint32_t stages);
 
+/* ---- split-KV decode with the exchange over peer memory ----------------------
+ * One process per GPU on one node.  Each rank creates its exchange area (device
+ * memory, picoattn_p2p_area_bytes) and gets a CUDA IPC handle for it; the caller
+ * moves the n_ranks handles between the processes (any transport) and opens the
+ * communicator with all of them, in rank order.  picoattn_decode_splitkv_p2p
+ * then runs picoattn_decode_shard into the area and ONE kernel that stores the
+ * shard result into every rank's area over NVLink, raises a per-row flag there,
+ * waits (bounded; PICOATTN_DEV_TIMEOUT in the workspace status) for every rank's
+ * row and combines them by log-sum-exp into out, on every rank.  Every rank must
+ * make the same sequence of calls.  Destroy only after every rank's last call
+ * has completed (a barrier).  No counterpart in the reference. */
+#define PICOATTN_P2P_HANDLE_BYTES 64
+size_t picoattn_p2p_area_bytes(const picoattn_config_t* cfg, int32_t n_seqs, int32_t n_ranks);
+int32_t picoattn_p2p_create(const picoattn_config_t* cfg, int32_t n_seqs, int32_t n_ranks, int32_t rank,
+                            void* ipc_handle_out, void** comm_out);
+int32_t picoattn_p2p_open(void* comm, const void* ipc_handles);
+int32_t picoattn_p2p_destroy(void* comm);
+int32_t picoattn_decode_splitkv_p2p(const picoattn_config_t* cfg, int32_t layer, int32_t n_seqs, int32_t max_ctx,
+                                    int32_t row_offset, int32_t local_rows,
+                                    const float* q, const float* k, const float* v,
+                                    const float* q_norm_w, const float* k_norm_w,
+                                    const float* rope_cos, const float* rope_sin,
+                                    uint16_t* const* k_cache, uint16_t* const* v_cache,
+                                    const int32_t* pos, float* out, void* workspace, size_t workspace_bytes,
+                                    void* comm, picoattn_stream_t stream);
+
 /* Which attention kernel picoattn_prefill launches for this shape on the
  * current device: PICOATTN_PREFILL_CTA_PAIR (head_dim 128, an even number of q
  * heads per KV head: two SMs per head pair, 2-CTA tensor-core instructions),

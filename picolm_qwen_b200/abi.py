@@ -38,6 +38,8 @@ PREFILL_SINGLE = 0
 PREFILL_HEAD_PAIR = 1
 PREFILL_CTA_PAIR = 2
 
+P2P_HANDLE_BYTES = 64
+
 ROPE_NEOX = 0
 ROPE_INTERLEAVED = 1
 DTYPE_F32 = 0
@@ -106,6 +108,12 @@ PROTOTYPES = {
                                          _P, _Z, _P, _P]),
     "picoattn_prefill_workspace_size": (_Z, [_CFG, _I]),
     "picoattn_prefill_kernel": (_I, [_CFG]),
+    "picoattn_p2p_area_bytes": (_Z, [_CFG, _I, _I]),
+    "picoattn_p2p_create": (_I, [_CFG, _I, _I, _I, _P, _P]),
+    "picoattn_p2p_open": (_I, [_P, _P]),
+    "picoattn_p2p_destroy": (_I, [_P]),
+    "picoattn_decode_splitkv_p2p": (_I, [_CFG, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                         _P, _Z, _P, _P]),
     "picoattn_prefill": (_I, [_CFG, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P]),
     "picoattn_prefill_staged": (_I, [_CFG, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P,
                                      C.c_uint32]),
