@@ -473,11 +473,12 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(DecodeArgs a, int G) 
         bc[1] = L;
     }
     __syncthreads();
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    // 8 independent accumulators: 8 loads of each thread in flight at once
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     int k = grp;
-    for (; k + 3 * NG < n_pieces; k += 4 * NG) {
+    for (; k + 7 * NG < n_pieces; k += 8 * NG) {
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
+        for (int u = 0; u < 8; u++) {
             const float wgt = w_s[k + u * NG];
             if (wgt != 0.f) acc[u] += wgt * a.part_o[piece(k + u * NG) * HD + d];
         }
@@ -486,7 +487,7 @@ __global__ void __launch_bounds__(256) decode_merge_kernel(DecodeArgs a, int G) 
         const float wgt = w_s[k];
         if (wgt != 0.f) acc[0] += wgt * a.part_o[piece(k) * HD + d];
     }
-    part[grp][dl] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    part[grp][dl] = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
     __syncthreads();
     if (grp == 0) {
         float o = part[0][dl];
@@ -554,11 +555,12 @@ bool make_decode_plan(const picoattn_config_t& cfg, int n_seqs, int max_ctx, Dec
     p.smem_bytes = 128 + p.stages * stage_bytes;
     if (p.smem_bytes > 200 * 1024 + 256) return false;
     // Persistent grid: as many CTAs as fit at once (smem-limited), but no more
-    // than one per 256 rows of the largest possible workload.
+    // than one per 64 rows of the largest possible workload (a 16K-row shard of
+    // one sequence still spreads over every SM).
     const int sms = device_sm_count();
     const int per_sm = p.smem_bytes <= 113 * 1024 ? 2 : 1;
     const long long work_rows = (long long)n_seqs * max_ctx;
-    long long g = std::min<long long>((long long)sms * per_sm, (work_rows + 255) / 256);
+    long long g = std::min<long long>((long long)sms * per_sm, (work_rows + 63) / 64);
     p.grid_ctas = (int)std::max<long long>(1, g);
     p.max_grid = sms * 2;
     // pieces per sequence <= grid_ctas * warps_per_head; the merge kernel holds
