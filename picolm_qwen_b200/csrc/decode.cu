@@ -25,6 +25,7 @@
 //          split across CTAs.
 #include <cmath>
 #include <cstdio>
+#include <utility>
 
 #include "device_common.cuh"
 #include "picoattn_internal.h"
@@ -68,11 +69,12 @@ __device__ __forceinline__ int cta_of_row(long long x, long long R, int G) {
 // ---------------------------------------------------------------------------
 
 // Exclusive scan of the attended lengths (pos+1, or 0 for a rejected position)
-// into prefix[0..n_seqs]; one block of 256 threads.
+// into prefix[0..n_seqs]; one block of NT threads.
+template <int NT>
 __device__ void scan_lengths(const DecodeArgs& a) {
-    __shared__ long long warp_tot[8];
+    __shared__ long long warp_tot[NT / 32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int per = (a.n_seqs + 255) / 256;
+    const int per = (a.n_seqs + NT - 1) / NT;
     const int b0 = min(tid * per, a.n_seqs), b1 = min(b0 + per, a.n_seqs);
     long long mine = 0;
     for (int b = b0; b < b1; b++) {
@@ -94,13 +96,19 @@ __device__ void scan_lengths(const DecodeArgs& a) {
         const int p = seq_pos(a, b);
         run += pos_ok(a, p) ? local_len(a, p) : 0;
     }
-    if (tid == 255) a.prefix[a.n_seqs] = base + incl;
+    if (tid == NT - 1) a.prefix[a.n_seqs] = base + incl;
 }
 
 template <int HD>
 __global__ void __launch_bounds__(256) decode_prep_kernel(DecodeArgs a) {
+    // The attention kernel after this one may launch at once; it waits for this
+    // kernel before it reads anything written here.
+    pdl_trigger();
+    // q/k/v may come from the kernel before, which may also still read the
+    // workspace written here
+    pdl_wait();
     if (blockIdx.y == (unsigned)a.n_seqs) {  // the extra block row: length prefix sums
-        if (blockIdx.x == 0) scan_lengths(a);
+        if (blockIdx.x == 0) scan_lengths<256>(a);
         return;
     }
     // 8 warps x 4 head vectors of one sequence per block (helpers: prep_common.cuh)
@@ -164,27 +172,290 @@ __global__ void __launch_bounds__(256) decode_prep_kernel(DecodeArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// merge: out = sum_p 2^(m_p - M) acc_p / sum_p 2^(m_p - M) l_p over the pieces
+// ---------------------------------------------------------------------------
+
+// Merges the partial (max, sum, acc) pieces of one (head, sequence) into its
+// output columns [z*DS, z*DS+DS), with NT threads (tid < NT) and `sync` as
+// their barrier.  The work is a chain of dependent steps, so it keeps to one
+// round of loads after the position and prefix sums: at once, (max, sum) of
+// every piece into shared memory (thread = piece) and the acc columns d..d+3 of
+// every NG-th piece (thread = (group, 4 columns)), RPT rows each held in
+// registers; then the block max M, the weights 2^(m - M), the block sum L of
+// weight * sum, and the weighted acc rows summed over the groups.  The pieces
+// are read from L2 (__ldcg), where the attention kernel just left them.
+// Shared memory: m_s, l_s [kMergeMaxPieces], red [NT/32].
+constexpr int kMergeMaxPieces = 1280;
+
+template <int HD, int DS, int NT, int RPT, class Sync>
+__device__ __forceinline__ void merge_slice(const DecodeArgs& a, int G, int b, int h, int z, float* m_s, float* l_s,
+                                            float* red, int tid, Sync sync) {
+    constexpr int C4 = DS / 4, NG = NT / C4, TPC = NT / DS;
+    static_assert(NG * DS <= kMergeMaxPieces, "group sums fit in l_s");
+    float* part = l_s;
+    const int lane = tid & 31, warp = tid >> 5;
+    const size_t row_stride = a.shard_out ? (size_t)(HD + 2) : (size_t)HD;
+    float* dst = (a.shard_out ? a.shard_out : a.out) + ((size_t)b * a.hq + h) * row_stride + z * DS;
+    const bool lse_writer = z == 0 && tid == 0;
+    const int pos = seq_pos(a, b);
+    long long R, p0, p1;
+    if (a.n_seqs == 1) {  // the attended rows follow from the position (no prefix pass may have run)
+        R = p1 = pos_ok(a, pos) ? local_len(a, pos) : 0;
+        p0 = 0;
+    } else {
+        R = a.prefix[a.n_seqs], p0 = a.prefix[b], p1 = a.prefix[b + 1];
+    }
+    if (!pos_ok(a, pos)) {
+        if (tid < DS) dst[tid] = __int_as_float(0x7fc00000);
+        if (a.shard_out && lse_writer) dst[HD] = __int_as_float(0x7fc00000);
+        return;
+    }
+    if (p0 == p1) {  // no rows of this sequence in this shard: empty partial
+        if (tid < DS) dst[tid] = 0.f;
+        if (a.shard_out && lse_writer) dst[HD] = -INFINITY;
+        return;
+    }
+    // the CTAs whose slices hold this sequence's rows (the last row is always in
+    // CTA G-1's slice; a sequence starting at row 0 starts in CTA 0's, which may
+    // be empty when R < G: such pieces are skipped)
+    const int i_lo = p0 == 0 ? 0 : cta_of_row(p0, R, G);
+    const int i_hi = p1 == R ? G - 1 : cta_of_row(p1 - 1, R, G);
+    const int W = a.warps_per_head, lw = __ffs(W) - 1;  // W is 1, 2, 4 or 8
+    if (i_lo == i_hi && W == 1) return;  // written directly by the attention kernel
+    const int n_pieces = (i_hi - i_lo + 1) * W;  // <= kMergeMaxPieces (checked on the host)
+    // piece k = (CTA i_lo + k/W, warp k%W) -> slot (cta + seq, warp), head h
+    auto slot_of = [&](int k) -> uint32_t {
+        return (uint32_t)((((i_lo + (k >> lw) + b) << lw) | (k & (W - 1))) * a.hq + h);
+    };
+    for (int k = tid; k < n_pieces; k += NT) {
+        const int i = i_lo + (k >> lw);
+        float2 ml = make_float2(-INFINITY, 0.f);
+        if (R >= G || slice_start(i, R, G) < slice_start(i + 1, R, G))
+            ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml + (size_t)slot_of(k) * 2));
+        m_s[k] = ml.x;
+        l_s[k] = ml.y;
+    }
+    const int c4 = tid % C4, grp = tid / C4;
+    const float* po = a.part_o + z * DS + c4 * 4;
+    float4 ov[RPT];
+#pragma unroll
+    for (int u = 0; u < RPT; u++) {
+        const int k = grp + u * NG;
+        ov[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (k < n_pieces) ov[u] = __ldcg(reinterpret_cast<const float4*>(po + (size_t)slot_of(k) * HD));
+    }
+    sync();
+    float mloc = -INFINITY;
+    for (int k = tid; k < n_pieces; k += NT) mloc = fmaxf(mloc, m_s[k]);
+    for (int o = 16; o; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
+    if (lane == 0) red[warp] = mloc;
+    sync();
+    float M = red[0];
+#pragma unroll
+    for (int w = 1; w < NT / 32; w++) M = fmaxf(M, red[w]);
+    float lloc = 0.f;
+    for (int k = tid; k < n_pieces; k += NT) {
+        const float m = m_s[k];
+        const float wgt = m == -INFINITY ? 0.f : ex2(m - M);
+        lloc += wgt * l_s[k];
+        m_s[k] = wgt;
+    }
+    for (int o = 16; o; o >>= 1) lloc += __shfl_xor_sync(0xffffffffu, lloc, o);
+    sync();  // every thread has read red[] for M; weights complete; l_s free
+    if (lane == 0) red[warp] = lloc;
+    // weighted acc rows (pieces of weight 0 may hold stale slots: skipped)
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < RPT; u++) {
+        const int k = grp + u * NG;
+        const float wgt = k < n_pieces ? m_s[k] : 0.f;
+        if (wgt != 0.f) acc.x += wgt * ov[u].x, acc.y += wgt * ov[u].y, acc.z += wgt * ov[u].z, acc.w += wgt * ov[u].w;
+    }
+    for (int k = grp + RPT * NG; k < n_pieces; k += NG) {  // beyond RPT rows per thread
+        const float wgt = m_s[k];
+        if (wgt != 0.f) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(po + (size_t)slot_of(k) * HD));
+            acc.x += wgt * v.x, acc.y += wgt * v.y, acc.z += wgt * v.z, acc.w += wgt * v.w;
+        }
+    }
+    *reinterpret_cast<float4*>(part + grp * DS + c4 * 4) = acc;
+    sync();
+    float L = 0.f;
+#pragma unroll
+    for (int w = 0; w < NT / 32; w++) L += red[w];
+    // the NG group sums of column col: TPC threads of one warp, NG / TPC each
+    const int col = tid / TPC, j = tid % TPC;
+    float o = 0.f;
+#pragma unroll
+    for (int g2 = j; g2 < NG; g2 += TPC) o += part[g2 * DS + col];
+#pragma unroll
+    for (int sh = TPC / 2; sh; sh >>= 1) o += __shfl_xor_sync(0xffffffffu, o, sh);
+    if (j == 0) dst[col] = o / L;
+    if (a.shard_out && lse_writer) dst[HD] = M + __log2f(L);
+    sync();  // m_s, l_s and red may be reused
+}
+
+// RPT: acc rows per thread held in registers, enough for one long sequence's
+// pieces (one per attention CTA) with 32- or 64-column slices; the whole-row
+// variant serves many short sequences of a few pieces each and keeps two.
+template <int HD, int DS, int NT>
+struct MergeRows {
+    static constexpr int NG = NT / (DS / 4);
+    static constexpr int value = DS == HD ? 2 : ((160 + NG - 1) / NG < 10 ? (160 + NG - 1) / NG : 10);
+};
+
+// The merge as its own kernel: block (head, sequence, column slice).  The next
+// kernel may launch at once (pdl_trigger first); with 256 threads, at most 64
+// registers and ~11 KB of shared memory a block fits on an SM beside an
+// attention CTA of the next call.
+template <int HD, int DS>
+__global__ void __launch_bounds__(256, 4) decode_merge_kernel(DecodeArgs a, int G) {
+    __shared__ float m_s[kMergeMaxPieces];
+    __shared__ float l_s[kMergeMaxPieces];
+    __shared__ float red[8];
+    pdl_trigger();
+    pdl_wait();
+    merge_slice<HD, DS, 256, MergeRows<HD, DS, 256>::value>(a, G, blockIdx.y, blockIdx.x, blockIdx.z, m_s, l_s, red,
+                                                            threadIdx.x, [] { __syncthreads(); });
+}
+
+// ---------------------------------------------------------------------------
 // attn: persistent split-KV GQA attention
 // ---------------------------------------------------------------------------
 
-// Calls fn(b, row_begin, row_end) for each sequence segment of this CTA's
-// slice, in order (rows local to the sequence).
+// Calls fn(b, row_begin, row_end, whole, seq_rows) for each sequence segment
+// of this CTA's slice, in order (rows local to the sequence; seq_rows = the
+// sequence's attended rows in this slab).
 template <typename F>
-__device__ __forceinline__ void for_each_segment(const DecodeArgs& a, long long R0, long long R1, F&& fn) {
+__device__ __forceinline__ void for_each_segment(const DecodeArgs& a, const long long* prefix, long long R0,
+                                                 long long R1, F&& fn) {
     // first sequence: the last b with prefix[b] <= R0 (binary search)
     int lo = 0, hi = a.n_seqs;  // prefix[lo] <= R0 < prefix[hi] for the answer lo
     while (hi - lo > 1) {
         const int mid = (lo + hi) >> 1;
-        if (a.prefix[mid] <= R0) lo = mid;
+        if (prefix[mid] <= R0) lo = mid;
         else hi = mid;
     }
     for (int b = lo; b < a.n_seqs; b++) {
-        const long long p0 = a.prefix[b], p1 = a.prefix[b + 1];
+        const long long p0 = prefix[b], p1 = prefix[b + 1];
         if (p0 >= R1) break;
         const long long s = max(R0, p0), e = min(R1, p1);
-        if (e > s) fn(b, (int)(s - p0), (int)(e - p0), p0 == s && p1 == e);
+        if (e > s) fn(b, (int)(s - p0), (int)(e - p0), p0 == s && p1 == e, (int)(p1 - p0));
     }
 }
+
+// The A operand of the QK^T MMA for the G q heads of KV head kvh of sequence b
+// (rows = heads, padded to 16 with zeros): per-head QK-RMSNorm and RoPE with
+// the prep helpers (the reference's operation order, prep_common.cuh), scaled
+// by log2(e)/sqrt(hd) so scores come out in log2 units (the reference divides by
+// sqrtf(hd) and uses expf), rounded to fp16.  Four heads at a time pass through
+// the warp's staging area sq (4*HD floats) into the lanes that hold their rows.
+template <int HD>
+__device__ __forceinline__ void q_fragments(const DecodeArgs& a, int b, int pos, int kvh, float* sq, int lane,
+                                            uint32_t (&qa)[HD / 16][4]) {
+    constexpr int V = HD / 32;
+    const int G_q = a.g, gid = lane >> 2, tig = lane & 3;
+    const float qscale = 1.4426950408889634f / sqrtf((float)HD);
+#pragma unroll
+    for (int kk = 0; kk < HD / 16; kk++) qa[kk][0] = qa[kk][1] = qa[kk][2] = qa[kk][3] = 0u;
+    RopeLane<HD> rl;
+    rope_lane_load<HD>(rl, a.rope_cos + (size_t)pos * (HD / 2), a.rope_sin + (size_t)pos * (HD / 2), a.rope_mode,
+                       lane);
+    float w[V];  // the q-norm weights of this lane's elements, shared by every head
+    if (a.qn_w) {
+#pragma unroll
+        for (int j = 0; j < V; j++) w[j] = a.qn_w[V * lane + j];
+    }
+    const float* qb = a.q + ((size_t)b * a.hq + (size_t)kvh * G_q) * HD;
+    for (int u0 = 0; u0 < G_q; u0 += 4) {
+        Vec<HD> x[4];
+        bool live[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            live[u] = u0 + u < G_q;
+            if (live[u]) vec_load<HD>(x[u], qb, (size_t)(u0 + u) * HD, PICOATTN_DTYPE_F32, lane);
+            else
+#pragma unroll
+                for (int j = 0; j < V; j++) x[u].x[j] = 0.f;
+        }
+        if (a.qn_w) vec_rmsnorm4<HD>(x, w, live, a.eps, sq, lane);
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            if (live[u]) {
+                vec_rope<HD>(x[u], rl, a.rope_mode, lane);
+                vec_store_f32<HD>(x[u], sq + u * HD, lane);
+            }
+        }
+        __syncwarp();
+        const int ra = gid - u0, rb = gid + 8 - u0;  // staging rows of this lane's two fragment rows
+        const bool ha = ra >= 0 && ra < 4 && gid < G_q, hb = rb >= 0 && rb < 4 && gid + 8 < G_q;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; kk++) {
+            const int c0 = kk * 16 + 2 * tig, c1 = c0 + 8;
+            if (ha) {
+                qa[kk][0] = pack_half2(sq[ra * HD + c0] * qscale, sq[ra * HD + c0 + 1] * qscale);
+                qa[kk][2] = pack_half2(sq[ra * HD + c1] * qscale, sq[ra * HD + c1 + 1] * qscale);
+            }
+            if (hb) {
+                qa[kk][1] = pack_half2(sq[rb * HD + c0] * qscale, sq[rb * HD + c0 + 1] * qscale);
+                qa[kk][3] = pack_half2(sq[rb * HD + c1] * qscale, sq[rb * HD + c1 + 1] * qscale);
+            }
+        }
+        __syncwarp();  // sq is reused
+    }
+}
+
+// The same A operand from the q rows the prep kernel rotated (workspace q_rot).
+template <int HD>
+__device__ __forceinline__ void q_from_rot(const DecodeArgs& a, int b, int kvh, int lane, uint32_t (&qa)[HD / 16][4]) {
+    const int G_q = a.g, gid = lane >> 2, tig = lane & 3;
+    const float qscale = 1.4426950408889634f / sqrtf((float)HD);
+    const float* qb = a.q_rot + ((size_t)b * a.hq + (size_t)kvh * G_q) * HD;
+    const bool ra = gid < G_q, rb = gid + 8 < G_q;
+#pragma unroll
+    for (int kk = 0; kk < HD / 16; kk++) {
+        const int c0 = kk * 16 + 2 * tig, c1 = c0 + 8;
+        const float2 v0 = ra ? *reinterpret_cast<const float2*>(qb + gid * HD + c0) : make_float2(0.f, 0.f);
+        const float2 v1 = rb ? *reinterpret_cast<const float2*>(qb + (gid + 8) * HD + c0) : make_float2(0.f, 0.f);
+        const float2 v2 = ra ? *reinterpret_cast<const float2*>(qb + gid * HD + c1) : make_float2(0.f, 0.f);
+        const float2 v3 = rb ? *reinterpret_cast<const float2*>(qb + (gid + 8) * HD + c1) : make_float2(0.f, 0.f);
+        qa[kk][0] = pack_half2(v0.x * qscale, v0.y * qscale);
+        qa[kk][1] = pack_half2(v1.x * qscale, v1.y * qscale);
+        qa[kk][2] = pack_half2(v2.x * qscale, v2.y * qscale);
+        qa[kk][3] = pack_half2(v3.x * qscale, v3.y * qscale);
+    }
+}
+
+// The new k/v row of KV head kvh for one sequence at position pos: QK-RMSNorm
+// and RoPE of k and the reference's fp16 rounding of both, the same helpers and
+// order as the prep kernel, stored at row lrow of the slab's k and v caches.
+template <int HD>
+__device__ __forceinline__ void append_row(const DecodeArgs& a, int pos, int kvh, uint16_t* krow, uint16_t* vrow,
+                                           float* sq, int lane) {
+    constexpr int V = HD / 32;
+    Vec<HD> xk, xv;
+    vec_load<HD>(xk, a.k, (size_t)kvh * HD, PICOATTN_DTYPE_F32, lane);
+    vec_load<HD>(xv, a.v, (size_t)kvh * HD, PICOATTN_DTYPE_F32, lane);
+    RopeLane<HD> rl;
+    rope_lane_load<HD>(rl, a.rope_cos + (size_t)pos * (HD / 2), a.rope_sin + (size_t)pos * (HD / 2), a.rope_mode,
+                       lane);
+    if (a.kn_w) {
+        float w[V];
+#pragma unroll
+        for (int j = 0; j < V; j++) w[j] = a.kn_w[V * lane + j];
+        vec_rmsnorm<HD>(xk, w, a.eps, sq, lane);
+    }
+    vec_rope<HD>(xk, rl, a.rope_mode, lane);
+    vec_store_ref16<HD>(xk, krow + (size_t)kvh * HD, lane);
+    vec_store_ref16<HD>(xv, vrow + (size_t)kvh * HD, lane);
+}
+
+// Dynamic shared memory of the attention kernel: a 128-byte header (stage
+// barriers <= 48 B, then the single-sequence prefix, position, cache bases and
+// the new-row barrier), the compute warps' q staging areas, the K/V tile stages.
+constexpr int kAttnHdrBytes = 128;
+constexpr int kAttnMaxSmem = 227 * 1024;
+__host__ __device__ constexpr int attn_qstage_bytes(int compute_warps, int hd) { return compute_warps * 4 * hd * 4; }
 
 template <int HD>
 __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
@@ -192,34 +463,76 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int NW = a.compute_warps, W = a.warps_per_head, T = a.tile_rows;
     const int G = gridDim.x, cta = blockIdx.x;
-    const long long R = a.prefix[a.n_seqs];
-    const long long R0 = slice_start(cta, R, G), R1 = slice_start(cta + 1, R, G);
-    if (R0 >= R1) return;
-
+    // The merge kernel may launch now: it waits for this grid to complete.
+    pdl_trigger();
     const uint32_t row_bytes = (uint32_t)a.kvd * 2u;
     const uint32_t stride = row_bytes + 16u;  // padded rows: ldmatrix is conflict-free
     const uint32_t tile_bytes = (uint32_t)T * stride;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + a.stages;
-    uint8_t* tiles = smem + 128;
+    long long* s_prefix = reinterpret_cast<long long*>(smem + 48);
+    int* s_pos = reinterpret_cast<int*>(smem + 64);
+    uint16_t** s_base = reinterpret_cast<uint16_t**>(smem + 72);
+    uint64_t* row_ready = reinterpret_cast<uint64_t*>(smem + 88);  // fused append: the new row is in memory
+    float* qstage = reinterpret_cast<float*>(smem + kAttnHdrBytes);
+    uint8_t* tiles = smem + kAttnHdrBytes + attn_qstage_bytes(NW, HD);
     const size_t slab = (size_t)a.layer * a.local_rows * a.kvd;
 
+    // Programmatic dependent launch: this kernel may start while the kernels
+    // before it still run.  With one sequence its attended rows follow from the
+    // position alone, so the CTAs lay out their slices, stream the cache rows
+    // that are already final and rotate q at once.  The new k/v row comes from
+    // the prep kernel (waited for before the tile that holds it) or, when all
+    // stages run in one call (fused_append), from this kernel: the CTA whose
+    // slice holds it computes and stores it first, and its producer waits for
+    // those stores.  Results are written only after pdl_wait(), since the kernel
+    // before may still read the partial slots.  With several sequences the CTAs
+    // wait for the prep kernel's row prefix sums first.  Every CTA waits before
+    // it exits, so this grid completes after the kernels before it.
+    const long long* prefix = a.prefix;
+    if (a.n_seqs == 1) {
+        if (threadIdx.x == 0) {
+            const int p = seq_pos(a, 0);
+            s_pos[0] = p;
+            s_prefix[0] = 0;
+            s_prefix[1] = pos_ok(a, p) ? local_len(a, p) : 0;
+            if (a.fused_append && !pos_ok(a, p) && cta == 0) atomicOr(a.status, PICOATTN_DEV_BAD_POS);
+        } else if (threadIdx.x == 32) {  // the cache bases, loaded alongside the position
+            s_base[0] = seq_kcache(a, 0);
+            s_base[1] = seq_vcache(a, 0);
+        }
+        prefix = s_prefix;
+    } else {
+        pdl_wait();
+    }
     if (threadIdx.x == 0) {
         for (int s = 0; s < a.stages; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], (uint32_t)NW);
         }
+        mbar_init(row_ready, (uint32_t)a.hkv);  // one writer warp per KV head
         fence_mbar_init();
     }
     __syncthreads();
+    const long long R = prefix[a.n_seqs];
+    const long long R0 = slice_start(cta, R, G), R1 = slice_start(cta + 1, R, G);
+    if (R0 >= R1) {
+        pdl_wait();
+        return;
+    }
+    // fused append: the new row (local row R-1 when it lies in this slab) is in
+    // this CTA's slice
+    const int new_lrow = a.fused_append ? s_pos[0] - a.row_offset : -1;
+    const bool has_new = a.fused_append && new_lrow >= 0 && new_lrow < a.local_rows && new_lrow == R - 1 &&
+                         R0 <= new_lrow && new_lrow < R1;
 
     if (warp == NW) {
         // ---------------- producer: TMA bulk copies of whole cache rows --------
         int t = 0;  // tile counter across segments
-        bool ok = true;
-        for_each_segment(a, R0, R1, [&](int b, int r0, int r1, bool) {
-            const uint16_t* kslab = seq_kcache(a, b) + slab;
-            const uint16_t* vslab = seq_vcache(a, b) + slab;
+        bool ok = true, dep_done = a.n_seqs > 1;
+        for_each_segment(a, prefix, R0, R1, [&](int b, int r0, int r1, bool, int seq_rows) {
+            const uint16_t* kslab = (a.n_seqs == 1 ? s_base[0] : seq_kcache(a, b)) + slab;
+            const uint16_t* vslab = (a.n_seqs == 1 ? s_base[1] : seq_vcache(a, b)) + slab;
             if (((uintptr_t)kslab | (uintptr_t)vslab) & 15u) {
                 // flagged; the tiles still arrive (with zero-length copies avoided by
                 // loading nothing and completing the barrier) so consumers stay in step
@@ -233,6 +546,14 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
                 if (kslab == nullptr) {
                     if (lane == 0) mbar_arrive(&full[s]);
                     continue;
+                }
+                if (row0 + T >= r1 && r1 == seq_rows) {  // the tile holds the new row
+                    if (has_new) {
+                        if (ok) ok = mbar_wait(row_ready, 0u, a.status);
+                    } else if (!dep_done && !a.fused_append) {
+                        pdl_wait();
+                        dep_done = true;
+                    }
                 }
                 if (lane == 0) mbar_arrive_expect_tx(&full[s], 2u * (uint32_t)T * row_bytes);
                 __syncwarp();
@@ -254,33 +575,34 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
     const int kvh = warp / W, wi = warp % W;
     const int gid = lane >> 2, tig = lane & 3;
     const int G_q = a.g;
-    const float qscale = 1.4426950408889634f / sqrtf((float)HD);
     const uint32_t k_lane = (uint32_t)((lane & 7) + ((lane >> 4) << 3)) * stride + (uint32_t)(((lane >> 3) & 1) * 16);
     const uint32_t v_lane = (uint32_t)((lane & 7) + (((lane >> 3) & 1) << 3)) * stride + (uint32_t)((lane >> 4) * 16);
     const uint32_t head_off = (uint32_t)kvh * HD * 2u;
     const uint32_t tiles_u32 = smem_u32(tiles);
+    float* sq = qstage + warp * 4 * HD;
     int t = 0;
+    bool dep_done = a.n_seqs > 1;
+    if (has_new && wi == 0) {  // the new row of this warp's KV head, before anything else
+        uint16_t* krow = s_base[0] + slab + (size_t)new_lrow * a.kvd;
+        uint16_t* vrow = s_base[1] + slab + (size_t)new_lrow * a.kvd;
+        append_row<HD>(a, s_pos[0], kvh, krow, vrow, sq, lane);
+        fence_proxy_async_global();  // the producer's bulk copies read these rows
+        __syncwarp();
+        if (lane == 0) mbar_arrive(row_ready);
+    }
 
-    for_each_segment(a, R0, R1, [&](int b, int r0, int r1, bool whole) {
-        // q of the G heads of this KV head as the A operand (rows = heads, padded
-        // to 16 with zeros), pre-scaled by log2(e)/sqrt(hd) so scores come out in
-        // log2 units (the reference divides by sqrtf(hd) and uses expf).
+    for_each_segment(a, prefix, R0, R1, [&](int b, int r0, int r1, bool whole, int) {
         uint32_t qa[HD / 16][4];
-        {
-            const float* qb = a.q_rot + ((size_t)b * a.hq + (size_t)kvh * G_q) * HD;
-            const bool ra = gid < G_q, rb = gid + 8 < G_q;
-#pragma unroll
-            for (int kk = 0; kk < HD / 16; kk++) {
-                const int c0 = kk * 16 + 2 * tig, c1 = c0 + 8;
-                float2 v0 = ra ? *reinterpret_cast<const float2*>(qb + gid * HD + c0) : make_float2(0.f, 0.f);
-                float2 v1 = rb ? *reinterpret_cast<const float2*>(qb + (gid + 8) * HD + c0) : make_float2(0.f, 0.f);
-                float2 v2 = ra ? *reinterpret_cast<const float2*>(qb + gid * HD + c1) : make_float2(0.f, 0.f);
-                float2 v3 = rb ? *reinterpret_cast<const float2*>(qb + (gid + 8) * HD + c1) : make_float2(0.f, 0.f);
-                qa[kk][0] = pack_half2(v0.x * qscale, v0.y * qscale);
-                qa[kk][1] = pack_half2(v1.x * qscale, v1.y * qscale);
-                qa[kk][2] = pack_half2(v2.x * qscale, v2.y * qscale);
-                qa[kk][3] = pack_half2(v3.x * qscale, v3.y * qscale);
+        if (a.fused_append) {
+            q_fragments<HD>(a, b, s_pos[0], kvh, sq, lane, qa);
+        } else {
+            // q rotated by the prep kernel (finished: waited for above or before
+            // the new row's tile, which every slice of one sequence reaches last)
+            if (!dep_done) {
+                pdl_wait();
+                dep_done = true;
             }
+            q_from_rot<HD>(a, b, kvh, lane, qa);
         }
         float m[2] = {-1e30f, -1e30f}, l[2] = {0.f, 0.f};
         float o[HD / 8][4];
@@ -357,7 +679,12 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
         }
 
         // flush this segment: normalised output if the CTA saw the whole
-        // sequence (and one warp per head), else the (max, sum, acc) partial
+        // sequence (and one warp per head), else the (max, sum, acc) partial.
+        // The kernel before may still read the partial slots and outputs.
+        if (!dep_done) {
+            pdl_wait();
+            dep_done = true;
+        }
         l[0] += __shfl_xor_sync(0xffffffffu, l[0], 1);
         l[0] += __shfl_xor_sync(0xffffffffu, l[0], 2);
         l[1] += __shfl_xor_sync(0xffffffffu, l[1], 1);
@@ -392,137 +719,76 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
     });
 }
 
-// ---------------------------------------------------------------------------
-// merge: out = sum_p 2^(m_p - M) acc_p / sum_p 2^(m_p - M) l_p over the pieces
-// ---------------------------------------------------------------------------
-
-// Merges the partial (max, sum, acc) pieces of one (head, sequence) into its
-// output; block z handles head-dim columns [z*DS, z*DS+DS), so that few long
-// sequences still spread over many blocks.
-template <int HD, int DS>
-__global__ void __launch_bounds__(256) decode_merge_kernel(DecodeArgs a, int G) {
-    // 256 threads: column d = z*DS + tid % DS, piece group = tid / DS; every group
-    // sums its pieces with 4 independent accumulators so many loads are in flight
-    constexpr int NT = 256, NG = NT / DS;
-    __shared__ float w_s[2048];
-    __shared__ float red[NT / 32];
-    __shared__ float bc[2];
-    __shared__ float part[NG][DS];
-    const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int dl = tid % DS, grp = tid / DS, d = blockIdx.z * DS + dl;
-    const bool lse_writer = blockIdx.z == 0 && dl == 0;
-    const size_t row_stride = a.shard_out ? (size_t)(HD + 2) : (size_t)HD;
-    float* dst = (a.shard_out ? a.shard_out : a.out) + ((size_t)b * a.hq + h) * row_stride + d;
-    const int pos = seq_pos(a, b);
-    if (!pos_ok(a, pos)) {
-        if (grp == 0) {
-            *dst = __int_as_float(0x7fc00000);
-            if (a.shard_out && lse_writer) dst[HD - d] = __int_as_float(0x7fc00000);
-        }
-        return;
-    }
-    const long long R = a.prefix[a.n_seqs];
-    const long long p0 = a.prefix[b], p1 = a.prefix[b + 1];
-    if (p0 == p1) {  // no rows of this sequence in this shard: empty partial
-        if (grp == 0) {
-            *dst = 0.f;
-            if (lse_writer) dst[HD] = -INFINITY;
-        }
-        return;
-    }
-    const int i_lo = cta_of_row(p0, R, G), i_hi = cta_of_row(p1 - 1, R, G);
-    const int W = a.warps_per_head;
-    if (i_lo == i_hi && W == 1) return;  // written directly by the attention kernel
-    const int n_pieces = (i_hi - i_lo + 1) * W;  // <= 2048 (checked on the host)
-    // piece k -> (cta i_lo + k/W, warp k%W); skipped if that CTA's slice is empty
-    auto piece = [&](int k) -> size_t { return ((size_t)(i_lo + k / W + b) * W + k % W) * a.hq + h; };
-    float mloc = -INFINITY;
-    for (int k = tid; k < n_pieces; k += NT) {
-        const int i = i_lo + k / W;
-        float m = -INFINITY;
-        if (slice_start(i, R, G) < slice_start(i + 1, R, G)) m = a.part_ml[piece(k) * 2];
-        w_s[k] = m;
-        mloc = fmaxf(mloc, m);
-    }
-    for (int o = 16; o; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
-    if (lane == 0) red[warp] = mloc;
-    __syncthreads();
-    if (tid == 0) {
-        float M = red[0];
-        for (int w = 1; w < NT / 32; w++) M = fmaxf(M, red[w]);
-        bc[0] = M;
-    }
-    __syncthreads();
-    const float M = bc[0];
-    float lloc = 0.f;
-    for (int k = tid; k < n_pieces; k += NT) {
-        float wgt = 0.f;
-        if (w_s[k] != -INFINITY) {
-            wgt = ex2(w_s[k] - M);
-            lloc += wgt * a.part_ml[piece(k) * 2 + 1];
-        }
-        w_s[k] = wgt;
-    }
-    for (int o = 16; o; o >>= 1) lloc += __shfl_xor_sync(0xffffffffu, lloc, o);
-    __syncthreads();
-    if (lane == 0) red[warp] = lloc;
-    __syncthreads();
-    if (tid == 0) {
-        float L = 0.f;
-        for (int w = 0; w < NT / 32; w++) L += red[w];
-        bc[1] = L;
-    }
-    __syncthreads();
-    // 8 independent accumulators: 8 loads of each thread in flight at once
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    int k = grp;
-    for (; k + 7 * NG < n_pieces; k += 8 * NG) {
-#pragma unroll
-        for (int u = 0; u < 8; u++) {
-            const float wgt = w_s[k + u * NG];
-            if (wgt != 0.f) acc[u] += wgt * a.part_o[piece(k + u * NG) * HD + d];
-        }
-    }
-    for (; k < n_pieces; k += NG) {
-        const float wgt = w_s[k];
-        if (wgt != 0.f) acc[0] += wgt * a.part_o[piece(k) * HD + d];
-    }
-    part[grp][dl] = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
-    __syncthreads();
-    if (grp == 0) {
-        float o = part[0][dl];
-#pragma unroll
-        for (int g2 = 1; g2 < NG; g2++) o += part[g2][dl];
-        *dst = o / bc[1];
-        if (a.shard_out && lse_writer) dst[HD] = M + __log2f(bc[1]);
-    }
+// Launch with programmatic stream serialisation: the kernel may start while the
+// one before it in the stream finishes (see pdl_wait / pdl_trigger).
+template <typename... P, typename... A>
+cudaError_t launch_pdl(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, A&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...);
 }
 
 template <int HD>
-cudaError_t launch_decode_hd(const DecodeArgs& a, const DecodePlan& plan, cudaStream_t stream, unsigned stages) {
+cudaError_t launch_decode_hd(const DecodeArgs& a_in, const DecodePlan& plan, cudaStream_t stream, unsigned stages) {
     static bool attr_done = false;
     if (!attr_done) {
+        // The small kernels ask for the largest shared-memory carveout, so that an
+        // attention CTA launched early (programmatic dependent launch) fits on an
+        // SM that still runs one of them.
         cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             200 * 1024 + 256);
+                                             kAttnMaxSmem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(decode_prep_kernel<HD>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(decode_merge_kernel<HD, HD>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(decode_merge_kernel<HD, 64>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(decode_merge_kernel<HD, 32>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
         if (e != cudaSuccess) return e;
         attr_done = true;
     }
-    const int n_slots = a.hq + 2 * a.hkv;
-    if (stages & PICOATTN_STAGE_PREPARE)
-        decode_prep_kernel<HD><<<dim3((unsigned)((n_slots + 31) / 32), (unsigned)a.n_seqs + 1), 256, 0, stream>>>(a);
-    if (stages & PICOATTN_STAGE_ATTEND)
-        decode_attn_kernel<HD><<<plan.grid_ctas, (plan.compute_warps + 1) * 32, plan.smem_bytes, stream>>>(a);
-    if (stages & PICOATTN_STAGE_COMBINE) {
-        // one block per (head, sequence) when those fill the GPU twice over, else
-        // each also split into HD/32 column slices
-        if ((long)a.hq * a.n_seqs >= 2L * plan.max_grid)
-            decode_merge_kernel<HD, HD><<<dim3((unsigned)a.hq, (unsigned)a.n_seqs, 1), 256, 0, stream>>>(
-                a, plan.grid_ctas);
+    // One sequence with every stage in this call: the attention kernel appends
+    // the new row itself and the merge derives the rows from the position, so
+    // no prep kernel runs.
+    DecodeArgs a = a_in;
+    a.fused_append = (stages == PICOATTN_STAGE_ALL && a.n_seqs == 1) ? 1 : 0;
+    cudaError_t e = cudaSuccess;
+    if ((stages & PICOATTN_STAGE_PREPARE) && !a.fused_append)
+        e = launch_pdl(decode_prep_kernel<HD>, dim3((unsigned)((a.hq + 2 * a.hkv + 31) / 32), (unsigned)a.n_seqs + 1),
+                       dim3(256), 0, stream, a);
+    if (e == cudaSuccess && (stages & PICOATTN_STAGE_ATTEND))
+        e = launch_pdl(decode_attn_kernel<HD>, dim3((unsigned)plan.grid_ctas), dim3((plan.compute_warps + 1) * 32),
+                       (size_t)plan.smem_bytes, stream, a);
+    if (e == cudaSuccess && (stages & PICOATTN_STAGE_COMBINE)) {
+        // column slices: the narrowest of 32 or 64 columns that keeps the grid
+        // within one block per SM (a block beside each attention CTA of the next
+        // call), else one block per (head, sequence)
+        const long units = (long)a.hq * a.n_seqs;
+        const int sms = plan.max_grid / 2;
+        const dim3 blk(256);
+        if (units * (HD / 32) <= sms)
+            e = launch_pdl(decode_merge_kernel<HD, 32>, dim3((unsigned)a.hq, (unsigned)a.n_seqs, HD / 32), blk, 0,
+                           stream, a, plan.grid_ctas);
+        else if (HD > 64 && units * (HD / 64) <= sms)
+            e = launch_pdl(decode_merge_kernel<HD, 64>, dim3((unsigned)a.hq, (unsigned)a.n_seqs, HD / 64), blk, 0,
+                           stream, a, plan.grid_ctas);
+        else if (units >= 2L * plan.max_grid)
+            e = launch_pdl(decode_merge_kernel<HD, HD>, dim3((unsigned)a.hq, (unsigned)a.n_seqs, 1), blk, 0, stream,
+                           a, plan.grid_ctas);
         else
-            decode_merge_kernel<HD, 32><<<dim3((unsigned)a.hq, (unsigned)a.n_seqs, HD / 32), 256, 0, stream>>>(
-                a, plan.grid_ctas);
+            e = launch_pdl(decode_merge_kernel<HD, 32>, dim3((unsigned)a.hq, (unsigned)a.n_seqs, HD / 32), blk, 0,
+                           stream, a, plan.grid_ctas);
     }
-    return cudaGetLastError();
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace
@@ -552,8 +818,8 @@ bool make_decode_plan(const picoattn_config_t& cfg, int n_seqs, int max_ctx, Dec
     }
     const int stage_bytes = 2 * p.tile_rows * stride;
     p.stages = 3 * stage_bytes <= 200 * 1024 ? 3 : 2;
-    p.smem_bytes = 128 + p.stages * stage_bytes;
-    if (p.smem_bytes > 200 * 1024 + 256) return false;
+    p.smem_bytes = kAttnHdrBytes + attn_qstage_bytes(p.compute_warps, hd) + p.stages * stage_bytes;
+    if (p.smem_bytes > kAttnMaxSmem) return false;
     // Persistent grid: as many CTAs as fit at once (smem-limited), but no more
     // than one per 64 rows of the largest possible workload (a 16K-row shard of
     // one sequence still spreads over every SM).
@@ -564,8 +830,8 @@ bool make_decode_plan(const picoattn_config_t& cfg, int n_seqs, int max_ctx, Dec
     p.grid_ctas = (int)std::max<long long>(1, g);
     p.max_grid = sms * 2;
     // pieces per sequence <= grid_ctas * warps_per_head; the merge kernel holds
-    // them in 2048 shared-memory slots
-    if (p.max_grid * p.warps_per_head > 2048) return false;
+    // them in kMergeMaxPieces shared-memory slots
+    if (p.max_grid * p.warps_per_head > kMergeMaxPieces) return false;
     const size_t slots = (size_t)(p.max_grid + n_seqs) * p.warps_per_head;
     size_t off = kWsHeaderBytes;
     p.ws_prefix = off;

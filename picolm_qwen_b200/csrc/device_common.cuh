@@ -63,6 +63,22 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialisation may start as soon as every CTA of the kernel before it in the
+// stream has called pdl_trigger() (or exited); pdl_wait() returns when that
+// kernel has completed and its memory is visible, and is a no-op without such a
+// dependency.  Every decode kernel calls pdl_wait() in every CTA before it
+// exits, so a kernel completes only after all the kernels before it, and it
+// calls pdl_wait() before touching anything those kernels may still use.  A
+// kernel launched without the attribute (any library or user kernel) starts
+// only after its predecessor completed, so chains begin and end cleanly.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Orders this thread's earlier generic-proxy global writes before later
+// async-proxy (TMA) accesses that another thread issues after synchronising.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

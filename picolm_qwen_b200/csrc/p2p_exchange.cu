@@ -97,6 +97,8 @@ __global__ void __launch_bounds__(128) exchange_combine_kernel(ExchangeArgs a) {
     const size_t rows = (size_t)a.n_seqs * a.hq, row_idx = (size_t)b * a.hq + h;
     __shared__ __align__(16) float s_row[ROW];
     __shared__ uint32_t s_seq;
+    pdl_wait();  // the shard result comes from the kernel before
+    pdl_trigger();
     if (t == 0) {
         const uint32_t c = a.counters[row_idx] + 1;
         a.counters[row_idx] = c;
@@ -254,10 +256,20 @@ int32_t picoattn_decode_splitkv_p2p(const picoattn_config_t* cfg, int32_t layer,
     a.rank = c->rank;
     a.n_seqs = n_seqs;
     a.hq = c->lay.hq;
-    const dim3 grid((unsigned)a.hq, (unsigned)n_seqs);
-    if (c->lay.hd == 64) exchange_combine_kernel<64><<<grid, 64, 0, s>>>(a);
-    else exchange_combine_kernel<128><<<grid, 128, 0, s>>>(a);
-    return cudaGetLastError() == cudaSuccess ? PICOATTN_OK : PICOATTN_ECUDA;
+    // programmatic stream serialisation: the blocks launch while the merge
+    // kernel finishes and wait for it in pdl_wait
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = dim3((unsigned)a.hq, (unsigned)n_seqs);
+    lc.blockDim = dim3((unsigned)c->lay.hd);
+    lc.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    const cudaError_t e = c->lay.hd == 64 ? cudaLaunchKernelEx(&lc, exchange_combine_kernel<64>, a)
+                                          : cudaLaunchKernelEx(&lc, exchange_combine_kernel<128>, a);
+    return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? PICOATTN_OK : PICOATTN_ECUDA;
 }
 
 }  // extern "C"

@@ -61,6 +61,7 @@ struct DecodeArgs {
     float* part_ml;            // [slot][warp][hq][2]  (max, sum) in log2 units; slot = cta + seq
     float* part_o;             // [slot][warp][hq][hd]
     int tile_rows, stages, warps_per_head, compute_warps;
+    int fused_append;          // one sequence, all stages: the attention kernel appends the new k/v row itself
 };
 
 bool make_decode_plan(const picoattn_config_t& cfg, int n_seqs, int max_ctx, DecodePlan* plan);

@@ -98,9 +98,15 @@ __device__ __forceinline__ void vec_rmsnorm(Vec<HD>& v, const float (&w)[HD / 32
 // run the reference's four interleaved lane sums of vector u side by side, lane
 // u folds them and computes vector u's scale, so one summation loop and one
 // divide/sqrt sequence serve four vectors.  sq: 4*HD floats of shared memory.
+// W is float[4][HD/32] (weights per vector) or float[HD/32] (one set for all).
 template <int HD>
-__device__ __forceinline__ void vec_rmsnorm4(Vec<HD> (&v)[4], const float (&w)[4][HD / 32], const bool (&norm)[4],
-                                             float eps, float* sq, int lane) {
+__device__ __forceinline__ float rms_w(const float (&w)[4][HD / 32], int u, int j) { return w[u][j]; }
+template <int HD>
+__device__ __forceinline__ float rms_w(const float (&w)[HD / 32], int, int j) { return w[j]; }
+
+template <int HD, class Wt>
+__device__ __forceinline__ void vec_rmsnorm4(Vec<HD> (&v)[4], const Wt& w, const bool (&norm)[4], float eps,
+                                             float* sq, int lane) {
     constexpr int V = HD / 32;
 #pragma unroll
     for (int u = 0; u < 4; u++)
@@ -124,7 +130,7 @@ __device__ __forceinline__ void vec_rmsnorm4(Vec<HD> (&v)[4], const float (&w)[4
         const float su = __shfl_sync(0xffffffffu, scale, u);
         if (norm[u]) {
 #pragma unroll
-            for (int j = 0; j < V; j++) v[u].x[j] = __fmul_rn(__fmul_rn(v[u].x[j], su), w[u][j]);
+            for (int j = 0; j < V; j++) v[u].x[j] = __fmul_rn(__fmul_rn(v[u].x[j], su), rms_w<HD>(w, u, j));
         }
     }
     __syncwarp();  // sq is reused

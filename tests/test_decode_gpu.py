@@ -245,3 +245,96 @@ def test_decode_is_deterministic(cuda):
     st.decode(0, q, k, v, pos, o2)
     torch.cuda.synchronize()
     assert torch.equal(o1, o2) and torch.isfinite(o1).all()
+
+
+@pytest.mark.parametrize("shape", [(40, 8, 128), (14, 2, 64), (16, 1, 128)])
+def test_single_sequence_short_rows_many_ctas_vs_oracle(cuda, oracle, shape):
+    """One sequence whose 31 rows are fewer than the CTAs sized for max_ctx:
+    most slices are empty, the attention kernel appends the new row itself and
+    the merge derives the rows from the position."""
+    from picolm_qwen_b200 import abi
+    hq, hkv, hd = shape
+    n, S = 31, 4096
+    kvd = hkv * hd
+    rng = np.random.default_rng(hq + hkv + hd)
+    cfg = abi.Config.make(2, hq, hkv, hd, S, 1e6)
+    st = make_state(cfg, n_seqs=1, max_ctx=S)
+    kc = np.zeros((S, kvd), np.uint16)
+    vc = np.zeros((S, kvd), np.uint16)
+    kc[:n - 1], vc[:n - 1] = random_cache_rows(oracle, rng, n - 1, kvd)
+    st.k_cache[0, 1] = dev(kc.view(np.int16))
+    st.v_cache[0, 1] = dev(vc.view(np.int16))
+    q = rng.standard_normal((1, hq * hd)).astype(np.float32)
+    k = rng.standard_normal((1, kvd)).astype(np.float32)
+    v = rng.standard_normal((1, kvd)).astype(np.float32)
+    cos_t, sin_t = oracle.rope_table(S, hd, 1e6)
+    pos = np.array([n - 1], np.int32)
+    ref = oracle.decode_batch(hq, hkv, hd, 0, q, k, v, None, None, cos_t, sin_t, [kc], [vc], pos, n_threads=1)
+    out = torch.empty((1, hq * hd), dtype=torch.float32, device="cuda")
+    st.decode(1, dev(q), dev(k), dev(v), dev(pos), out, max_ctx=S)
+    torch.cuda.synchronize()
+    assert st.status() == 0
+    assert_close(out.cpu().numpy()[0], ref[0], f"{shape}")
+    _, krot = oracle.rope(0, np.zeros(hq * hd, np.float32), k[0], hd, hq, hkv, cos_t[n - 1], sin_t[n - 1])
+    assert np.array_equal(st.k_cache[0, 1, n - 1].cpu().numpy().view(np.uint16), oracle.f32_to_f16(krot))
+    assert np.array_equal(st.v_cache[0, 1, n - 1].cpu().numpy().view(np.uint16), oracle.f32_to_f16(v[0]))
+
+
+def test_single_sequence_layer_chain_graph_replay(cuda):
+    """Consecutive single-sequence calls over several layers, captured in one
+    CUDA graph and replayed: each launch may start while the one before it
+    finishes (programmatic dependent launch); replays give the eager results
+    bit for bit."""
+    from picolm_qwen_b200 import abi
+    hq, hkv, hd, L, S = 40, 8, 128, 4, 20000
+    cfg = abi.Config.make(L, hq, hkv, hd, S, 1e6)
+    st = make_state(cfg, n_seqs=1, max_ctx=S)
+    st.k_cache.random_(-20000, 20000)
+    st.v_cache.random_(-20000, 20000)
+    st.k_cache &= 0x3bff
+    st.v_cache &= 0x3bff
+    q = torch.randn(L, 1, hq * hd, device="cuda")
+    k = torch.randn(L, 1, hkv * hd, device="cuda")
+    v = torch.randn(L, 1, hkv * hd, device="cuda")
+    pos = torch.tensor([S - 1], dtype=torch.int32, device="cuda")
+    eager = torch.empty(L, 1, hq * hd, device="cuda")
+    for l in range(L):
+        st.decode(l, q[l], k[l], v[l], pos, eager[l])
+    torch.cuda.synchronize()
+    assert st.status() == 0
+    out = torch.zeros_like(eager)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        st.decode(0, q[0], k[0], v[0], pos, out[0], stream=s)  # warm-up on the capture stream
+        s.synchronize()
+        with torch.cuda.graph(g, stream=s):
+            for l in range(L):
+                st.decode(l, q[l], k[l], v[l], pos, out[l], stream=s)
+    for _ in range(3):
+        out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, eager)
+    assert st.status() == 0
+    del g
+
+
+def test_single_sequence_bad_position_is_flagged(cuda):
+    from picolm_qwen_b200 import abi
+    cfg = abi.Config.make(1, 40, 8, 128, 1024, 1e6)
+    st = make_state(cfg, n_seqs=1, max_ctx=1024)
+    q = torch.randn(1, 40 * 128, device="cuda")
+    k = torch.randn(1, 1024, device="cuda")
+    v = torch.randn(1, 1024, device="cuda")
+    out = torch.zeros(1, 40 * 128, device="cuda")
+    st.decode(0, q, k, v, torch.tensor([-3], dtype=torch.int32, device="cuda"), out)
+    torch.cuda.synchronize()
+    assert st.status() & abi.DEV_BAD_POS
+    assert np.isnan(out.cpu().numpy()).all()
+    assert int(st.k_cache.abs().sum()) == 0
+    # the workspace stays usable
+    st.decode(0, q, k, v, torch.tensor([100], dtype=torch.int32, device="cuda"), out)
+    torch.cuda.synchronize()
+    assert st.status() == 0 and torch.isfinite(out).all()
