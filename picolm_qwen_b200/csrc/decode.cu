@@ -187,6 +187,101 @@ __global__ void __launch_bounds__(256) decode_prep_kernel(DecodeArgs a) {
 // Shared memory: m_s, l_s [kMergeMaxPieces], red [NT/32].
 constexpr int kMergeMaxPieces = 1280;
 
+// One exchange word: a value and the call's sequence number in one 8-byte
+// store (single-copy atomic), so the reader needs no fence.
+__device__ __forceinline__ void st_word(uint64_t* p, float v, uint32_t seq) {
+    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(seq) : "memory");
+}
+
+__device__ __forceinline__ void ld_word(const uint64_t* p, float& v, uint32_t& seq) {
+    uint32_t a, b;
+    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(a), "=r"(b) : "l"(p) : "memory");
+    v = __uint_as_float(a);
+    seq = b;
+}
+
+// Waits (bounded) for the word at p to carry sequence number seq; its value.
+__device__ __forceinline__ float wait_word(const uint64_t* p, uint32_t seq, unsigned int* status) {
+    float v;
+    uint32_t s;
+    ld_word(p, v, s);
+    if (s == seq) return v;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t it = 0;; ++it) {
+        ld_word(p, v, s);
+        if (s == seq) return v;
+        if ((it & 255u) == 255u) {
+            if (*reinterpret_cast<volatile unsigned int*>(status) & PICOATTN_DEV_TIMEOUT) return __int_as_float(0x7fc00000);
+            if (global_timer_ns() - t0 > 2000000000ull) {
+                atomicOr(status, PICOATTN_DEV_TIMEOUT);
+                return __int_as_float(0x7fc00000);
+            }
+        }
+    }
+}
+
+// Exchange of one (head, 32-column slice) of the shard result with the other
+// ranks, by the threads of the merge block.  res (held by the threads with
+// holder set, column col) and lse are this rank's values.  Per call the block
+// bumps its slice counter to seq (every rank makes the same calls, so the
+// counters advance in lockstep) and stores its slice row, as (value, seq)
+// words, into slot [seq % 2][rank][slice] of every rank's area; each holder
+// then waits (bounded) for its column's and the log2-sum-exp words of every
+// rank in its own area and combines them:
+//   out = sum_r 2^(lse_r - Lm) o_r / sum_r 2^(lse_r - Lm),  Lm = max_r lse_r,
+// skipping ranks without rows of the sequence (lse_r = -inf), as
+// picoattn_combine_shards does.  Parity double-buffering makes slot reuse
+// safe: a rank writes call n+2 into a slot only after its call n+1 saw every
+// rank's call n+1 words, written after that rank finished reading call n.
+// sbuf: kXchgWords floats of shared memory.
+template <int HD, class Sync>
+__device__ __forceinline__ void exchange_slice(const DecodeArgs& a, int b, int h, int z, float res, float lse,
+                                               bool holder, int col, float* sbuf, uint32_t* s_seq, int tid,
+                                               Sync sync) {
+    const XchgArgs& x = a.x;
+    constexpr int NS = HD / kXchgCols;
+    const size_t rows = (size_t)a.n_seqs * a.hq * NS, idx = ((size_t)b * a.hq + h) * NS + z;
+    if (tid == 0) {
+        uint32_t* ctr = reinterpret_cast<uint32_t*>(x.peers[x.rank] + x.counters) + idx;
+        const uint32_t c = *ctr + 1;
+        *ctr = c;
+        *s_seq = c;
+        sbuf[kXchgCols] = lse;
+    }
+    if (holder) sbuf[col] = res;
+    sync();
+    const uint32_t seq = *s_seq, par = seq & 1u;
+    const size_t my_slot = ((size_t)par * x.n_ranks + x.rank) * rows + idx;
+    constexpr int NW = kXchgCols + 1;  // words carrying data
+    for (int i = tid; i < NW * x.n_ranks; i += blockDim.x)
+        st_word(reinterpret_cast<uint64_t*>(x.peers[i / NW] + x.slots) + my_slot * kXchgWords + i % NW, sbuf[i % NW],
+                seq);
+    if (holder) {
+        const uint64_t* base = reinterpret_cast<const uint64_t*>(x.peers[x.rank] + x.slots);
+        auto src = [&](int r) { return base + (((size_t)par * x.n_ranks + r) * rows + idx) * kXchgWords; };
+        float lr[8], o[8];  // n_ranks <= 8
+        float Lm = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < 8; r++) {
+            if (r < x.n_ranks) {
+                lr[r] = wait_word(src(r) + kXchgCols, seq, a.status);
+                o[r] = wait_word(src(r) + col, seq, a.status);
+                Lm = fmaxf(Lm, lr[r]);
+            }
+        }
+        float L = 0.f, acc = 0.f;
+#pragma unroll
+        for (int r = 0; r < 8; r++) {
+            if (r < x.n_ranks && lr[r] != -INFINITY) {  // skip a rank without rows of this sequence
+                const float w = ex2(lr[r] - Lm);
+                L += w;
+                acc += w * o[r];
+            }
+        }
+        x.out[((size_t)b * a.hq + h) * HD + z * kXchgCols + col] = acc / L;
+    }
+}
+
 template <int HD, int DS, int NT, int RPT, class Sync>
 __device__ __forceinline__ void merge_slice(const DecodeArgs& a, int G, int b, int h, int z, float* m_s, float* l_s,
                                             float* red, int tid, Sync sync) {
@@ -197,6 +292,9 @@ __device__ __forceinline__ void merge_slice(const DecodeArgs& a, int G, int b, i
     const size_t row_stride = a.shard_out ? (size_t)(HD + 2) : (size_t)HD;
     float* dst = (a.shard_out ? a.shard_out : a.out) + ((size_t)b * a.hq + h) * row_stride + z * DS;
     const bool lse_writer = z == 0 && tid == 0;
+    // exchanging with the other ranks (32-column slices only): every block takes part
+    const bool xchg = DS == kXchgCols && a.x.peers != nullptr;
+    const int col = tid / TPC, j = tid % TPC;  // output column of this thread (holder: j == 0)
     const int pos = seq_pos(a, b);
     long long R, p0, p1;
     if (a.n_seqs == 1) {  // the attended rows follow from the position (no prefix pass may have run)
@@ -205,94 +303,215 @@ __device__ __forceinline__ void merge_slice(const DecodeArgs& a, int G, int b, i
     } else {
         R = a.prefix[a.n_seqs], p0 = a.prefix[b], p1 = a.prefix[b + 1];
     }
-    if (!pos_ok(a, pos)) {
-        if (tid < DS) dst[tid] = __int_as_float(0x7fc00000);
-        if (a.shard_out && lse_writer) dst[HD] = __int_as_float(0x7fc00000);
-        return;
-    }
-    if (p0 == p1) {  // no rows of this sequence in this shard: empty partial
-        if (tid < DS) dst[tid] = 0.f;
-        if (a.shard_out && lse_writer) dst[HD] = -INFINITY;
-        return;
-    }
-    // the CTAs whose slices hold this sequence's rows (the last row is always in
-    // CTA G-1's slice; a sequence starting at row 0 starts in CTA 0's, which may
-    // be empty when R < G: such pieces are skipped)
-    const int i_lo = p0 == 0 ? 0 : cta_of_row(p0, R, G);
-    const int i_hi = p1 == R ? G - 1 : cta_of_row(p1 - 1, R, G);
-    const int W = a.warps_per_head, lw = __ffs(W) - 1;  // W is 1, 2, 4 or 8
-    if (i_lo == i_hi && W == 1) return;  // written directly by the attention kernel
-    const int n_pieces = (i_hi - i_lo + 1) * W;  // <= kMergeMaxPieces (checked on the host)
-    // piece k = (CTA i_lo + k/W, warp k%W) -> slot (cta + seq, warp), head h
-    auto slot_of = [&](int k) -> uint32_t {
-        return (uint32_t)((((i_lo + (k >> lw) + b) << lw) | (k & (W - 1))) * a.hq + h);
-    };
-    for (int k = tid; k < n_pieces; k += NT) {
-        const int i = i_lo + (k >> lw);
-        float2 ml = make_float2(-INFINITY, 0.f);
-        if (R >= G || slice_start(i, R, G) < slice_start(i + 1, R, G))
-            ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml + (size_t)slot_of(k) * 2));
-        m_s[k] = ml.x;
-        l_s[k] = ml.y;
-    }
-    const int c4 = tid % C4, grp = tid / C4;
-    const float* po = a.part_o + z * DS + c4 * 4;
-    float4 ov[RPT];
+    float res, lse;  // this block's column value (holders) and log2-sum-exp
+    if (!pos_ok(a, pos) || p0 == p1) {
+        // a rejected position: NaN; no rows of this sequence in this shard: an empty partial
+        res = pos_ok(a, pos) ? 0.f : __int_as_float(0x7fc00000);
+        lse = pos_ok(a, pos) ? -INFINITY : __int_as_float(0x7fc00000);
+    } else {
+        // the CTAs whose slices hold this sequence's rows (the last row is always in
+        // CTA G-1's slice; a sequence starting at row 0 starts in CTA 0's, which may
+        // be empty when R < G: such pieces are skipped)
+        const int i_lo = p0 == 0 ? 0 : cta_of_row(p0, R, G);
+        const int i_hi = p1 == R ? G - 1 : cta_of_row(p1 - 1, R, G);
+        const int W = a.warps_per_head, lw = __ffs(W) - 1;  // W is 1, 2, 4 or 8
+        if (i_lo == i_hi && W == 1 && !xchg) return;  // written directly by the attention kernel
+        const int n_pieces = (i_hi - i_lo + 1) * W;  // <= kMergeMaxPieces (checked on the host)
+        // piece k = (CTA i_lo + k/W, warp k%W) -> slot (cta + seq, warp), head h
+        auto slot_of = [&](int k) -> uint32_t {
+            return (uint32_t)((((i_lo + (k >> lw) + b) << lw) | (k & (W - 1))) * a.hq + h);
+        };
+        for (int k = tid; k < n_pieces; k += NT) {
+            const int i = i_lo + (k >> lw);
+            float2 ml = make_float2(-INFINITY, 0.f);
+            if (R >= G || slice_start(i, R, G) < slice_start(i + 1, R, G))
+                ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml + (size_t)slot_of(k) * 2));
+            m_s[k] = ml.x;
+            l_s[k] = ml.y;
+        }
+        const int c4 = tid % C4, grp = tid / C4;
+        const float* po = a.part_o + z * DS + c4 * 4;
+        float4 ov[RPT];
 #pragma unroll
-    for (int u = 0; u < RPT; u++) {
-        const int k = grp + u * NG;
-        ov[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (k < n_pieces) ov[u] = __ldcg(reinterpret_cast<const float4*>(po + (size_t)slot_of(k) * HD));
-    }
-    sync();
-    float mloc = -INFINITY;
-    for (int k = tid; k < n_pieces; k += NT) mloc = fmaxf(mloc, m_s[k]);
-    for (int o = 16; o; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
-    if (lane == 0) red[warp] = mloc;
-    sync();
-    float M = red[0];
+        for (int u = 0; u < RPT; u++) {
+            const int k = grp + u * NG;
+            ov[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (k < n_pieces) ov[u] = __ldcg(reinterpret_cast<const float4*>(po + (size_t)slot_of(k) * HD));
+        }
+        sync();
+        float mloc = -INFINITY;
+        for (int k = tid; k < n_pieces; k += NT) mloc = fmaxf(mloc, m_s[k]);
+        for (int o = 16; o; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
+        if (lane == 0) red[warp] = mloc;
+        sync();
+        float M = red[0];
 #pragma unroll
-    for (int w = 1; w < NT / 32; w++) M = fmaxf(M, red[w]);
-    float lloc = 0.f;
-    for (int k = tid; k < n_pieces; k += NT) {
-        const float m = m_s[k];
-        const float wgt = m == -INFINITY ? 0.f : ex2(m - M);
-        lloc += wgt * l_s[k];
-        m_s[k] = wgt;
-    }
-    for (int o = 16; o; o >>= 1) lloc += __shfl_xor_sync(0xffffffffu, lloc, o);
-    sync();  // every thread has read red[] for M; weights complete; l_s free
-    if (lane == 0) red[warp] = lloc;
-    // weighted acc rows (pieces of weight 0 may hold stale slots: skipped)
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int w = 1; w < NT / 32; w++) M = fmaxf(M, red[w]);
+        float lloc = 0.f;
+        for (int k = tid; k < n_pieces; k += NT) {
+            const float m = m_s[k];
+            const float wgt = m == -INFINITY ? 0.f : ex2(m - M);
+            lloc += wgt * l_s[k];
+            m_s[k] = wgt;
+        }
+        for (int o = 16; o; o >>= 1) lloc += __shfl_xor_sync(0xffffffffu, lloc, o);
+        sync();  // every thread has read red[] for M; weights complete; l_s free
+        if (lane == 0) red[warp] = lloc;
+        // weighted acc rows (pieces of weight 0 may hold stale slots: skipped)
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int u = 0; u < RPT; u++) {
-        const int k = grp + u * NG;
-        const float wgt = k < n_pieces ? m_s[k] : 0.f;
-        if (wgt != 0.f) acc.x += wgt * ov[u].x, acc.y += wgt * ov[u].y, acc.z += wgt * ov[u].z, acc.w += wgt * ov[u].w;
+        for (int u = 0; u < RPT; u++) {
+            const int k = grp + u * NG;
+            const float wgt = k < n_pieces ? m_s[k] : 0.f;
+            if (wgt != 0.f)
+                acc.x += wgt * ov[u].x, acc.y += wgt * ov[u].y, acc.z += wgt * ov[u].z, acc.w += wgt * ov[u].w;
+        }
+        for (int k = grp + RPT * NG; k < n_pieces; k += NG) {  // beyond RPT rows per thread
+            const float wgt = m_s[k];
+            if (wgt != 0.f) {
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(po + (size_t)slot_of(k) * HD));
+                acc.x += wgt * v.x, acc.y += wgt * v.y, acc.z += wgt * v.z, acc.w += wgt * v.w;
+            }
+        }
+        *reinterpret_cast<float4*>(part + grp * DS + c4 * 4) = acc;
+        sync();
+        float L = 0.f;
+#pragma unroll
+        for (int w = 0; w < NT / 32; w++) L += red[w];
+        // the NG group sums of column col: TPC threads of one warp, NG / TPC each
+        float o = 0.f;
+#pragma unroll
+        for (int g2 = j; g2 < NG; g2 += TPC) o += part[g2 * DS + col];
+#pragma unroll
+        for (int sh = TPC / 2; sh; sh >>= 1) o += __shfl_xor_sync(0xffffffffu, o, sh);
+        res = o / L;
+        lse = M + __log2f(L);
+        sync();  // m_s, l_s and red may be reused
     }
-    for (int k = grp + RPT * NG; k < n_pieces; k += NG) {  // beyond RPT rows per thread
-        const float wgt = m_s[k];
-        if (wgt != 0.f) {
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(po + (size_t)slot_of(k) * HD));
-            acc.x += wgt * v.x, acc.y += wgt * v.y, acc.z += wgt * v.z, acc.w += wgt * v.w;
+    if (xchg) {
+        exchange_slice<HD>(a, b, h, z, res, lse, j == 0, col, m_s, reinterpret_cast<uint32_t*>(red), tid, sync);
+    } else {
+        if (j == 0) dst[col] = res;
+        if (a.shard_out && lse_writer) dst[HD] = lse;
+    }
+}
+
+// Exchange of one (head, 32-column slice) by one warp (lane = column): the
+// same protocol and words as exchange_slice.
+__device__ __forceinline__ float warp_exchange(const DecodeArgs& a, int h, int z, int NS, float res, float lse,
+                                               int lane) {
+    const XchgArgs& x = a.x;
+    const size_t rows = (size_t)a.hq * NS, idx = (size_t)h * NS + z;
+    uint32_t seq = 0;
+    if (lane == 0) {
+        uint32_t* ctr = reinterpret_cast<uint32_t*>(x.peers[x.rank] + x.counters) + idx;
+        seq = *ctr + 1;
+        *ctr = seq;
+    }
+    seq = __shfl_sync(0xffffffffu, seq, 0);
+    const uint32_t par = seq & 1u;
+    const size_t my_slot = ((size_t)par * x.n_ranks + x.rank) * rows + idx;
+    for (int p = 0; p < x.n_ranks; p++) {
+        uint64_t* dst = reinterpret_cast<uint64_t*>(x.peers[p] + x.slots) + my_slot * kXchgWords;
+        st_word(dst + lane, res, seq);
+        if (lane == 0) st_word(dst + kXchgCols, lse, seq);
+    }
+    const uint64_t* base = reinterpret_cast<const uint64_t*>(x.peers[x.rank] + x.slots);
+    float lr[8], o[8];  // n_ranks <= 8
+    float Lm = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < 8; r++) {
+        if (r < x.n_ranks) {
+            const uint64_t* src = base + (((size_t)par * x.n_ranks + r) * rows + idx) * kXchgWords;
+            lr[r] = wait_word(src + kXchgCols, seq, a.status);
+            o[r] = wait_word(src + lane, seq, a.status);
+            Lm = fmaxf(Lm, lr[r]);
         }
     }
-    *reinterpret_cast<float4*>(part + grp * DS + c4 * 4) = acc;
-    sync();
-    float L = 0.f;
+    float L = 0.f, acc = 0.f;
 #pragma unroll
-    for (int w = 0; w < NT / 32; w++) L += red[w];
-    // the NG group sums of column col: TPC threads of one warp, NG / TPC each
-    const int col = tid / TPC, j = tid % TPC;
-    float o = 0.f;
+    for (int r = 0; r < 8; r++) {
+        if (r < x.n_ranks && lr[r] != -INFINITY) {  // skip a rank without rows of this sequence
+            const float w = ex2(lr[r] - Lm);
+            L += w;
+            acc += w * o[r];
+        }
+    }
+    return acc / L;
+}
+
+// Merge for one sequence.  Its attention kernel leaves plan.merge_blocks SMs
+// free (the grid is sized that way), so the blocks of this kernel, launched
+// while that kernel runs, land there, and the next call's attention CTAs take
+// the SMs the attention kernel frees without waiting for this merge.  A warp
+// per (head, 32-column slice), lane = column, folds the G*W pieces in chunks
+// of 32 with a running log2-sum-exp: per chunk one load of (max, sum) per lane
+// and 32 acc loads per lane, all in flight together.  With an exchange the
+// warp then trades its slice with the other ranks (warp_exchange).
+
+template <int HD>
+__global__ void __launch_bounds__(512, 1) decode_merge_seq_kernel(DecodeArgs a, int G) {
+    pdl_trigger();
+    pdl_wait();
+    constexpr int NS = HD / 32;
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int pos = seq_pos(a, 0);
+    const bool ok = pos_ok(a, pos);
+    const long long R = ok ? local_len(a, pos) : 0;
+    const int W = a.warps_per_head, lw = __ffs(W) - 1;  // W is 1, 2, 4 or 8
+    const bool xchg = a.x.peers != nullptr;
+    const size_t row_stride = a.shard_out ? (size_t)(HD + 2) : (size_t)HD;
+    const int n_pieces = G * W;
+    for (int u = blockIdx.x * nwarps + wib; u < a.hq * NS; u += gridDim.x * nwarps) {
+        const int h = u / NS, z = u % NS, col = z * 32 + lane;
+        float res, lse;
+        if (!ok || R == 0) {  // a rejected position: NaN; no rows in this shard: an empty partial
+            res = ok ? 0.f : __int_as_float(0x7fc00000);
+            lse = ok ? -INFINITY : __int_as_float(0x7fc00000);
+        } else {
+            if (G == 1 && W == 1 && !xchg) continue;  // written directly by the attention kernel
+            float M = -INFINITY, L = 0.f, acc = 0.f;
+            for (int k0 = 0; k0 < n_pieces; k0 += 32) {
+                // piece k -> slot (cta k/W, warp k%W) of head h; CTAs with empty slices
+                // (R < G) left nothing
+                const int k = k0 + lane, i = k >> lw;
+                float2 ml = make_float2(-INFINITY, 0.f);
+                if (k < n_pieces && (R >= G || slice_start(i, R, G) < slice_start(i + 1, R, G)))
+                    ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml + ((size_t)k * a.hq + h) * 2));
+                float ov[32];
 #pragma unroll
-    for (int g2 = j; g2 < NG; g2 += TPC) o += part[g2 * DS + col];
+                for (int j = 0; j < 32; j++)
+                    ov[j] = k0 + j < n_pieces ? __ldcg(a.part_o + ((size_t)(k0 + j) * a.hq + h) * HD + col) : 0.f;
+                float cm = ml.x;
+                for (int o = 16; o; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
+                const float Mn = fmaxf(M, cm);
+                if (Mn == -INFINITY) continue;  // nothing yet
+                const float keep = M == -INFINITY ? 0.f : ex2(M - Mn);
+                acc *= keep;
+                L *= keep;
+                const float w = ml.x == -INFINITY ? 0.f : ex2(ml.x - Mn);
+                float lw_sum = w * ml.y;
+                for (int o = 16; o; o >>= 1) lw_sum += __shfl_xor_sync(0xffffffffu, lw_sum, o);
+                L += lw_sum;
 #pragma unroll
-    for (int sh = TPC / 2; sh; sh >>= 1) o += __shfl_xor_sync(0xffffffffu, o, sh);
-    if (j == 0) dst[col] = o / L;
-    if (a.shard_out && lse_writer) dst[HD] = M + __log2f(L);
-    sync();  // m_s, l_s and red may be reused
+                for (int j = 0; j < 32; j++) {
+                    const float wj = __shfl_sync(0xffffffffu, w, j);
+                    if (wj != 0.f) acc += wj * ov[j];  // pieces of weight 0 may hold stale slots
+                }
+                M = Mn;
+            }
+            res = acc / L;
+            lse = M + __log2f(L);
+        }
+        if (xchg) {
+            const float v = warp_exchange(a, h, z, NS, res, lse, lane);
+            a.x.out[(size_t)h * HD + col] = v;
+        } else {
+            float* dst = (a.shard_out ? a.shard_out : a.out) + (size_t)h * row_stride;
+            dst[col] = res;
+            if (a.shard_out && z == 0 && lane == 0) dst[HD] = lse;
+        }
+    }
 }
 
 // RPT: acc rows per thread held in registers, enough for one long sequence's
@@ -689,7 +908,7 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
         l[0] += __shfl_xor_sync(0xffffffffu, l[0], 2);
         l[1] += __shfl_xor_sync(0xffffffffu, l[1], 1);
         l[1] += __shfl_xor_sync(0xffffffffu, l[1], 2);
-        const bool direct = whole && W == 1;
+        const bool direct = whole && W == 1 && a.x.peers == nullptr;
         const size_t pbase = ((size_t)(cta + b) * W + wi) * a.hq;
 #pragma unroll
         for (int half = 0; half < 2; half++) {
@@ -753,6 +972,8 @@ cudaError_t launch_decode_hd(const DecodeArgs& a_in, const DecodePlan& plan, cud
             e = cudaFuncSetAttribute(decode_merge_kernel<HD, 64>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(decode_merge_kernel<HD, 32>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(decode_merge_seq_kernel<HD>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
         if (e != cudaSuccess) return e;
         attr_done = true;
     }
@@ -768,14 +989,17 @@ cudaError_t launch_decode_hd(const DecodeArgs& a_in, const DecodePlan& plan, cud
     if (e == cudaSuccess && (stages & PICOATTN_STAGE_ATTEND))
         e = launch_pdl(decode_attn_kernel<HD>, dim3((unsigned)plan.grid_ctas), dim3((plan.compute_warps + 1) * 32),
                        (size_t)plan.smem_bytes, stream, a);
-    if (e == cudaSuccess && (stages & PICOATTN_STAGE_COMBINE)) {
+    if (e == cudaSuccess && (stages & PICOATTN_STAGE_COMBINE) && a.n_seqs == 1) {
+        e = launch_pdl(decode_merge_seq_kernel<HD>, dim3((unsigned)plan.merge_blocks), dim3(512), 0, stream, a,
+                       plan.grid_ctas);
+    } else if (e == cudaSuccess && (stages & PICOATTN_STAGE_COMBINE)) {
         // column slices: the narrowest of 32 or 64 columns that keeps the grid
         // within one block per SM (a block beside each attention CTA of the next
         // call), else one block per (head, sequence)
         const long units = (long)a.hq * a.n_seqs;
         const int sms = plan.max_grid / 2;
         const dim3 blk(256);
-        if (units * (HD / 32) <= sms)
+        if (a.x.peers != nullptr || units * (HD / 32) <= sms)  // the exchange works on 32-column slices
             e = launch_pdl(decode_merge_kernel<HD, 32>, dim3((unsigned)a.hq, (unsigned)a.n_seqs, HD / 32), blk, 0,
                            stream, a, plan.grid_ctas);
         else if (HD > 64 && units * (HD / 64) <= sms)
@@ -822,11 +1046,18 @@ bool make_decode_plan(const picoattn_config_t& cfg, int n_seqs, int max_ctx, Dec
     if (p.smem_bytes > kAttnMaxSmem) return false;
     // Persistent grid: as many CTAs as fit at once (smem-limited), but no more
     // than one per 64 rows of the largest possible workload (a 16K-row shard of
-    // one sequence still spreads over every SM).
+    // one sequence still spreads over the SMs).
     const int sms = device_sm_count();
     const int per_sm = p.smem_bytes <= 113 * 1024 ? 2 : 1;
     const long long work_rows = (long long)n_seqs * max_ctx;
-    long long g = std::min<long long>((long long)sms * per_sm, (work_rows + 63) / 64);
+    // One sequence: some SMs stay free for the merge kernel, which then overlaps
+    // the next call's attention.  A short shard needs the merge done quickly
+    // (16 blocks); a long one gains more from attention bandwidth than it loses
+    // in merge time (measured on B200: 16 blocks best up to 32K rows, 8 at 64K,
+    // 4 at 128K).
+    p.merge_blocks = work_rows <= 40 * 1024 ? 16 : (work_rows <= 80 * 1024 ? 8 : 4);
+    const int attn_sms = n_seqs == 1 ? std::max(1, sms - p.merge_blocks) : sms;
+    long long g = std::min<long long>((long long)attn_sms * per_sm, (work_rows + 63) / 64);
     p.grid_ctas = (int)std::max<long long>(1, g);
     p.max_grid = sms * 2;
     // pieces per sequence <= grid_ctas * warps_per_head; the merge kernel holds

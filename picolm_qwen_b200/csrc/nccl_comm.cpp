@@ -15,11 +15,6 @@
 #include "picoattn_internal.h"
 
 namespace picoattn {
-int32_t decode_shard_impl(const picoattn_config_t* cfg, int32_t layer, int32_t n_seqs, int32_t max_ctx,
-                          int32_t row_offset, int32_t local_rows, const float* q, const float* k, const float* v,
-                          const float* qn, const float* kn, const float* rc, const float* rs,
-                          uint16_t* const* kcp, uint16_t* const* vcp, const int32_t* pos, float* partial, void* ws,
-                          size_t ws_bytes, cudaStream_t stream);
 cudaError_t launch_combine_shards(const float* parts, float* out, int n_seqs, int hq, int hd, int n_shards,
                                   cudaStream_t stream);
 }  // namespace picoattn
@@ -117,7 +112,7 @@ int32_t picoattn_decode_splitkv_nccl(const picoattn_config_t* cfg, int32_t layer
     float* mine = gather + per * c->rank;
     int32_t st = decode_shard_impl(cfg, layer, n_seqs, max_ctx, row_offset, local_rows, q, k, v, q_norm_w, k_norm_w,
                                    rope_cos, rope_sin, k_cache, v_cache, pos, mine, workspace, workspace_bytes,
-                                   (cudaStream_t)stream);
+                                   (cudaStream_t)stream, nullptr);
     if (st != PICOATTN_OK) return st;
     st = settle(c, ncclAllGather(mine, gather, per, ncclFloat, c->comm, (cudaStream_t)stream));
     if (st != PICOATTN_OK) return st;

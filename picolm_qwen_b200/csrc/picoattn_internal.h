@@ -29,9 +29,28 @@ struct DecodePlan {
     int tile_rows;        // rows per pipeline stage (multiple of 16*warps_per_head)
     int stages;           // pipeline depth
     int grid_ctas;        // persistent CTAs of the attention kernel
+    int merge_blocks;     // one sequence: blocks of the merge kernel, on SMs the attention grid leaves free
     int max_grid;         // upper bound on grid_ctas (sizes the partial slots)
     int smem_bytes;       // dynamic shared memory per CTA
     size_t ws_prefix, ws_qrot, ws_ml, ws_o, ws_total;  // workspace offsets and size
+};
+
+// Split-KV decode over the GPUs of one node with the shard results exchanged
+// through peer memory by the merge kernel: each (head, 32-column slice) block
+// stores its slice and log2-sum-exp into every rank's exchange area and
+// combines the ranks' slices from its own.  Every 8-byte word carries a value
+// and the call's sequence number, written with one store, so a reader that
+// sees the number sees the value: no fence or separate flag is needed.
+// Area layout (per rank, offsets below):
+//   slots    [2 parities][n_ranks][n_seqs * hq * hd/32][kXchgWords] u64 words
+//   counters [n_seqs * hq * hd/32] u32   calls so far, this rank only
+constexpr int kXchgCols = 32;
+constexpr int kXchgWords = kXchgCols + 2;  // the slice, its log2-sum-exp, one word of padding
+struct XchgArgs {
+    uint8_t* const* peers;  // [n_ranks] exchange areas (device array), this rank's own included; null: no exchange
+    size_t slots, counters;
+    int rank, n_ranks;
+    float* out;             // [n_seqs][hq][hd] the combined output
 };
 
 struct DecodeArgs {
@@ -62,9 +81,19 @@ struct DecodeArgs {
     float* part_o;             // [slot][warp][hq][hd]
     int tile_rows, stages, warps_per_head, compute_warps;
     int fused_append;          // one sequence, all stages: the attention kernel appends the new k/v row itself
+    XchgArgs x;                // the merge kernel exchanges the shard results (x.peers non-null)
 };
 
 bool make_decode_plan(const picoattn_config_t& cfg, int n_seqs, int max_ctx, DecodePlan* plan);
+
+// Decode over a slab of local cache rows (split-KV shard), all stages; the
+// result goes to partial ([n_seqs][hq][hd+2]: normalised output, log2-sum-exp)
+// or, with x, is exchanged with the other ranks and combined into x->out.
+int32_t decode_shard_impl(const picoattn_config_t* cfg, int32_t layer, int32_t n_seqs, int32_t max_ctx,
+                          int32_t row_offset, int32_t local_rows, const float* q, const float* k, const float* v,
+                          const float* qn, const float* kn, const float* rc, const float* rs,
+                          uint16_t* const* kcp, uint16_t* const* vcp, const int32_t* pos, float* partial, void* ws,
+                          size_t ws_bytes, cudaStream_t stream, const XchgArgs* x);
 cudaError_t launch_decode(const DecodeArgs& a, const DecodePlan& plan, cudaStream_t stream, unsigned stages);
 
 struct PrefillArgs {

@@ -50,7 +50,7 @@ int32_t decode_shard_impl(const picoattn_config_t* cfg, int32_t layer, int32_t n
                           int32_t row_offset, int32_t local_rows, const float* q, const float* k, const float* v,
                           const float* qn, const float* kn, const float* rc, const float* rs,
                           uint16_t* const* kcp, uint16_t* const* vcp, const int32_t* pos, float* partial, void* ws,
-                          size_t ws_bytes, cudaStream_t stream) {
+                          size_t ws_bytes, cudaStream_t stream, const XchgArgs* x) {
     int32_t st = picoattn_config_check(cfg);
     if (st != PICOATTN_OK) return st;
     if (layer < 0 || layer >= cfg->n_layers || n_seqs <= 0) return PICOATTN_EINVAL;
@@ -89,6 +89,7 @@ int32_t decode_shard_impl(const picoattn_config_t* cfg, int32_t layer, int32_t n
     a.row_offset = row_offset;
     a.local_rows = local_rows;
     a.shard_out = partial;
+    if (x) a.x = *x;
     a.tile_rows = plan.tile_rows;
     a.stages = plan.stages;
     a.warps_per_head = plan.warps_per_head;
@@ -115,7 +116,7 @@ int32_t picoattn_decode_shard(const picoattn_config_t* cfg, int32_t layer, int32
                               picoattn_stream_t stream) {
     return decode_shard_impl(cfg, layer, n_seqs, max_ctx, row_offset, local_rows, q, k, v, q_norm_w, k_norm_w,
                              rope_cos, rope_sin, k_cache, v_cache, pos, partial, workspace, workspace_bytes,
-                             (cudaStream_t)stream);
+                             (cudaStream_t)stream, nullptr);
 }
 
 int32_t picoattn_combine_shards(const picoattn_config_t* cfg, int32_t n_seqs, int32_t n_shards,
