@@ -200,24 +200,65 @@ __device__ __forceinline__ void ld_word(const uint64_t* p, float& v, uint32_t& s
     seq = b;
 }
 
-// Waits (bounded) for the word at p to carry sequence number seq; its value.
-__device__ __forceinline__ float wait_word(const uint64_t* p, uint32_t seq, unsigned int* status) {
-    float v;
-    uint32_t s;
-    ld_word(p, v, s);
-    if (s == seq) return v;
-    const uint64_t t0 = global_timer_ns();
+// Waits (bounded) until, for every rank r < n, the words lse_src(r) and
+// o_src(r) carry sequence number seq; their values go to lr[r], o[r].  Each
+// pass loads every missing word at once, so the ranks' words arrive in
+// parallel rather than one round trip after another.  A wait that gives up
+// leaves NaN (and PICOATTN_DEV_TIMEOUT set).
+template <class Src>
+__device__ __forceinline__ void wait_words(int n, Src src, int col, uint32_t seq, float (&lr)[8], float (&o)[8],
+                                           unsigned int* status) {
+    uint32_t done = 0u;
+    const uint32_t all = (1u << n) - 1u;
+    uint64_t t0 = 0;
     for (uint32_t it = 0;; ++it) {
-        ld_word(p, v, s);
-        if (s == seq) return v;
-        if ((it & 255u) == 255u) {
-            if (*reinterpret_cast<volatile unsigned int*>(status) & PICOATTN_DEV_TIMEOUT) return __int_as_float(0x7fc00000);
-            if (global_timer_ns() - t0 > 2000000000ull) {
+#pragma unroll
+        for (int r = 0; r < 8; r++) {
+            if (r < n && !(done & (1u << r))) {
+                float v0, v1;
+                uint32_t s0, s1;
+                ld_word(src(r) + kXchgCols, v0, s0);
+                ld_word(src(r) + col, v1, s1);
+                if (s0 == seq && s1 == seq) {
+                    lr[r] = v0;
+                    o[r] = v1;
+                    done |= 1u << r;
+                }
+            }
+        }
+        if (done == all) return;
+        if ((it & 63u) == 0u) {
+            const uint64_t now = global_timer_ns();
+            if (it == 0u) t0 = now;
+            else if ((*reinterpret_cast<volatile unsigned int*>(status) & PICOATTN_DEV_TIMEOUT) ||
+                     now - t0 > 2000000000ull) {
                 atomicOr(status, PICOATTN_DEV_TIMEOUT);
-                return __int_as_float(0x7fc00000);
+#pragma unroll
+                for (int r = 0; r < 8; r++)
+                    if (r < n && !(done & (1u << r))) lr[r] = o[r] = __int_as_float(0x7fc00000);
+                return;
             }
         }
     }
+}
+
+// out = sum_r 2^(lse_r - Lm) o_r / sum_r 2^(lse_r - Lm), Lm = max_r lse_r, over
+// the ranks with rows of the sequence (lse_r > -inf).
+__device__ __forceinline__ float combine_ranks(int n, const float (&lr)[8], const float (&o)[8]) {
+    float Lm = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < 8; r++)
+        if (r < n) Lm = fmaxf(Lm, lr[r]);
+    float L = 0.f, acc = 0.f;
+#pragma unroll
+    for (int r = 0; r < 8; r++) {
+        if (r < n && lr[r] != -INFINITY) {
+            const float w = ex2(lr[r] - Lm);
+            L += w;
+            acc += w * o[r];
+        }
+    }
+    return acc / L;
 }
 
 // Exchange of one (head, 32-column slice) of the shard result with the other
@@ -260,25 +301,8 @@ __device__ __forceinline__ void exchange_slice(const DecodeArgs& a, int b, int h
         const uint64_t* base = reinterpret_cast<const uint64_t*>(x.peers[x.rank] + x.slots);
         auto src = [&](int r) { return base + (((size_t)par * x.n_ranks + r) * rows + idx) * kXchgWords; };
         float lr[8], o[8];  // n_ranks <= 8
-        float Lm = -INFINITY;
-#pragma unroll
-        for (int r = 0; r < 8; r++) {
-            if (r < x.n_ranks) {
-                lr[r] = wait_word(src(r) + kXchgCols, seq, a.status);
-                o[r] = wait_word(src(r) + col, seq, a.status);
-                Lm = fmaxf(Lm, lr[r]);
-            }
-        }
-        float L = 0.f, acc = 0.f;
-#pragma unroll
-        for (int r = 0; r < 8; r++) {
-            if (r < x.n_ranks && lr[r] != -INFINITY) {  // skip a rank without rows of this sequence
-                const float w = ex2(lr[r] - Lm);
-                L += w;
-                acc += w * o[r];
-            }
-        }
-        x.out[((size_t)b * a.hq + h) * HD + z * kXchgCols + col] = acc / L;
+        wait_words(x.n_ranks, src, col, seq, lr, o, a.status);
+        x.out[((size_t)b * a.hq + h) * HD + z * kXchgCols + col] = combine_ranks(x.n_ranks, lr, o);
     }
 }
 
@@ -417,27 +441,10 @@ __device__ __forceinline__ float warp_exchange(const DecodeArgs& a, int h, int z
         if (lane == 0) st_word(dst + kXchgCols, lse, seq);
     }
     const uint64_t* base = reinterpret_cast<const uint64_t*>(x.peers[x.rank] + x.slots);
+    auto src = [&](int r) { return base + (((size_t)par * x.n_ranks + r) * rows + idx) * kXchgWords; };
     float lr[8], o[8];  // n_ranks <= 8
-    float Lm = -INFINITY;
-#pragma unroll
-    for (int r = 0; r < 8; r++) {
-        if (r < x.n_ranks) {
-            const uint64_t* src = base + (((size_t)par * x.n_ranks + r) * rows + idx) * kXchgWords;
-            lr[r] = wait_word(src + kXchgCols, seq, a.status);
-            o[r] = wait_word(src + lane, seq, a.status);
-            Lm = fmaxf(Lm, lr[r]);
-        }
-    }
-    float L = 0.f, acc = 0.f;
-#pragma unroll
-    for (int r = 0; r < 8; r++) {
-        if (r < x.n_ranks && lr[r] != -INFINITY) {  // skip a rank without rows of this sequence
-            const float w = ex2(lr[r] - Lm);
-            L += w;
-            acc += w * o[r];
-        }
-    }
-    return acc / L;
+    wait_words(x.n_ranks, src, lane, seq, lr, o, a.status);
+    return combine_ranks(x.n_ranks, lr, o);
 }
 
 // Merge for one sequence.  Its attention kernel leaves plan.merge_blocks SMs
