@@ -316,12 +316,14 @@ int32_t picoattn_prefill_staged(const picoattn_config_t* cfg, int32_t layer, int
  * memory, picoattn_p2p_area_bytes) and gets a CUDA IPC handle for it; the caller
  * moves the n_ranks handles between the processes (any transport) and opens the
  * communicator with all of them, in rank order.  picoattn_decode_splitkv_p2p
- * then runs picoattn_decode_shard into the area and ONE kernel that stores the
- * shard result into every rank's area over NVLink, raises a per-row flag there,
- * waits (bounded; PICOATTN_DEV_TIMEOUT in the workspace status) for every rank's
- * row and combines them by log-sum-exp into out, on every rank.  Every rank must
- * make the same sequence of calls.  Destroy only after every rank's last call
- * has completed (a barrier).  No counterpart in the reference. */
+ * then runs the decode over this rank's rows (as picoattn_decode_shard), and
+ * its merge kernel stores each head slice of the shard result, with its
+ * log-sum-exp, into every rank's area over NVLink as (value, call number)
+ * words, waits (bounded; PICOATTN_DEV_TIMEOUT in the workspace status) for every
+ * rank's words of the same call in its own area and combines them by
+ * log-sum-exp into out, on every rank.  Every rank must make the same sequence
+ * of calls.  Destroy only after every rank's last call has completed (a
+ * barrier).  No counterpart in the reference. */
 #define PICOATTN_P2P_HANDLE_BYTES 64
 size_t picoattn_p2p_area_bytes(const picoattn_config_t* cfg, int32_t n_seqs, int32_t n_ranks);
 int32_t picoattn_p2p_create(const picoattn_config_t* cfg, int32_t n_seqs, int32_t n_ranks, int32_t rank,
