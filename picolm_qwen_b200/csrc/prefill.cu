@@ -905,26 +905,34 @@ __global__ void __maxnreg__(168)
 // peer's softmax and epilogue arrive on the leader's barriers through cluster
 // addresses.  Items go to clusters statically, longest first, in serpentine
 // order.
-// Half of a KV tile (64 of its 128 key columns, half 0 or 1) of the online
-// softmax for the q row of this thread; the warp holding the other half of the
-// same 32 rows runs the same steps, and the two agree through named barrier
-// `bar` (the 64 threads of both warps) and the exchange area `xs` (128 floats):
-//   xs[0..31]   half 0's first-tile max estimate, per lane
-//   xs[32..95]  each half's tile max on the exact path [half][lane]
-//   xs[96..99]  per-tile flags [tile parity][half]
-// Both halves keep the same running max m_run; l_run is this half's partial
-// sum.  P (fp16) of the half's keys goes to TMEM columns [64*half, 64*half+32)
-// of the S buffer, which this half has already read.  On the first tile the
-// running max starts as the max of the tile's first 32 columns (half 0's, and
-// column 0 is visible to every row).  If any p of either half would exceed
-// 2^15 both take the exact path: shared new max, each rescales its half of O
-// and its partial sum, then recomputes P.
-template <int HD, class WaitPrevPV>
-__device__ __forceinline__ void softmax_half(uint32_t tS, uint32_t tO, uint32_t lane_off, int half, int j, int t,
+// One part (KP = BN/NP of the tile's key columns, part q) of a KV tile of the
+// online softmax for the q row of this thread; the warps holding the other
+// parts of the same 32 rows (NP in all, one sub-partition) run the same steps,
+// and they agree through named barrier `bar` (their NP*32 threads) and the
+// exchange area `xs` (SoftmaxXs<NP>::kFloats floats):
+//   xs[0..31]            part 0's first-tile max estimate, per lane
+//   xs[32 + 32q + lane]  part q's tile max on the exact path
+//   flags after that     per-tile flags [tile parity][part]
+// All parts keep the same running max m_run; l_run is this part's partial sum.
+// P (fp16) of the part's keys goes to TMEM columns [KP*q, KP*q + KP/2) of the S
+// buffer, which this part has already read.  On the first tile the running max
+// starts as the max of the tile's first 32 columns (part 0's; column 0 is
+// visible to every row).  If any p of any part would exceed 2^15 all take the
+// exact path: shared new max, each rescales its columns of O and its partial
+// sum, then recomputes P.
+template <int NP>
+struct SoftmaxXs {
+    static constexpr int kFlags = 32 + 32 * NP;
+    static constexpr int kFloats = kFlags + 2 * NP + (NP == 4 ? 0 : 4);  // a multiple of 4
+};
+
+template <int HD, int NP, class WaitPrevPV>
+__device__ __forceinline__ void softmax_part(uint32_t tS, uint32_t tO, uint32_t lane_off, int part, int j, int t,
                                              int kbase, int qpos, bool diag, float& m_run, float& l_run, int bar,
                                              float* xs, int lane, WaitPrevPV wait_prev_pv) {
-    const int col0 = half * 64;
-    // one 32-column chunk of this half's scores, masked beyond the diagonal
+    constexpr int KP = BN / NP, NC = KP / 32;  // columns per part, 32-column chunks per part
+    const int col0 = part * KP;
+    // one 32-column chunk of this part's scores, masked beyond the diagonal
     auto load_chunk = [&](int c, uint32_t (&sr)[32]) {
         tmem_ld32(tS + col0 + c * 32 + lane_off, sr);
         tmem_ld_wait();
@@ -935,7 +943,7 @@ __device__ __forceinline__ void softmax_half(uint32_t tS, uint32_t tO, uint32_t 
         }
     };
     if (j == 0) {  // running max estimate from the tile's first 32 columns
-        if (half == 0) {
+        if (part == 0) {
             uint32_t sr[32];
             load_chunk(0, sr);
             float m0 = -INFINITY;
@@ -943,22 +951,23 @@ __device__ __forceinline__ void softmax_half(uint32_t tS, uint32_t tO, uint32_t 
             for (int e = 0; e < 32; e++) m0 = fmaxf(m0, __uint_as_float(sr[e]));
             xs[lane] = m0;
         }
-        named_bar_sync(bar, 64);
+        named_bar_sync(bar, NP * 32);
         m_run = xs[lane];
     }
-    uint32_t pk[32];
-    // p = 2^(s - m_run) for the half's 64 scores into pk; partial sum and max p.
-    // The second chunk's TMEM load is in flight while the first is processed.
+    uint32_t pk[KP / 2];
+    // p = 2^(s - m_run) for the part's scores into pk; partial sum and max p.
+    // With two chunks the second one's TMEM load is in flight while the first
+    // is processed.
     auto p_pass = [&](float& psum, float& pmax) {
         const uint64_t mm2 = f2_pack(m_run, m_run);
         uint64_t ls2[4] = {0ull, 0ull, 0ull, 0ull};
         __half2 hm[2] = {__float2half2_rn(0.f), __float2half2_rn(0.f)};
-        uint32_t sb[2][32];
+        uint32_t sb[NC][32];
         tmem_ld32(tS + col0 + lane_off, sb[0]);
 #pragma unroll
-        for (int c = 0; c < 2; c++) {
+        for (int c = 0; c < NC; c++) {
             tmem_ld_wait();
-            if (c == 0) tmem_ld32(tS + col0 + 32 + lane_off, sb[1]);
+            if (c + 1 < NC) tmem_ld32(tS + col0 + (c + 1) * 32 + lane_off, sb[c + 1]);
             uint32_t (&sr)[32] = sb[c];
             if (diag) {
 #pragma unroll
@@ -984,37 +993,42 @@ __device__ __forceinline__ void softmax_half(uint32_t tS, uint32_t tO, uint32_t 
     };
     float psum, pmax;
     p_pass(psum, pmax);
-    // both halves must accept the stale max for these rows
-    int* flags = reinterpret_cast<int*>(xs + 96);
+    // every part must accept the stale max for these rows
+    int* flags = reinterpret_cast<int*>(xs + SoftmaxXs<NP>::kFlags);
     const bool ok = __all_sync(0xffffffffu, pmax <= 32768.0f);
-    if (lane == 0) flags[(t & 1) * 2 + half] = ok ? 1 : 0;
-    named_bar_sync(bar, 64);
-    const bool ok_both = flags[(t & 1) * 2] != 0 && flags[(t & 1) * 2 + 1] != 0;
-    if (!ok_both) {
-        // exact path: the new row max over both halves
+    if (lane == 0) flags[(t & 1) * NP + part] = ok ? 1 : 0;
+    named_bar_sync(bar, NP * 32);
+    bool ok_all = true;
+#pragma unroll
+    for (int q = 0; q < NP; q++) ok_all &= flags[(t & 1) * NP + q] != 0;
+    if (!ok_all) {
+        // exact path: the new row max over all parts
         float mx = -INFINITY;
 #pragma unroll 1
-        for (int c = 0; c < 2; c++) {
+        for (int c = 0; c < NC; c++) {
             uint32_t sr[32];
             load_chunk(c, sr);
 #pragma unroll
             for (int e = 0; e < 32; e++) mx = fmaxf(mx, __uint_as_float(sr[e]));
         }
-        xs[32 + half * 32 + lane] = mx;
-        named_bar_sync(bar, 64);
-        const float m_new = fmaxf(j == 0 ? -INFINITY : m_run, fmaxf(mx, xs[32 + (1 - half) * 32 + lane]));
-        if (j > 0) {  // rescale this half's O columns (sum through tile j-1) and partial sum
+        xs[32 + part * 32 + lane] = mx;
+        named_bar_sync(bar, NP * 32);
+        float m_new = j == 0 ? -INFINITY : m_run;
+#pragma unroll
+        for (int q = 0; q < NP; q++) m_new = fmaxf(m_new, xs[32 + q * 32 + lane]);
+        if (j > 0) {  // rescale this part's O columns (sum through tile j-1) and partial sum
             const float corr = ex2(m_run - m_new);
             wait_prev_pv();
             tc_fence_after();
+            constexpr int OC = HD / NP;  // O columns of this part
 #pragma unroll 1
-            for (int c = 0; c < 2; c++) {
+            for (int c = 0; c < OC / 32; c++) {
                 uint32_t o[32];
-                tmem_ld32(tO + col0 + c * 32 + lane_off, o);
+                tmem_ld32(tO + part * OC + c * 32 + lane_off, o);
                 tmem_ld_wait();
 #pragma unroll
                 for (int e = 0; e < 32; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
-                tmem_st32(tO + col0 + c * 32 + lane_off, o);
+                tmem_st32(tO + part * OC + c * 32 + lane_off, o);
             }
             tmem_st_wait();
             l_run *= corr;
@@ -1022,10 +1036,20 @@ __device__ __forceinline__ void softmax_half(uint32_t tS, uint32_t tO, uint32_t 
         m_run = m_new;
         p_pass(psum, pmax);
     }
-    tmem_st32(tS + col0 + lane_off, pk);
+    if constexpr (KP / 2 == 32) {
+        tmem_st32(tS + col0 + lane_off, pk);
+    } else {
+        tmem_st16(tS + col0 + lane_off, pk);
+    }
     l_run += psum;
     tmem_st_wait();
 }
+
+// Softmax parts per tile row in the CTA-pair kernel: four warps per
+// sub-partition share its exponential unit (each 32 columns per row), so one
+// warp's loads, stores and waits hide behind the others' exponentials.
+constexpr int kPairParts = 4;
+constexpr int kPairThreads = kPairParts * 128 + 64 + 128;  // softmax, TMA + MMA, epilogue
 
 struct PairSmem {
     static constexpr int kQBytes = 2 * BM * 128;    // 128 rows x 128 hd columns (two 64-column boxes)
@@ -1036,16 +1060,16 @@ struct PairSmem {
     static constexpr int kK = kQ + 2 * kQBytes;
     static constexpr int kV = kK + NK * kKBytes;
     static constexpr int kStage = kV + NV * kVBytes;  // epilogue: 32 x 32 fp32 per epilogue warp
-    static constexpr int kLsum = kStage + 4 * 4096;   // row sums handed to the epilogue [O buffer][half][128]
-    static constexpr int kXch = kLsum + 2 * 2 * 128 * 4;  // softmax half exchange, 128 floats per warp pair
-    static constexpr int kBars = kXch + 4 * 128 * 4;
+    static constexpr int kLsum = kStage + 4 * 4096;   // row sums handed to the epilogue [O buffer][part][128]
+    static constexpr int kXch = kLsum + 2 * kPairParts * 128 * 4;  // softmax part exchange, per row group
+    static constexpr int kBars = kXch + 4 * SoftmaxXs<kPairParts>::kFloats * 4;
     static constexpr int kEnd = kBars + 512;
     static constexpr int kDynBytes = kEnd + 1024;
 };
 
-// 448 threads: 14 warps, four of them on two of the SM's sub-partitions, whose
-// 16,384 registers then allow 128 per thread
-__global__ void __launch_bounds__(448, 1)
+// kPairThreads = 704 threads: 22 warps, six of them on two of the SM's
+// sub-partitions, whose 16,384 registers then allow 80 per thread
+__global__ void __launch_bounds__(kPairThreads, 1)
     prefill_attn_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKh,
                              const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                              PrefillArgs a) {
@@ -1067,12 +1091,12 @@ __global__ void __launch_bounds__(448, 1)
     uint64_t* v_full = k_empty + L::NK;   // [NV] leader
     uint64_t* v_empty = v_full + L::NV;   // [NV] both
     uint64_t* s_full = v_empty + L::NV;   // [2] both, per S buffer
-    uint64_t* p_full = s_full + 2;        // [2] leader, 16 arrivals (8 softmax warps x 2 CTAs)
+    uint64_t* p_full = s_full + 2;        // [2] leader, one arrival per softmax warp of both CTAs
     // PV(t) completes pv_done[t % 2]: with QK(t+1) issued before PV(t) a single
     // barrier could run two phases behind a waiter, which a parity wait cannot tell
     uint64_t* pv_done = p_full + 2;       // [2] both
     uint64_t* o_full = pv_done + 2;       // [2] both, per O buffer: the item's last PV done
-    uint64_t* l_full = o_full + 2;        // [2] own, 8 arrivals: row sums written
+    uint64_t* l_full = o_full + 2;        // [2] own, one arrival per softmax warp: row sums written
     uint64_t* o_free = l_full + 2;        // [2] leader, 8 arrivals (4 epilogue warps x 2 CTAs)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 2);
     float* lsum = reinterpret_cast<float*>(smem + L::kLsum);
@@ -1083,12 +1107,13 @@ __global__ void __launch_bounds__(448, 1)
         for (int s = 0; s < L::NK; s++) mbar_init(&k_full[s], 1), mbar_init(&k_empty[s], 1);
         for (int s = 0; s < L::NV; s++) mbar_init(&v_full[s], 1), mbar_init(&v_empty[s], 1);
         for (int b = 0; b < 2; b++) {
-            mbar_init(&s_full[b], 1), mbar_init(&p_full[b], 16), mbar_init(&pv_done[b], 1);
-            mbar_init(&o_full[b], 1), mbar_init(&l_full[b], 8), mbar_init(&o_free[b], 8);
+            mbar_init(&s_full[b], 1), mbar_init(&p_full[b], 2 * 4 * kPairParts), mbar_init(&pv_done[b], 1);
+            mbar_init(&o_full[b], 1), mbar_init(&l_full[b], 4 * kPairParts), mbar_init(&o_free[b], 8);
         }
         fence_mbar_init();
     }
-    if (warp == 9) tmem_alloc_pair(tmem_slot, 512);
+    constexpr int W_TMA = 4 * kPairParts, W_MMA = W_TMA + 1, W_EPI = W_TMA + 2;
+    if (warp == W_MMA) tmem_alloc_pair(tmem_slot, 512);
     tc_fence_before();
     cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated in both
     tc_fence_after();
@@ -1104,7 +1129,7 @@ __global__ void __launch_bounds__(448, 1)
         return (a.start + q_last) / BN + 1;
     };
 
-    if (warp == 8) {
+    if (warp == W_TMA) {
         // ---------------- TMA producer (both CTAs) ----------------
         if (lane == 0) {
             prefetch_tmap(&tmQ);
@@ -1155,7 +1180,7 @@ __global__ void __launch_bounds__(448, 1)
             }
         }
         __syncwarp();
-    } else if (warp == 9) {
+    } else if (warp == W_MMA) {
         // ---------------- MMA issuer (leader lane 0) ----------------
         if (rank == 0 && lane == 0) {
             constexpr uint32_t idesc_qk = idesc_f16_f32(2 * BM, BN, false, false);
@@ -1221,11 +1246,13 @@ __global__ void __launch_bounds__(448, 1)
                     tc_fence_after();
                     const uint64_t vd = desc_advance(dv, sv * L::kVBytes);
                     const uint32_t dS = tmem + (uint32_t)((t & 1) * 128);
-                    // P of keys [0,64) in S columns [0,32), of keys [64,128) in [64,96)
+                    // P of part q's keys (KP = BN/NP of them) in S columns [KP*q, KP*q + KP/2);
+                    // K step kk covers keys [16kk, 16kk+16): 8 packed columns
+                    constexpr int KP = BN / kPairParts;
 #pragma unroll
                     for (int kk = 0; kk < BN / 16; kk++)
-                        umma2_ts(tO, dS + (kk < 4 ? kk * 8 : 64 + (kk - 4) * 8), desc_advance(vd, kk * 16 * 128),
-                                 idesc_pv, (!first || kk > 0) ? 1u : 0u);
+                        umma2_ts(tO, dS + (uint32_t)((kk * 16 / KP) * KP + (kk * 16 % KP) / 2),
+                                 desc_advance(vd, kk * 16 * 128), idesc_pv, (!first || kk > 0) ? 1u : 0u);
                     umma2_commit_both(&pv_done[t & 1]);
                     umma2_commit_both(&v_empty[sv]);
                     if (j + 1 == n_kv) umma2_commit_both(&o_full[ob]);
@@ -1234,13 +1261,13 @@ __global__ void __launch_bounds__(448, 1)
             }
         }
         __syncwarp();
-    } else if (warp < 8) {
-        // ---------------- softmax (both CTAs): warps 0-3 keys [0,64), 4-7 keys [64,128) ----------------
-        const int half = warp >> 2;
+    } else if (warp < W_TMA) {
+        // ---------------- softmax (both CTAs): warps 4q..4q+3 take key columns [KP*q, KP*q + KP) ----------------
+        const int part = warp >> 2;
         const int r = threadIdx.x & 127;  // q row == TMEM lane
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-        const int bar = 1 + (warp & 3);  // with the warp of the other half over the same rows
-        float* xs = xch + (warp & 3) * 128;
+        const int bar = 1 + (warp & 3);  // with the warps of the other parts over the same rows
+        float* xs = xch + (warp & 3) * SoftmaxXs<kPairParts>::kFloats;
         const uint32_t p_full_l0 = mapa_shared(&p_full[0], 0), p_full_l1 = mapa_shared(&p_full[1], 0);
         int t = 0;
         for (int k = 0;; k++) {
@@ -1259,8 +1286,9 @@ __global__ void __launch_bounds__(448, 1)
                 const int kbase = j * BN;
                 const bool diag = kbase + BN - 1 > a.start + q0;
                 const uint32_t tS = tmem + (uint32_t)((t & 1) * 128);
-                softmax_half<HD>(tS, tO, lane_off, half, j, t, kbase, qpos, diag, m_run, l_run, bar, xs, lane,
-                                 [&] { mbar_wait(&pv_done[(t - 1) & 1], (uint32_t)(((t - 1) >> 1) & 1), a.status); });
+                softmax_part<HD, kPairParts>(
+                    tS, tO, lane_off, part, j, t, kbase, qpos, diag, m_run, l_run, bar, xs, lane,
+                    [&] { mbar_wait(&pv_done[(t - 1) & 1], (uint32_t)(((t - 1) >> 1) & 1), a.status); });
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive_remote((t & 1) ? p_full_l1 : p_full_l0);
@@ -1268,15 +1296,15 @@ __global__ void __launch_bounds__(448, 1)
             // hand the partial row sums to the epilogue warps.  lsum[k % 2] is free
             // again: item k-2's epilogue read it before releasing O_(k%2), which
             // this item's first PV waited for
-            lsum[((k & 1) * 2 + half) * 128 + r] = l_run;
+            lsum[((k & 1) * kPairParts + part) * 128 + r] = l_run;
             __syncwarp();
             if (lane == 0) mbar_arrive(&l_full[k & 1]);
         }
-    } else if (warp >= 10) {
+    } else if (warp >= W_EPI) {
         // ---------------- epilogue (both CTAs) ----------------
         const int sub = warp & 3;  // TMEM subpartition of this warp: rows 32*sub ..
         const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
-        float* stage = reinterpret_cast<float*>(smem + L::kStage + (warp - 10) * 4096);
+        float* stage = reinterpret_cast<float*>(smem + L::kStage + (warp - W_EPI) * 4096);
         int k = 0;
         for (;; k++) {
             const int it = item_of(k);
@@ -1287,8 +1315,10 @@ __global__ void __launch_bounds__(448, 1)
             mbar_wait(&o_full[ob], (uint32_t)((k >> 1) & 1), a.status);
             mbar_wait(&l_full[ob], (uint32_t)((k >> 1) & 1), a.status);
             tc_fence_after();
-            const float inv =
-                1.0f / (lsum[(ob * 2 + 0) * 128 + sub * 32 + lane] + lsum[(ob * 2 + 1) * 128 + sub * 32 + lane]);
+            float lsum_row = 0.f;
+#pragma unroll
+            for (int q = 0; q < kPairParts; q++) lsum_row += lsum[(ob * kPairParts + q) * 128 + sub * 32 + lane];
+            const float inv = 1.0f / lsum_row;
             const int row0 = qt * BM + sub * 32;
 #pragma unroll 1
             for (int c = 0; c < HD / 32; c++) {
@@ -1307,7 +1337,7 @@ __global__ void __launch_bounds__(448, 1)
     }
     tc_fence_before();
     cluster_sync_all();  // no CTA leaves while its peer may still signal it
-    if (warp == 9) {
+    if (warp == W_MMA) {
         tc_fence_after();
         tmem_dealloc_pair(tmem, 512);
     }
@@ -1365,7 +1395,7 @@ bool make_out_map(CUtensorMap* m, float* base, uint64_t inner, uint64_t rows) {
 
 // One-time, per-device setup of the attention kernels for one head_dim: their
 // shared-memory limits, and whether the CTA-pair and head-pair kernels can be
-// resident (the CTA pair needs 448 threads x 128 registers and 2-CTA clusters).
+// resident (the CTA pair needs kPairThreads threads x 80 registers and 2-CTA clusters).
 struct PrefillSetup {
     bool done = false;
     cudaError_t err = cudaSuccess;
@@ -1402,7 +1432,7 @@ const PrefillSetup& prefill_setup() {
         attr[0].id = cudaLaunchAttributeClusterDimension;
         attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
         cfg.gridDim = dim3(2, 1, 1);
-        cfg.blockDim = dim3(448, 1, 1);
+        cfg.blockDim = dim3(kPairThreads, 1, 1);
         cfg.dynamicSmemBytes = PairSmem::kDynBytes;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
@@ -1451,7 +1481,7 @@ cudaError_t launch_prefill_hd(const PrefillArgs& a, cudaStream_t stream, unsigne
             attr[0].id = cudaLaunchAttributeClusterDimension;
             attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
             cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
-            cfg.blockDim = dim3(448, 1, 1);
+            cfg.blockDim = dim3(kPairThreads, 1, 1);
             cfg.dynamicSmemBytes = PairSmem::kDynBytes;
             cfg.stream = stream;
             cfg.attrs = attr;

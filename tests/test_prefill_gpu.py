@@ -67,7 +67,7 @@ def test_prefill_matches_reference_golden(cuda, golden_dir):
     assert st.status() == 0
 
 
-def run_case(oracle, hq, hkv, hd, n_tok, start, mode=0, norm=True, f16=True, seed=0, layer=0, threads=16):
+def run_case(oracle, hq, hkv, hd, n_tok, start, mode=0, norm=True, f16=True, seed=0, layer=0, threads=16, qscale=1.0):
     from picolm_qwen_b200 import abi
     rng = np.random.default_rng(seed)
     kvd = hkv * hd
@@ -82,7 +82,7 @@ def run_case(oracle, hq, hkv, hd, n_tok, start, mode=0, norm=True, f16=True, see
         vc[:start] = oracle.f32_to_f16(rng.standard_normal(start * kvd).astype(np.float32)).reshape(start, kvd)
         st.k_cache[0, layer, :start] = dev(kc[:start].view(np.int16))
         st.v_cache[0, layer, :start] = dev(vc[:start].view(np.int16))
-    q = rng.standard_normal((n_tok, hq * hd)).astype(np.float32)
+    q = (qscale * rng.standard_normal((n_tok, hq * hd))).astype(np.float32)
     k = rng.standard_normal((n_tok, kvd)).astype(np.float32)
     v = rng.standard_normal((n_tok, kvd)).astype(np.float32)
     if f16:
@@ -112,6 +112,7 @@ def run_case(oracle, hq, hkv, hd, n_tok, start, mode=0, norm=True, f16=True, see
     dict(hq=14, hkv=2, hd=64, n_tok=129, start=0, norm=False),       # Qwen2.5-0.5B heads
     dict(hq=4, hkv=4, hd=64, n_tok=1, start=0),                      # a one-token prompt
     dict(hq=4, hkv=4, hd=128, n_tok=1, start=300),                   # one token after a long cache
+    dict(hq=16, hkv=4, hd=128, n_tok=333, start=1000, norm=False),   # long cached prefix
 ])
 def test_prefill_vs_oracle(cuda, oracle, case):
     st, got, ref, kc, vc = run_case(oracle, **case)
@@ -119,6 +120,52 @@ def test_prefill_vs_oracle(cuda, oracle, case):
     start, n = case["start"], case["n_tok"]
     assert np.array_equal(st.k_cache[0, 0, start:start + n].cpu().numpy().view(np.uint16), kc[start:start + n])
     assert np.array_equal(st.v_cache[0, 0, start:start + n].cpu().numpy().view(np.uint16), vc[start:start + n])
+
+
+def fp16_datapath_reference(oracle, hq, hkv, hd, q, kc, vc, start, cos_t, sin_t):
+    """The attention the tensor-core path computes, in numpy: rotated q pre-scaled
+    by log2(e)/sqrt(hd) and rounded to fp16 (the workspace operand), fp32 scores
+    against the fp16 cache, base-2 softmax in fp32, p rounded to fp16 for P.V,
+    the sum over the unrounded p.  Only for inputs whose scores are so wide that
+    the fp16 rounding of q alone moves the output past the tolerance against the
+    fp32 reference."""
+    n_tok = q.shape[0]
+    g = hq // hkv
+    K = oracle.f16_to_f32(kc.ravel()).reshape(kc.shape)
+    V = oracle.f16_to_f32(vc.ravel()).reshape(vc.shape)
+    out = np.zeros((n_tok, hq * hd), np.float32)
+    scale = np.float32(1.4426950408889634 / np.sqrt(hd))
+    for i in range(n_tok):
+        pos = start + i
+        qr, _ = oracle.rope(0, q[i], np.zeros(hkv * hd, np.float32), hd, hq, hkv, cos_t[pos], sin_t[pos])
+        q16 = (qr * scale).astype(np.float16).astype(np.float32).reshape(hq, hd)
+        for h in range(hq):
+            kvh = h // g
+            sc = K[:pos + 1, kvh * hd:(kvh + 1) * hd] @ q16[h]
+            p = np.exp2(sc - sc.max()).astype(np.float32)
+            p16 = p.astype(np.float16).astype(np.float32)
+            out[i, h * hd:(h + 1) * hd] = (p16 @ V[:pos + 1, kvh * hd:(kvh + 1) * hd]) / p.sum()
+    return out
+
+
+def test_prefill_wide_scores_rescale_paths(cuda, oracle):
+    """Wide scores (q x 6, no norm): row maxima jump between and within key tiles,
+    so the softmax lifts its running max mid-tile and rescales the stored P, the
+    sums and O.  Checked against the same fp16 datapath in numpy (tolerance as
+    everywhere); the k/v rows against the reference bit for bit."""
+    hq, hkv, hd, n_tok, start = 8, 2, 128, 400, 150
+    st, got, _, kc, vc = run_case(oracle, hq, hkv, hd, n_tok, start, norm=False, qscale=6.0, seed=4, threads=8)
+    S = start + n_tok
+    cos_t, sin_t = oracle.rope_table(S, hd, 1e6)
+    rng = np.random.default_rng(4)  # the same draws as run_case
+    kvd = hkv * hd
+    rng.standard_normal(start * kvd), rng.standard_normal(start * kvd)
+    q = (6.0 * rng.standard_normal((n_tok, hq * hd))).astype(np.float32).astype(np.float16).astype(np.float32)
+    kc_all = st.k_cache[0, 0, :S].cpu().numpy().view(np.uint16)
+    vc_all = st.v_cache[0, 0, :S].cpu().numpy().view(np.uint16)
+    assert np.array_equal(kc_all[start:], kc[start:S]) and np.array_equal(vc_all[start:], vc[start:S])
+    want = fp16_datapath_reference(oracle, hq, hkv, hd, q, kc_all, vc_all, start, cos_t, sin_t)
+    assert_close(got, want, "wide scores")
 
 
 def test_prefill_full_qwen3_layer_vs_oracle(cuda, oracle):
