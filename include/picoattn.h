@@ -54,6 +54,8 @@ typedef struct CUstream_st* picoattn_stream_t;
 #define PICOATTN_ETIMEOUT     -7  /* a bounded wait ran out */
 #define PICOATTN_EDEVICE      -8  /* current device is not sm_100 */
 #define PICOATTN_EDEVSTATUS   -9  /* a kernel flagged bad input (see workspace status) */
+#define PICOATTN_EIO         -10  /* a file could not be opened, read or written */
+#define PICOATTN_EFORMAT     -11  /* not a KVCP file, or its shape does not match the config */
 
 /* Device-side sticky status bits (picoattn_workspace_status). */
 #define PICOATTN_DEV_BAD_POS      0x1u  /* pos[b] < 0, >= max_seq_len or >= max_ctx */
@@ -338,6 +340,41 @@ int32_t picoattn_decode_splitkv_p2p(const picoattn_config_t* cfg, int32_t layer,
                                     uint16_t* const* k_cache, uint16_t* const* v_cache,
                                     const int32_t* pos, float* out, void* workspace, size_t workspace_bytes,
                                     void* comm, picoattn_stream_t stream);
+
+/* ---- KV-cache persistence in the C engine's KVCP file format ----------------
+ * The reference saves a prompt's KV cache to skip its prefill next time
+ * (picolm/model.c:870-983, kvcache_save / kvcache_load; magic "KVCP",
+ * picolm/model.h:12).  File layout, little-endian:
+ *   u32 magic 0x4B564350, u32 n_pos, u32 n_layers, u32 kv_dim,
+ *   K rows 0..n_pos-1 of layer 0, of layer 1, ... (fp16, kv_dim each),
+ *   V rows in the same order.
+ * These entries read and write that format straight from and to a device
+ * cache in the library's layout ([n_layers][max_seq_len][kv_dim] fp16, the
+ * reference's own), so files are interchangeable with the reference's.
+ *
+ * picoattn_kvcp_bytes: size of the file for n_pos positions.
+ * picoattn_kvcp_save: n_pos in [1, max_seq_len] (else PICOATTN_ERANGE); the
+ *   device rows are copied out in stream order (the call returns when the file
+ *   is written).
+ * picoattn_kvcp_load: fills rows 0..n_pos-1 of every layer and returns n_pos;
+ *   PICOATTN_EIO when the file cannot be read, PICOATTN_EFORMAT for a bad magic,
+ *   a layer count or kv_dim other than the config's, n_pos outside
+ *   [0, max_seq_len] or a short file (the reference reports all of these as 0
+ *   cached positions); *n_pos_out = 0 on any error.
+ * picoattn_kvcp_pack / _unpack: the same bytes in a caller buffer (host or
+ *   device memory) instead of a file, stream-ordered (pack: dst_bytes >=
+ *   picoattn_kvcp_bytes; unpack reads the header synchronously).
+ * Not on the attention call path: save and load allocate pinned staging. */
+#define PICOATTN_KVCP_MAGIC 0x4B564350u
+size_t picoattn_kvcp_bytes(const picoattn_config_t* cfg, int32_t n_pos);
+int32_t picoattn_kvcp_save(const picoattn_config_t* cfg, int32_t n_pos, const uint16_t* k_cache,
+                           const uint16_t* v_cache, const char* path, picoattn_stream_t stream);
+int32_t picoattn_kvcp_load(const picoattn_config_t* cfg, const char* path, uint16_t* k_cache, uint16_t* v_cache,
+                           int32_t* n_pos_out, picoattn_stream_t stream);
+int32_t picoattn_kvcp_pack(const picoattn_config_t* cfg, int32_t n_pos, const uint16_t* k_cache,
+                           const uint16_t* v_cache, void* dst, size_t dst_bytes, picoattn_stream_t stream);
+int32_t picoattn_kvcp_unpack(const picoattn_config_t* cfg, const void* src, size_t src_bytes, uint16_t* k_cache,
+                             uint16_t* v_cache, int32_t* n_pos_out, picoattn_stream_t stream);
 
 /* Which attention kernel picoattn_prefill launches for this shape on the
  * current device: PICOATTN_PREFILL_CTA_PAIR (head_dim 128, an even number of q

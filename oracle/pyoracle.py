@@ -193,7 +193,26 @@ class RefHarness:
                                              _f32p, _f32p, _f32p, C.c_void_p, C.c_void_p,
                                              _f32p, _f32p, C.c_void_p, C.c_void_p, _i32p, _f32p,
                                              C.c_int]
+        for n in ("pref_kvcp_save", "pref_kvcp_load"):
+            getattr(L, n).restype = C.c_int
+        L.pref_kvcp_save.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, _u16p, _u16p, C.c_char_p, C.c_int]
+        L.pref_kvcp_load.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, _u16p, _u16p, C.c_char_p]
         self.L = L
+
+    def kvcp_save(self, kc, vc, n_kv_heads, head_dim, path, n_pos):
+        """The C engine's kvcache_save (picolm/model.c:884-926) of caches kc, vc
+        ([n_layers][max_seq][kv_dim] uint16); returns its status (0 or -1)."""
+        kc = np.ascontiguousarray(kc, np.uint16)
+        vc = np.ascontiguousarray(vc, np.uint16)
+        L, S, _ = kc.shape
+        return self.L.pref_kvcp_save(L, n_kv_heads, head_dim, S, kc, vc, path.encode(), n_pos)
+
+    def kvcp_load(self, kc, vc, n_kv_heads, head_dim, path):
+        """The C engine's kvcache_load (picolm/model.c:928-983) into kc, vc (filled
+        in place, C-contiguous uint16 arrays); returns the positions loaded (0: none)."""
+        L, S, _ = kc.shape
+        assert kc.flags.c_contiguous and vc.flags.c_contiguous and kc.dtype == np.uint16
+        return self.L.pref_kvcp_load(L, n_kv_heads, head_dim, S, kc, vc, path.encode())
 
     def f32_to_f16(self, x):
         x = np.ascontiguousarray(x, np.float32).ravel()

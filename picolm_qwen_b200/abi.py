@@ -24,6 +24,10 @@ PICOATTN_ENCCL = -6
 PICOATTN_ETIMEOUT = -7
 PICOATTN_EDEVICE = -8
 PICOATTN_EDEVSTATUS = -9
+PICOATTN_EIO = -10
+PICOATTN_EFORMAT = -11
+
+KVCP_MAGIC = 0x4B564350
 
 DEV_BAD_POS = 0x1
 DEV_MISALIGNED = 0x2
@@ -117,6 +121,11 @@ PROTOTYPES = {
     "picoattn_prefill": (_I, [_CFG, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P]),
     "picoattn_prefill_staged": (_I, [_CFG, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P,
                                      C.c_uint32]),
+    "picoattn_kvcp_bytes": (_Z, [_CFG, _I]),
+    "picoattn_kvcp_save": (_I, [_CFG, _I, _P, _P, C.c_char_p, _P]),
+    "picoattn_kvcp_load": (_I, [_CFG, C.c_char_p, _P, _P, C.POINTER(C.c_int32), _P]),
+    "picoattn_kvcp_pack": (_I, [_CFG, _I, _P, _P, _P, _Z, _P]),
+    "picoattn_kvcp_unpack": (_I, [_CFG, _P, _Z, _P, _P, C.POINTER(C.c_int32), _P]),
 }
 
 _lib = None

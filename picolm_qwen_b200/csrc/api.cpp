@@ -111,6 +111,8 @@ const char* picoattn_strerror(int32_t s) {
         case PICOATTN_ETIMEOUT: return "timed out";
         case PICOATTN_EDEVICE: return "device is not sm_100";
         case PICOATTN_EDEVSTATUS: return "a kernel flagged bad input";
+        case PICOATTN_EIO: return "file could not be opened, read or written";
+        case PICOATTN_EFORMAT: return "not a KVCP file of this shape";
         default: return "unknown status";
     }
 }

@@ -83,6 +83,24 @@ class AttnState:
             self.k_cache[seq].data_ptr(), self.v_cache[seq].data_ptr(), out.data_ptr(),
             self.workspace.data_ptr(), self.workspace.numel(), stream_handle(stream))
 
+    # -- KV-cache persistence in the C engine's KVCP format (picolm/model.c:870-983)
+    def kvcp_save(self, path: str, n_pos: int, seq: int = 0, stream: torch.cuda.Stream | None = None) -> None:
+        """Rows 0..n_pos-1 of every layer of sequence `seq` -> a KVCP file (kvcache_save)."""
+        abi.check(abi.lib().picoattn_kvcp_save(C.byref(self.cfg), n_pos, self.k_cache[seq].data_ptr(),
+                                               self.v_cache[seq].data_ptr(), path.encode(), stream_handle(stream)),
+                  "picoattn_kvcp_save")
+
+    def kvcp_load(self, path: str, seq: int = 0, stream: torch.cuda.Stream | None = None) -> int:
+        """A KVCP file -> rows 0..n_pos-1 of sequence `seq`; returns n_pos, or 0 when
+        the file is missing or does not fit this model (kvcache_load's contract)."""
+        n = C.c_int32(0)
+        st = abi.lib().picoattn_kvcp_load(C.byref(self.cfg), path.encode(), self.k_cache[seq].data_ptr(),
+                                          self.v_cache[seq].data_ptr(), C.byref(n), stream_handle(stream))
+        if st in (abi.PICOATTN_EIO, abi.PICOATTN_EFORMAT):
+            return 0
+        abi.check(st, "picoattn_kvcp_load")
+        return n.value
+
     # -- the call that replaces cpp/model.hpp:493-593 (forward_batch) ------------
     def prefill(self, layer: int, start_pos: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                 out: torch.Tensor, q_norm_w: torch.Tensor | None = None, k_norm_w: torch.Tensor | None = None,
