@@ -341,9 +341,9 @@ __device__ __forceinline__ void merge_slice(const DecodeArgs& a, int G, int b, i
         const int W = a.warps_per_head, lw = __ffs(W) - 1;  // W is 1, 2, 4 or 8
         if (i_lo == i_hi && W == 1 && !xchg) return;  // written directly by the attention kernel
         const int n_pieces = (i_hi - i_lo + 1) * W;  // <= kMergeMaxPieces (checked on the host)
-        // piece k = (CTA i_lo + k/W, warp k%W) -> slot (cta + seq, warp), head h
+        // piece k = (CTA i_lo + k/W, warp k%W) -> slot (cta + seq, warp) of head h
         auto slot_of = [&](int k) -> uint32_t {
-            return (uint32_t)((((i_lo + (k >> lw) + b) << lw) | (k & (W - 1))) * a.hq + h);
+            return (uint32_t)h * (uint32_t)a.n_slots + (uint32_t)(((i_lo + (k >> lw) + b) << lw) | (k & (W - 1)));
         };
         for (int k = tid; k < n_pieces; k += NT) {
             const int i = i_lo + (k >> lw);
@@ -421,9 +421,13 @@ __device__ __forceinline__ void merge_slice(const DecodeArgs& a, int G, int b, i
 }
 
 // Exchange of one (head, 32-column slice) by one warp (lane = column): the
-// same protocol and words as exchange_slice.
-__device__ __forceinline__ float warp_exchange(const DecodeArgs& a, int h, int z, int NS, float res, float lse,
-                                               int lane) {
+// same protocol and words as exchange_slice, in two halves.  xchg_post bumps
+// the slice's call counter and stores this rank's words into every rank's
+// area; xchg_collect waits (bounded) for every rank's words of that call in
+// this rank's own area and combines them.  Posting never waits, so a block
+// posts the slices of all its heads before it waits for any.
+__device__ __forceinline__ uint32_t xchg_post(const DecodeArgs& a, int h, int z, int NS, float res, float lse,
+                                              int lane) {
     const XchgArgs& x = a.x;
     const size_t rows = (size_t)a.hq * NS, idx = (size_t)h * NS + z;
     uint32_t seq = 0;
@@ -433,13 +437,19 @@ __device__ __forceinline__ float warp_exchange(const DecodeArgs& a, int h, int z
         *ctr = seq;
     }
     seq = __shfl_sync(0xffffffffu, seq, 0);
-    const uint32_t par = seq & 1u;
-    const size_t my_slot = ((size_t)par * x.n_ranks + x.rank) * rows + idx;
+    const size_t my_slot = ((size_t)(seq & 1u) * x.n_ranks + x.rank) * rows + idx;
     for (int p = 0; p < x.n_ranks; p++) {
         uint64_t* dst = reinterpret_cast<uint64_t*>(x.peers[p] + x.slots) + my_slot * kXchgWords;
         st_word(dst + lane, res, seq);
         if (lane == 0) st_word(dst + kXchgCols, lse, seq);
     }
+    return seq;
+}
+
+__device__ __forceinline__ float xchg_collect(const DecodeArgs& a, int h, int z, int NS, uint32_t seq, int lane) {
+    const XchgArgs& x = a.x;
+    const size_t rows = (size_t)a.hq * NS, idx = (size_t)h * NS + z;
+    const uint32_t par = seq & 1u;
     const uint64_t* base = reinterpret_cast<const uint64_t*>(x.peers[x.rank] + x.slots);
     auto src = [&](int r) { return base + (((size_t)par * x.n_ranks + r) * rows + idx) * kXchgWords; };
     float lr[8], o[8];  // n_ranks <= 8
@@ -450,73 +460,178 @@ __device__ __forceinline__ float warp_exchange(const DecodeArgs& a, int h, int z
 // Merge for one sequence.  Its attention kernel leaves plan.merge_blocks SMs
 // free (the grid is sized that way), so the blocks of this kernel, launched
 // while that kernel runs, land there, and the next call's attention CTAs take
-// the SMs the attention kernel frees without waiting for this merge.  A warp
-// per (head, 32-column slice), lane = column, folds the G*W pieces in chunks
-// of 32 with a running log2-sum-exp: per chunk one load of (max, sum) per lane
-// and 32 acc loads per lane, all in flight together.  With an exchange the
-// warp then trades its slice with the other ranks (warp_exchange).
+// the SMs the attention kernel frees without waiting for this merge.  Block i
+// takes heads i, i + gridDim.x, ...; a head's G*W pieces (acc rows, and their
+// (max, sum) pairs) are contiguous in the partial slots.  While the next
+// call's attention keeps the memory system busy an L2 read takes microseconds,
+// so the merge's time is set by the bytes it has in flight: each chunk of up
+// to MergeSeqShape::CK pieces (a whole head for one piece per attention CTA)
+// arrives by one bulk copy (TMA: its cost is per copy, not per byte), and the
+// block keeps kMergeSeqRing chunks, its whole share for a 16K-row shard, in
+// flight.  Per chunk warp 0 folds the (max, sum) pairs into the running
+// log2-sum-exp and writes each piece's weight to shared memory; then thread
+// (column, group) adds the weighted acc rows of every NG-th piece (four
+// independent sums, no branch), and the groups are added when the head is
+// done.  With an exchange the block posts each finished head's slices to every
+// rank at once and waits for the other ranks' words after its last head.
+constexpr int kMergeSeqThreads = 512;
+constexpr int kMergeSeqRing = 3;
+constexpr int kMergeSeqMaxUnits = 512;  // (head, 32-column slice) units of one block: hq <= 128
 
 template <int HD>
-__global__ void __launch_bounds__(512, 1) decode_merge_seq_kernel(DecodeArgs a, int G) {
+struct MergeSeqShape {
+    static constexpr int CK = HD == 128 ? 144 : 280;  // pieces per chunk slot (72 / 70 KB of acc rows)
+    static constexpr int NG = kMergeSeqThreads / HD;
+    static constexpr int off_bar = 0;
+    static constexpr int off_seq = 32;
+    static constexpr int off_w = off_seq + kMergeSeqMaxUnits * 4;  // [CK] weights, then keep, L, M
+    static constexpr int off_ml = (off_w + (CK + 32) * 4 + 15) / 16 * 16;
+    static constexpr int off_buf = (off_ml + kMergeSeqRing * (CK + 2) * 8 + 127) / 128 * 128;
+    static constexpr int off_red = off_buf + kMergeSeqRing * CK * HD * 4;
+    static constexpr int bytes = off_red + 2 * NG * HD * 4;  // group sums, double-buffered by head
+    static_assert(bytes <= 227 * 1024, "one block per SM");
+};
+
+template <int HD>
+__global__ void __launch_bounds__(kMergeSeqThreads, 1) decode_merge_seq_kernel(DecodeArgs a, int G) {
     pdl_trigger();
     pdl_wait();
-    constexpr int NS = HD / 32;
-    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    using Sh = MergeSeqShape<HD>;
+    constexpr int NS = HD / 32, NG = Sh::NG, CK = Sh::CK, NR = kMergeSeqRing;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Sh::off_bar);
+    uint32_t* s_seq = reinterpret_cast<uint32_t*>(smem + Sh::off_seq);
+    float* w_s = reinterpret_cast<float*>(smem + Sh::off_w);
+    float2* ml_s = reinterpret_cast<float2*>(smem + Sh::off_ml);
+    float* buf = reinterpret_cast<float*>(smem + Sh::off_buf);
+    float* red = reinterpret_cast<float*>(smem + Sh::off_red);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int col = tid % HD, grp = tid / HD;
     const int pos = seq_pos(a, 0);
     const bool ok = pos_ok(a, pos);
     const long long R = ok ? local_len(a, pos) : 0;
     const int W = a.warps_per_head, lw = __ffs(W) - 1;  // W is 1, 2, 4 or 8
     const bool xchg = a.x.peers != nullptr;
-    const size_t row_stride = a.shard_out ? (size_t)(HD + 2) : (size_t)HD;
+    const bool empty = !ok || R == 0;  // a rejected position: NaN; no rows in this shard: an empty partial
+    if (!empty && G == 1 && W == 1 && !xchg) return;  // written directly by the attention kernel
+    const int n_heads = (int)blockIdx.x < a.hq ? (a.hq - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
     const int n_pieces = G * W;
-    for (int u = blockIdx.x * nwarps + wib; u < a.hq * NS; u += gridDim.x * nwarps) {
-        const int h = u / NS, z = u % NS, col = z * 32 + lane;
-        float res, lse;
-        if (!ok || R == 0) {  // a rejected position: NaN; no rows in this shard: an empty partial
-            res = ok ? 0.f : __int_as_float(0x7fc00000);
-            lse = ok ? -INFINITY : __int_as_float(0x7fc00000);
-        } else {
-            if (G == 1 && W == 1 && !xchg) continue;  // written directly by the attention kernel
-            float M = -INFINITY, L = 0.f, acc = 0.f;
-            for (int k0 = 0; k0 < n_pieces; k0 += 32) {
-                // piece k -> slot (cta k/W, warp k%W) of head h; CTAs with empty slices
-                // (R < G) left nothing
-                const int k = k0 + lane, i = k >> lw;
-                float2 ml = make_float2(-INFINITY, 0.f);
-                if (k < n_pieces && (R >= G || slice_start(i, R, G) < slice_start(i + 1, R, G)))
-                    ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml + ((size_t)k * a.hq + h) * 2));
-                float ov[32];
-#pragma unroll
-                for (int j = 0; j < 32; j++)
-                    ov[j] = k0 + j < n_pieces ? __ldcg(a.part_o + ((size_t)(k0 + j) * a.hq + h) * HD + col) : 0.f;
-                float cm = ml.x;
-                for (int o = 16; o; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
-                const float Mn = fmaxf(M, cm);
-                if (Mn == -INFINITY) continue;  // nothing yet
-                const float keep = M == -INFINITY ? 0.f : ex2(M - Mn);
-                acc *= keep;
-                L *= keep;
-                const float w = ml.x == -INFINITY ? 0.f : ex2(ml.x - Mn);
-                float lw_sum = w * ml.y;
-                for (int o = 16; o; o >>= 1) lw_sum += __shfl_xor_sync(0xffffffffu, lw_sum, o);
-                L += lw_sum;
-#pragma unroll
-                for (int j = 0; j < 32; j++) {
-                    const float wj = __shfl_sync(0xffffffffu, w, j);
-                    if (wj != 0.f) acc += wj * ov[j];  // pieces of weight 0 may hold stale slots
-                }
-                M = Mn;
-            }
-            res = acc / L;
-            lse = M + __log2f(L);
-        }
+    const int n_chunks = (n_pieces + CK - 1) / CK;
+    const int cpc = ((n_pieces + n_chunks - 1) / n_chunks + 1) & ~1;  // pieces per chunk: even, <= CK
+    const int n_steps = empty ? 0 : n_heads * n_chunks;
+    auto head_of = [&](int hi) { return (int)blockIdx.x + hi * (int)gridDim.x; };
+    // a finished head: threads tid < HD hold column tid (warp z = slice z)
+    auto finish = [&](int hi, float res, float lse) {
+        const int h = head_of(hi);
         if (xchg) {
-            const float v = warp_exchange(a, h, z, NS, res, lse, lane);
-            a.x.out[(size_t)h * HD + col] = v;
+            const uint32_t seq = xchg_post(a, h, warp, NS, res, lse, lane);
+            if (lane == 0) s_seq[hi * NS + warp] = seq;
         } else {
+            const size_t row_stride = a.shard_out ? (size_t)(HD + 2) : (size_t)HD;
             float* dst = (a.shard_out ? a.shard_out : a.out) + (size_t)h * row_stride;
-            dst[col] = res;
-            if (a.shard_out && z == 0 && lane == 0) dst[HD] = lse;
+            dst[tid] = res;
+            if (a.shard_out && tid == 0) dst[HD] = lse;
+        }
+    };
+    // step -> (head hi, chunk c) in ring slot step % NR, by thread 0: two bulk
+    // copies (acc rows; the (max, sum) pairs rounded up to an even count, a
+    // 16-byte multiple: the slot after a head's last piece exists, n_slots > G*W,
+    // and chunk starts are even, n_slots even)
+    auto issue = [&](int step) {
+        const int hi = step / n_chunks, c = step % n_chunks, sl = step % NR;
+        const int k0 = c * cpc, cnt = min(cpc, n_pieces - k0);
+        const size_t first = (size_t)head_of(hi) * a.n_slots + k0;
+        const uint32_t ob = (uint32_t)cnt * HD * 4u, mb = (uint32_t)((cnt + 1) & ~1) * 8u;
+        mbar_arrive_expect_tx(&full[sl], ob + mb);
+        bulk_g2s(buf + (size_t)sl * CK * HD, a.part_o + first * HD, ob, &full[sl]);
+        bulk_g2s(ml_s + sl * (CK + 2), a.part_ml + first * 2, mb, &full[sl]);
+    };
+    if (tid == 0) {
+        for (int sl = 0; sl < NR; sl++) mbar_init(&full[sl], 1);
+        fence_mbar_init();
+        for (int j = 0; j < NR && j < n_steps; j++) issue(j);
+    }
+    __syncthreads();
+    if (empty && tid < HD)
+        for (int hi = 0; hi < n_heads; hi++)
+            finish(hi, ok ? 0.f : __int_as_float(0x7fc00000), ok ? -INFINITY : __int_as_float(0x7fc00000));
+    float M = -INFINITY, L = 0.f;  // running log2-sum-exp of the head (warp 0)
+    float acc = 0.f;               // this thread's group sum of column col
+    bool live = true;              // the waits have not timed out
+    for (int step = 0; step < n_steps; step++) {
+        const int hi = step / n_chunks, c = step % n_chunks, sl = step % NR;
+        const int k0 = c * cpc, cnt = min(cpc, n_pieces - k0);
+        if (live) live = mbar_wait(&full[sl], (uint32_t)((step / NR) & 1), a.status);
+        const float2* mls = ml_s + sl * (CK + 2);
+        const float* bs = buf + (size_t)sl * CK * HD;
+        if (warp == 0) {
+            // pieces of CTAs with empty slices (R < G) hold stale slots: weight 0
+            float cm = -INFINITY;
+            for (int j = lane; j < cnt; j += 32) {
+                const int i = (k0 + j) >> lw;
+                if (R >= G || slice_start(i, R, G) < slice_start(i + 1, R, G)) cm = fmaxf(cm, mls[j].x);
+            }
+            for (int o = 16; o; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
+            const float Mn = fmaxf(M, cm);
+            const float keep = Mn == -INFINITY ? 1.f : ex2(M - Mn);  // 0 while M = -inf
+            float ls = 0.f;
+            for (int j = lane; j < cnt; j += 32) {
+                const int i = (k0 + j) >> lw;
+                const bool v = Mn != -INFINITY && (R >= G || slice_start(i, R, G) < slice_start(i + 1, R, G));
+                const float wj = v ? ex2(mls[j].x - Mn) : 0.f;
+                w_s[j] = wj;
+                if (v) ls += wj * mls[j].y;
+            }
+            for (int o = 16; o; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+            L = L * keep + ls;
+            M = Mn;
+            if (lane == 0) w_s[CK] = keep, w_s[CK + 1] = L, w_s[CK + 2] = M;
+        }
+        __syncthreads();  // weights of this chunk
+        // read now: warp 0 rewrites them in the next step, after the barrier below
+        const float keep = w_s[CK], Lh = w_s[CK + 1], Mh = w_s[CK + 2];
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        int j = grp;
+        for (; j + 3 * NG < cnt; j += 4 * NG) {
+            const float w0 = w_s[j], w1 = w_s[j + NG], w2 = w_s[j + 2 * NG], w3 = w_s[j + 3 * NG];
+            const float v0 = bs[j * HD + col], v1 = bs[(j + NG) * HD + col];
+            const float v2 = bs[(j + 2 * NG) * HD + col], v3 = bs[(j + 3 * NG) * HD + col];
+            s0 += w0 != 0.f ? w0 * v0 : 0.f;  // weight 0: a stale slot may hold anything
+            s1 += w1 != 0.f ? w1 * v1 : 0.f;
+            s2 += w2 != 0.f ? w2 * v2 : 0.f;
+            s3 += w3 != 0.f ? w3 * v3 : 0.f;
+        }
+        for (; j < cnt; j += NG) {
+            const float w0 = w_s[j];
+            s0 += w0 != 0.f ? w0 * bs[j * HD + col] : 0.f;
+        }
+        acc = acc * keep + ((s0 + s1) + (s2 + s3));
+        const bool last = c == n_chunks - 1;
+        float* rh = red + (hi & 1) * NG * HD;
+        if (last) rh[grp * HD + col] = acc;
+        __syncthreads();  // slot sl and the weights are read; group sums complete
+        // the slot is free: the chunk NR steps ahead goes into it
+        if (tid == 0 && step + NR < n_steps) issue(step + NR);
+        if (last) {
+            // the head is done: its group sums, in the half of red for its parity
+            // (the next head's sums may be written while the column threads still
+            // read these; the head after that writes here only after they passed
+            // another barrier)
+            if (tid < HD) {
+                float o = 0.f;
+#pragma unroll
+                for (int g2 = 0; g2 < NG; g2++) o += rh[g2 * HD + tid];
+                finish(hi, o / Lh, Mh + __log2f(Lh));
+            }
+            acc = 0.f;
+            M = -INFINITY, L = 0.f;
+        }
+    }
+    if (xchg) {
+        __syncthreads();  // s_seq complete
+        for (int u = warp; u < n_heads * NS; u += kMergeSeqThreads / 32) {
+            const int hi = u / NS, z = u % NS, h = head_of(hi);
+            a.x.out[(size_t)h * HD + z * 32 + lane] = xchg_collect(a, h, z, NS, s_seq[u], lane);
         }
     }
 }
@@ -593,17 +708,28 @@ __device__ __forceinline__ void q_fragments(const DecodeArgs& a, int b, int pos,
         for (int j = 0; j < V; j++) w[j] = a.qn_w[V * lane + j];
     }
     const float* qb = a.q + ((size_t)b * a.hq + (size_t)kvh * G_q) * HD;
+    // four heads at a time; the next four heads' loads are issued before this
+    // group's arithmetic, so their latency overlaps it
+    Vec<HD> xn[4];
+    auto load4 = [&](int u0) {
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            if (u0 + u < G_q) vec_load<HD>(xn[u], qb, (size_t)(u0 + u) * HD, PICOATTN_DTYPE_F32, lane);
+            else
+#pragma unroll
+                for (int j = 0; j < V; j++) xn[u].x[j] = 0.f;
+        }
+    };
+    load4(0);
     for (int u0 = 0; u0 < G_q; u0 += 4) {
         Vec<HD> x[4];
         bool live[4];
 #pragma unroll
         for (int u = 0; u < 4; u++) {
+            x[u] = xn[u];
             live[u] = u0 + u < G_q;
-            if (live[u]) vec_load<HD>(x[u], qb, (size_t)(u0 + u) * HD, PICOATTN_DTYPE_F32, lane);
-            else
-#pragma unroll
-                for (int j = 0; j < V; j++) x[u].x[j] = 0.f;
         }
+        if (u0 + 4 < G_q) load4(u0 + 4);
         if (a.qn_w) vec_rmsnorm4<HD>(x, w, live, a.eps, sq, lane);
 #pragma unroll
         for (int u = 0; u < 4; u++) {
@@ -677,8 +803,9 @@ __device__ __forceinline__ void append_row(const DecodeArgs& a, int pos, int kvh
 }
 
 // Dynamic shared memory of the attention kernel: a 128-byte header (stage
-// barriers <= 48 B, then the single-sequence prefix, position, cache bases and
-// the new-row barrier), the compute warps' q staging areas, the K/V tile stages.
+// barriers <= 48 B, then the single-sequence prefix, position, cache bases, the
+// new-row barrier and the CTA's slice), the compute warps' q staging areas, the
+// K/V tile stages.
 constexpr int kAttnHdrBytes = 128;
 constexpr int kAttnMaxSmem = 227 * 1024;
 __host__ __device__ constexpr int attn_qstage_bytes(int compute_warps, int hd) { return compute_warps * 4 * hd * 4; }
@@ -688,7 +815,6 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int NW = a.compute_warps, W = a.warps_per_head, T = a.tile_rows;
-    const int G = gridDim.x, cta = blockIdx.x;
     // The merge kernel may launch now: it waits for this grid to complete.
     pdl_trigger();
     const uint32_t row_bytes = (uint32_t)a.kvd * 2u;
@@ -700,6 +826,7 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
     int* s_pos = reinterpret_cast<int*>(smem + 64);
     uint16_t** s_base = reinterpret_cast<uint16_t**>(smem + 72);
     uint64_t* row_ready = reinterpret_cast<uint64_t*>(smem + 88);  // fused append: the new row is in memory
+    long long* s_slice = reinterpret_cast<long long*>(smem + 96);  // R, R0, R1 (below)
     float* qstage = reinterpret_cast<float*>(smem + kAttnHdrBytes);
     uint8_t* tiles = smem + kAttnHdrBytes + attn_qstage_bytes(NW, HD);
     const size_t slab = (size_t)a.layer * a.local_rows * a.kvd;
@@ -715,33 +842,61 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
     // before may still read the partial slots.  With several sequences the CTAs
     // wait for the prep kernel's row prefix sums first.  Every CTA waits before
     // it exits, so this grid completes after the kernels before it.
-    const long long* prefix = a.prefix;
-    if (a.n_seqs == 1) {
-        if (threadIdx.x == 0) {
-            const int p = seq_pos(a, 0);
-            s_pos[0] = p;
-            s_prefix[0] = 0;
-            s_prefix[1] = pos_ok(a, p) ? local_len(a, p) : 0;
-            if (a.fused_append && !pos_ok(a, p) && cta == 0) atomicOr(a.status, PICOATTN_DEV_BAD_POS);
-        } else if (threadIdx.x == 32) {  // the cache bases, loaded alongside the position
-            s_base[0] = seq_kcache(a, 0);
-            s_base[1] = seq_vcache(a, 0);
+    //
+    // The producer warp sets the CTA up (position, cache bases, barriers, its
+    // slice) and starts streaming at once; the compute warps of a fused call
+    // rotate q meanwhile (they load the position themselves) and meet the
+    // producer's setup at a named barrier.
+    const long long* prefix = a.n_seqs == 1 ? s_prefix : a.prefix;
+    if (a.n_seqs != 1) pdl_wait();
+    uint32_t qa[HD / 16][4];  // the q rows of this compute warp's KV head (MMA A operand)
+    constexpr int kSetupBar = 1;
+    if (warp == NW) {
+        if (a.n_seqs == 1) {
+            if (lane == 0) {
+                const int p = seq_pos(a, 0);
+                s_pos[0] = p;
+                s_prefix[0] = 0;
+                s_prefix[1] = pos_ok(a, p) ? local_len(a, p) : 0;
+                if (a.fused_append && !pos_ok(a, p) && blockIdx.x == 0) atomicOr(a.status, PICOATTN_DEV_BAD_POS);
+            } else if (lane == 1) {  // the cache bases, loaded alongside the position
+                s_base[0] = seq_kcache(a, 0);
+                s_base[1] = seq_vcache(a, 0);
+            }
+            __syncwarp();
         }
-        prefix = s_prefix;
+        if (lane == 0) {
+            for (int s = 0; s < a.stages; s++) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], (uint32_t)NW);
+            }
+            mbar_init(row_ready, (uint32_t)a.hkv);  // one writer warp per KV head
+            fence_mbar_init();
+            // this CTA's slice [R0, R1) of the R concatenated rows, computed once
+            const int G = (int)gridDim.x, cta = (int)blockIdx.x;
+            const long long R = prefix[a.n_seqs];
+            s_slice[0] = R;
+            if ((unsigned long long)R * (unsigned)G < (1ull << 32)) {  // the same quotients in 32 bits
+                const unsigned r = (unsigned)R, g = (unsigned)G, c = (unsigned)cta;
+                s_slice[1] = c * r / g;
+                s_slice[2] = (c + 1u) * r / g;
+            } else {
+                s_slice[1] = slice_start(cta, R, G);
+                s_slice[2] = slice_start(cta + 1, R, G);
+            }
+        }
+        __syncwarp();
+        named_bar_arrive(kSetupBar, blockDim.x);
     } else {
-        pdl_wait();
-    }
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < a.stages; s++) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], (uint32_t)NW);
+        if (a.fused_append) {  // one sequence: q from the caller's buffer, rotated here
+            int p = 0;
+            if (lane == 0) p = seq_pos(a, 0);
+            p = __shfl_sync(0xffffffffu, p, 0);
+            q_fragments<HD>(a, 0, p, warp / W, qstage + warp * 4 * HD, lane, qa);
         }
-        mbar_init(row_ready, (uint32_t)a.hkv);  // one writer warp per KV head
-        fence_mbar_init();
+        named_bar_sync(kSetupBar, blockDim.x);
     }
-    __syncthreads();
-    const long long R = prefix[a.n_seqs];
-    const long long R0 = slice_start(cta, R, G), R1 = slice_start(cta + 1, R, G);
+    const long long R = s_slice[0], R0 = s_slice[1], R1 = s_slice[2];
     if (R0 >= R1) {
         pdl_wait();
         return;
@@ -818,10 +973,7 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
     }
 
     for_each_segment(a, prefix, R0, R1, [&](int b, int r0, int r1, bool whole, int) {
-        uint32_t qa[HD / 16][4];
-        if (a.fused_append) {
-            q_fragments<HD>(a, b, s_pos[0], kvh, sq, lane, qa);
-        } else {
+        if (!a.fused_append) {
             // q rotated by the prep kernel (finished: waited for above or before
             // the new row's tile, which every slice of one sequence reaches last)
             if (!dep_done) {
@@ -916,7 +1068,7 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
         l[1] += __shfl_xor_sync(0xffffffffu, l[1], 1);
         l[1] += __shfl_xor_sync(0xffffffffu, l[1], 2);
         const bool direct = whole && W == 1 && a.x.peers == nullptr;
-        const size_t pbase = ((size_t)(cta + b) * W + wi) * a.hq;
+        const size_t slot = (size_t)(blockIdx.x + b) * W + wi;
 #pragma unroll
         for (int half = 0; half < 2; half++) {
             const int r = gid + 8 * half;
@@ -933,12 +1085,13 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
                     if (a.shard_out && tig == 0)  // log2-sum-exp of this shard's scores
                         a.shard_out[((size_t)b * a.hq + h) * (HD + 2) + HD] = m[half] + __log2f(l[half]);
                 } else {
-                    float* od = a.part_o + (pbase + h) * HD + 2 * tig;
+                    const size_t pi = (size_t)h * a.n_slots + slot;
+                    float* od = a.part_o + pi * HD + 2 * tig;
 #pragma unroll
                     for (int i = 0; i < HD / 8; i++)
                         *reinterpret_cast<float2*>(od + i * 8) = make_float2(o[i][2 * half], o[i][2 * half + 1]);
                     if (tig == 0)
-                        *reinterpret_cast<float2*>(a.part_ml + (pbase + h) * 2) = make_float2(m[half], l[half]);
+                        *reinterpret_cast<float2*>(a.part_ml + pi * 2) = make_float2(m[half], l[half]);
                 }
             }
         }
@@ -980,7 +1133,8 @@ cudaError_t launch_decode_hd(const DecodeArgs& a_in, const DecodePlan& plan, cud
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(decode_merge_kernel<HD, 32>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(decode_merge_seq_kernel<HD>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+            e = cudaFuncSetAttribute(decode_merge_seq_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     MergeSeqShape<HD>::bytes);
         if (e != cudaSuccess) return e;
         attr_done = true;
     }
@@ -997,8 +1151,8 @@ cudaError_t launch_decode_hd(const DecodeArgs& a_in, const DecodePlan& plan, cud
         e = launch_pdl(decode_attn_kernel<HD>, dim3((unsigned)plan.grid_ctas), dim3((plan.compute_warps + 1) * 32),
                        (size_t)plan.smem_bytes, stream, a);
     if (e == cudaSuccess && (stages & PICOATTN_STAGE_COMBINE) && a.n_seqs == 1) {
-        e = launch_pdl(decode_merge_seq_kernel<HD>, dim3((unsigned)plan.merge_blocks), dim3(512), 0, stream, a,
-                       plan.grid_ctas);
+        e = launch_pdl(decode_merge_seq_kernel<HD>, dim3((unsigned)plan.merge_blocks), dim3(kMergeSeqThreads),
+                       (size_t)MergeSeqShape<HD>::bytes, stream, a, plan.grid_ctas);
     } else if (e == cudaSuccess && (stages & PICOATTN_STAGE_COMBINE)) {
         // column slices: the narrowest of 32 or 64 columns that keeps the grid
         // within one block per SM (a block beside each attention CTA of the next
@@ -1070,7 +1224,8 @@ bool make_decode_plan(const picoattn_config_t& cfg, int n_seqs, int max_ctx, Dec
     // pieces per sequence <= grid_ctas * warps_per_head; the merge kernel holds
     // them in kMergeMaxPieces shared-memory slots
     if (p.max_grid * p.warps_per_head > kMergeMaxPieces) return false;
-    const size_t slots = (size_t)(p.max_grid + n_seqs) * p.warps_per_head;
+    p.n_slots = ((p.max_grid + n_seqs) * p.warps_per_head + 1) & ~1;
+    const size_t slots = (size_t)p.n_slots;
     size_t off = kWsHeaderBytes;
     p.ws_prefix = off;
     off = align_up(off + (size_t)(n_seqs + 1) * 8, 256);

@@ -104,6 +104,7 @@ extern "C" int32_t picoattn_decode_noalloc(const picoattn_config_t* cfg, int32_t
     a.q_rot = reinterpret_cast<float*>(w + plan.ws_qrot);
     a.part_ml = reinterpret_cast<float*>(w + plan.ws_ml);
     a.part_o = reinterpret_cast<float*>(w + plan.ws_o);
+    a.n_slots = plan.n_slots;
     a.prefix = reinterpret_cast<long long*>(w + plan.ws_prefix);
     a.row_offset = 0;
     a.local_rows = cfg->max_seq_len;

@@ -31,6 +31,7 @@ struct DecodePlan {
     int grid_ctas;        // persistent CTAs of the attention kernel
     int merge_blocks;     // one sequence: blocks of the merge kernel, on SMs the attention grid leaves free
     int max_grid;         // upper bound on grid_ctas (sizes the partial slots)
+    int n_slots;          // partial slots per head: (max_grid + n_seqs) * warps_per_head, rounded up to even
     int smem_bytes;       // dynamic shared memory per CTA
     size_t ws_prefix, ws_qrot, ws_ml, ws_o, ws_total;  // workspace offsets and size
 };
@@ -77,8 +78,9 @@ struct DecodeArgs {
     int row_offset;            // absolute position of local cache row 0 (0 unless the rows are sharded)
     int local_rows;            // cache rows per layer in the local slab (max_seq unless sharded)
     float* shard_out;          // non-null: write [n_seqs][hq][hd+2] = (acc/sum, log2-sum-exp) instead of out
-    float* part_ml;            // [slot][warp][hq][2]  (max, sum) in log2 units; slot = cta + seq
-    float* part_o;             // [slot][warp][hq][hd]
+    float* part_ml;            // [hq][n_slots][2]  (max, sum) in log2 units; slot = (cta + seq) * warps_per_head + warp
+    float* part_o;             // [hq][n_slots][hd]  (a head's pieces are contiguous: the merge bulk-copies them)
+    int n_slots;
     int tile_rows, stages, warps_per_head, compute_warps;
     int fused_append;          // one sequence, all stages: the attention kernel appends the new k/v row itself
     XchgArgs x;                // the merge kernel exchanges the shard results (x.peers non-null)

@@ -85,6 +85,7 @@ int32_t decode_shard_impl(const picoattn_config_t* cfg, int32_t layer, int32_t n
     a.q_rot = reinterpret_cast<float*>(w + plan.ws_qrot);
     a.part_ml = reinterpret_cast<float*>(w + plan.ws_ml);
     a.part_o = reinterpret_cast<float*>(w + plan.ws_o);
+    a.n_slots = plan.n_slots;
     a.prefix = reinterpret_cast<long long*>(w + plan.ws_prefix);
     a.row_offset = row_offset;
     a.local_rows = local_rows;
