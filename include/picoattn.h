@@ -387,6 +387,69 @@ int32_t picoattn_kvcp_unpack(const picoattn_config_t* cfg, const void* src, size
 #define PICOATTN_PREFILL_CTA_PAIR 2
 int32_t picoattn_prefill_kernel(const picoattn_config_t* cfg);
 
+/* ---- Projections around the attention step ---------------------------------
+ *
+ * The q/k/v projections with their biases (cpp/model.hpp:318-366) and the
+ * output projection with its bias and the residual add (cpp/model.hpp:420-427)
+ * on the GPU, for the weight formats TensorOps::matmul_bias multiplies with
+ * (cpp/tensor.hpp:110-143, formats cpp/quant.hpp:16-74).  Weights stay in
+ * their GGUF block layout, row-major as in the file (n_out rows of
+ * picoattn_weight_bytes(type, n_in, 1) bytes); each is turned into fp32 with
+ * the reference's dequantize_row_* arithmetic (bit-identical weights) and
+ * multiplied in fp32 (sums in the GPU's order: results agree to rounding).
+ * Biases are fp32 (the reference dequantises them once at load,
+ * cpp/model.hpp:948-983).  Weight pointers: 4-byte aligned; x, out: 16.
+ */
+#define PICOATTN_WT_F32  1
+#define PICOATTN_WT_F16  2
+#define PICOATTN_WT_Q4_0 3
+#define PICOATTN_WT_Q8_0 9
+#define PICOATTN_WT_Q4_K 13
+#define PICOATTN_WT_Q6_K 15
+
+/* Bytes of n_out rows of n_in weights of a PICOATTN_WT_* type (gguf_type_row_size,
+ * cpp/quant.hpp:170-175); 0 for an unsupported type or n_in not a multiple of
+ * the type's block (32, or 256 for Q4_K and Q6_K). */
+size_t picoattn_weight_bytes(int32_t w_type, int32_t n_in, int32_t n_out);
+
+/* out[v*n_out + d] = W[d,:] . x[v*n_in : (v+1)*n_in] (+ bias[d]) for v < n_vec
+ * (accumulate != 0: added to out, as vec_add does with the residual).
+ * Replaces TensorOps::matmul_bias (cpp/tensor.hpp:110-143) on the device. */
+int32_t picoattn_matvec(const void* w, int32_t w_type, const float* bias, int32_t n_in, int32_t n_out,
+                        int32_t n_vec, const float* x, float* out, int32_t accumulate, picoattn_stream_t stream);
+
+/* One layer's attention weights as the model file holds them. */
+typedef struct {
+    const void* wq;  /* [n_heads*head_dim][dim]   */
+    const void* wk;  /* [n_kv_heads*head_dim][dim] */
+    const void* wv;  /* [n_kv_heads*head_dim][dim] */
+    const void* wo;  /* [dim][n_heads*head_dim]   */
+    int32_t wq_type, wk_type, wv_type, wo_type;  /* PICOATTN_WT_* */
+    const float* bq; /* fp32 biases, or NULL */
+    const float* bk;
+    const float* bv;
+    const float* bo;
+} picoattn_layer_weights_t;
+
+size_t picoattn_decode_layer_workspace_size(const picoattn_config_t* cfg, int32_t dim, int32_t n_seqs,
+                                            int32_t max_ctx);
+
+/* The attention block of one layer for n_seqs sequences, from the normalised
+ * hidden state xb [n_seqs][dim] to the residual x [n_seqs][dim]:
+ *   q = Wq.xb + bq, k = Wk.xb + bk, v = Wv.xb + bv       (cpp/model.hpp:318-366)
+ *   QK-norm, RoPE, cache append at pos, attention        (picoattn_decode)
+ *   x += Wo.attn + bo                                    (cpp/model.hpp:420-427)
+ * in one stream-ordered chain (three projections in one kernel, the decode
+ * kernels, the output projection).  Caches, positions and norms as for
+ * picoattn_decode.  The workspace begins with a decode workspace: initialise
+ * it with picoattn_workspace_init; picoattn_workspace_status reads it. */
+int32_t picoattn_decode_layer(const picoattn_config_t* cfg, int32_t layer, int32_t dim, int32_t n_seqs,
+                              int32_t max_ctx, const float* xb, const picoattn_layer_weights_t* weights,
+                              const float* q_norm_w, const float* k_norm_w, const float* rope_cos,
+                              const float* rope_sin, uint16_t* const* k_cache, uint16_t* const* v_cache,
+                              const int32_t* pos, float* x, void* workspace, size_t workspace_bytes,
+                              picoattn_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -400,3 +400,156 @@ int ora_decode_batch(int B, int hq, int hkv, int hd, int rope_mode, float eps,
     run_tasks(batch_task, &ctx, B, n_threads);
     return 0;
 }
+
+/* ------------------------------------------------------------------------ */
+/* Projections: GGUF block dequantisation and the mat-vec                   */
+/* ------------------------------------------------------------------------ */
+
+/* gguf_type_block_size / gguf_type_quant_size, cpp/quant.hpp:137-166 */
+int ora_weight_block(int type, int* elems, int* bytes) {
+    int e = 0, b = 0;
+    switch (type) {
+        case 1: e = 1; b = 4; break;     /* F32 */
+        case 2: e = 1; b = 2; break;     /* F16 */
+        case 3: e = 32; b = 18; break;   /* Q4_0: fp16 d, 16 bytes of nibbles */
+        case 9: e = 32; b = 34; break;   /* Q8_0: fp16 d, 32 int8 */
+        case 13: e = 256; b = 144; break; /* Q4_K: d, dmin, 12 scale bytes, 128 nibble bytes */
+        case 15: e = 256; b = 210; break; /* Q6_K: 128 low, 64 high bytes, 16 int8 scales, d */
+        default: return 0;
+    }
+    if (elems) *elems = e;
+    if (bytes) *bytes = b;
+    return 1;
+}
+
+static uint16_t rd16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+/* get_scale_min_k4, cpp/quant.hpp:210-218 */
+static void scale_min_k4(int j, const uint8_t* q, int* sc, int* mn) {
+    if (j < 4) {
+        *sc = q[j] & 63;
+        *mn = q[j + 4] & 63;
+    } else {
+        *sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+        *mn = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+}
+
+void ora_dequant_row(const void* src, float* dst, int n, int type) {
+    const uint8_t* p = (const uint8_t*)src;
+    switch (type) {
+        case 1: memcpy(dst, src, (size_t)n * sizeof(float)); return;        /* quant.hpp:175-177 */
+        case 2:                                                           /* quant.hpp:180-185 */
+            for (int i = 0; i < n; i++) dst[i] = ora_f16_to_f32(rd16(p + 2 * i));
+            return;
+        case 3:                                                           /* quant.hpp:197-207 */
+            for (int b = 0; b < n / 32; b++, p += 18) {
+                const float d = ora_f16_to_f32(rd16(p));
+                for (int j = 0; j < 32; j++) {
+                    const int nib = j < 16 ? (p[2 + j] & 0xF) : (p[2 + j - 16] >> 4);
+                    dst[32 * b + j] = d * ((float)nib - 8.0f);
+                }
+            }
+            return;
+        case 9:                                                           /* quant.hpp:187-195 */
+            for (int b = 0; b < n / 32; b++, p += 34) {
+                const float d = ora_f16_to_f32(rd16(p));
+                for (int j = 0; j < 32; j++) dst[32 * b + j] = d * (float)(int8_t)p[2 + j];
+            }
+            return;
+        case 13:                                                          /* quant.hpp:220-251 */
+            for (int b = 0; b < n / 256; b++, p += 144) {
+                const float d = ora_f16_to_f32(rd16(p)), dmin = ora_f16_to_f32(rd16(p + 2));
+                const uint8_t* q = p + 16;
+                float* y = dst + 256 * b;
+                for (int j = 0; j < 4; j++, y += 64, q += 32) {
+                    int sc, mn;
+                    scale_min_k4(2 * j, p + 4, &sc, &mn);
+                    const float d1 = d * (float)sc, m1 = dmin * (float)mn;
+                    scale_min_k4(2 * j + 1, p + 4, &sc, &mn);
+                    const float d2 = d * (float)sc, m2 = dmin * (float)mn;
+                    for (int l = 0; l < 32; l++) y[l] = d1 * (float)(q[l] & 0xF) - m1;
+                    for (int l = 0; l < 32; l++) y[l + 32] = d2 * (float)(q[l] >> 4) - m2;
+                }
+            }
+            return;
+        case 15:                                                          /* quant.hpp:253-281 */
+            for (int b = 0; b < n / 256; b++, p += 210) {
+                const uint8_t* ql = p;
+                const uint8_t* qh = p + 128;
+                const int8_t* sc = (const int8_t*)(p + 192);
+                const float d = ora_f16_to_f32(rd16(p + 208));
+                float* y = dst + 256 * b;
+                for (int c = 0; c < 2; c++, y += 128, ql += 64, qh += 32) {
+                    const int is = 8 * c;
+                    for (int l = 0; l < 32; l++) {
+                        const int q1 = (int)((ql[l] & 0xF) | (((qh[l] >> 0) & 3) << 4)) - 32;
+                        const int q2 = (int)((ql[l + 32] & 0xF) | (((qh[l] >> 2) & 3) << 4)) - 32;
+                        const int q3 = (int)((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32;
+                        const int q4 = (int)((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32;
+                        const int il = is + l / 16;
+                        y[l] = d * (float)sc[il] * (float)q1;
+                        y[l + 32] = d * (float)sc[il + 2] * (float)q2;
+                        y[l + 64] = d * (float)sc[il + 4] * (float)q3;
+                        y[l + 96] = d * (float)sc[il + 6] * (float)q4;
+                    }
+                }
+            }
+            return;
+        default:
+            for (int i = 0; i < n; i++) dst[i] = 0.f;
+    }
+}
+
+/* vec_dot_f32_f32 with PICOLM_SSE2 (cpp/quant.hpp:296-323): two 4-lane
+ * accumulators over 8 elements per step (product rounded, then added), the
+ * lanes summed (v0+v2)+(v1+v3) (hsum_sse), then the tail in order. */
+static float dot_f32(const float* w, const float* x, int n) {
+    float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
+    int i = 0;
+    for (; i + 7 < n; i += 8)
+        for (int j = 0; j < 4; j++) {
+            a0[j] = a0[j] + w[i + j] * x[i + j];
+            a1[j] = a1[j] + w[i + 4 + j] * x[i + 4 + j];
+        }
+    float v[4];
+    for (int j = 0; j < 4; j++) v[j] = a0[j] + a1[j];
+    float sum = (v[0] + v[2]) + (v[1] + v[3]);
+    for (; i < n; i++) sum += w[i] * x[i];
+    return sum;
+}
+
+float ora_vec_dot(const void* row, const float* x, int n, int type) {
+    if (type == 1) return dot_f32((const float*)row, x, n);
+    if (type == 9) {  /* vec_dot_q8_0_f32, cpp/quant.hpp:325-343 */
+        const uint8_t* p = (const uint8_t*)row;
+        float sumf = 0.0f;
+        for (int b = 0; b < n / 32; b++, p += 34) {
+            const float d = ora_f16_to_f32(rd16(p));
+            float sum = 0.0f;
+            for (int j = 0; j < 32; j++) sum += (float)(int8_t)p[2 + j] * x[32 * b + j];
+            sumf += d * sum;
+        }
+        return sumf;
+    }
+    float* buf = (float*)malloc((size_t)n * sizeof(float));   /* cpp/quant.hpp:349-355 */
+    if (!buf) return 0.0f;
+    ora_dequant_row(row, buf, n, type);
+    const float s = dot_f32(buf, x, n);
+    free(buf);
+    return s;
+}
+
+void ora_matvec(const void* w, int type, const float* bias, int n_in, int n_out, int n_vec,
+                const float* x, float* out, int accumulate) {
+    int e = 0, b = 0;
+    if (!ora_weight_block(type, &e, &b)) return;
+    const size_t row_bytes = (size_t)(n_in / e) * (size_t)b;
+    for (int v = 0; v < n_vec; v++)
+        for (int d = 0; d < n_out; d++) {
+            float y = ora_vec_dot((const uint8_t*)w + (size_t)d * row_bytes, x + (size_t)v * n_in, n_in, type);
+            if (bias) y += bias[d];                              /* matmul_bias: vec_add of the bias */
+            float* o = out + (size_t)v * n_out + d;
+            *o = accumulate ? *o + y : y;                        /* the residual add, cpp/model.hpp:427 */
+        }
+}

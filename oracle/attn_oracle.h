@@ -99,6 +99,25 @@ int ora_decode_batch(int B, int hq, int hkv, int hd, int rope_mode, float eps,
                      uint16_t* const* kc, uint16_t* const* vc,
                      const int* pos, float* out, int n_threads);
 
+/*
+ * Projections around the attention step (TensorOps::matmul_bias,
+ * cpp/tensor.hpp:110-143) for the weight formats the C++ engine multiplies
+ * with.  type: GGUF tensor type (1 F32, 2 F16, 3 Q4_0, 9 Q8_0, 13 Q4_K,
+ * 15 Q6_K; cpp/quant.hpp:16-31).
+ */
+/* Weights per block and bytes per block (cpp/quant.hpp:137-166); 0 if unsupported. */
+int ora_weight_block(int type, int* elems, int* bytes);
+/* One row of n weights to fp32 (dequantize_row, cpp/quant.hpp:175-295). */
+void ora_dequant_row(const void* src, float* dst, int n, int type);
+/* W[row] . x in the reference's order (vec_dot, cpp/quant.hpp:304-358: the
+ * SSE2 two-accumulator order for F32 and the dequantised formats, per-block
+ * scalar sums for Q8_0). */
+float ora_vec_dot(const void* row, const float* x, int n, int type);
+/* out[v*n_out + d] = W[d].x[v] (+ bias[d]), or added to out (accumulate):
+ * matmul_bias then vec_add (cpp/model.hpp:420-427). */
+void ora_matvec(const void* w, int type, const float* bias, int n_in, int n_out, int n_vec,
+                const float* x, float* out, int accumulate);
+
 #ifdef __cplusplus
 }
 #endif

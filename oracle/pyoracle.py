@@ -67,7 +67,41 @@ class Oracle:
         L.ora_decode_batch.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
                                        _f32p, _f32p, _f32p, C.c_void_p, C.c_void_p,
                                        _f32p, _f32p, C.c_void_p, C.c_void_p, _i32p, _f32p, C.c_int]
+        L.ora_weight_block.restype = C.c_int
+        L.ora_weight_block.argtypes = [C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int)]
+        L.ora_dequant_row.argtypes = [C.c_void_p, _f32p, C.c_int, C.c_int]
+        L.ora_vec_dot.restype = C.c_float
+        L.ora_vec_dot.argtypes = [C.c_void_p, _f32p, C.c_int, C.c_int]
+        L.ora_matvec.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int, _f32p, _f32p,
+                                 C.c_int]
         self.L = L
+
+    def weight_block(self, wtype: int):
+        """(weights per block, bytes per block) of a GGUF type, or None."""
+        e, b = C.c_int(), C.c_int()
+        return (e.value, b.value) if self.L.ora_weight_block(wtype, C.byref(e), C.byref(b)) else None
+
+    def dequant(self, w: np.ndarray, wtype: int, n_in: int, n_out: int) -> np.ndarray:
+        """All n_out rows of a weight matrix (uint8 bytes) as fp32 [n_out, n_in]."""
+        e, b = self.weight_block(wtype)
+        row = n_in // e * b
+        w = np.ascontiguousarray(w, np.uint8).ravel()
+        out = np.empty((n_out, n_in), np.float32)
+        for d in range(n_out):
+            buf = np.empty(n_in, np.float32)
+            self.L.ora_dequant_row(w[d * row:(d + 1) * row].ctypes.data, buf, n_in, wtype)
+            out[d] = buf
+        return out
+
+    def matvec(self, w, wtype, bias, n_in, n_out, x, out=None, accumulate=False):
+        """out[v, d] = W[d] . x[v] (+ bias[d]) (+ out[v, d]) in the reference's order."""
+        w = np.ascontiguousarray(w, np.uint8).ravel()
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, n_in)
+        res = np.zeros((x.shape[0], n_out), np.float32) if out is None else np.ascontiguousarray(out, np.float32).copy()
+        b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        self.L.ora_matvec(w.ctypes.data, wtype, None if b is None else b.ctypes.data, n_in, n_out, x.shape[0],
+                          x, res, 1 if accumulate else 0)
+        return res
 
     def f32_to_f16(self, x: np.ndarray) -> np.ndarray:
         x = np.ascontiguousarray(x, np.float32).ravel()
@@ -197,7 +231,27 @@ class RefHarness:
             getattr(L, n).restype = C.c_int
         L.pref_kvcp_save.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, _u16p, _u16p, C.c_char_p, C.c_int]
         L.pref_kvcp_load.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, _u16p, _u16p, C.c_char_p]
+        L.pref_dequant_row.argtypes = [C.c_void_p, _f32p, C.c_int, C.c_int]
+        L.pref_matvec.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int, _f32p, _f32p]
         self.L = L
+
+    def dequant_row(self, row: np.ndarray, wtype: int, n: int) -> np.ndarray:
+        """The reference's dequantize_row (cpp/quant.hpp:283-295) of one row."""
+        row = np.ascontiguousarray(row, np.uint8)
+        out = np.empty(n, np.float32)
+        self.L.pref_dequant_row(row.ctypes.data, out, n, wtype)
+        return out
+
+    def matvec(self, w, wtype, bias, n_in, n_out, x):
+        """The reference's TensorOps::matmul_bias (cpp/tensor.hpp:110-143) per vector:
+        [n_vec, n_out]."""
+        w = np.ascontiguousarray(w, np.uint8).ravel()
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, n_in)
+        out = np.empty((x.shape[0], n_out), np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        self.L.pref_matvec(w.ctypes.data, wtype, None if b is None else b.ctypes.data, n_in, n_out, x.shape[0],
+                           x, out)
+        return out
 
     def kvcp_save(self, kc, vc, n_kv_heads, head_dim, path, n_pos):
         """The C engine's kvcache_save (picolm/model.c:884-926) of caches kc, vc

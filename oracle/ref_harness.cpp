@@ -451,4 +451,18 @@ const float* pref_full_rope_sin(void* hp) { return ((FullHarness*)hp)->model.sta
 uint16_t* pref_full_kcache(void* hp) { return ((FullHarness*)hp)->model.state.key_cache.data(); }
 uint16_t* pref_full_vcache(void* hp) { return ((FullHarness*)hp)->model.state.val_cache.data(); }
 
+// Projections with the reference's own code: one row dequantised
+// (dequantize_row, cpp/quant.hpp:283-295) and matmul_bias per vector
+// (cpp/tensor.hpp:110-143; the bias as the F32 array the engine keeps).
+void pref_dequant_row(const void* src, float* dst, int n, int type) {
+    dequantize_row(src, dst, n, (GGUFType)type);
+}
+void pref_matvec(const void* w, int type, const float* bias, int n_in, int n_out, int n_vec, const float* x,
+                 float* out) {
+    std::vector<float> scratch((size_t)n_out);
+    for (int v = 0; v < n_vec; v++)
+        TensorOps::matmul_bias(out + (size_t)v * n_out, x + (size_t)v * n_in, w, bias, n_in, n_out,
+                               (GGUFType)type, bias ? GGUFType::F32 : GGUFType::NONE, scratch.data());
+}
+
 }  // extern "C"

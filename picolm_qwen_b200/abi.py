@@ -49,6 +49,14 @@ ROPE_INTERLEAVED = 1
 DTYPE_F32 = 0
 DTYPE_F16 = 1
 
+# projection weight formats (GGUF tensor types)
+WT_F32 = 1
+WT_F16 = 2
+WT_Q4_0 = 3
+WT_Q8_0 = 9
+WT_Q4_K = 13
+WT_Q6_K = 15
+
 
 class Config(C.Structure):
     """picoattn_config_t."""
@@ -76,6 +84,15 @@ class Config(C.Structure):
     @property
     def q_dim(self) -> int:
         return self.n_heads * self.head_dim
+
+
+class LayerWeights(C.Structure):
+    """picoattn_layer_weights_t: device pointers and PICOATTN_WT_* types."""
+    _fields_ = [
+        ("wq", C.c_void_p), ("wk", C.c_void_p), ("wv", C.c_void_p), ("wo", C.c_void_p),
+        ("wq_type", C.c_int32), ("wk_type", C.c_int32), ("wv_type", C.c_int32), ("wo_type", C.c_int32),
+        ("bq", C.c_void_p), ("bk", C.c_void_p), ("bv", C.c_void_p), ("bo", C.c_void_p),
+    ]
 
 
 _P = C.c_void_p
@@ -126,6 +143,11 @@ PROTOTYPES = {
     "picoattn_kvcp_load": (_I, [_CFG, C.c_char_p, _P, _P, C.POINTER(C.c_int32), _P]),
     "picoattn_kvcp_pack": (_I, [_CFG, _I, _P, _P, _P, _Z, _P]),
     "picoattn_kvcp_unpack": (_I, [_CFG, _P, _Z, _P, _P, C.POINTER(C.c_int32), _P]),
+    "picoattn_weight_bytes": (_Z, [_I, _I, _I]),
+    "picoattn_matvec": (_I, [_P, _I, _P, _I, _I, _I, _P, _P, _I, _P]),
+    "picoattn_decode_layer_workspace_size": (_Z, [_CFG, _I, _I, _I]),
+    "picoattn_decode_layer": (_I, [_CFG, _I, _I, _I, _I, _P, C.POINTER(LayerWeights), _P, _P, _P, _P, _P, _P, _P,
+                                   _P, _P, _Z, _P]),
 }
 
 _lib = None

@@ -5,6 +5,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <initializer_list>
 
 #include <cuda_runtime.h>
 
@@ -43,7 +44,7 @@ int32_t decode_common(const picoattn_config_t* cfg, int32_t layer, int32_t n_seq
                       const float* q, const float* k, const float* v, const float* qn, const float* kn,
                       const float* rc, const float* rs, uint16_t* const* kcp, uint16_t* const* vcp,
                       uint16_t* kc1, uint16_t* vc1, const int32_t* pos_dev, int32_t pos_host, float* out,
-                      void* ws, size_t ws_bytes, cudaStream_t stream, uint32_t stages) {
+                      void* ws, size_t ws_bytes, cudaStream_t stream, uint32_t stages, int wait_inputs = 0) {
     int32_t st = picoattn_config_check(cfg);
     if (stages == 0 || (stages & ~PICOATTN_STAGE_ALL)) return PICOATTN_EINVAL;
     if (st != PICOATTN_OK) return st;
@@ -91,7 +92,26 @@ int32_t decode_common(const picoattn_config_t* cfg, int32_t layer, int32_t n_seq
     a.stages = plan.stages;
     a.warps_per_head = plan.warps_per_head;
     a.compute_warps = plan.compute_warps;
+    a.wait_inputs = wait_inputs;
     return cuda_status(launch_decode(a, plan, stream, stages));
+}
+
+// Workspace of picoattn_decode_layer: the decode workspace first (its status
+// header at offset 0), then q, k, v and the attention output, fp32.
+struct LayerWs {
+    size_t decode, q, k, v, attn, total;
+};
+bool layer_ws(const picoattn_config_t& cfg, int n_seqs, int max_ctx, LayerWs* l) {
+    DecodePlan plan;
+    if (!make_decode_plan(cfg, n_seqs, max_ctx, &plan)) return false;
+    const size_t qd = (size_t)cfg.n_heads * cfg.head_dim, kvd = (size_t)cfg.n_kv_heads * cfg.head_dim;
+    l->decode = 0;
+    l->q = align_up(plan.ws_total, 256);
+    l->k = align_up(l->q + (size_t)n_seqs * qd * 4, 256);
+    l->v = align_up(l->k + (size_t)n_seqs * kvd * 4, 256);
+    l->attn = align_up(l->v + (size_t)n_seqs * kvd * 4, 256);
+    l->total = align_up(l->attn + (size_t)n_seqs * qd * 4, 256);
+    return true;
 }
 
 }  // namespace
@@ -274,6 +294,92 @@ int32_t picoattn_prefill(const picoattn_config_t* cfg, int32_t layer, int32_t n_
     return picoattn_prefill_staged(cfg, layer, n_tok, start_pos, in_dtype, q, k, v, q_norm_w, k_norm_w, rope_cos,
                                    rope_sin, k_cache, v_cache, out, workspace, workspace_bytes, stream,
                                    PICOATTN_STAGE_PREPARE | PICOATTN_STAGE_ATTEND);
+}
+
+size_t picoattn_weight_bytes(int32_t w_type, int32_t n_in, int32_t n_out) {
+    const int be = weight_block_elems(w_type);
+    if (be == 0 || n_in <= 0 || n_out <= 0 || n_in % be != 0) return 0;
+    MatvecPart p;
+    float dummy;
+    if (!matvec_part(w_type, &dummy, nullptr, n_in, n_out, &dummy, 0, &p)) return 0;
+    return p.row_bytes * (size_t)n_out;
+}
+
+int32_t picoattn_matvec(const void* w, int32_t w_type, const float* bias, int32_t n_in, int32_t n_out,
+                        int32_t n_vec, const float* x, float* out, int32_t accumulate, picoattn_stream_t stream) {
+    if (!w || !x || !out || n_vec <= 0 || n_in <= 0 || n_out <= 0) return PICOATTN_EINVAL;
+    if (weight_block_elems(w_type) == 0) return PICOATTN_EUNSUPPORTED;
+    if (!aligned16(x) || !aligned16(out) || ((uintptr_t)w & 3u)) return PICOATTN_EINVAL;
+    MatvecArgs a{};
+    if (!matvec_part(w_type, w, bias, n_in, n_out, out, (size_t)n_out, &a.part[0])) return PICOATTN_EINVAL;
+    const int32_t st = device_ok();
+    if (st != PICOATTN_OK) return st;
+    a.n_parts = 1;
+    a.n_in = n_in;
+    a.n_vec = n_vec;
+    a.rows_total = n_out;
+    a.accumulate = accumulate ? 1 : 0;
+    a.x = x;
+    return cuda_status(launch_matvec(a, (cudaStream_t)stream));
+}
+
+size_t picoattn_decode_layer_workspace_size(const picoattn_config_t* cfg, int32_t dim, int32_t n_seqs,
+                                            int32_t max_ctx) {
+    if (picoattn_config_check(cfg) != PICOATTN_OK || dim <= 0 || n_seqs <= 0 || max_ctx <= 0) return 0;
+    LayerWs l;
+    return layer_ws(*cfg, n_seqs, max_ctx, &l) ? l.total : 0;
+}
+
+int32_t picoattn_decode_layer(const picoattn_config_t* cfg, int32_t layer, int32_t dim, int32_t n_seqs,
+                              int32_t max_ctx, const float* xb, const picoattn_layer_weights_t* wt,
+                              const float* q_norm_w, const float* k_norm_w, const float* rope_cos,
+                              const float* rope_sin, uint16_t* const* k_cache, uint16_t* const* v_cache,
+                              const int32_t* pos, float* x, void* workspace, size_t workspace_bytes,
+                              picoattn_stream_t stream) {
+    int32_t st = picoattn_config_check(cfg);
+    if (st != PICOATTN_OK) return st;
+    if (!wt || !xb || !x || !k_cache || !v_cache || !pos || !workspace || dim <= 0 || n_seqs <= 0)
+        return PICOATTN_EINVAL;
+    if (!aligned16(xb) || !aligned16(x) || !aligned16(workspace)) return PICOATTN_EINVAL;
+    const int qd = cfg->n_heads * cfg->head_dim, kvd = cfg->n_kv_heads * cfg->head_dim;
+    LayerWs l;
+    if (max_ctx <= 0 || max_ctx > cfg->max_seq_len) return PICOATTN_ERANGE;
+    if (!layer_ws(*cfg, n_seqs, max_ctx, &l)) return PICOATTN_EUNSUPPORTED;
+    if (workspace_bytes < l.total) return PICOATTN_ENOSPACE;
+    uint8_t* w = static_cast<uint8_t*>(workspace);
+    float* q = reinterpret_cast<float*>(w + l.q);
+    float* k = reinterpret_cast<float*>(w + l.k);
+    float* v = reinterpret_cast<float*>(w + l.v);
+    float* attn = reinterpret_cast<float*>(w + l.attn);
+    for (int32_t t : {wt->wq_type, wt->wk_type, wt->wv_type, wt->wo_type})
+        if (weight_block_elems(t) == 0) return PICOATTN_EUNSUPPORTED;
+    MatvecArgs qkv{};
+    if (!matvec_part(wt->wq_type, wt->wq, wt->bq, dim, qd, q, (size_t)qd, &qkv.part[0]) ||
+        !matvec_part(wt->wk_type, wt->wk, wt->bk, dim, kvd, k, (size_t)kvd, &qkv.part[1]) ||
+        !matvec_part(wt->wv_type, wt->wv, wt->bv, dim, kvd, v, (size_t)kvd, &qkv.part[2]))
+        return PICOATTN_EINVAL;
+    MatvecArgs o{};
+    if (!matvec_part(wt->wo_type, wt->wo, wt->bo, qd, dim, x, (size_t)dim, &o.part[0])) return PICOATTN_EINVAL;
+    st = device_ok();
+    if (st != PICOATTN_OK) return st;
+    const cudaStream_t s = (cudaStream_t)stream;
+    qkv.n_parts = 3;
+    qkv.n_in = dim;
+    qkv.n_vec = n_seqs;
+    qkv.rows_total = qd + 2 * kvd;
+    qkv.x = xb;
+    st = cuda_status(launch_matvec(qkv, s));
+    if (st != PICOATTN_OK) return st;
+    st = decode_common(cfg, layer, n_seqs, max_ctx, q, k, v, q_norm_w, k_norm_w, rope_cos, rope_sin, k_cache,
+                       v_cache, nullptr, nullptr, pos, 0, attn, workspace, l.q, s, PICOATTN_STAGE_ALL, 1);
+    if (st != PICOATTN_OK) return st;
+    o.n_parts = 1;
+    o.n_in = qd;
+    o.n_vec = n_seqs;
+    o.rows_total = dim;
+    o.accumulate = 1;
+    o.x = attn;
+    return cuda_status(launch_matvec(o, s));
 }
 
 }  // extern "C"

@@ -889,10 +889,13 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
         named_bar_arrive(kSetupBar, blockDim.x);
     } else {
         if (a.fused_append) {  // one sequence: q from the caller's buffer, rotated here
+            if (a.wait_inputs) pdl_wait();  // written by the projection kernel before this one
             int p = 0;
             if (lane == 0) p = seq_pos(a, 0);
             p = __shfl_sync(0xffffffffu, p, 0);
-            q_fragments<HD>(a, 0, p, warp / W, qstage + warp * 4 * HD, lane, qa);
+            // a rejected position leaves no rows (the CTA exits below) and must not
+            // index the RoPE table
+            if (pos_ok(a, p)) q_fragments<HD>(a, 0, p, warp / W, qstage + warp * 4 * HD, lane, qa);
         }
         named_bar_sync(kSetupBar, blockDim.x);
     }

@@ -83,6 +83,7 @@ struct DecodeArgs {
     int n_slots;
     int tile_rows, stages, warps_per_head, compute_warps;
     int fused_append;          // one sequence, all stages: the attention kernel appends the new k/v row itself
+    int wait_inputs;           // q/k/v come from the kernel before (projections): wait for it before reading them
     XchgArgs x;                // the merge kernel exchanges the shard results (x.peers non-null)
 };
 
@@ -97,6 +98,27 @@ int32_t decode_shard_impl(const picoattn_config_t* cfg, int32_t layer, int32_t n
                           uint16_t* const* kcp, uint16_t* const* vcp, const int32_t* pos, float* partial, void* ws,
                           size_t ws_bytes, cudaStream_t stream, const XchgArgs* x);
 cudaError_t launch_decode(const DecodeArgs& a, const DecodePlan& plan, cudaStream_t stream, unsigned stages);
+int device_sm_count();
+
+// Projections (matvec.cu): out[v * out_stride + row] = W[row] . x[v] (+ bias[row]),
+// or added into out.  Up to three matrices that read the same x in one launch.
+struct MatvecPart {
+    const uint8_t* w;   // n_out rows of row_bytes, in the GGUF block layout of `type`
+    const float* bias;  // [n_out] or null
+    float* out;
+    size_t out_stride, row_bytes;
+    int type, n_out, block_bytes;
+};
+struct MatvecArgs {
+    MatvecPart part[3];
+    int n_parts, n_in, n_vec, rows_total, accumulate;
+    const float* x;  // [n_vec][n_in], 16-byte aligned
+};
+int weight_block_elems(int type);  // weights per block of a PICOATTN_WT_* type (0: unsupported)
+int weight_block_bytes(int type);
+bool matvec_part(int type, const void* w, const float* bias, int n_in, int n_out, float* out, size_t out_stride,
+                 MatvecPart* p);
+cudaError_t launch_matvec(const MatvecArgs& a, cudaStream_t stream);
 
 struct PrefillArgs {
     int hq, hkv, g, hd, kvd, max_seq, layer, n_tok, start, n_qtiles;

@@ -30,6 +30,27 @@ def stream_handle(stream: torch.cuda.Stream | None = None) -> int:
     return s.cuda_stream
 
 
+def matvec(w: torch.Tensor, w_type: int, n_in: int, n_out: int, x: torch.Tensor, out: torch.Tensor,
+           bias: torch.Tensor | None = None, accumulate: bool = False,
+           stream: torch.cuda.Stream | None = None) -> None:
+    """out[v] (=|+=) W . x[v] (+ bias) on the device (TensorOps::matmul_bias,
+    cpp/tensor.hpp:110-143); w holds the GGUF blocks as uint8."""
+    n_vec = x.numel() // n_in
+    st = abi.lib().picoattn_matvec(w.data_ptr(), w_type, abi.ptr(bias), n_in, n_out, n_vec, x.data_ptr(),
+                                   out.data_ptr(), 1 if accumulate else 0, stream_handle(stream))
+    abi.check(st, "picoattn_matvec")
+
+
+class LayerProj:
+    """One layer's q/k/v/o weights on the device (uint8 GGUF blocks) and fp32 biases."""
+
+    def __init__(self, wq, wk, wv, wo, types, bq=None, bk=None, bv=None, bo=None):
+        self.tensors = (wq, wk, wv, wo, bq, bk, bv, bo)  # kept alive with the struct
+        self.struct = abi.LayerWeights(
+            wq.data_ptr(), wk.data_ptr(), wv.data_ptr(), wo.data_ptr(), *types,
+            abi.ptr(bq), abi.ptr(bk), abi.ptr(bv), abi.ptr(bo))
+
+
 class AttnState:
     """KV caches of n_seqs sequences in the reference layout plus RoPE tables.
 
@@ -72,6 +93,28 @@ class AttnState:
             pos.data_ptr(), out.data_ptr(), self.workspace.data_ptr(), self.workspace.numel(),
             stream_handle(stream))
         abi.check(st, "picoattn_decode")
+
+    def decode_layer(self, layer: int, dim: int, xb: torch.Tensor, proj: LayerProj, pos: torch.Tensor,
+                     x: torch.Tensor, q_norm_w: torch.Tensor | None = None, k_norm_w: torch.Tensor | None = None,
+                     stream: torch.cuda.Stream | None = None) -> None:
+        """The attention block from the normalised hidden state xb [B, dim] into
+        the residual x [B, dim] (cpp/model.hpp:318-427): projections, decode step,
+        output projection added to x."""
+        B = xb.shape[0]
+        if getattr(self, "layer_ws", None) is None or self.layer_ws_key != (dim, B):
+            n = abi.lib().picoattn_decode_layer_workspace_size(C.byref(self.cfg), dim, B, self.max_ctx)
+            if n == 0:
+                raise abi.PicoAttnError(abi.PICOATTN_EUNSUPPORTED, "decode_layer_workspace_size")
+            self.layer_ws = torch.zeros(n, dtype=torch.uint8, device=self.device)
+            self.layer_ws_key = (dim, B)
+            abi.check(abi.lib().picoattn_workspace_init(self.layer_ws.data_ptr(), n, stream_handle(stream)),
+                      "ws init")
+        st = abi.lib().picoattn_decode_layer(
+            C.byref(self.cfg), layer, dim, B, self.max_ctx, xb.data_ptr(), C.byref(proj.struct),
+            abi.ptr(q_norm_w), abi.ptr(k_norm_w), self.rope_cos.data_ptr(), self.rope_sin.data_ptr(),
+            self.k_ptrs.data_ptr(), self.v_ptrs.data_ptr(), pos.data_ptr(), x.data_ptr(),
+            self.layer_ws.data_ptr(), self.layer_ws.numel(), stream_handle(stream))
+        abi.check(st, "picoattn_decode_layer")
 
     def decode_one(self, layer: int, pos: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                    out: torch.Tensor, q_norm_w: torch.Tensor | None = None, k_norm_w: torch.Tensor | None = None,

@@ -1,0 +1,179 @@
+"""Projections on the B200 against the reference's own mat-vec.
+
+picoattn_matvec is checked against TensorOps::matmul_bias compiled from the
+reference's sources (oracle/_ref) for every weight format.  The weights are
+dequantised bit-identically; the fp32 dot product sums in another order, so
+the tolerance is on the sum's magnitude:
+    |gpu - ref| <= 3e-5 * (sum_i |w_i x_i| + |bias|)      (elementwise)
+picoattn_decode_layer (projections + decode step + output projection into the
+residual) is checked against the same chain built from the reference's
+mat-vec and the oracle's decode step, with the attention-output tolerance
+    |gpu - ref| <= 2e-3 + 1e-2 * |ref|.
+"""
+import numpy as np
+import pytest
+
+from tests import weightgen as wg
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+FORMATS = sorted(wg.BLOCK)
+
+
+@pytest.fixture(scope="module")
+def cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from picolm_qwen_b200 import abi
+    assert abi.lib().picoattn_device_check() == 0, "not an sm_100 device"
+    return torch.device("cuda")
+
+
+@pytest.fixture(scope="module")
+def ref():
+    from oracle.pyoracle import RefHarness
+    return RefHarness()
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def magnitude(oracle, w, wtype, n_in, n_out, x, bias):
+    W = oracle.dequant(w, wtype, n_in, n_out).astype(np.float64)
+    m = np.abs(x.astype(np.float64)) @ np.abs(W).T
+    return m + (0 if bias is None else np.abs(bias.astype(np.float64)))
+
+
+@pytest.mark.parametrize("wtype", FORMATS, ids=[wg.NAMES[t] for t in FORMATS])
+@pytest.mark.parametrize("n_in,n_out,n_vec", [(3584, 512, 1), (1024, 1000, 3), (4096, 64, 8), (512, 33, 2)])
+def test_matvec_vs_reference(cuda, oracle, ref, wtype, n_in, n_out, n_vec):
+    from picolm_qwen_b200.runtime import matvec
+    rng = np.random.default_rng(wtype * 7919 + n_in + n_vec)
+    w = wg.make(wtype, n_in, n_out, rng)
+    x = rng.standard_normal((n_vec, n_in)).astype(np.float32)
+    bias = rng.standard_normal(n_out).astype(np.float32) if n_vec != 2 else None
+    exp = ref.matvec(w, wtype, bias, n_in, n_out, x)
+    out = torch.full((n_vec, n_out), float("nan"), device="cuda")
+    matvec(dev(w), wtype, n_in, n_out, dev(x), out, None if bias is None else dev(bias))
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    bound = 3e-5 * magnitude(oracle, w, wtype, n_in, n_out, x, bias)
+    err = np.abs(got.astype(np.float64) - exp)
+    assert (err <= bound).all(), f"max err {err.max():.3g}, bound there {bound.flat[err.argmax()]:.3g}"
+    # accumulate: the residual add (vec_add) on top of the previous contents
+    res0 = rng.standard_normal((n_vec, n_out)).astype(np.float32)
+    out = dev(res0)
+    matvec(dev(w), wtype, n_in, n_out, dev(x), out, None if bias is None else dev(bias), accumulate=True)
+    torch.cuda.synchronize()
+    err = np.abs(out.cpu().numpy().astype(np.float64) - (res0.astype(np.float64) + exp))
+    assert (err <= bound + 1e-6 * np.abs(res0)).all()
+
+
+SHAPES = {
+    # name: (hq, hkv, hd, dim, rope_mode, qk_norm, types q/k/v/o, biases)
+    "qwen2.5-7b-q4km": (28, 4, 128, 3584, 0, False, (13, 13, 15, 13), True),
+    "qwen3-8b-q8_0": (32, 8, 128, 4096, 0, True, (9, 9, 9, 9), False),
+    "tinyllama-f16": (32, 4, 64, 2048, 1, False, (2, 2, 2, 2), False),
+    "small-f32-q4_0": (8, 2, 128, 1024, 0, True, (1, 3, 3, 1), True),
+}
+
+
+@pytest.mark.parametrize("name", sorted(SHAPES))
+def test_decode_layer_vs_reference_chain(cuda, oracle, ref, name):
+    from picolm_qwen_b200 import abi
+    from picolm_qwen_b200.runtime import AttnState, LayerProj
+    hq, hkv, hd, dim, mode, qk_norm, types, biases = SHAPES[name]
+    qd, kvd = hq * hd, hkv * hd
+    rng = np.random.default_rng(sum(map(ord, name)))
+    lens = np.array([1, 77, 600], np.int32)  # attended rows = pos + 1
+    B, S, layer = len(lens), 640, 1
+    cfg = abi.Config.make(2, hq, hkv, hd, S, 1e6 if mode == 0 else 1e4, mode)
+    st = AttnState(cfg, n_seqs=B, max_ctx=S)
+    cos_t, sin_t = oracle.rope_table(S, hd, cfg.rope_freq_base)
+    kcs, vcs = [], []
+    for b in range(B):
+        kc = np.zeros((S, kvd), np.uint16)
+        vc = np.zeros((S, kvd), np.uint16)
+        n = int(lens[b]) - 1
+        if n:
+            kc[:n] = oracle.f32_to_f16((rng.standard_normal((n, kvd)) * 0.5).astype(np.float32)).reshape(n, kvd)
+            vc[:n] = oracle.f32_to_f16((rng.standard_normal((n, kvd)) * 0.5).astype(np.float32)).reshape(n, kvd)
+        kcs.append(kc)
+        vcs.append(vc)
+        st.k_cache[b, layer] = dev(kc.view(np.int16))
+        st.v_cache[b, layer] = dev(vc.view(np.int16))
+    wq = wg.make(types[0], dim, qd, rng)
+    wk = wg.make(types[1], dim, kvd, rng)
+    wv = wg.make(types[2], dim, kvd, rng)
+    wo = wg.make(types[3], qd, dim, rng)
+    bq, bk, bv, bo = ((rng.standard_normal(n) * 0.1).astype(np.float32) if biases else None
+                      for n in (qd, kvd, kvd, dim))
+    qn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32) if qk_norm else None
+    kn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32) if qk_norm else None
+    xb = rng.standard_normal((B, dim)).astype(np.float32)
+    x0 = rng.standard_normal((B, dim)).astype(np.float32)
+    # the reference chain: its mat-vec, the oracle's decode step, its mat-vec again
+    q = ref.matvec(wq, types[0], bq, dim, qd, xb)
+    k = ref.matvec(wk, types[1], bk, dim, kvd, xb)
+    v = ref.matvec(wv, types[2], bv, dim, kvd, xb)
+    pos = lens - 1
+    attn = oracle.decode_batch(hq, hkv, hd, mode, q, k, v, qn, kn, cos_t, sin_t, kcs, vcs, pos, n_threads=8)
+    x_ref = x0 + ref.matvec(wo, types[3], bo, qd, dim, attn)
+    # the library: one call
+    d = lambda a: None if a is None else dev(a)
+    proj = LayerProj(dev(wq), dev(wk), dev(wv), dev(wo), types, d(bq), d(bk), d(bv), d(bo))
+    x = dev(x0)
+    st.decode_layer(layer, dim, dev(xb), proj, dev(pos), x, d(qn), d(kn))
+    torch.cuda.synchronize()
+    assert st.status() == 0
+    got = x.cpu().numpy()
+    err = np.abs(got.astype(np.float64) - x_ref)
+    bound = 2e-3 + 1e-2 * np.abs(x_ref)
+    assert (err <= bound).all(), f"max err {err.max():.3g} (ref {x_ref.flat[err.argmax()]:.3g})"
+    # the new cache rows: the reference's fp16 rounding of projections that agree
+    # to fp32 rounding, so equal or one fp16 ulp apart
+    for b in range(B):
+        for c, refc in ((st.k_cache, kcs), (st.v_cache, vcs)):
+            row = c[b, layer, pos[b]].cpu().numpy().view(np.uint16).astype(np.int32)
+            diff = np.abs(row - refc[b][pos[b]].astype(np.int32))
+            assert diff.max() <= 1, f"seq {b}: cache row off by {diff.max()} fp16 steps"
+
+
+def test_decode_layer_graph_replay_matches_eager(cuda, oracle):
+    """The whole layer chain captured once and replayed gives the eager result."""
+    from picolm_qwen_b200 import abi
+    from picolm_qwen_b200.runtime import AttnState, LayerProj
+    hq, hkv, hd, dim = 28, 4, 128, 3584
+    rng = np.random.default_rng(5)
+    cfg = abi.Config.make(1, hq, hkv, hd, 4096, 1e6)
+    st = AttnState(cfg, n_seqs=1, max_ctx=4096)
+    st.k_cache.copy_(torch.randint(-12000, 12000, st.k_cache.shape, dtype=torch.int16, device="cuda") & 0x3BFF)
+    st.v_cache.copy_(torch.randint(-12000, 12000, st.v_cache.shape, dtype=torch.int16, device="cuda") & 0x3BFF)
+    types = (13, 13, 15, 13)
+    ws = [dev(wg.make(t, n_in, n_out, rng)) for t, n_in, n_out in
+          zip(types, (dim, dim, dim, hq * hd), (hq * hd, hkv * hd, hkv * hd, dim))]
+    proj = LayerProj(*ws, types)
+    xb = dev(rng.standard_normal((1, dim)).astype(np.float32))
+    pos = torch.tensor([3000], dtype=torch.int32, device="cuda")
+    kc0, vc0 = st.k_cache.clone(), st.v_cache.clone()
+    x = torch.zeros((1, dim), device="cuda")
+    st.decode_layer(0, dim, xb, proj, pos, x)
+    torch.cuda.synchronize()
+    eager = x.clone()
+    st.k_cache.copy_(kc0)
+    st.v_cache.copy_(vc0)
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        x.zero_()
+        with torch.cuda.graph(g, stream=s):
+            st.decode_layer(0, dim, xb, proj, pos, x, stream=s)
+    for _ in range(3):
+        x.zero_()
+        g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(x, eager)
+    assert st.status() == 0
