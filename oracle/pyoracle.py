@@ -380,6 +380,15 @@ class RefFullModel:
             for n in ("pref_full_rope_cos", "pref_full_rope_sin"):
                 getattr(L, n).restype = C.POINTER(C.c_float)
                 getattr(L, n).argtypes = [C.c_void_p]
+            L.pref_full_set_attn_weights.restype = C.c_int
+            L.pref_full_set_attn_weights.argtypes = [C.c_void_p, C.c_int, C.c_uint64]
+            L.pref_full_attn_norm.argtypes = [C.c_void_p, C.c_int, _f32p, _f32p]
+            L.pref_full_attn_weight.restype = C.c_void_p
+            L.pref_full_attn_weight.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_int),
+                                                C.POINTER(C.c_size_t)]
+            L.pref_full_attn_bias.restype = C.POINTER(C.c_float)
+            L.pref_full_attn_bias.argtypes = [C.c_void_p, C.c_int, C.c_int]
+            L.pref_full_ffn.argtypes = [C.c_void_p, C.c_int, _f32p]
             L._full_proto = True
         self.ref, self.L = ref, L
         self.nl, self.hq, self.hkv, self.hd, self.vocab, self.S = n_layers, hq, hkv, hd, vocab, max_seq
@@ -429,6 +438,30 @@ class RefFullModel:
         if not self.qk_norm:
             return None
         return np.ctypeslib.as_array(self.L.pref_full_norm_w(self.h, layer, which), shape=(self.hd,)).copy()
+
+    def set_attn_weights(self, wtype: int, seed: int = 1) -> None:
+        """Every layer's q/k/v/o weights as seeded random blocks of a GGUF type."""
+        assert self.L.pref_full_set_attn_weights(self.h, int(wtype), seed) == 0
+
+    def attn_norm(self, layer, x):
+        xb = np.empty(self.dim, np.float32)
+        self.L.pref_full_attn_norm(self.h, layer, np.ascontiguousarray(x, np.float32), xb)
+        return xb
+
+    def attn_weight(self, layer, which):
+        """(bytes as uint8, GGUF type) of projection which: 0 q, 1 k, 2 v, 3 o."""
+        t, n = C.c_int(), C.c_size_t()
+        p = self.L.pref_full_attn_weight(self.h, layer, which, C.byref(t), C.byref(n))
+        return np.ctypeslib.as_array((C.c_uint8 * n.value).from_address(p)).copy(), t.value
+
+    def attn_bias(self, layer, which):
+        n = self.kvd if which in (1, 2) else self.dim
+        return np.ctypeslib.as_array(self.L.pref_full_attn_bias(self.h, layer, which), shape=(n,)).copy()
+
+    def ffn(self, layer, x):
+        x = np.ascontiguousarray(x, np.float32).copy()
+        self.L.pref_full_ffn(self.h, layer, x)
+        return x
 
     def close(self):
         if self.h:

@@ -279,6 +279,7 @@ struct FullHarness {
     int L, hq, hkv, hd, dim, kvd, n_ffn, vocab, max_seq;
     Model model;
     std::vector<std::vector<float>> store;  // every weight array, owned here
+    std::vector<std::vector<uint8_t>> qstore;  // quantised attention weights (pref_full_set_attn_weights)
     std::vector<float> xb, q, k, v, xb2, hb, hb2;
     const float* add(std::vector<float>&& w) {
         store.push_back(std::move(w));
@@ -408,6 +409,8 @@ void pref_full_pre_attn(void* hp, int l, const float* x, float* q, float* k, flo
                            (GGUFType)ve.type, (GGUFType)vb.type, st.dequant_scratch.data());
 }
 
+static void full_ffn(FullHarness* h, int l, float* x);
+
 // output projection, residual, FFN, residual (cpp/model.hpp:420-452); x in place
 void pref_full_post_attn(void* hp, int l, float* x, const float* attn) {
     auto* h = (FullHarness*)hp;
@@ -418,6 +421,14 @@ void pref_full_post_attn(void* hp, int l, float* x, const float* attn) {
     TensorOps::matmul_bias(h->xb2.data(), attn, oe.ptr, st.attn_output_bias[l].data(), dim, dim,
                            (GGUFType)oe.type, (GGUFType)ob.type, st.dequant_scratch.data());
     TensorOps::vec_add(x, h->xb2.data(), dim);
+    full_ffn(h, l, x);
+}
+
+// FFN and its residual (cpp/model.hpp:429-452); x in place
+static void full_ffn(FullHarness* h, int l, float* x) {
+    auto& st = h->model.state;
+    LayerWeights& lw = h->model.weights.get_layer(l);
+    const int dim = h->dim, n_ffn = h->n_ffn;
     TensorOps::rmsnorm(h->xb.data(), x, st.ffn_norm_w[l].data(), dim);
     auto ge = lw.get(layer::FFN_GATE), gb = lw.get(layer::FFN_GATE_B);
     TensorOps::matmul_bias(h->hb.data(), h->xb.data(), ge.ptr, st.ffn_gate_bias[l].data(), dim, n_ffn,
@@ -450,6 +461,87 @@ const float* pref_full_rope_cos(void* hp) { return ((FullHarness*)hp)->model.sta
 const float* pref_full_rope_sin(void* hp) { return ((FullHarness*)hp)->model.state.rope_sin.data(); }
 uint16_t* pref_full_kcache(void* hp) { return ((FullHarness*)hp)->model.state.key_cache.data(); }
 uint16_t* pref_full_vcache(void* hp) { return ((FullHarness*)hp)->model.state.val_cache.data(); }
+
+// Replaces every layer's q/k/v/o projection weights with seeded random blocks
+// of a GGUF type (1 F32 stays as created; 2 F16, 3 Q4_0, 9 Q8_0, 13 Q4_K,
+// 15 Q6_K), scaled so W.x keeps roughly unit variance; the engine then
+// dequantises them in its matmul as it would a model file's.  0 or -1.
+int pref_full_set_attn_weights(void* hp, int type, uint64_t seed) {
+    auto* h = (FullHarness*)hp;
+    int be = 0, bb = 0;
+    switch (type) {
+        case 2: be = 1; bb = 2; break;
+        case 3: be = 32; bb = 18; break;
+        case 9: be = 32; bb = 34; break;
+        case 13: be = 256; bb = 144; break;
+        case 15: be = 256; bb = 210; break;
+        default: return -1;
+    }
+    Rng r{seed};
+    auto u01 = [&]() { return 0.5f * (r.next(1.0f) + 1.0f); };
+    auto f16 = [&](float v, uint8_t* p) {
+        const uint16_t b = fp32_to_fp16(v);
+        p[0] = (uint8_t)(b & 0xFF);
+        p[1] = (uint8_t)(b >> 8);
+    };
+    const int dims_in[4] = {h->dim, h->dim, h->dim, h->dim};
+    const int dims_out[4] = {h->dim, h->kvd, h->kvd, h->dim};
+    const char* const keys[4] = {layer::ATTN_Q, layer::ATTN_K, layer::ATTN_V, layer::ATTN_OUTPUT};
+    for (int l = 0; l < h->L; l++) {
+        LayerWeights& lw = h->model.weights.get_layer(l);
+        for (int w = 0; w < 4; w++) {
+            const int n_in = dims_in[w], n_out = dims_out[w];
+            if (n_in % be) return -1;
+            const size_t nb = (size_t)n_out * (n_in / be);
+            std::vector<uint8_t> bytes(nb * bb);
+            const float a = 1.0f / std::sqrt((float)n_in);
+            for (size_t i = 0; i < nb; i++) {
+                uint8_t* p = bytes.data() + i * bb;
+                for (int j = 0; j < bb; j++) p[j] = (uint8_t)(r.next(1.0f) * 127.5f + 127.5f);
+                switch (type) {
+                    case 2: f16((2.0f * u01() - 1.0f) * 1.7320508f * a, p); break;
+                    case 3: f16(a / 4.6f * (0.5f + u01()), p); break;
+                    case 9: f16(a / 74.0f * (0.5f + u01()), p); break;
+                    case 13: f16(a / 140.0f * (0.5f + u01()), p); f16(a / 100.0f * u01(), p + 2); break;
+                    case 15: f16(a / (74.0f * 18.0f) * (0.5f + u01()), p + 208); break;
+                }
+            }
+            h->qstore.push_back(std::move(bytes));
+            lw.set(keys[w], h->qstore.back().data(), (uint32_t)type);
+        }
+    }
+    return 0;
+}
+
+// attention norm of layer l: xb = rmsnorm(x) (cpp/model.hpp:317)
+void pref_full_attn_norm(void* hp, int l, const float* x, float* xb) {
+    auto* h = (FullHarness*)hp;
+    TensorOps::rmsnorm(xb, x, h->model.state.attn_norm_w[l].data(), h->dim);
+}
+
+// layer l's projection weights as the engine holds them (which: 0 q, 1 k, 2 v,
+// 3 o), their GGUF type and byte count; and the fp32 biases it keeps
+const void* pref_full_attn_weight(void* hp, int l, int which, int* type, size_t* bytes) {
+    auto* h = (FullHarness*)hp;
+    const char* const keys[4] = {layer::ATTN_Q, layer::ATTN_K, layer::ATTN_V, layer::ATTN_OUTPUT};
+    auto e = h->model.weights.get_layer(l).get(keys[which]);
+    const int n_out = which == 1 || which == 2 ? h->kvd : h->dim;
+    *type = (int)e.type;
+    *bytes = gguf_type_row_size((GGUFType)e.type, h->dim) * (size_t)n_out;
+    return e.ptr;
+}
+const float* pref_full_attn_bias(void* hp, int l, int which) {
+    auto& st = ((FullHarness*)hp)->model.state;
+    switch (which) {
+        case 0: return st.attn_q_bias[l].data();
+        case 1: return st.attn_k_bias[l].data();
+        case 2: return st.attn_v_bias[l].data();
+        default: return st.attn_output_bias[l].data();
+    }
+}
+
+// FFN block and residual of layer l on x, whose attention block is done
+void pref_full_ffn(void* hp, int l, float* x) { full_ffn((FullHarness*)hp, l, x); }
 
 // Projections with the reference's own code: one row dequantised
 // (dequantize_row, cpp/quant.hpp:283-295) and matmul_bias per vector

@@ -24,10 +24,35 @@ namespace picoattn {
 namespace {
 
 constexpr int kMvWarps = 8;           // warps per block
-constexpr int kMvChunkWords = 1024;   // staged bytes per warp: 32 units of F32 = 4 KB
+constexpr int kMvRingWords = 2064;    // per warp: DEPTH chunk slots of (2064 / DEPTH) words
+constexpr size_t kMvSmem = (size_t)kMvWarps * kMvRingWords * 4;
+// A chunk (32 units) of F32 weights is 4 KB, of F16 2 KB, of the block formats
+// at most 1088 B: F32 gets two 4 KB slots, the rest four 2 KB slots (each slot
+// with spare words for the 4-byte-boundary start and the unaligned reads).
 
-__device__ __forceinline__ float half_bits(uint16_t h) { return __half2float(__ushort_as_half(h)); }
-__device__ __forceinline__ uint16_t lds16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
+// 4 bytes at any byte offset of a staged chunk (two aligned reads, a funnel
+// shift; the buffer has a spare word at its end).
+__device__ __forceinline__ uint32_t ld4(const uint8_t* p) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~(uintptr_t)3);
+    return __funnelshift_r(w[0], w[1], (uint32_t)(a & 3) * 8u);
+}
+
+__device__ __forceinline__ float half_at(const uint8_t* p, int hi) {
+    const uint32_t v = ld4(p);
+    return __half2float(__ushort_as_half((uint16_t)(hi ? v >> 16 : v & 0xFFFF)));
+}
+
+// Four bytes (0..255 each) of v as exact floats 2^23 + b, in two pairs; the
+// caller subtracts 2^23 (+ an offset) with one packed subtraction per pair,
+// which is exact, so the result is the integer (minus the offset) exactly,
+// as the reference's (float) conversions give.
+__device__ __forceinline__ void bytes_biased(uint32_t v, uint64_t& p01, uint64_t& p23) {
+    p01 = f2_pack(__uint_as_float(__byte_perm(v, 0x4B000000u, 0x7540)),
+                  __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7541)));
+    p23 = f2_pack(__uint_as_float(__byte_perm(v, 0x4B000000u, 0x7542)),
+                  __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7543)));
+}
 
 // get_scale_min_k4, cpp/quant.hpp:210-218: the 6-bit scale and min of
 // sub-block j of a Q4_K block.
@@ -41,63 +66,117 @@ __device__ __forceinline__ void scale_min_k4(int j, const uint8_t* q, int& sc, i
     }
 }
 
-// The 32 weights of unit `sub` of the block at `blk` (shared memory).
-__device__ __forceinline__ void decode_unit(int type, const uint8_t* blk, int sub, float (&w)[32]) {
+// acc[v] += w . x[v] over the 32 weights of unit `sub` of the block at `blk`
+// (a staged chunk), whose x starts at xu.  The weights are the reference's
+// dequantize_row_* values exactly: every product and difference rounded on its
+// own (packed f32x2 operations round each lane like the scalar ones).
+// xq(v, j): elements 4j..4j+3 of vector v's 32 x values for this unit.
+template <int NV, class XQ>
+__device__ __forceinline__ void unit_dot(int type, const uint8_t* blk, int sub, XQ xq, int nv, uint64_t (&acc)[NV]) {
+    // fma4(j, ...): the weights 4j..4j+3 as two pairs
+    auto fma4 = [&](int j, uint64_t w01, uint64_t w23) {
+#pragma unroll
+        for (int v = 0; v < NV; v++) {
+            if (v < nv) {
+                const float4 x = xq(v, j);
+                acc[v] = f2_fma(w01, f2_pack(x.x, x.y), acc[v]);
+                acc[v] = f2_fma(w23, f2_pack(x.z, x.w), acc[v]);
+            }
+        }
+    };
     switch (type) {
         case PICOATTN_WT_F32:
 #pragma unroll
-            for (int i = 0; i < 32; i++) w[i] = reinterpret_cast<const float*>(blk)[i];
+            for (int j = 0; j < 8; j++) {
+                const float4 w = *reinterpret_cast<const float4*>(blk + 16 * j);
+                fma4(j, f2_pack(w.x, w.y), f2_pack(w.z, w.w));
+            }
             break;
         case PICOATTN_WT_F16:
 #pragma unroll
-            for (int i = 0; i < 32; i++) w[i] = half_bits(lds16(blk + 2 * i));
+            for (int j = 0; j < 8; j++) {
+                const uint32_t a = ld4(blk + 8 * j), b = ld4(blk + 8 * j + 4);
+                const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&a));
+                const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&b));
+                fma4(j, f2_pack(f0.x, f0.y), f2_pack(f1.x, f1.y));
+            }
             break;
-        case PICOATTN_WT_Q4_0: {  // dequantize_row_q4_0, cpp/quant.hpp:197-207
-            const float d = half_bits(lds16(blk));
+        case PICOATTN_WT_Q4_0: {  // dequantize_row_q4_0, cpp/quant.hpp:197-207: d * ((float)nib - 8)
+            const float d = half_at(blk, 0);
+            const uint64_t dd = f2_pack(d, d), off = f2_pack(8388616.f, 8388616.f);
 #pragma unroll
-            for (int i = 0; i < 16; i++) {
-                const int b = blk[2 + i];
-                w[i] = __fmul_rn(d, (float)(b & 0xF) - 8.0f);
-                w[i + 16] = __fmul_rn(d, (float)(b >> 4) - 8.0f);
+            for (int j = 0; j < 4; j++) {
+                const uint32_t v = ld4(blk + 2 + 4 * j);
+                uint64_t a, b;
+                bytes_biased(v & 0x0F0F0F0Fu, a, b);  // weights 4j.. (low nibbles)
+                fma4(j, f2_mul(dd, f2_sub(a, off)), f2_mul(dd, f2_sub(b, off)));
+                bytes_biased((v >> 4) & 0x0F0F0F0Fu, a, b);  // weights 16+4j.. (high nibbles)
+                fma4(4 + j, f2_mul(dd, f2_sub(a, off)), f2_mul(dd, f2_sub(b, off)));
             }
             break;
         }
-        case PICOATTN_WT_Q8_0: {  // dequantize_row_q8_0, cpp/quant.hpp:187-195
-            const float d = half_bits(lds16(blk));
+        case PICOATTN_WT_Q8_0: {  // dequantize_row_q8_0, cpp/quant.hpp:187-195: d * (float)q
+            const float d = half_at(blk, 0);
+            const uint64_t dd = f2_pack(d, d), off = f2_pack(8388736.f, 8388736.f);  // 2^23 + 128
 #pragma unroll
-            for (int i = 0; i < 32; i++) w[i] = __fmul_rn(d, (float)(int8_t)blk[2 + i]);
+            for (int j = 0; j < 8; j++) {
+                uint64_t a, b;
+                bytes_biased(ld4(blk + 2 + 4 * j) ^ 0x80808080u, a, b);
+                fma4(j, f2_mul(dd, f2_sub(a, off)), f2_mul(dd, f2_sub(b, off)));
+            }
             break;
         }
-        case PICOATTN_WT_Q4_K: {  // dequantize_row_q4_K, cpp/quant.hpp:220-251
+        case PICOATTN_WT_Q4_K: {  // dequantize_row_q4_K, cpp/quant.hpp:220-251: d1 * q - m1
             // unit sub = 2*j + h: pair j of 32 quant bytes, low (h = 0) or high nibbles
-            const float d = half_bits(lds16(blk)), dmin = half_bits(lds16(blk + 2));
+            const uint32_t h = ld4(blk);
+            const float d = __half2float(__ushort_as_half((uint16_t)(h & 0xFFFF)));
+            const float dmin = __half2float(__ushort_as_half((uint16_t)(h >> 16)));
             int sc, mn;
             scale_min_k4(sub, blk + 4, sc, mn);
             const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mn);
+            const uint64_t dd = f2_pack(d1, d1), mm = f2_pack(m1, m1), off = f2_pack(8388608.f, 8388608.f);
             const uint8_t* q = blk + 16 + 32 * (sub >> 1);
-            const int sh = (sub & 1) * 4;
+            const uint32_t sh = (sub & 1) * 4;
+            uint32_t qw[8];
+            if ((reinterpret_cast<uintptr_t>(q) & 15u) == 0) {  // blocks 16-byte aligned: two 16-byte reads
+                const uint4 q0 = *reinterpret_cast<const uint4*>(q), q1 = *reinterpret_cast<const uint4*>(q + 16);
+                qw[0] = q0.x, qw[1] = q0.y, qw[2] = q0.z, qw[3] = q0.w;
+                qw[4] = q1.x, qw[5] = q1.y, qw[6] = q1.z, qw[7] = q1.w;
+            } else {
 #pragma unroll
-            for (int l = 0; l < 32; l++) w[l] = __fsub_rn(__fmul_rn(d1, (float)((q[l] >> sh) & 0xF)), m1);
+                for (int j = 0; j < 8; j++) qw[j] = ld4(q + 4 * j);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                uint64_t a, b;
+                bytes_biased((qw[j] >> sh) & 0x0F0F0F0Fu, a, b);
+                fma4(j, f2_sub(f2_mul(dd, f2_sub(a, off)), mm), f2_sub(f2_mul(dd, f2_sub(b, off)), mm));
+            }
             break;
         }
-        case PICOATTN_WT_Q6_K: {  // dequantize_row_q6_K, cpp/quant.hpp:253-281
+        case PICOATTN_WT_Q6_K: {  // dequantize_row_q6_K, cpp/quant.hpp:253-281: d * sc * (q - 32)
             // unit sub = 4*c + qq: chunk c of 128 weights, quarter qq
             const int c = sub >> 2, qq = sub & 3;
             const uint8_t* ql = blk + 64 * c + (qq & 1) * 32;
             const uint8_t* qh = blk + 128 + 32 * c;
             const int8_t* scl = reinterpret_cast<const int8_t*>(blk + 192) + 8 * c + 2 * qq;
-            const float d = half_bits(lds16(blk + 208));
-            const int lsh = (qq >> 1) * 4, hsh = 2 * qq;
+            const float d = half_at(blk + 208, 0);
+            const float ds0 = __fmul_rn(d, (float)scl[0]), ds1 = __fmul_rn(d, (float)scl[1]);
+            const uint32_t lsh = (qq >> 1) * 4, hsh = 2 * qq;
+            const uint64_t off = f2_pack(8388640.f, 8388640.f);  // 2^23 + 32
 #pragma unroll
-            for (int l = 0; l < 32; l++) {
-                const int q = (((ql[l] >> lsh) & 0xF) | (((qh[l] >> hsh) & 3) << 4)) - 32;
-                w[l] = __fmul_rn(__fmul_rn(d, (float)scl[l / 16]), (float)q);
+            for (int j = 0; j < 8; j++) {
+                const uint32_t qv = ((ld4(ql + 4 * j) >> lsh) & 0x0F0F0F0Fu) | (((ld4(qh + 4 * j) >> hsh) & 0x03030303u) << 4);
+                const float ds = j < 4 ? ds0 : ds1;  // weights 0..15 and 16..31
+                const uint64_t dd = f2_pack(ds, ds);
+                uint64_t a, b;
+                bytes_biased(qv, a, b);
+                fma4(j, f2_mul(dd, f2_sub(a, off)), f2_mul(dd, f2_sub(b, off)));
             }
             break;
         }
         default:
-#pragma unroll
-            for (int i = 0; i < 32; i++) w[i] = 0.f;
+            break;
     }
 }
 
@@ -105,84 +184,222 @@ __device__ __forceinline__ int units_per_block(int type) {
     return (type == PICOATTN_WT_Q4_K || type == PICOATTN_WT_Q6_K) ? 8 : 1;
 }
 
-// NV vectors per pass over a row: the weights are decoded once per pass.
-template <int NV>
+// The matrix (of up to three) that holds global row r, and r's row in it.
+__device__ __forceinline__ MatvecPart part_of(const MatvecArgs& a, int r, int& row) {
+    row = r;
+    const bool in1 = a.n_parts > 1 && row >= a.part[0].n_out;
+    if (in1) row -= a.part[0].n_out;
+    const bool in2 = in1 && a.n_parts > 2 && row >= a.part[1].n_out;
+    if (in2) row -= a.part[1].n_out;
+    return in2 ? a.part[2] : (in1 ? a.part[1] : a.part[0]);
+}
+
+// Every warp walks its rows chunk by chunk (32 units of 32 weights); chunk j+1
+// is copied into the warp's other buffer (cp.async, 4-byte words) while chunk j
+// is decoded, so a row costs about one memory round trip, not one per chunk.
+template <int NV, int DEPTH>
 __global__ void __launch_bounds__(kMvWarps * 32, 2) matvec_kernel(MatvecArgs a) {
-    __shared__ __align__(16) uint32_t stage[kMvWarps][kMvChunkWords + 4];
+    constexpr int kSlotWords = kMvRingWords / DEPTH;  // 1032 or 516 words: 16-byte multiples
+    static_assert(kSlotWords % 4 == 0, "16-byte aligned slots");
+    extern __shared__ __align__(16) uint32_t mv_smem[];
     // The next kernel may launch now; inputs are read after the kernel before
     // this one completed (every CTA waits before it exits, see pdl_wait).
     pdl_trigger();
     pdl_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint32_t* st = stage[warp];
-    const int n_units = a.n_in / 32;
-    for (int r = blockIdx.x * kMvWarps + warp; r < a.rows_total; r += gridDim.x * kMvWarps) {
-        // the matrix holding global row r (selected, not indexed: the parts stay
-        // in the parameter space)
-        int row = r;
-        const bool in1 = a.n_parts > 1 && row >= a.part[0].n_out;
-        if (in1) row -= a.part[0].n_out;
-        const bool in2 = in1 && a.n_parts > 2 && row >= a.part[1].n_out;
-        if (in2) row -= a.part[1].n_out;
-        const MatvecPart P = in2 ? a.part[2] : (in1 ? a.part[1] : a.part[0]);
-        const int type = P.type, upb = units_per_block(type), qsz = (int)(P.block_bytes);
+    uint32_t* bufs = mv_smem + (size_t)warp * kMvRingWords;
+    const int n_units = a.n_in / 32, cpr = (n_units + 31) / 32;  // chunks per row
+    const int gw = blockIdx.x * kMvWarps + warp, nw = gridDim.x * kMvWarps;
+    const int my_rows = gw < a.rows_total ? (a.rows_total - 1 - gw) / nw + 1 : 0;
+    const int n_chunks = my_rows * cpr;
+    // chunk j: row gw + (j / cpr) * nw, units from (j % cpr) * 32; its bytes
+    // [g0, g1) staged from the 4-byte boundary a0 <= g0
+    auto chunk = [&](int j, MatvecPart& P, int& row, int& b0, uintptr_t& g0, uintptr_t& a0, int& nwords,
+                     int& tail) {
+        P = part_of(a, gw + (j / cpr) * nw, row);
+        const int upb = units_per_block(P.type), u0 = (j % cpr) * 32;
+        b0 = u0 / upb;
+        const int b1 = (min(n_units, u0 + 32) + upb - 1) / upb;
         const uint8_t* rowp = P.w + (size_t)row * P.row_bytes;
-        for (int v0 = 0; v0 < a.n_vec; v0 += NV) {
-            float acc[NV];
+        g0 = reinterpret_cast<uintptr_t>(rowp + (size_t)b0 * P.block_bytes);
+        const uintptr_t g1 = reinterpret_cast<uintptr_t>(rowp + (size_t)b1 * P.block_bytes);
+        a0 = g0 & ~(uintptr_t)3;
+        nwords = (int)((g1 - a0) >> 2);
+        tail = (int)((g1 - a0) & 3);
+    };
+    auto issue = [&](int j) {
+        if (j < n_chunks) {
+            MatvecPart P;
+            int row, b0, nwords, tail;
+            uintptr_t g0, a0;
+            chunk(j, P, row, b0, g0, a0, nwords, tail);
+            uint32_t* dst = bufs + (j % DEPTH) * kSlotWords;
+            for (int i = lane; i < nwords; i += 32) cp_async4(dst + i, reinterpret_cast<const uint32_t*>(a0) + i);
+            if (tail && lane == 0) {  // the matrix may end inside a word: no read past it
+                uint32_t t = 0;
+                for (int k = 0; k < tail; k++)
+                    t |= (uint32_t)__ldg(reinterpret_cast<const uint8_t*>(a0) + 4 * nwords + k) << (8 * k);
+                dst[nwords] = t;
+            }
+        }
+        cp_async_commit();
+    };
+    for (int v0 = 0; v0 < a.n_vec; v0 += NV) {
+        const int nv = min(NV, a.n_vec - v0);
+        uint64_t acc[NV];
 #pragma unroll
-            for (int v = 0; v < NV; v++) acc[v] = 0.f;
-            for (int u0 = 0; u0 < n_units; u0 += 32) {
-                // stage blocks [b0, b1) that hold units [u0, u0 + 32)
-                const int b0 = u0 / upb, b1 = (min(n_units, u0 + 32) + upb - 1) / upb;
-                const uintptr_t g0 = (uintptr_t)(rowp + (size_t)b0 * qsz), g1 = (uintptr_t)(rowp + (size_t)b1 * qsz);
-                const uintptr_t a0 = g0 & ~(uintptr_t)3;
-                const int nwords = (int)((g1 - a0) >> 2), tail = (int)((g1 - a0) & 3);
-                __syncwarp();  // the previous chunk's reads are done
-                for (int i = lane; i < nwords; i += 32) st[i] = __ldg(reinterpret_cast<const uint32_t*>(a0) + i);
-                if (tail && lane == 0) {  // the last bytes of the matrix may end inside a word
-                    uint32_t t = 0;
-                    for (int k = 0; k < tail; k++) t |= (uint32_t)__ldg(reinterpret_cast<const uint8_t*>(a0) + 4 * nwords + k) << (8 * k);
-                    st[nwords] = t;
+        for (int v = 0; v < NV; v++) acc[v] = 0ull;
+        for (int j = 0; j < DEPTH - 1; j++) issue(j);
+        for (int j = 0; j < n_chunks; j++) {
+            issue(j + DEPTH - 1);  // into the slot chunk j - 1 used
+            cp_async_wait<DEPTH - 1>();
+            __syncwarp();  // chunk j is in its slot (every lane's copies and the tail)
+            MatvecPart P;
+            int row, b0, nwords, tail;
+            uintptr_t g0, a0;
+            chunk(j, P, row, b0, g0, a0, nwords, tail);
+            const int upb = units_per_block(P.type), u = (j % cpr) * 32 + lane;
+            if (u < n_units) {
+                const int k = u - b0 * upb;
+                const uint8_t* blk = reinterpret_cast<const uint8_t*>(bufs + (j % DEPTH) * kSlotWords) + (g0 - a0) +
+                                     (size_t)(k / upb) * P.block_bytes;
+                const float* xu = a.x + (size_t)v0 * a.n_in + 32 * u;
+                unit_dot<NV>(P.type, blk, k % upb,
+                             [&](int v, int jj) {
+                                 return __ldg(reinterpret_cast<const float4*>(xu + (size_t)v * a.n_in) + jj);
+                             },
+                             nv, acc);
+            }
+            __syncwarp();  // the slot is read before chunk j + DEPTH overwrites it
+            if (j % cpr == cpr - 1) {  // the row is done
+                float y[NV];
+#pragma unroll
+                for (int v = 0; v < NV; v++) {
+                    float lo, hi;
+                    f2_unpack(acc[v], lo, hi);
+                    y[v] = lo + hi;
+#pragma unroll
+                    for (int o = 16; o; o >>= 1) y[v] += __shfl_xor_sync(0xffffffffu, y[v], o);
+                    acc[v] = 0ull;
                 }
-                __syncwarp();
-                const int u = u0 + lane;
-                if (u < n_units) {
-                    const int k = u - b0 * upb;
-                    float w[32];
-                    decode_unit(type, reinterpret_cast<const uint8_t*>(st) + (g0 - a0) + (size_t)(k / upb) * qsz,
-                                k % upb, w);
+                if (lane == 0) {
 #pragma unroll
                     for (int v = 0; v < NV; v++) {
-                        if (v0 + v < a.n_vec) {
-                            const float4* xv = reinterpret_cast<const float4*>(a.x + (size_t)(v0 + v) * a.n_in + 32 * u);
-#pragma unroll
-                            for (int g = 0; g < 8; g++) {
-                                const float4 xx = __ldg(xv + g);
-                                acc[v] = fmaf(w[4 * g], xx.x, acc[v]);
-                                acc[v] = fmaf(w[4 * g + 1], xx.y, acc[v]);
-                                acc[v] = fmaf(w[4 * g + 2], xx.z, acc[v]);
-                                acc[v] = fmaf(w[4 * g + 3], xx.w, acc[v]);
-                            }
+                        if (v < nv) {
+                            // matmul, then the bias added (vec_add), then the residual
+                            float yv = y[v];
+                            if (P.bias) yv = __fadd_rn(yv, P.bias[row]);
+                            float* o = P.out + (size_t)(v0 + v) * P.out_stride + row;
+                            *o = a.accumulate ? __fadd_rn(*o, yv) : yv;
                         }
                     }
                 }
             }
-#pragma unroll
-            for (int v = 0; v < NV; v++) {
-#pragma unroll
-                for (int o = 16; o; o >>= 1) acc[v] += __shfl_xor_sync(0xffffffffu, acc[v], o);
-            }
-            if (lane == 0) {
-#pragma unroll
-                for (int v = 0; v < NV; v++) {
-                    if (v0 + v < a.n_vec) {
-                        // matmul, then the bias added (vec_add), then the residual
-                        float y = acc[v];
-                        if (P.bias) y = __fadd_rn(y, P.bias[row]);
-                        float* o = P.out + (size_t)(v0 + v) * P.out_stride + row;
-                        *o = a.accumulate ? __fadd_rn(*o, y) : y;
-                    }
+        }
+        cp_async_wait<0>();
+        __syncwarp();
+    }
+}
+
+// One vector: a warp takes groups of kMvRows consecutive rows (one matrix: the
+// host checks that every matrix's row count is a multiple of kMvRows) and
+// walks a group chunk step by chunk step, the group's rows in turn at each
+// step, so a lane loads its unit's 32 x values into registers once per step
+// and applies them to every row of the group: the x traffic through L1 falls
+// kMvRows-fold (in the row-at-a-time order it bounded the kernel), and the
+// group's matrix is looked up once.  Chunk slots as in matvec_kernel (block
+// formats and F16 only: F32 chunks need the larger slots).
+constexpr int kMvRows = 4;
+
+template <int DEPTH>
+__global__ void __launch_bounds__(kMvWarps * 32, 2) matvec1_kernel(MatvecArgs a) {
+    constexpr int kSlotWords = kMvRingWords / DEPTH;
+    extern __shared__ __align__(16) uint32_t mv_smem[];
+    pdl_trigger();
+    pdl_wait();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint32_t* bufs = mv_smem + (size_t)warp * kMvRingWords;
+    const int n_units = a.n_in / 32, cpr = (n_units + 31) / 32;
+    const int n_groups = a.rows_total / kMvRows;
+    for (int grp = blockIdx.x * kMvWarps + warp; grp < n_groups; grp += gridDim.x * kMvWarps) {
+        int row0;
+        const MatvecPart P = part_of(a, grp * kMvRows, row0);
+        const int upb = units_per_block(P.type), bb = P.block_bytes;
+        const uint8_t* base = P.w + (size_t)row0 * P.row_bytes;
+        const int n_chunks = cpr * kMvRows;
+        // chunk c: step c / kMvRows (units from 32 * step), row row0 + c % kMvRows
+        auto span = [&](int c, int& b0, uintptr_t& g0, uintptr_t& a0, int& nwords, int& tail) {
+            const int u0 = (c / kMvRows) * 32;
+            b0 = u0 / upb;
+            const int b1 = (min(n_units, u0 + 32) + upb - 1) / upb;
+            const uint8_t* rowp = base + (size_t)(c % kMvRows) * P.row_bytes;
+            g0 = reinterpret_cast<uintptr_t>(rowp + (size_t)b0 * bb);
+            const uintptr_t g1 = reinterpret_cast<uintptr_t>(rowp + (size_t)b1 * bb);
+            a0 = g0 & ~(uintptr_t)3;
+            nwords = (int)((g1 - a0) >> 2);
+            tail = (int)((g1 - a0) & 3);
+        };
+        auto issue = [&](int c) {
+            if (c < n_chunks) {
+                int b0, nwords, tail;
+                uintptr_t g0, a0;
+                span(c, b0, g0, a0, nwords, tail);
+                uint32_t* dst = bufs + (c % DEPTH) * kSlotWords;
+                for (int i = lane; i < nwords; i += 32) cp_async4(dst + i, reinterpret_cast<const uint32_t*>(a0) + i);
+                if (tail && lane == 0) {  // the matrix may end inside a word: no read past it
+                    uint32_t t = 0;
+                    for (int k = 0; k < tail; k++)
+                        t |= (uint32_t)__ldg(reinterpret_cast<const uint8_t*>(a0) + 4 * nwords + k) << (8 * k);
+                    dst[nwords] = t;
                 }
+            }
+            cp_async_commit();
+        };
+        uint64_t acc[kMvRows];
+#pragma unroll
+        for (int r = 0; r < kMvRows; r++) acc[r] = 0ull;
+        float4 xr[8];  // this lane's unit of x at the current step
+        for (int c = 0; c < DEPTH - 1; c++) issue(c);
+        for (int st = 0; st < cpr; st++) {
+            const int u = st * 32 + lane;
+            if (u < n_units) {
+#pragma unroll
+                for (int jj = 0; jj < 8; jj++) xr[jj] = __ldg(reinterpret_cast<const float4*>(a.x + 32 * u) + jj);
+            }
+#pragma unroll
+            for (int r = 0; r < kMvRows; r++) {
+                const int c = st * kMvRows + r;
+                issue(c + DEPTH - 1);
+                cp_async_wait<DEPTH - 1>();
+                __syncwarp();  // chunk c is in its slot (every lane's copies and the tail)
+                if (u < n_units) {
+                    int b0, nwords, tail;
+                    uintptr_t g0, a0;
+                    span(c, b0, g0, a0, nwords, tail);
+                    const int k = u - b0 * upb;
+                    const uint8_t* blk = reinterpret_cast<const uint8_t*>(bufs + (c % DEPTH) * kSlotWords) +
+                                         (g0 - a0) + (size_t)(k / upb) * bb;
+                    uint64_t one[1] = {acc[r]};
+                    unit_dot<1>(P.type, blk, k % upb, [&](int, int jj) { return xr[jj]; }, 1, one);
+                    acc[r] = one[0];
+                }
+                __syncwarp();  // the slot is read before chunk c + DEPTH overwrites it
+            }
+        }
+        cp_async_wait<0>();
+        __syncwarp();
+#pragma unroll
+        for (int r = 0; r < kMvRows; r++) {
+            float lo, hi;
+            f2_unpack(acc[r], lo, hi);
+            float y = lo + hi;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) y += __shfl_xor_sync(0xffffffffu, y, o);
+            if (lane == 0) {
+                // matmul, then the bias added (vec_add), then the residual
+                if (P.bias) y = __fadd_rn(y, P.bias[row0 + r]);
+                float* o = P.out + row0 + r;
+                *o = a.accumulate ? __fadd_rn(*o, y) : y;
             }
         }
     }
@@ -235,16 +452,38 @@ cudaError_t launch_matvec(const MatvecArgs& a, cudaStream_t stream) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)std::max(1, grid));
     cfg.blockDim = dim3(kMvWarps * 32);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = kMvSmem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (a.n_vec == 1) return cudaLaunchKernelEx(&cfg, matvec_kernel<1>, a);
-    if (a.n_vec == 2) return cudaLaunchKernelEx(&cfg, matvec_kernel<2>, a);
-    return cudaLaunchKernelEx(&cfg, matvec_kernel<4>, a);
+    static bool attr_done = false;
+    if (!attr_done) {
+        for (auto k : {matvec_kernel<1, 2>, matvec_kernel<2, 2>, matvec_kernel<4, 2>, matvec_kernel<1, 4>,
+                       matvec_kernel<2, 4>, matvec_kernel<4, 4>, matvec1_kernel<4>}) {
+            const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMvSmem);
+            if (e != cudaSuccess) return e;
+        }
+        attr_done = true;
+    }
+    bool f32 = false;  // F32 chunks need the 4 KB slots
+    for (int p = 0; p < a.n_parts; p++) f32 = f32 || a.part[p].type == PICOATTN_WT_F32;
+    if (f32) {
+        if (a.n_vec == 1) return cudaLaunchKernelEx(&cfg, matvec_kernel<1, 2>, a);
+        if (a.n_vec == 2) return cudaLaunchKernelEx(&cfg, matvec_kernel<2, 2>, a);
+        return cudaLaunchKernelEx(&cfg, matvec_kernel<4, 2>, a);
+    }
+    bool groups = a.n_vec == 1;  // row groups need every matrix's rows in whole groups
+    for (int p = 0; p < a.n_parts; p++) groups = groups && a.part[p].n_out % kMvRows == 0;
+    if (groups) {
+        const long long want1 = ((long long)a.rows_total / kMvRows + kMvWarps - 1) / kMvWarps;
+        cfg.gridDim = dim3((unsigned)std::max<long long>(1, std::min<long long>(want1, (long long)sms * 8)));
+        return cudaLaunchKernelEx(&cfg, matvec1_kernel<4>, a);
+    }
+    if (a.n_vec == 2) return cudaLaunchKernelEx(&cfg, matvec_kernel<2, 4>, a);
+    return cudaLaunchKernelEx(&cfg, matvec_kernel<4, 4>, a);
 }
 
 }  // namespace picoattn

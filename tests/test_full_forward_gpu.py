@@ -86,3 +86,67 @@ def test_full_forward_qwen3_like_cta_pair(cuda):
 
 def test_full_forward_qwen2_like_no_qk_norm(cuda):
     _run(hq=6, hkv=2, hd=128, qk_norm=0, seed=12)
+
+
+@pytest.mark.parametrize("wtype", [9, 13], ids=["Q8_0", "Q4_K"])
+def test_full_forward_decode_layer_quantized_weights(cuda, wtype):
+    """Quantised attention weights; each decode step's whole attention block
+    (q/k/v projections with biases, QK-norm, RoPE, cache append, attention,
+    output projection into the residual) is one picoattn_decode_layer call on
+    the device, the rest the reference's stages.  Same bars as above."""
+    from picolm_qwen_b200 import abi
+    from picolm_qwen_b200.runtime import AttnState, LayerProj
+    if not __import__("os").path.exists(pyoracle.REF_SO):
+        pytest.skip("oracle/_ref not built")
+    ref = pyoracle.RefHarness()
+    hq, hkv, hd, seed = 4, 2, 128, 21
+    L, S, vocab, n_prompt, n_gen = 3, 96, 211, 16, 24
+    kw = dict(n_layers=L, hq=hq, hkv=hkv, hd=hd, n_ffn=512, vocab=vocab, max_seq=S, rope_base=1e6,
+              rope_mode=0, qk_norm=1, seed=seed)
+    m_ref, m = pyoracle.RefFullModel(ref, **kw), pyoracle.RefFullModel(ref, **kw)
+    m_ref.set_attn_weights(wtype, 8)
+    m.set_attn_weights(wtype, 8)
+    dim = hq * hd
+    cfg = abi.Config.make(L, hq, hkv, hd, S, 1e6, abi.ROPE_NEOX)
+    st = AttnState(cfg, n_seqs=1, max_ctx=S)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    norms = [(dev(m.norm_w(l, 0)), dev(m.norm_w(l, 1))) for l in range(L)]
+    projs = []
+    for l in range(L):
+        ws = [m.attn_weight(l, i) for i in range(4)]
+        projs.append(LayerProj(*(dev(w) for w, _ in ws), [t for _, t in ws],
+                               *(dev(m.attn_bias(l, i)) for i in range(4))))
+    rng = np.random.default_rng(seed)
+    prompt = rng.integers(0, vocab, n_prompt).astype(np.int32)
+    # prompt through the prefill path (the reference's projections)
+    xs = np.stack([m.embed(t) for t in prompt])
+    for l in range(L):
+        qkv = [m.pre_attn(l, x) for x in xs]
+        q = dev(np.stack([a[0] for a in qkv])); k = dev(np.stack([a[1] for a in qkv]))
+        v = dev(np.stack([a[2] for a in qkv]))
+        out = torch.empty((n_prompt, hq * hd), device="cuda")
+        assert st.prefill(l, 0, q, k, v, out, *norms[l]) == 0
+        attn = out.cpu().numpy()
+        xs = np.stack([m.post_attn(l, xs[i], attn[i]) for i in range(n_prompt)])
+    got = [m.logits(xs[-1])]
+    want = [m_ref.forward_batch(prompt, 0)]
+    tok = int(np.argmax(want[0]))
+    for step in range(n_gen):
+        pos = n_prompt + step
+        want.append(m_ref.forward(tok, pos))
+        x = m.embed(tok)
+        pos_t = torch.tensor([pos], dtype=torch.int32, device="cuda")
+        for l in range(L):
+            xd = dev(x[None])
+            st.decode_layer(l, dim, dev(m.attn_norm(l, x)[None]), projs[l], pos_t, xd, *norms[l])
+            x = m.ffn(l, xd.cpu().numpy()[0])
+        got.append(m.logits(x))
+        tok = int(np.argmax(want[-1]))
+    torch.cuda.synchronize()
+    assert st.status() == 0
+    got, want = np.stack(got), np.stack(want)
+    same = (np.argmax(got, 1) == np.argmax(want, 1))
+    assert same.all(), f"argmax differs at steps {np.nonzero(~same)[0].tolist()}"
+    scale = np.abs(want).max()
+    err = np.abs(got - want).max()
+    assert err <= 2e-2 * scale, f"max logit error {err:.3g} of scale {scale:.3g}"
