@@ -403,6 +403,10 @@ def run_ours(args) -> None:
     if not args.no_longctx:
         torch.cuda.empty_cache()
         longctx_line = run_longctx(args, dev, world, rank, local)
+    layer_line = None
+    if world == 1 and not args.no_layer:
+        torch.cuda.empty_cache()
+        layer_line = run_layer(args, dev)
 
     nbytes = step_bytes(lens, L, kvd)
     times = torch.tensor([elapsed_ms, e2e_ms, float(nbytes)], dtype=torch.float64, device=dev)
@@ -447,6 +451,8 @@ def run_ours(args) -> None:
             line["prefill"] = prefill_line
         if longctx_line is not None:
             line["long_context"] = longctx_line
+        if layer_line is not None:
+            line["decode_layer"] = layer_line
         if world == 1 and not args.no_cpu:
             try:
                 line["cpu_baseline"] = cpu_baseline(lens)
@@ -709,6 +715,116 @@ def run_longctx(args, dev, world, rank, local) -> dict:
                        if world > 1 else "single GPU"}}
 
 
+LAYER = dict(name="qwen2.5-7b-decode-layer-q4km", n_layers=28, n_heads=28, n_kv_heads=4, head_dim=128, dim=3584,
+             rope_base=1e6, ctx=4096, types=(13, 13, 15, 13), seed=0)
+
+
+def run_layer(args, dev) -> dict:
+    """The attention block of a whole decode step on the device
+    (picoattn_decode_layer: q/k/v projections with biases in one kernel, the
+    decode step, the output projection into the residual), Qwen2.5-7B shape,
+    one sequence at position ctx - 1, Q4_K_M-style weights (q, k, o Q4_K; v
+    Q6_K; seeded random blocks), each layer its own weights; the 28 calls
+    replayed as one CUDA graph.  HBM-bound: bytes per step = every layer's
+    weight bytes + the K/V rows attended."""
+    import ctypes as C
+    import torch
+    from picolm_qwen_b200 import abi
+    from picolm_qwen_b200.runtime import AttnState, LayerProj
+    p = LAYER
+    L, hq, hkv, hd, dim, S = p["n_layers"], p["n_heads"], p["n_kv_heads"], p["head_dim"], p["dim"], p["ctx"]
+    qd, kvd = hq * hd, hkv * hd
+    lib = abi.lib()
+    cfg = abi.Config.make(L, hq, hkv, hd, S, p["rope_base"], abi.ROPE_NEOX)
+    st = AttnState(cfg, n_seqs=1, max_ctx=S)
+    g = torch.Generator(device=dev).manual_seed(p["seed"])
+    # finite fp16 cache rows: magnitude < 1, either sign (bit patterns in int16 containers)
+    for c in (st.k_cache, st.v_cache):
+        mag = torch.randint(0, 0x3C00, c.shape, generator=g, device=dev, dtype=torch.int32)
+        sgn = torch.randint(0, 2, c.shape, generator=g, device=dev, dtype=torch.int32) * 0x8000
+        c.copy_(((mag | sgn) - ((mag | sgn) >= 0x8000).to(torch.int32) * 0x10000).to(torch.int16))
+    shapes = ((dim, qd), (dim, kvd), (dim, kvd), (qd, dim))
+    rng = np.random.default_rng(p["seed"])
+    projs, wbytes = [], 0
+    for _ in range(L):
+        ws = []
+        for t, (n_in, n_out) in zip(p["types"], shapes):
+            nb = lib.picoattn_weight_bytes(t, n_in, n_out)
+            blk = rng.integers(0, 256, nb, dtype=np.uint8)
+            ws.append(torch.from_numpy(blk).to(dev))
+            wbytes += nb
+        # scales: small positive fp16 (the first two bytes of every block are a scale in Q4_K;
+        # Q6_K keeps its scale last) so activations stay finite
+        for w, t in zip(ws, p["types"]):
+            bsz = 144 if t == 13 else 210
+            v = w.view(-1, bsz)
+            at = 0 if t == 13 else 208
+            v[:, at:at + 2] = torch.tensor([0x00, 0x10], dtype=torch.uint8, device=dev)  # fp16 0x1000 ~ 2.4e-4
+            if t == 13:
+                v[:, 2:4] = torch.tensor([0x00, 0x08], dtype=torch.uint8, device=dev)
+        bias = [torch.zeros(n, device=dev) for n in (qd, kvd, kvd, dim)]
+        projs.append(LayerProj(*ws, p["types"], *bias))
+    xb = torch.randn(1, dim, generator=g, device=dev)
+    x = torch.zeros(1, dim, device=dev)
+    pos = torch.tensor([S - 1], dtype=torch.int32, device=dev)
+    kv_bytes = L * 2 * S * kvd * 2
+    for l in range(L):
+        st.decode_layer(l, dim, xb, projs[l], pos, x)
+    torch.cuda.synchronize()
+    if st.status() != 0:
+        raise RuntimeError("decode_layer flagged bad input")
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            for l in range(L):
+                st.decode_layer(l, dim, xb, projs[l], pos, x, stream=s)
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    torch.cuda.synchronize()
+    steps = max(5, args.steps // 4)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    # the projection kernel alone, for its roofline: the O projection of every
+    # layer (Q4_K 3584 x 3584) as one graph of picoattn_matvec calls
+    attn = torch.randn(1, qd, generator=g, device=dev)
+    graph2 = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph2, stream=s):
+            for l in range(L):
+                lib.picoattn_matvec(projs[l].tensors[3].data_ptr(), p["types"][3], None, qd, dim, 1,
+                                    attn.data_ptr(), x.data_ptr(), 1, s.cuda_stream)
+    for _ in range(3):
+        graph2.replay()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(steps):
+        graph2.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    mv_us = e0.elapsed_time(e1) / steps / L * 1e3
+    mv_bytes = lib.picoattn_weight_bytes(p["types"][3], qd, dim)
+    peak, peak_kind = measured_peaks()
+    total = wbytes + kv_bytes
+    gbs = total / (ms / 1e3) / 1e9
+    del graph, graph2, st
+    return {"metric": "decode-layer attention block HBM GB/s", "value": round(gbs, 1), "unit": "GB/s",
+            "ms_per_step": round(ms, 4), "us_per_layer": round(ms / L * 1e3, 2), "steps": steps,
+            "config": {"workload": p["name"], "layers": L, "heads_q_kv_dim": [hq, hkv, hd], "dim": dim,
+                       "cached_rows": S - 1, "weights": "q,k,o Q4_K; v Q6_K (seeded random blocks)",
+                       "bytes_per_step": total, "weight_bytes": wbytes, "kv_bytes": kv_bytes},
+            "frac_of_hbm": round(gbs / peak, 4),
+            "roofline": {"bound": "hbm", "kernel": "matvec1_kernel<4> (Q4_K, 3584 x 3584, one vector)",
+                         "achieved": round(mv_bytes / (mv_us / 1e6) / 1e9, 1), "peak": peak, "peak_kind": peak_kind,
+                         "unit": "GB/s", "frac": round(mv_bytes / (mv_us / 1e6) / 1e9 / peak, 4),
+                         "us_per_launch": round(mv_us, 2), "weight_bytes_per_launch": mv_bytes}}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -718,6 +834,8 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill (Qwen3-8B) leg")
     ap.add_argument("--no-longctx", action="store_true", help="skip the long-context (Qwen2.5-32B, 128K) leg")
+    ap.add_argument("--no-layer", action="store_true",
+                    help="skip the decode-layer leg (projections + attention, Qwen2.5-7B, Q4_K_M weights)")
     ap.add_argument("--seqs", type=int, default=WORKLOAD["n_seqs"],
                     help="sequences per GPU (default 64 = the benchmark; smaller only for profiling)")
     args = ap.parse_args()
