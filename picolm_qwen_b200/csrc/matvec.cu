@@ -301,35 +301,39 @@ __global__ void __launch_bounds__(kMvWarps * 32, 2) matvec_kernel(MatvecArgs a) 
     }
 }
 
-// One vector: a warp takes groups of kMvRows consecutive rows (one matrix: the
-// host checks that every matrix's row count is a multiple of kMvRows) and
-// walks a group chunk step by chunk step, the group's rows in turn at each
-// step, so a lane loads its unit's 32 x values into registers once per step
-// and applies them to every row of the group: the x traffic through L1 falls
-// kMvRows-fold (in the row-at-a-time order it bounded the kernel), and the
-// group's matrix is looked up once.  Chunk slots as in matvec_kernel (block
-// formats and F16 only: F32 chunks need the larger slots).
+// One vector: a block takes a group of kMvRows consecutive rows (one matrix:
+// the host checks that every matrix's row count is a multiple of kMvRows) and
+// its warps take the group's chunk steps (32 units of 32 weights) in turn.  At
+// each of its steps a warp loads its lanes' units of x into registers once and
+// applies them to the group's rows (x traffic through L1 falls kMvRows-fold:
+// in the row-at-a-time order it bounded the kernel); the warps' partial sums
+// are added in warp order through shared memory, so results do not depend on
+// timing.  Many warps per row keep enough copies in flight even for the
+// 3,584-row matrices of a decode layer.  Chunk slots as in matvec_kernel
+// (block formats and F16 only: F32 chunks need the larger slots).
 constexpr int kMvRows = 4;
 
 template <int DEPTH>
 __global__ void __launch_bounds__(kMvWarps * 32, 2) matvec1_kernel(MatvecArgs a) {
     constexpr int kSlotWords = kMvRingWords / DEPTH;
     extern __shared__ __align__(16) uint32_t mv_smem[];
+    __shared__ float part_sums[kMvWarps][kMvRows];
     pdl_trigger();
     pdl_wait();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwb = blockDim.x >> 5;
     uint32_t* bufs = mv_smem + (size_t)warp * kMvRingWords;
     const int n_units = a.n_in / 32, cpr = (n_units + 31) / 32;
     const int n_groups = a.rows_total / kMvRows;
-    for (int grp = blockIdx.x * kMvWarps + warp; grp < n_groups; grp += gridDim.x * kMvWarps) {
+    for (int grp = blockIdx.x; grp < n_groups; grp += gridDim.x) {
         int row0;
         const MatvecPart P = part_of(a, grp * kMvRows, row0);
         const int upb = units_per_block(P.type), bb = P.block_bytes;
         const uint8_t* base = P.w + (size_t)row0 * P.row_bytes;
-        const int n_chunks = cpr * kMvRows;
-        // chunk c: step c / kMvRows (units from 32 * step), row row0 + c % kMvRows
+        // this warp's steps: warp, warp + nwb, ...; chunk c = (its k-th step, row c % kMvRows)
+        const int my_steps = warp < cpr ? (cpr - 1 - warp) / nwb + 1 : 0;
+        const int n_chunks = my_steps * kMvRows;
         auto span = [&](int c, int& b0, uintptr_t& g0, uintptr_t& a0, int& nwords, int& tail) {
-            const int u0 = (c / kMvRows) * 32;
+            const int u0 = (warp + (c / kMvRows) * nwb) * 32;
             b0 = u0 / upb;
             const int b1 = (min(n_units, u0 + 32) + upb - 1) / upb;
             const uint8_t* rowp = base + (size_t)(c % kMvRows) * P.row_bytes;
@@ -360,15 +364,15 @@ __global__ void __launch_bounds__(kMvWarps * 32, 2) matvec1_kernel(MatvecArgs a)
         for (int r = 0; r < kMvRows; r++) acc[r] = 0ull;
         float4 xr[8];  // this lane's unit of x at the current step
         for (int c = 0; c < DEPTH - 1; c++) issue(c);
-        for (int st = 0; st < cpr; st++) {
-            const int u = st * 32 + lane;
+        for (int k = 0; k < my_steps; k++) {
+            const int u = (warp + k * nwb) * 32 + lane;
             if (u < n_units) {
 #pragma unroll
                 for (int jj = 0; jj < 8; jj++) xr[jj] = __ldg(reinterpret_cast<const float4*>(a.x + 32 * u) + jj);
             }
 #pragma unroll
             for (int r = 0; r < kMvRows; r++) {
-                const int c = st * kMvRows + r;
+                const int c = k * kMvRows + r;
                 issue(c + DEPTH - 1);
                 cp_async_wait<DEPTH - 1>();
                 __syncwarp();  // chunk c is in its slot (every lane's copies and the tail)
@@ -376,18 +380,17 @@ __global__ void __launch_bounds__(kMvWarps * 32, 2) matvec1_kernel(MatvecArgs a)
                     int b0, nwords, tail;
                     uintptr_t g0, a0;
                     span(c, b0, g0, a0, nwords, tail);
-                    const int k = u - b0 * upb;
+                    const int ku = u - b0 * upb;
                     const uint8_t* blk = reinterpret_cast<const uint8_t*>(bufs + (c % DEPTH) * kSlotWords) +
-                                         (g0 - a0) + (size_t)(k / upb) * bb;
+                                         (g0 - a0) + (size_t)(ku / upb) * bb;
                     uint64_t one[1] = {acc[r]};
-                    unit_dot<1>(P.type, blk, k % upb, [&](int, int jj) { return xr[jj]; }, 1, one);
+                    unit_dot<1>(P.type, blk, ku % upb, [&](int, int jj) { return xr[jj]; }, 1, one);
                     acc[r] = one[0];
                 }
                 __syncwarp();  // the slot is read before chunk c + DEPTH overwrites it
             }
         }
         cp_async_wait<0>();
-        __syncwarp();
 #pragma unroll
         for (int r = 0; r < kMvRows; r++) {
             float lo, hi;
@@ -395,13 +398,19 @@ __global__ void __launch_bounds__(kMvWarps * 32, 2) matvec1_kernel(MatvecArgs a)
             float y = lo + hi;
 #pragma unroll
             for (int o = 16; o; o >>= 1) y += __shfl_xor_sync(0xffffffffu, y, o);
-            if (lane == 0) {
-                // matmul, then the bias added (vec_add), then the residual
-                if (P.bias) y = __fadd_rn(y, P.bias[row0 + r]);
-                float* o = P.out + row0 + r;
-                *o = a.accumulate ? __fadd_rn(*o, y) : y;
-            }
+            if (lane == 0) part_sums[warp][r] = y;
         }
+        __syncthreads();  // every warp's partial sums
+        if (warp == 0 && lane < kMvRows) {
+            float y = part_sums[0][lane];
+            for (int w2 = 1; w2 < nwb; w2++) y += part_sums[w2][lane];
+            // matmul, then the bias added (vec_add), then the residual
+            const int row = row0 + lane;
+            if (P.bias) y = __fadd_rn(y, P.bias[row]);
+            float* o = P.out + row;
+            *o = a.accumulate ? __fadd_rn(*o, y) : y;
+        }
+        __syncthreads();  // part_sums and the slots are free for the next group
     }
 }
 
@@ -478,8 +487,13 @@ cudaError_t launch_matvec(const MatvecArgs& a, cudaStream_t stream) {
     bool groups = a.n_vec == 1;  // row groups need every matrix's rows in whole groups
     for (int p = 0; p < a.n_parts; p++) groups = groups && a.part[p].n_out % kMvRows == 0;
     if (groups) {
-        const long long want1 = ((long long)a.rows_total / kMvRows + kMvWarps - 1) / kMvWarps;
-        cfg.gridDim = dim3((unsigned)std::max<long long>(1, std::min<long long>(want1, (long long)sms * 8)));
+        // a block per group of rows, a warp per chunk step (up to kMvWarps)
+        const int cpr = (a.n_in / 32 + 31) / 32;
+        const int nwb = std::min(kMvWarps, cpr);
+        const long long n_groups = a.rows_total / kMvRows;
+        cfg.gridDim = dim3((unsigned)std::max<long long>(1, std::min<long long>(n_groups, (long long)sms * 16)));
+        cfg.blockDim = dim3((unsigned)(nwb * 32));
+        cfg.dynamicSmemBytes = (size_t)nwb * kMvRingWords * 4;
         return cudaLaunchKernelEx(&cfg, matvec1_kernel<4>, a);
     }
     if (a.n_vec == 2) return cudaLaunchKernelEx(&cfg, matvec_kernel<2, 4>, a);
