@@ -359,6 +359,10 @@ __global__ void __launch_bounds__(kMvWarps * 32, 2) matvec1_kernel(MatvecArgs a)
             }
             cp_async_commit();
         };
+        // the group's row sums, rotated one place per row so that the current
+        // row's is always acc[0]: the row loop stays rolled (one copy of the
+        // decode in the instruction cache, not one per row) without indexing
+        // registers at run time
         uint64_t acc[kMvRows];
 #pragma unroll
         for (int r = 0; r < kMvRows; r++) acc[r] = 0ull;
@@ -370,7 +374,7 @@ __global__ void __launch_bounds__(kMvWarps * 32, 2) matvec1_kernel(MatvecArgs a)
 #pragma unroll
                 for (int jj = 0; jj < 8; jj++) xr[jj] = __ldg(reinterpret_cast<const float4*>(a.x + 32 * u) + jj);
             }
-#pragma unroll
+#pragma unroll 1
             for (int r = 0; r < kMvRows; r++) {
                 const int c = k * kMvRows + r;
                 issue(c + DEPTH - 1);
@@ -383,10 +387,14 @@ __global__ void __launch_bounds__(kMvWarps * 32, 2) matvec1_kernel(MatvecArgs a)
                     const int ku = u - b0 * upb;
                     const uint8_t* blk = reinterpret_cast<const uint8_t*>(bufs + (c % DEPTH) * kSlotWords) +
                                          (g0 - a0) + (size_t)(ku / upb) * bb;
-                    uint64_t one[1] = {acc[r]};
+                    uint64_t one[1] = {acc[0]};
                     unit_dot<1>(P.type, blk, ku % upb, [&](int, int jj) { return xr[jj]; }, 1, one);
-                    acc[r] = one[0];
+                    acc[0] = one[0];
                 }
+                const uint64_t t = acc[0];
+#pragma unroll
+                for (int q = 0; q + 1 < kMvRows; q++) acc[q] = acc[q + 1];
+                acc[kMvRows - 1] = t;
                 __syncwarp();  // the slot is read before chunk c + DEPTH overwrites it
             }
         }
