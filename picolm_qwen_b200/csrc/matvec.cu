@@ -180,8 +180,11 @@ __device__ __forceinline__ void unit_dot(int type, const uint8_t* blk, int sub, 
     }
 }
 
-__device__ __forceinline__ int units_per_block(int type) {
-    return (type == PICOATTN_WT_Q4_K || type == PICOATTN_WT_Q6_K) ? 8 : 1;
+// log2 of the 32-weight units per block (8 for Q4_K and Q6_K, else 1): the
+// chunk arithmetic shifts and masks instead of dividing by a run-time value (a
+// 32-bit division is a long instruction sequence)
+__device__ __forceinline__ int units_per_block_log2(int type) {
+    return (type == PICOATTN_WT_Q4_K || type == PICOATTN_WT_Q6_K) ? 3 : 0;
 }
 
 // The matrix (of up to three) that holds global row r, and r's row in it.
@@ -217,9 +220,9 @@ __global__ void __launch_bounds__(kMvWarps * 32, 2) matvec_kernel(MatvecArgs a) 
     auto chunk = [&](int j, MatvecPart& P, int& row, int& b0, uintptr_t& g0, uintptr_t& a0, int& nwords,
                      int& tail) {
         P = part_of(a, gw + (j / cpr) * nw, row);
-        const int upb = units_per_block(P.type), u0 = (j % cpr) * 32;
-        b0 = u0 / upb;
-        const int b1 = (min(n_units, u0 + 32) + upb - 1) / upb;
+        const int lu = units_per_block_log2(P.type), u0 = (j % cpr) * 32;
+        b0 = u0 >> lu;
+        const int b1 = (min(n_units, u0 + 32) + (1 << lu) - 1) >> lu;
         const uint8_t* rowp = P.w + (size_t)row * P.row_bytes;
         g0 = reinterpret_cast<uintptr_t>(rowp + (size_t)b0 * P.block_bytes);
         const uintptr_t g1 = reinterpret_cast<uintptr_t>(rowp + (size_t)b1 * P.block_bytes);
@@ -258,13 +261,13 @@ __global__ void __launch_bounds__(kMvWarps * 32, 2) matvec_kernel(MatvecArgs a) 
             int row, b0, nwords, tail;
             uintptr_t g0, a0;
             chunk(j, P, row, b0, g0, a0, nwords, tail);
-            const int upb = units_per_block(P.type), u = (j % cpr) * 32 + lane;
+            const int lu = units_per_block_log2(P.type), u = (j % cpr) * 32 + lane;
             if (u < n_units) {
-                const int k = u - b0 * upb;
+                const int k = u - (b0 << lu);
                 const uint8_t* blk = reinterpret_cast<const uint8_t*>(bufs + (j % DEPTH) * kSlotWords) + (g0 - a0) +
-                                     (size_t)(k / upb) * P.block_bytes;
+                                     (size_t)(k >> lu) * P.block_bytes;
                 const float* xu = a.x + (size_t)v0 * a.n_in + 32 * u;
-                unit_dot<NV>(P.type, blk, k % upb,
+                unit_dot<NV>(P.type, blk, k & ((1 << lu) - 1),
                              [&](int v, int jj) {
                                  return __ldg(reinterpret_cast<const float4*>(xu + (size_t)v * a.n_in) + jj);
                              },
@@ -327,15 +330,15 @@ __global__ void __launch_bounds__(kMvWarps * 32, 2) matvec1_kernel(MatvecArgs a)
     for (int grp = blockIdx.x; grp < n_groups; grp += gridDim.x) {
         int row0;
         const MatvecPart P = part_of(a, grp * kMvRows, row0);
-        const int upb = units_per_block(P.type), bb = P.block_bytes;
+        const int lu = units_per_block_log2(P.type), bb = P.block_bytes;
         const uint8_t* base = P.w + (size_t)row0 * P.row_bytes;
         // this warp's steps: warp, warp + nwb, ...; chunk c = (its k-th step, row c % kMvRows)
         const int my_steps = warp < cpr ? (cpr - 1 - warp) / nwb + 1 : 0;
         const int n_chunks = my_steps * kMvRows;
         auto span = [&](int c, int& b0, uintptr_t& g0, uintptr_t& a0, int& nwords, int& tail) {
             const int u0 = (warp + (c / kMvRows) * nwb) * 32;
-            b0 = u0 / upb;
-            const int b1 = (min(n_units, u0 + 32) + upb - 1) / upb;
+            b0 = u0 >> lu;
+            const int b1 = (min(n_units, u0 + 32) + (1 << lu) - 1) >> lu;
             const uint8_t* rowp = base + (size_t)(c % kMvRows) * P.row_bytes;
             g0 = reinterpret_cast<uintptr_t>(rowp + (size_t)b0 * bb);
             const uintptr_t g1 = reinterpret_cast<uintptr_t>(rowp + (size_t)b1 * bb);
@@ -384,11 +387,11 @@ __global__ void __launch_bounds__(kMvWarps * 32, 2) matvec1_kernel(MatvecArgs a)
                     int b0, nwords, tail;
                     uintptr_t g0, a0;
                     span(c, b0, g0, a0, nwords, tail);
-                    const int ku = u - b0 * upb;
+                    const int ku = u - (b0 << lu);
                     const uint8_t* blk = reinterpret_cast<const uint8_t*>(bufs + (c % DEPTH) * kSlotWords) +
-                                         (g0 - a0) + (size_t)(ku / upb) * bb;
+                                         (g0 - a0) + (size_t)(ku >> lu) * bb;
                     uint64_t one[1] = {acc[0]};
-                    unit_dot<1>(P.type, blk, ku % upb, [&](int, int jj) { return xr[jj]; }, 1, one);
+                    unit_dot<1>(P.type, blk, ku & ((1 << lu) - 1), [&](int, int jj) { return xr[jj]; }, 1, one);
                     acc[0] = one[0];
                 }
                 const uint64_t t = acc[0];
