@@ -40,8 +40,9 @@ namespace {
 constexpr int BM = 128;  // q rows per tile
 constexpr int BN = 128;  // keys per tile
 constexpr float kRescaleThreshold = 8.0f;
-// stale-max margin of the single-pass softmax: p <= 2^15 < 65504 stays finite and exact in fp16
-constexpr float kStaleMaxMargin = 15.0f;
+// largest p = 2^(s - stale max) the single-pass softmax keeps: 2^15 < 65504
+// stays finite and exact in fp16
+constexpr float kStaleMaxP = 32768.0f;
 
 // ---------------------------------------------------------------------------
 // prep (head-vector helpers in prep_common.cuh)
@@ -522,10 +523,10 @@ __device__ __forceinline__ void softmax_tile(uint32_t tS, uint32_t tO, uint32_t 
         }
         const float2 hmax = __half22float2(__hmax2(__hmax2(hm[0], hm[1]), __hmax2(hm[2], hm[3])));
         const float pmax = fmaxf(hmax.x, hmax.y);
-        if (!__any_sync(0xffffffffu, !(pmax <= 32768.0f))) {
+        if (!__any_sync(0xffffffffu, !(pmax <= kStaleMaxP))) {
             tmem_st32(tS + 0 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
             tmem_st32(tS + 32 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
-            float a0, a1, b0, b1;
+            float a0, a1;
             f2_unpack(f2_add(f2_add(ls2[0], ls2[1]), f2_add(ls2[2], ls2[3])), a0, a1);
             l_run += a0 + a1;
             done = true;
@@ -995,7 +996,7 @@ __device__ __forceinline__ void softmax_part(uint32_t tS, uint32_t tO, uint32_t 
     p_pass(psum, pmax);
     // every part must accept the stale max for these rows
     int* flags = reinterpret_cast<int*>(xs + SoftmaxXs<NP>::kFlags);
-    const bool ok = __all_sync(0xffffffffu, pmax <= 32768.0f);
+    const bool ok = __all_sync(0xffffffffu, pmax <= kStaleMaxP);
     if (lane == 0) flags[(t & 1) * NP + part] = ok ? 1 : 0;
     named_bar_sync(bar, NP * 32);
     bool ok_all = true;
