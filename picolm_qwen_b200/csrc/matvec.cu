@@ -352,7 +352,12 @@ __global__ void __launch_bounds__(kMvWarps * 32, 2) matvec1_kernel(MatvecArgs a)
                 uintptr_t g0, a0;
                 span(c, b0, g0, a0, nwords, tail);
                 uint32_t* dst = bufs + (c % DEPTH) * kSlotWords;
-                for (int i = lane; i < nwords; i += 32) cp_async4(dst + i, reinterpret_cast<const uint32_t*>(a0) + i);
+                // 16-byte copies where the chunk starts on a 16-byte boundary (the
+                // slots do), 4-byte copies for the rest
+                const int n16 = (a0 & 15u) == 0 ? nwords >> 2 : 0;
+                for (int i = lane; i < n16; i += 32) cp_async16(dst + 4 * i, reinterpret_cast<const uint32_t*>(a0) + 4 * i);
+                for (int i = 4 * n16 + lane; i < nwords; i += 32)
+                    cp_async4(dst + i, reinterpret_cast<const uint32_t*>(a0) + i);
                 if (tail && lane == 0) {  // the matrix may end inside a word: no read past it
                     uint32_t t = 0;
                     for (int k = 0; k < tail; k++)
