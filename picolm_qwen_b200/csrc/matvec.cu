@@ -3,16 +3,21 @@
 // engine multiplies with (TensorOps::matmul_bias, cpp/tensor.hpp:110-143;
 // block layouts cpp/quant.hpp:33-74, dequantisation cpp/quant.hpp:175-295).
 //
-// One warp per output row.  The warp stages the bytes of 32 consecutive
-// 32-weight units of its row into shared memory with coalesced 4-byte loads,
-// then each lane turns one unit into 32 fp32 weights with the same float
-// operations as the reference's dequantize_row_* (each product and difference
-// rounded on its own: no contraction, so the weights are bit-identical) and
-// accumulates their products with x in fp32.  The dot product's summation
-// order is the GPU's own (the reference sums in SSE lanes), so results agree
-// to rounding, not bit for bit.  Several matrices that read the same x (q, k
-// and v) go out in one launch, their rows dealt to warps in one sequence.
-// Bound by HBM: every weight byte is read once per group of NV vectors.
+// Work is cut into chunks: the bytes of 32 consecutive 32-weight units of one
+// row, copied into a warp's shared-memory slot with asynchronous copies, a few
+// chunks ahead of the one being used.  Each lane turns one unit into 32 fp32
+// weights with the same float operations as the reference's dequantize_row_*
+// (each product and difference rounded on its own: no contraction, so the
+// weights are bit-identical) and accumulates their products with x in fp32.
+// The dot product's summation order is the GPU's own (the reference sums in
+// SSE lanes), so results agree to rounding, not bit for bit.  One vector
+// (matvec1_kernel): a block per group of four consecutive rows, its warps
+// taking the group's chunk steps and holding their x values in registers for
+// the four rows.  Several vectors, or F32 weights (matvec_kernel): a warp per
+// row.  Several matrices that read the same x (q, k and v) go out in one
+// launch.  Every weight byte is read once per pass over the vectors; the
+// kernels are meant to be bound by HBM and today are bound by instruction
+// issue.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
