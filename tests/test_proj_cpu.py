@@ -97,3 +97,30 @@ def test_matvec_rejects_bad_arguments_on_the_host():
     assert call(t=7) == abi.PICOATTN_EUNSUPPORTED
     assert call(n_in=48) == abi.PICOATTN_EINVAL            # not whole Q8_0 blocks
     assert call(n_vec=0) == abi.PICOATTN_EINVAL
+
+
+def test_decode_layer_checks_arguments_on_the_host():
+    """picoattn_decode_layer rejects bad arguments before it touches the device."""
+    L = abi.lib()
+    cfg = abi.Config.make(2, 28, 4, 128, 1024, 1e6)
+    cp = C.byref(cfg)
+    dim = 3584
+    n = L.picoattn_decode_layer_workspace_size(cp, dim, 1, 1024)
+    assert n > L.picoattn_decode_workspace_size(cp, 1, 1024)  # decode scratch + q, k, v, attention output
+    assert L.picoattn_decode_layer_workspace_size(cp, 0, 1, 1024) == 0
+    buf = (C.c_uint8 * 256)()
+    a16 = (C.addressof(buf) + 15) & ~15
+    fake = a16  # never dereferenced: every case below fails its host check first
+
+    def call(wq_type=abi.WT_Q4_K, d=dim, xb=fake, ws_bytes=n, max_ctx=1024):
+        w = abi.LayerWeights(fake, fake, fake, fake, wq_type, abi.WT_Q4_K, abi.WT_Q6_K, abi.WT_Q4_K,
+                             None, None, None, None)
+        return L.picoattn_decode_layer(cp, 0, d, 1, max_ctx, xb, C.byref(w), None, None, fake, fake, fake, fake,
+                                       fake, fake, fake, ws_bytes, None)
+
+    assert call(xb=None) == abi.PICOATTN_EINVAL
+    assert call(xb=fake + 4) == abi.PICOATTN_EINVAL            # not 16-byte aligned
+    assert call(ws_bytes=n - 1) == abi.PICOATTN_ENOSPACE
+    assert call(wq_type=7) == abi.PICOATTN_EUNSUPPORTED        # Q5_0: not a format of the engine's mat-vec
+    assert call(d=3584 + 128) == abi.PICOATTN_EINVAL           # not whole 256-weight Q4_K blocks
+    assert call(max_ctx=2048) == abi.PICOATTN_ERANGE           # beyond max_seq_len
