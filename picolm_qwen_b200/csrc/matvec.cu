@@ -320,12 +320,15 @@ __global__ void __launch_bounds__(kMvWarps * 32, 2) matvec_kernel(MatvecArgs a) 
 // 3,584-row matrices of a decode layer.  Chunk slots as in matvec_kernel
 // (block formats and F16 only: F32 chunks need the larger slots).
 constexpr int kMvRows = 4;
+// warps per block of matvec1_kernel: at most four, so that the register bound
+// below lets five or more blocks share an SM (more copies in flight)
+constexpr int kMv1Warps = 4;
 
 template <int DEPTH>
-__global__ void __launch_bounds__(kMvWarps * 32, 2) matvec1_kernel(MatvecArgs a) {
+__global__ void __launch_bounds__(kMv1Warps * 32, 5) matvec1_kernel(MatvecArgs a) {
     constexpr int kSlotWords = kMvRingWords / DEPTH;
     extern __shared__ __align__(16) uint32_t mv_smem[];
-    __shared__ float part_sums[kMvWarps][kMvRows];
+    __shared__ float part_sums[kMv1Warps][kMvRows];
     pdl_trigger();
     pdl_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwb = blockDim.x >> 5;
@@ -508,9 +511,10 @@ cudaError_t launch_matvec(const MatvecArgs& a, cudaStream_t stream) {
     bool groups = a.n_vec == 1;  // row groups need every matrix's rows in whole groups
     for (int p = 0; p < a.n_parts; p++) groups = groups && a.part[p].n_out % kMvRows == 0;
     if (groups) {
-        // a block per group of rows, a warp per chunk step (up to kMvWarps)
+        // a block per group of rows, a warp per chunk step (up to kMv1Warps;
+        // with more steps each warp takes several in turn)
         const int cpr = (a.n_in / 32 + 31) / 32;
-        const int nwb = std::min(kMvWarps, cpr);
+        const int nwb = std::min(kMv1Warps, cpr);
         const long long n_groups = a.rows_total / kMvRows;
         cfg.gridDim = dim3((unsigned)std::max<long long>(1, std::min<long long>(n_groups, (long long)sms * 16)));
         cfg.blockDim = dim3((unsigned)(nwb * 32));

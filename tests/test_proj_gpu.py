@@ -48,7 +48,8 @@ def magnitude(oracle, w, wtype, n_in, n_out, x, bias):
 
 
 @pytest.mark.parametrize("wtype", FORMATS, ids=[wg.NAMES[t] for t in FORMATS])
-@pytest.mark.parametrize("n_in,n_out,n_vec", [(3584, 512, 1), (1024, 1000, 3), (4096, 64, 8), (512, 33, 2)])
+@pytest.mark.parametrize("n_in,n_out,n_vec", [(3584, 512, 1), (1024, 1000, 3), (4096, 64, 8), (512, 33, 2),
+                                               (8192, 96, 1)])
 def test_matvec_vs_reference(cuda, oracle, ref, wtype, n_in, n_out, n_vec):
     from picolm_qwen_b200.runtime import matvec
     rng = np.random.default_rng(wtype * 7919 + n_in + n_vec)
