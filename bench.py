@@ -431,7 +431,9 @@ def run_ours(args) -> None:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f16 cache, f32 accumulate", "data": "synthetic",
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 cache; q (pre-scaled) and softmax P rounded to f16 as tensor-core operands; f32 accumulate",
+            "data": "synthetic",
             "config": {"workload": w["name"], "layers": L, "sequences_per_gpu": B,
                        "heads_q_kv_dim": [hq, hkv, hd], "cached_len_range": [w["len_lo"], w["len_hi"]],
                        "bytes_per_step_per_gpu": nbytes, "l2": "inputs (15.8 GiB/step) larger than L2, no flush",

@@ -204,7 +204,9 @@ int32_t picoattn_decode_one(const picoattn_config_t* cfg, int32_t layer, int32_t
  *   (different streams) race and must not be issued.
  *   status_out (host, optional): when non-NULL the call synchronises `stream`
  *   and stores the device status bits (PICOATTN_DEV_*) there; a non-zero value
- *   is also returned as PICOATTN_EDEVSTATUS.
+ *   is also returned as PICOATTN_EDEVSTATUS.  This is the only way to observe
+ *   them: with status_out NULL the bits stay in the shared array, which the
+ *   next call clears, and no other entry point reads them.
  * Other arguments as for picoattn_decode.
  */
 int32_t picoattn_decode_noalloc(const picoattn_config_t* cfg, int32_t layer, int32_t n_seqs, int32_t max_ctx,

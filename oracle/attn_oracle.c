@@ -401,6 +401,35 @@ int ora_decode_batch(int B, int hq, int hkv, int hd, int rope_mode, float eps,
     return 0;
 }
 
+typedef struct {
+    int hq, hkv, hd, n_parts;
+    const float* qrot;
+    const uint16_t *kc, *vc;
+    int pos;
+    float* out;
+} heads_ctx_t;
+
+static int heads_task(void* vctx, int task) {
+    heads_ctx_t* c = (heads_ctx_t*)vctx;
+    const int h0 = (int)((long long)task * c->hq / c->n_parts), h1 = (int)((long long)(task + 1) * c->hq / c->n_parts);
+    attend_token(c->hq, c->hkv, c->hd, c->qrot, c->kc, c->vc, c->pos, c->out, 0, h0, h1);
+    return 0;
+}
+
+/* ora_decode_step (variant 0) with the q heads spread over n_threads host
+ * threads: the same per-head arithmetic, for one long sequence. */
+int ora_decode_step_mt(int hq, int hkv, int hd, int rope_mode, float eps,
+                       float* q, float* k, const float* v,
+                       const float* qn_w, const float* kn_w,
+                       const float* cos_row, const float* sin_row,
+                       uint16_t* kc, uint16_t* vc, int pos, float* out, int n_threads) {
+    if (bad_shape(hq, hkv, hd) || pos < 0 || !q || !k || !v || !kc || !vc || !out) return -1;
+    prep_token(hq, hkv, hd, rope_mode, eps, q, k, v, qn_w, kn_w, cos_row, sin_row, kc, vc, pos);
+    heads_ctx_t ctx = {hq, hkv, hd, hq, q, kc, vc, pos, out};
+    run_tasks(heads_task, &ctx, hq, n_threads);
+    return 0;
+}
+
 /* ------------------------------------------------------------------------ */
 /* Projections: GGUF block dequantisation and the mat-vec                   */
 /* ------------------------------------------------------------------------ */

@@ -60,6 +60,14 @@ int ora_decode_step(int hq, int hkv, int hd, int rope_mode, float eps,
                     const float* cos_row, const float* sin_row,
                     uint16_t* kc, uint16_t* vc, int pos, float* out, int variant);
 
+/* ora_decode_step variant 0 with the q heads spread over n_threads host
+ * threads (same per-head arithmetic); for long single sequences. */
+int ora_decode_step_mt(int hq, int hkv, int hd, int rope_mode, float eps,
+                       float* q, float* k, const float* v,
+                       const float* qn_w, const float* kn_w,
+                       const float* cos_row, const float* sin_row,
+                       uint16_t* kc, uint16_t* vc, int pos, float* out, int n_threads);
+
 /*
  * Attention only over rows [row_begin, row_end) of an already-filled cache,
  * returning the un-normalised online-softmax state per q head:

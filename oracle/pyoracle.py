@@ -57,6 +57,10 @@ class Oracle:
         L.ora_decode_step.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
                                       _f32p, _f32p, _f32p, C.c_void_p, C.c_void_p,
                                       _f32p, _f32p, _u16p, _u16p, C.c_int, _f32p, C.c_int]
+        L.ora_decode_step_mt.restype = C.c_int
+        L.ora_decode_step_mt.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
+                                         _f32p, _f32p, _f32p, C.c_void_p, C.c_void_p,
+                                         _f32p, _f32p, _u16p, _u16p, C.c_int, _f32p, C.c_int]
         L.ora_attend_rows.argtypes = [C.c_int, C.c_int, C.c_int, _f32p, _u16p, _u16p,
                                       C.c_int, C.c_int, _f32p, _f32p, _f32p]
         L.ora_prefill.restype = C.c_int
@@ -149,6 +153,23 @@ class Oracle:
                                     c, s, kc, vc, pos, out, variant)
         assert rc == 0
         return out, q, k
+
+    def decode_step_mt(self, hq, hkv, hd, rope_mode, q, k, v, qn_w, kn_w, cos_t, sin_t,
+                       kc, vc, pos, n_threads, eps=1e-6):
+        """decode_step (C++ engine order) with the q heads spread over host threads."""
+        q = np.array(q, np.float32)
+        k = np.array(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        out = np.empty(hq * hd, np.float32)
+        half = hd // 2
+        c = np.ascontiguousarray(cos_t[pos], np.float32).reshape(half)
+        s = np.ascontiguousarray(sin_t[pos], np.float32).reshape(half)
+        qn = None if qn_w is None else np.ascontiguousarray(qn_w, np.float32)
+        kn = None if kn_w is None else np.ascontiguousarray(kn_w, np.float32)
+        rc = self.L.ora_decode_step_mt(hq, hkv, hd, rope_mode, eps, q, k, v, _opt(qn), _opt(kn),
+                                       c, s, kc, vc, pos, out, n_threads)
+        assert rc == 0
+        return out
 
     def attend_rows(self, hq, hkv, hd, q_rot, kc, vc, b, e):
         m = np.empty(hq, np.float32)

@@ -15,36 +15,41 @@
 using namespace picoattn;
 
 namespace {
-
 thread_local cudaError_t g_last_cuda_error = cudaSuccess;
+}  // namespace
 
-int32_t cuda_status(cudaError_t e) {
+int32_t picoattn::cuda_status(cudaError_t e) {
     if (e == cudaSuccess) return PICOATTN_OK;
     g_last_cuda_error = e;
     return PICOATTN_ECUDA;
 }
 
+namespace {
+
 bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
-// Cached per process: the sm_100 check runs once per device.
+// The sm_100 check, once per device (cached; thread-safe).  A device of
+// another architecture reads as cudaErrorNoKernelImageForDevice inside the
+// cache and maps to PICOATTN_EDEVICE.
 int32_t device_ok() {
-    static int checked_dev = -1;
-    static int32_t verdict = PICOATTN_EDEVICE;
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return PICOATTN_ECUDA;
-    if (dev == checked_dev) return verdict;
-    cudaDeviceProp prop;
-    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return PICOATTN_ECUDA;
-    verdict = prop.major == 10 && prop.minor == 0 ? PICOATTN_OK : PICOATTN_EDEVICE;
-    checked_dev = dev;
-    return verdict;
+    static PerDeviceOnce check;
+    const cudaError_t e = check.run([] {
+        int dev = 0, major = 0, minor = 0;
+        cudaError_t r = cudaGetDevice(&dev);
+        if (r == cudaSuccess) r = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+        if (r == cudaSuccess) r = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+        if (r != cudaSuccess) return r;
+        return major == 10 && minor == 0 ? cudaSuccess : cudaErrorNoKernelImageForDevice;
+    });
+    if (e == cudaErrorNoKernelImageForDevice) return PICOATTN_EDEVICE;
+    return cuda_status(e);
 }
 
 int32_t decode_common(const picoattn_config_t* cfg, int32_t layer, int32_t n_seqs, int32_t max_ctx,
                       const float* q, const float* k, const float* v, const float* qn, const float* kn,
                       const float* rc, const float* rs, uint16_t* const* kcp, uint16_t* const* vcp,
                       uint16_t* kc1, uint16_t* vc1, const int32_t* pos_dev, int32_t pos_host, float* out,
-                      void* ws, size_t ws_bytes, cudaStream_t stream, uint32_t stages, int wait_inputs = 0) {
+                      void* ws, size_t ws_bytes, cudaStream_t stream, uint32_t stages) {
     int32_t st = picoattn_config_check(cfg);
     if (stages == 0 || (stages & ~PICOATTN_STAGE_ALL)) return PICOATTN_EINVAL;
     if (st != PICOATTN_OK) return st;
@@ -92,7 +97,6 @@ int32_t decode_common(const picoattn_config_t* cfg, int32_t layer, int32_t n_seq
     a.stages = plan.stages;
     a.warps_per_head = plan.warps_per_head;
     a.compute_warps = plan.compute_warps;
-    a.wait_inputs = wait_inputs;
     return cuda_status(launch_decode(a, plan, stream, stages));
 }
 
@@ -371,7 +375,7 @@ int32_t picoattn_decode_layer(const picoattn_config_t* cfg, int32_t layer, int32
     st = cuda_status(launch_matvec(qkv, s));
     if (st != PICOATTN_OK) return st;
     st = decode_common(cfg, layer, n_seqs, max_ctx, q, k, v, q_norm_w, k_norm_w, rope_cos, rope_sin, k_cache,
-                       v_cache, nullptr, nullptr, pos, 0, attn, workspace, l.q, s, PICOATTN_STAGE_ALL, 1);
+                       v_cache, nullptr, nullptr, pos, 0, attn, workspace, l.q, s, PICOATTN_STAGE_ALL);
     if (st != PICOATTN_OK) return st;
     o.n_parts = 1;
     o.n_in = qd;

@@ -833,8 +833,10 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
 
     // Programmatic dependent launch: this kernel may start while the kernels
     // before it still run.  With one sequence its attended rows follow from the
-    // position alone, so the CTAs lay out their slices, stream the cache rows
-    // that are already final and rotate q at once.  The new k/v row comes from
+    // position alone, so the CTAs lay out their slices and stream the cache
+    // rows that are already final at once; q, k and v are caller inputs that the
+    // kernel before may still be writing, so the compute warps wait for it
+    // before they read and rotate them.  The new k/v row comes from
     // the prep kernel (waited for before the tile that holds it) or, when all
     // stages run in one call (fused_append), from this kernel: the CTA whose
     // slice holds it computes and stores it first, and its producer waits for
@@ -845,8 +847,8 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
     //
     // The producer warp sets the CTA up (position, cache bases, barriers, its
     // slice) and starts streaming at once; the compute warps of a fused call
-    // rotate q meanwhile (they load the position themselves) and meet the
-    // producer's setup at a named barrier.
+    // wait for the kernel before, rotate q (they load the position themselves)
+    // and meet the producer's setup at a named barrier.
     const long long* prefix = a.n_seqs == 1 ? s_prefix : a.prefix;
     if (a.n_seqs != 1) pdl_wait();
     uint32_t qa[HD / 16][4];  // the q rows of this compute warp's KV head (MMA A operand)
@@ -889,7 +891,9 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
         named_bar_arrive(kSetupBar, blockDim.x);
     } else {
         if (a.fused_append) {  // one sequence: q from the caller's buffer, rotated here
-            if (a.wait_inputs) pdl_wait();  // written by the projection kernel before this one
+            // q, k and v may come from the kernel before this one (a projection
+            // that let this kernel launch early): wait for it before reading them
+            pdl_wait();
             int p = 0;
             if (lane == 0) p = seq_pos(a, 0);
             p = __shfl_sync(0xffffffffu, p, 0);
@@ -1120,8 +1124,8 @@ cudaError_t launch_pdl(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem,
 
 template <int HD>
 cudaError_t launch_decode_hd(const DecodeArgs& a_in, const DecodePlan& plan, cudaStream_t stream, unsigned stages) {
-    static bool attr_done = false;
-    if (!attr_done) {
+    static PerDeviceOnce setup;
+    const cudaError_t se = setup.run([] {
         // The small kernels ask for the largest shared-memory carveout, so that an
         // attention CTA launched early (programmatic dependent launch) fits on an
         // SM that still runs one of them.
@@ -1138,9 +1142,9 @@ cudaError_t launch_decode_hd(const DecodeArgs& a_in, const DecodePlan& plan, cud
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(decode_merge_seq_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      MergeSeqShape<HD>::bytes);
-        if (e != cudaSuccess) return e;
-        attr_done = true;
-    }
+        return e;
+    });
+    if (se != cudaSuccess) return se;
     // One sequence with every stage in this call: the attention kernel appends
     // the new row itself and the merge derives the rows from the position, so
     // no prep kernel runs.

@@ -78,11 +78,13 @@ extern "C" int32_t picoattn_decode_noalloc(const picoattn_config_t* cfg, int32_t
     st = picoattn_device_check();
     if (st != PICOATTN_OK) return st;
     void* scratch = nullptr;
-    if (scratch_address(&scratch) != cudaSuccess) return PICOATTN_ECUDA;
+    st = cuda_status(scratch_address(&scratch));
+    if (st != PICOATTN_OK) return st;
     cudaStream_t s = (cudaStream_t)stream;
     // the sticky status word must start each call at zero; everything else in
     // the scratch is written by the kernels before it is read
-    if (cudaMemsetAsync(scratch, 0, kWsHeaderBytes, s) != cudaSuccess) return PICOATTN_ECUDA;
+    st = cuda_status(cudaMemsetAsync(scratch, 0, kWsHeaderBytes, s));
+    if (st != PICOATTN_OK) return st;
 
     uint8_t* w = static_cast<uint8_t*>(scratch);
     DecodeArgs a{};
@@ -113,12 +115,14 @@ extern "C" int32_t picoattn_decode_noalloc(const picoattn_config_t* cfg, int32_t
     a.stages = plan.stages;
     a.warps_per_head = plan.warps_per_head;
     a.compute_warps = plan.compute_warps;
-    if (launch_decode(a, plan, s, PICOATTN_STAGE_ALL) != cudaSuccess) return PICOATTN_ECUDA;
+    st = cuda_status(launch_decode(a, plan, s, PICOATTN_STAGE_ALL));
+    if (st != PICOATTN_OK) return st;
     if (status_out) {
         unsigned int dev_status = 0;
-        if (cudaMemcpyAsync(&dev_status, scratch, sizeof dev_status, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
-            cudaStreamSynchronize(s) != cudaSuccess)
-            return PICOATTN_ECUDA;
+        cudaError_t e = cudaMemcpyAsync(&dev_status, scratch, sizeof dev_status, cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        st = cuda_status(e);
+        if (st != PICOATTN_OK) return st;
         *status_out = dev_status;
         if (dev_status) return PICOATTN_EDEVSTATUS;
     }

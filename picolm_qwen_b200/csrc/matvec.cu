@@ -492,15 +492,16 @@ cudaError_t launch_matvec(const MatvecArgs& a, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    static bool attr_done = false;
-    if (!attr_done) {
+    static PerDeviceOnce setup;
+    const cudaError_t se = setup.run([] {
         for (auto k : {matvec_kernel<1, 2>, matvec_kernel<2, 2>, matvec_kernel<4, 2>, matvec_kernel<1, 4>,
                        matvec_kernel<2, 4>, matvec_kernel<4, 4>, matvec1_kernel<4>}) {
             const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMvSmem);
             if (e != cudaSuccess) return e;
         }
-        attr_done = true;
-    }
+        return cudaSuccess;
+    });
+    if (se != cudaSuccess) return se;
     bool f32 = false;  // F32 chunks need the 4 KB slots
     for (int p = 0; p < a.n_parts; p++) f32 = f32 || a.part[p].type == PICOATTN_WT_F32;
     if (f32) {

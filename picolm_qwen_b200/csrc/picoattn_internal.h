@@ -3,6 +3,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <mutex>
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -19,6 +20,38 @@ struct WsHeader {
 constexpr size_t kWsHeaderBytes = 256;
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// One-time setup per CUDA device.  Kernel attributes (the dynamic shared-memory
+// limit, the carveout) belong to a device, so a process that drives several
+// GPUs sets them on each; run() calls setup() the first time it sees the
+// current device and returns that result on every later call with the same
+// device current.  Thread-safe.
+class PerDeviceOnce {
+  public:
+    template <class F>
+    cudaError_t run(F&& setup) {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        if (dev < 0 || dev >= kMaxDev) return cudaErrorInvalidDevice;
+        std::lock_guard<std::mutex> lock(mu_);
+        if (!done_[dev]) {
+            err_[dev] = setup();
+            done_[dev] = true;
+        }
+        return err_[dev];
+    }
+
+  private:
+    static constexpr int kMaxDev = 64;
+    std::mutex mu_;
+    bool done_[kMaxDev] = {};
+    cudaError_t err_[kMaxDev] = {};
+};
+
+// Records a CUDA error for picoattn_last_cuda_error() on the calling thread and
+// maps it to a status: PICOATTN_OK for cudaSuccess, else PICOATTN_ECUDA.
+int32_t cuda_status(cudaError_t e);
 
 // Decode launch plan: how the cache rows of a sequence are cut into chunks
 // (one CTA each), tiles (one pipeline stage each) and row groups (16 rows, one
@@ -83,7 +116,6 @@ struct DecodeArgs {
     int n_slots;
     int tile_rows, stages, warps_per_head, compute_warps;
     int fused_append;          // one sequence, all stages: the attention kernel appends the new k/v row itself
-    int wait_inputs;           // q/k/v come from the kernel before (projections): wait for it before reading them
     XchgArgs x;                // the merge kernel exchanges the shard results (x.peers non-null)
 };
 

@@ -95,7 +95,7 @@ int32_t decode_shard_impl(const picoattn_config_t* cfg, int32_t layer, int32_t n
     a.stages = plan.stages;
     a.warps_per_head = plan.warps_per_head;
     a.compute_warps = plan.compute_warps;
-    return launch_decode(a, plan, stream, PICOATTN_STAGE_ALL) == cudaSuccess ? PICOATTN_OK : PICOATTN_ECUDA;
+    return cuda_status(launch_decode(a, plan, stream, PICOATTN_STAGE_ALL));
 }
 
 }  // namespace picoattn
@@ -127,10 +127,8 @@ int32_t picoattn_combine_shards(const picoattn_config_t* cfg, int32_t n_seqs, in
     if (n_seqs <= 0 || n_shards <= 0 || !partials || !out) return PICOATTN_EINVAL;
     st = picoattn_device_check();
     if (st != PICOATTN_OK) return st;
-    return launch_combine_shards(partials, out, n_seqs, cfg->n_heads, cfg->head_dim, n_shards,
-                                 (cudaStream_t)stream) == cudaSuccess
-               ? PICOATTN_OK
-               : PICOATTN_ECUDA;
+    return cuda_status(
+        launch_combine_shards(partials, out, n_seqs, cfg->n_heads, cfg->head_dim, n_shards, (cudaStream_t)stream));
 }
 
 }  // extern "C"

@@ -1,4 +1,4 @@
-"""Full-forward parity on the GPU (SURVEY-style oracle c2): a 3-layer model with
+"""Full-forward parity on the GPU (the full-forward oracle): a 3-layer model with
 seeded random weights, run by the reference's unmodified Model::forward_batch
 (a 40-token prompt) and Model::forward (24 decode steps), against the same model
 run by a host loop whose attention block is this library through the C ABI

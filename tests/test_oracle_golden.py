@@ -127,3 +127,17 @@ def test_c_engine_order_agrees_within_noise(oracle, golden_dir):
     o1, _, _ = oracle.decode_step(hq, hkv, hd, 0, g["q"][i], g["k"][i], g["v"][i], None, None,
                                   cos_t, sin_t, kc, vc, last, variant=1)
     assert np.max(np.abs(o1 - g["out"][i])) < 1e-5
+
+
+def test_head_threaded_step_matches_reference_golden(oracle, golden_dir):
+    """The head-parallel driver used for the long-context parity checks gives
+    the reference's outputs bit for bit (same per-head arithmetic)."""
+    g = _load(golden_dir, "decode_cfg5_qwen32b.npz")
+    hq, hkv, hd, last = int(g["hq"]), int(g["hkv"]), int(g["hd"]), int(g["last_pos"])
+    cos_t, sin_t = oracle.rope_table(last + 1, hd, float(g["rope_base"]))
+    kc, vc = g["kcache"].copy(), g["vcache"].copy()
+    i = int(g["keep"]) - 1
+    out = oracle.decode_step_mt(hq, hkv, hd, int(g["rope_mode"]), g["q"][i], g["k"][i], g["v"][i], None, None,
+                                cos_t, sin_t, kc, vc, last, n_threads=7)
+    assert np.array_equal(out, g["out"][i])
+    assert np.array_equal(kc[last], g["kcache"][last]) and np.array_equal(vc[last], g["vcache"][last])

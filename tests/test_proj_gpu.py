@@ -178,3 +178,56 @@ def test_decode_layer_graph_replay_matches_eager(cuda, oracle):
     torch.cuda.synchronize()
     assert torch.equal(x, eager)
     assert st.status() == 0
+
+
+def test_public_matvec_then_decode_one_back_to_back(cuda, oracle, ref):
+    """A host that runs its projections with picoattn_matvec and then calls
+    picoattn_decode_one on the same stream, with no synchronisation between
+    them.  The projection kernel lets the next kernel launch before it has
+    stored its outputs, so the decode kernels must wait for it before they read
+    q, k and v: outputs and new cache rows must match the reference chain on
+    every one of several repetitions."""
+    from picolm_qwen_b200 import abi
+    from picolm_qwen_b200.runtime import AttnState, matvec
+    hq, hkv, hd, dim, S = 28, 4, 128, 3584, 4096
+    qd, kvd = hq * hd, hkv * hd
+    rng = np.random.default_rng(77)
+    cfg = abi.Config.make(1, hq, hkv, hd, S, 1e6)
+    st = AttnState(cfg, n_seqs=1, max_ctx=S)
+    n = 4000  # cached rows; the new token sits at pos n
+    kc = np.zeros((S, kvd), np.uint16)
+    vc = np.zeros((S, kvd), np.uint16)
+    kc[:n] = oracle.f32_to_f16((rng.standard_normal((n, kvd)) * 0.5).astype(np.float32)).reshape(n, kvd)
+    vc[:n] = oracle.f32_to_f16((rng.standard_normal((n, kvd)) * 0.5).astype(np.float32)).reshape(n, kvd)
+    types = (13, 13, 15)
+    wq, wk, wv = (wg.make(t, dim, n_out, rng) for t, n_out in zip(types, (qd, kvd, kvd)))
+    dwq, dwk, dwv = dev(wq), dev(wk), dev(wv)
+    cos_t, sin_t = oracle.rope_table(S, hd, 1e6)
+    q_buf = torch.empty((1, qd), device="cuda")
+    k_buf = torch.empty((1, kvd), device="cuda")
+    v_buf = torch.empty((1, kvd), device="cuda")
+    out = torch.empty(qd, device="cuda")
+    for rep in range(4):
+        xb = rng.standard_normal((1, dim)).astype(np.float32)
+        q = ref.matvec(wq, types[0], None, dim, qd, xb)
+        k = ref.matvec(wk, types[1], None, dim, kvd, xb)
+        v = ref.matvec(wv, types[2], None, dim, kvd, xb)
+        kr, vr = kc.copy(), vc.copy()
+        want, _, _ = oracle.decode_step(hq, hkv, hd, 0, q[0], k[0], v[0], None, None, cos_t, sin_t, kr, vr, n)
+        st.k_cache[0, 0] = dev(kc.view(np.int16))
+        st.v_cache[0, 0] = dev(vc.view(np.int16))
+        dxb = dev(xb)
+        for buf in (q_buf, k_buf, v_buf, out):
+            buf.fill_(float("nan"))
+        matvec(dwq, types[0], dim, qd, dxb, q_buf)
+        matvec(dwk, types[1], dim, kvd, dxb, k_buf)
+        matvec(dwv, types[2], dim, kvd, dxb, v_buf)
+        assert st.decode_one(0, n, q_buf, k_buf, v_buf, out) == 0
+        torch.cuda.synchronize()
+        assert st.status() == 0
+        got = out.cpu().numpy()
+        err = np.abs(got.astype(np.float64) - want)
+        assert (err <= 2e-3 + 1e-2 * np.abs(want)).all(), f"rep {rep}: max err {np.nanmax(err):.3g}"
+        for c, r in ((st.k_cache, kr), (st.v_cache, vr)):
+            row = c[0, 0, n].cpu().numpy().view(np.uint16).astype(np.int32)
+            assert np.abs(row - r[n].astype(np.int32)).max() <= 1, f"rep {rep}: new cache row"

@@ -6,7 +6,10 @@ RunState once) or a host whose device memory belongs to another allocator.
 For them picoattn_decode_noalloc keeps its scratch in a fixed 8 MiB array
 inside the library.  This test calls it through the C ABI twice in a row and
 checks each result against picoattn_decode (the workspace entry point) on the
-same inputs, with the tolerance the other decode tests use.
+same inputs.  Both run the same kernels on the same data, so the outputs and
+cache rows must be identical bit for bit; the first call is also checked
+against the oracle's restatement of the reference loop, with the tolerance the
+other decode tests use.
 
 Kept in a file of its own, named to be collected last.
 """
@@ -37,7 +40,7 @@ def cuda():
     return torch.device("cuda")
 
 
-def test_noalloc_decode_matches_workspace_decode_twice(cuda):
+def test_noalloc_decode_matches_workspace_decode_twice(cuda, oracle):
     from picolm_qwen_b200 import abi
     from picolm_qwen_b200.runtime import AttnState, stream_handle
 
@@ -67,6 +70,12 @@ def test_noalloc_decode_matches_workspace_decode_twice(cuda):
         v = torch.randn((B, hkv * hd), generator=g, device="cuda")
         want = torch.empty((B, hq * hd), device="cuda")
         got = torch.full((B, hq * hd), float("nan"), device="cuda")
+        if call == 0:  # the oracle on the caches as they are before this call
+            kcs = [ref.k_cache[b, layer].cpu().numpy().view(np.uint16).copy() for b in range(B)]
+            vcs = [ref.v_cache[b, layer].cpu().numpy().view(np.uint16).copy() for b in range(B)]
+            cos_t, sin_t = ref.rope_cos.cpu().numpy(), ref.rope_sin.cpu().numpy()
+            ora = oracle.decode_batch(hq, hkv, hd, 0, q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy(), None, None,
+                                      cos_t, sin_t, kcs, vcs, (lens + extra).astype(np.int32), n_threads=4)
         ref.decode(layer, q, k, v, pos, want, max_ctx=max_ctx)
         status = C.c_uint32(12345)
         st = L.picoattn_decode_noalloc(C.byref(cfg), layer, B, max_ctx, q.data_ptr(), k.data_ptr(), v.data_ptr(),
@@ -76,8 +85,10 @@ def test_noalloc_decode_matches_workspace_decode_twice(cuda):
         assert st == abi.PICOATTN_OK, L.picoattn_strerror(st)
         assert status.value == 0
         torch.cuda.synchronize()
-        assert_close(got.cpu().numpy(), want.cpu().numpy(), f"call {call}")
+        assert torch.equal(got, want), f"call {call}: outputs differ from picoattn_decode's"
         assert torch.equal(mine.k_cache, ref.k_cache) and torch.equal(mine.v_cache, ref.v_cache)
+        if call == 0:
+            assert_close(got.cpu().numpy(), ora, "call 0 vs oracle")
 
 
 def test_noalloc_rejects_requests_beyond_its_scratch(cuda):
