@@ -12,8 +12,14 @@ needed between steps.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Under torchrun (N > 1) every rank runs its own 64 sequences (weak scaling; no
-collective on the data path) and rank 0 prints one JSON line.
+Under torchrun (N > 1) the same 64 sequences are dealt to the ranks
+longest-first onto the least-loaded rank (strong scaling; no collective on the
+data path), the step time is the maximum over ranks, and rank 0 prints one
+JSON line.  Further legs in the same line: prefill (Qwen3-8B, 2048 tokens;
+KV-head groups sharded across ranks), long-context decode (Qwen2.5-32B, 128K
+rows; rows sharded, exchange over NVLink), the two small single-sequence
+configurations (TinyLlama at position 511, Qwen2.5-0.5B at 4096; N=1) and the
+decode layer with its projections (N=1).
 """
 from __future__ import annotations
 
@@ -55,12 +61,13 @@ def measured_peaks() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
-def profiled_traffic() -> float | None:
-    """DRAM bytes per attention launch from the committed ncu summary, if any."""
+def profiled_traffic(leg: str = "batched") -> float | None:
+    """DRAM bytes per attention launch of a leg from the committed ncu summary, if any."""
     p = os.path.join(ROOT, "profiles", "decode_attn_traffic.json")
     try:
         with open(p) as f:
-            return float(json.load(f)["dram_bytes_per_launch"])
+            d = json.load(f)
+        return float(d["dram_bytes_per_launch"] if leg == "batched" else d[leg]["dram_bytes_per_launch"])
     except Exception:
         return None
 
@@ -191,10 +198,17 @@ def cpu_baseline(lens: np.ndarray) -> dict:
     cores = os.cpu_count() or 1
     secs = run_cpu_sample(runner, lens, S, kcs, vcs, cores, rng)
     gbs = step_bytes(lens, 1, kvd) / secs / 1e9
+    # reference-faithful: one thread, as the reference runs its attention loop
+    n1 = 4
+    secs1 = run_cpu_sample(runner, lens[:n1], S, kcs[:n1], vcs[:n1], 1, rng)
+    gbs1 = step_bytes(lens[:n1], 1, kvd) / secs1 / 1e9
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
             "sample": f"1 of 28 layers x {len(lens)} sequences (same lengths), {secs:.2f} s wall, "
                       f"one host thread per sequence; the reference's attention loop (cpp/model.hpp:326-418) "
-                      f"compiled from its sources"}
+                      f"compiled from its sources",
+            "one_core": {"value": round(gbs1, 4), "unit": "GB/s", "cores": 1, "kind": kind,
+                         "sample": f"1 layer x the first {n1} sequences on one thread ({secs1:.2f} s), "
+                                   f"the reference's own single-threaded loop"}}
 
 
 def run_reference_arm(args) -> None:
@@ -224,7 +238,7 @@ def run_reference_arm(args) -> None:
     gbs = nbytes / total / 1e9
     line = {"metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "impl": "reference",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32 (fp16 cache)", "data": "synthetic",
             "config": {"workload": w["name"] + " (CPU sample)", "layers_per_step": 1, "sequences": n_sample,
                        "heads": [w["n_heads"], w["n_kv_heads"], w["head_dim"]]},
@@ -254,10 +268,14 @@ def run_ours(args) -> None:
     from picolm_qwen_b200 import abi
     from picolm_qwen_b200.runtime import AttnState, stream_handle
 
+    from picolm_qwen_b200 import sharding
+
     w = WORKLOAD
     L, hq, hkv, hd = w["n_layers"], w["n_heads"], w["n_kv_heads"], w["head_dim"]
     kvd, qd = hkv * hd, hq * hd
-    lens = seq_lengths(rank)
+    lens_all = seq_lengths(0)
+    mine = sharding.lpt_assign(lens_all, world)[rank]  # this rank's sequences (strong scaling)
+    lens = lens_all[mine]
     B = len(lens)
     S = int(lens.max()) + 1
     max_ctx = S
@@ -407,18 +425,25 @@ def run_ours(args) -> None:
     if world == 1 and not args.no_layer:
         torch.cuda.empty_cache()
         layer_line = run_layer(args, dev)
+    small_lines = []
+    if world == 1 and not args.no_small:
+        for spec in SMALL:
+            torch.cuda.empty_cache()
+            small_lines.append(run_small(args, dev, spec))
 
     nbytes = step_bytes(lens, L, kvd)
-    times = torch.tensor([elapsed_ms, e2e_ms, float(nbytes)], dtype=torch.float64, device=dev)
+    total_bytes = float(step_bytes(lens_all, L, kvd))  # the whole job: every sequence once per step
+    h2d_rank, d2h_rank = int(L * qkv_host[0].numel() * 4), int(L * hout[0].numel() * 4)
+    times = torch.tensor([elapsed_ms, e2e_ms, float(h2d_rank), float(d2h_rank)], dtype=torch.float64, device=dev)
     if world > 1:
         tmax = times.clone()
         dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
         tsum = times.clone()
         dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
         elapsed_ms, e2e_ms = float(tmax[0]), float(tmax[1])
-        total_bytes = float(tsum[2])
+        h2d_all, d2h_all = int(tsum[2]), int(tsum[3])
     else:
-        total_bytes = float(nbytes)
+        h2d_all, d2h_all = h2d_rank, d2h_rank
 
     if rank == 0:
         value = total_bytes * args.steps / (elapsed_ms / 1e3) / 1e9
@@ -431,21 +456,22 @@ def run_ours(args) -> None:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
+            "scaling": "strong", "vs_baseline": None,
             "dtype": "f16 cache; q (pre-scaled) and softmax P rounded to f16 as tensor-core operands; f32 accumulate",
             "data": "synthetic",
-            "config": {"workload": w["name"], "layers": L, "sequences_per_gpu": B,
-                       "heads_q_kv_dim": [hq, hkv, hd], "cached_len_range": [w["len_lo"], w["len_hi"]],
-                       "bytes_per_step_per_gpu": nbytes, "l2": "inputs (15.8 GiB/step) larger than L2, no flush",
-                       "parallelism": f"sequence-sharded x{world}" if world > 1 else "single GPU"},
+            "config": {"workload": w["name"], "layers": L, "sequences": len(lens_all),
+                       "sequences_rank0": B, "heads_q_kv_dim": [hq, hkv, hd],
+                       "cached_len_range": [w["len_lo"], w["len_hi"]], "bytes_per_step": int(total_bytes),
+                       "bytes_per_step_rank0": nbytes, "l2": "inputs (15.8 GiB/step) larger than L2, no flush",
+                       "parallelism": (f"sequences dealt to {world} GPUs longest-first (LPT), no collective"
+                                       if world > 1 else "single GPU")},
             "roofline": {"bound": "hbm", "kernel": "decode_attn_kernel<128>", "achieved": round(achieved, 1),
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": profiled_traffic(), "algorithmic_bytes_per_launch": per_launch,
                          "mean_launch_ms": round(mean_attn_ms, 5)},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
-                    "h2d_bytes_per_step": int(L * qkv_host[0].numel() * 4),
-                    "d2h_bytes_per_step": int(L * hout[0].numel() * 4),
-                    "timing": "CUDA graph of the 28 per-layer uploads, calls and read-backs"},
+                    "h2d_bytes_per_step": h2d_all, "d2h_bytes_per_step": d2h_all,
+                    "timing": "CUDA graph of the 28 per-layer uploads, calls and read-backs; max over ranks"},
             "gpu_launches": 3 * L * args.steps,
             "clocks": clocks,
         }
@@ -455,6 +481,8 @@ def run_ours(args) -> None:
             line["long_context"] = longctx_line
         if layer_line is not None:
             line["decode_layer"] = layer_line
+        for sl in small_lines:
+            line["small_cfg%d" % sl["config"]["baseline_config"]] = sl
         if world == 1 and not args.no_cpu:
             try:
                 line["cpu_baseline"] = cpu_baseline(lens)
@@ -475,14 +503,21 @@ def prefill_flops(n_tok: int, n_heads: int, head_dim: int) -> float:
 
 
 def run_prefill(args, dev, world, rank, local) -> dict:
-    """36 layers x 2048-token prompt, QK-norm, fp16 q/k/v in."""
+    """36 layers x 2048-token prompt, QK-norm, fp16 q/k/v in.
+    Across N GPUs the KV-head groups are dealt to the ranks (sharding.kv_head_groups):
+    each rank holds the q/k/v columns and the cache of its KV heads, as in a
+    tensor-parallel layer, and calls picoattn_prefill with a config of its
+    heads; attention needs no exchange.  Total work is fixed (strong scaling)."""
     import torch
     import torch.distributed as dist
-    from picolm_qwen_b200 import abi
+    from picolm_qwen_b200 import abi, sharding
     from picolm_qwen_b200.runtime import AttnState, stream_handle
 
     p = PREFILL
-    L, hq, hkv, hd, n = p["n_layers"], p["n_heads"], p["n_kv_heads"], p["head_dim"], p["n_tok"]
+    L, hq_all, hkv_all, hd, n = p["n_layers"], p["n_heads"], p["n_kv_heads"], p["head_dim"], p["n_tok"]
+    groups = sharding.kv_head_groups(hkv_all, world, rank)
+    hkv = len(groups)
+    hq = hkv * (hq_all // hkv_all)  # this rank's q heads
     kvd = hkv * hd
     cfg = abi.Config.make(L, hq, hkv, hd, n, p["rope_base"], abi.ROPE_NEOX)
     st = AttnState(cfg, n_seqs=1, device=dev, max_ctx=1)
@@ -556,8 +591,8 @@ def run_prefill(args, dev, world, rank, local) -> dict:
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t[0])
-    flops_layer = prefill_flops(n, hq, hd)
-    total = flops_layer * L * steps * world
+    flops_layer = prefill_flops(n, hq, hd)  # this rank's launch
+    total = prefill_flops(n, hq_all, hd) * L * steps  # the whole job
     peaks = {}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -571,10 +606,14 @@ def run_prefill(args, dev, world, rank, local) -> dict:
               abi.PREFILL_HEAD_PAIR: "prefill_attn2_kernel<128> (head pair, 1 SM)",
               abi.PREFILL_SINGLE: "prefill_attn_kernel<128> (single head)"}.get(variant, f"status {variant}")
     return {"metric": "prefill attn TFLOP/s", "value": round(total / (ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
-            "steps": steps, "ms_per_step": round(ms / steps, 4), "dtype": "f16 operands, f32 accumulate",
-            "config": {"workload": p["name"], "layers": L, "heads_q_kv_dim": [hq, hkv, hd], "prompt_tokens": n,
-                       "qk_norm": True, "flops_per_step": flops_layer * L,
-                       "flops_note": "causally visible pairs only, QK^T + PV"},
+            "steps": steps, "ms_per_step": round(ms / steps, 4), "scaling": "strong",
+            "dtype": "f16 operands (q, k, v, softmax P), f32 accumulate",
+            "config": {"workload": p["name"], "layers": L, "heads_q_kv_dim": [hq_all, hkv_all, hd],
+                       "heads_q_kv_rank0": [hq, hkv], "prompt_tokens": n,
+                       "qk_norm": True, "flops_per_step": prefill_flops(n, hq_all, hd) * L,
+                       "flops_note": "causally visible pairs only, QK^T + PV",
+                       "parallelism": (f"KV-head groups dealt to {world} GPUs, no exchange" if world > 1
+                                       else "single GPU")},
             "roofline": {"bound": "tensor", "kernel": kernel, "achieved": round(achieved, 1),
                          "peak": peak, "peak_kind": "measured" if peaks else "fallback", "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4), "mean_launch_ms": round(attn_ms, 5),
@@ -696,6 +735,29 @@ def run_longctx(args, dev, world, rank, local) -> dict:
     barrier()
     if graph is not None:
         del graph
+    roof = None
+    if world == 1:
+        # the attention kernel alone: events around every ATTEND stage of one step
+        att = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+        for l in range(L):
+            for stg, evi in ((abi.STAGE_PREPARE, None), (abi.STAGE_ATTEND, att[l]), (abi.STAGE_COMBINE, None)):
+                if evi is not None:
+                    evi[0].record(stream)
+                r = lib.picoattn_decode_staged(cfgp, l, 1, S, q[l].data_ptr(), k[l].data_ptr(), v[l].data_ptr(),
+                                               None, None, *common, out[l].data_ptr(), ws.data_ptr(), ws_n, sh, stg)
+                if r != 0:
+                    raise abi.PicoAttnError(r, "picoattn_decode_staged")
+                if evi is not None:
+                    evi[1].record(stream)
+        torch.cuda.synchronize(dev)
+        attn_ms = float(np.mean([a.elapsed_time(b) for a, b in att]))
+        per_launch = 2 * S * kvd * 2
+        peak, peak_kind = measured_peaks()
+        ach = per_launch / (attn_ms / 1e3) / 1e9
+        roof = {"bound": "hbm", "kernel": "decode_attn_kernel<128>", "achieved": round(ach, 1), "peak": peak,
+                "peak_kind": peak_kind, "unit": "GB/s", "frac": round(ach / peak, 4),
+                "mean_launch_ms": round(attn_ms, 5), "algorithmic_bytes_per_launch": per_launch,
+                "traffic": profiled_traffic("long_context")}
     dev_status = C.c_uint32(0)
     lib.picoattn_workspace_status(ws.data_ptr(), sh, C.byref(dev_status))
     if dev_status.value != 0:
@@ -707,7 +769,9 @@ def run_longctx(args, dev, world, rank, local) -> dict:
         dist.barrier(device_ids=[local])  # every rank's last exchange is done before the areas go
         lib.picoattn_p2p_destroy(comm)
     total_bytes = float(L) * 2 * S * kvd * 2  # every layer's K and V rows 0..131071, all ranks together
-    return {"metric": "long-context decode attn HBM GB/s", "value": round(total_bytes * steps / (ms / 1e3) / 1e9, 2),
+    extra = {"roofline": roof} if roof is not None else {}
+    return {**extra, "metric": "long-context decode attn HBM GB/s",
+            "value": round(total_bytes * steps / (ms / 1e3) / 1e9, 2),
             "unit": "GB/s", "ms_per_step": round(ms / steps, 4), "steps": steps, "scaling": "strong",
             "timing": timing,
             "config": {"workload": p["name"], "layers": L, "heads_q_kv_dim": [hq, hkv, hd], "cached_rows": S - 1,
@@ -715,6 +779,144 @@ def run_longctx(args, dev, world, rank, local) -> dict:
                        "parallelism": f"sequence-sharded x{world}, per-layer exchange + LSE combine in one kernel "
                                       "over NVLink peer memory"
                        if world > 1 else "single GPU"}}
+
+
+SMALL = (
+    dict(name="tinyllama-1.1b-decode-p511", cfg=1, n_layers=22, n_heads=32, n_kv_heads=4, head_dim=64,
+         rope_base=1e4, rope_mode=1, pos=511, seed=0),
+    dict(name="qwen2.5-0.5b-decode-4096", cfg=2, n_layers=24, n_heads=14, n_kv_heads=2, head_dim=64,
+         rope_base=1e6, rope_mode=0, pos=4095, seed=0),
+)
+
+
+def run_small(args, dev, spec) -> dict:
+    """BASELINE.json configs[0] and [1]: one sequence, one new token at `pos` in
+    every layer (TinyLlama with interleaved RoPE at 511; Qwen2.5-0.5B at 4095).
+    The step (every layer's picoattn_decode call) is one CUDA graph.  The whole
+    step's K/V (11 MiB / 48 MiB) fits in L2, so a 512 MiB buffer is written
+    between timed steps and every step is timed alone with CUDA events.  The
+    reference's loop is timed on one host thread over the same step."""
+    import torch
+    from picolm_qwen_b200 import abi
+    from picolm_qwen_b200.runtime import AttnState, stream_handle
+
+    L, hq, hkv, hd = spec["n_layers"], spec["n_heads"], spec["n_kv_heads"], spec["head_dim"]
+    kvd, qd, p = hkv * hd, hq * hd, spec["pos"]
+    S = p + 1
+    lib = abi.lib()
+    cfg = abi.Config.make(L, hq, hkv, hd, S, spec["rope_base"], spec["rope_mode"])
+    cfgp = C.byref(cfg)
+    st = AttnState(cfg, n_seqs=1, device=dev, max_ctx=S)
+    g = torch.Generator(device=dev).manual_seed(4000 + spec["cfg"])
+    for c in (st.k_cache, st.v_cache):
+        c[0, :, :p].copy_((torch.randn((L, p, kvd), generator=g, device=dev) * 0.5).half().view(torch.int16))
+    q = torch.randn((L, qd), generator=g, device=dev)
+    k = torch.randn((L, kvd), generator=g, device=dev)
+    v = torch.randn((L, kvd), generator=g, device=dev)
+    out = torch.empty((L, qd), device=dev)
+    pos = torch.tensor([p], dtype=torch.int32, device=dev)
+    common = (st.rope_cos.data_ptr(), st.rope_sin.data_ptr(), st.k_ptrs.data_ptr(), st.v_ptrs.data_ptr(),
+              pos.data_ptr())
+    ws, ws_n = st.workspace.data_ptr(), st.workspace.numel()
+
+    def call(l, stages, sh):
+        r = lib.picoattn_decode_staged(cfgp, l, 1, S, q[l].data_ptr(), k[l].data_ptr(), v[l].data_ptr(), None,
+                                       None, *common, out[l].data_ptr(), ws, ws_n, sh, stages)
+        if r != 0:
+            raise abi.PicoAttnError(r, "picoattn_decode_staged")
+
+    stream = torch.cuda.current_stream(dev)
+    sh = stream_handle(stream)
+    for _ in range(max(3, args.warmup)):
+        for l in range(L):
+            call(l, abi.STAGE_ALL, sh)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        gh = torch.cuda.current_stream(dev).cuda_stream
+        for l in range(L):
+            call(l, abi.STAGE_ALL, gh)
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(3):
+        flush.zero_()
+        graph.replay()
+    steps = max(5, args.steps // 4)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for e0, e1 in ev:
+        flush.zero_()
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
+    del graph
+    # the attention kernel alone: events around every ATTEND stage (staged calls), L2 flushed per step
+    att = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+           for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        for l in range(L):
+            call(l, abi.STAGE_PREPARE, sh)
+            att[i][l][0].record(stream)
+            call(l, abi.STAGE_ATTEND, sh)
+            att[i][l][1].record(stream)
+            call(l, abi.STAGE_COMBINE, sh)
+    torch.cuda.synchronize(dev)
+    attn_ms = float(np.mean([a.elapsed_time(b) for e in att for (a, b) in e]))
+    if st.status() != 0:
+        raise RuntimeError(f"{spec['name']}: device status set")
+    step_b = L * 2 * S * kvd * 2
+    layer_b = 2 * S * kvd * 2
+    peak, peak_kind = measured_peaks()
+    gbs = step_b / (ms / 1e3) / 1e9
+    line = {"metric": "decode attn HBM GB/s", "value": round(gbs, 2), "unit": "GB/s", "steps": steps,
+            "ms_per_step": round(ms, 5), "us_per_layer": round(ms / L * 1e3, 3),
+            "config": {"workload": spec["name"], "baseline_config": spec["cfg"], "layers": L,
+                       "heads_q_kv_dim": [hq, hkv, hd], "pos": p,
+                       "rope": "interleaved" if spec["rope_mode"] == 1 else "neox", "bytes_per_step": step_b,
+                       "l2": "512 MiB written between timed steps; each step timed alone",
+                       "timing": f"CUDA graph of the {L} layer calls"},
+            "roofline": {"bound": "hbm (launch-latency dominated at this size)", "kernel": "decode_attn_kernel<64>",
+                         "achieved": round(layer_b / (attn_ms / 1e3) / 1e9, 1), "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(layer_b / (attn_ms / 1e3) / 1e9 / peak, 4),
+                         "mean_launch_ms": round(attn_ms, 5), "algorithmic_bytes_per_launch": layer_b,
+                         "step_frac": round(gbs / peak, 4)}}
+    del st, flush
+    if not args.no_cpu:
+        try:
+            from oracle import pyoracle
+            runner = pyoracle.RefHarness() if os.path.exists(pyoracle.REF_SO) else None
+            kind = "reference"
+            if runner is None:
+                pyoracle.build()
+                runner, kind = pyoracle.Oracle(), "port"
+            rng = np.random.default_rng(spec["seed"])
+            kcs = [np.zeros((S, kvd), np.uint16) for _ in range(L)]
+            vcs = [np.zeros((S, kvd), np.uint16) for _ in range(L)]
+            for a in kcs + vcs:
+                a[:p] = (rng.standard_normal((p, kvd), dtype=np.float32) * 0.5).astype(np.float16).view(np.uint16)
+            ct, stt = pyoracle.Oracle().rope_table(S, hd, spec["rope_base"])
+            hq_, hkv_, hd_ = hq, hkv, hd
+            t0 = time.perf_counter()
+            for l in range(L):  # the reference's forward: one layer after another, one thread
+                qq = rng.standard_normal((1, qd), dtype=np.float32)
+                kk = rng.standard_normal((1, kvd), dtype=np.float32)
+                vv = rng.standard_normal((1, kvd), dtype=np.float32)
+                pp = np.array([p], np.int32)
+                if kind == "reference":
+                    runner.attn_decode_batch(hq_, hkv_, hd_, spec["rope_mode"], qq, kk, vv, None, None, ct, stt,
+                                             [kcs[l]], [vcs[l]], pp, 1)
+                else:
+                    runner.decode_batch(hq_, hkv_, hd_, spec["rope_mode"], qq, kk, vv, None, None, ct, stt,
+                                        [kcs[l]], [vcs[l]], pp, 1)
+            secs = time.perf_counter() - t0
+            line["cpu_baseline"] = {"value": round(step_b / secs / 1e9, 4), "unit": "GB/s", "cores": 1,
+                                    "kind": kind, "sample": f"the whole {L}-layer step on one thread "
+                                                            f"({secs * 1e3:.1f} ms), as the reference runs it"}
+        except Exception as e:  # the CPU leg never hides a GPU number
+            line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+    return line
 
 
 LAYER = dict(name="qwen2.5-7b-decode-layer-q4km", n_layers=28, n_heads=28, n_kv_heads=4, head_dim=128, dim=3584,
@@ -838,6 +1040,8 @@ def main() -> None:
     ap.add_argument("--no-longctx", action="store_true", help="skip the long-context (Qwen2.5-32B, 128K) leg")
     ap.add_argument("--no-layer", action="store_true",
                     help="skip the decode-layer leg (projections + attention, Qwen2.5-7B, Q4_K_M weights)")
+    ap.add_argument("--no-small", action="store_true",
+                    help="skip the small single-sequence legs (TinyLlama p=511, Qwen2.5-0.5B 4096)")
     ap.add_argument("--seqs", type=int, default=WORKLOAD["n_seqs"],
                     help="sequences per GPU (default 64 = the benchmark; smaller only for profiling)")
     args = ap.parse_args()

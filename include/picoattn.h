@@ -334,6 +334,11 @@ int32_t picoattn_p2p_create(const picoattn_config_t* cfg, int32_t n_seqs, int32_
                             void* ipc_handle_out, void** comm_out);
 int32_t picoattn_p2p_open(void* comm, const void* ipc_handles);
 int32_t picoattn_p2p_destroy(void* comm);
+/* Bound on each wait for the other ranks' words, in seconds (0 < timeout_s <=
+ * 60; 2 s after create).  A wait that runs out leaves NaN in the outputs it
+ * was to combine and sets PICOATTN_DEV_TIMEOUT in the workspace status, so a
+ * rank that stops calling costs the others one bounded wait, not a hang. */
+int32_t picoattn_p2p_set_timeout(void* comm, double timeout_s);
 int32_t picoattn_decode_splitkv_p2p(const picoattn_config_t* cfg, int32_t layer, int32_t n_seqs, int32_t max_ctx,
                                     int32_t row_offset, int32_t local_rows,
                                     const float* q, const float* k, const float* v,

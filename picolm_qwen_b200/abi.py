@@ -133,6 +133,7 @@ PROTOTYPES = {
     "picoattn_p2p_create": (_I, [_CFG, _I, _I, _I, _P, _P]),
     "picoattn_p2p_open": (_I, [_P, _P]),
     "picoattn_p2p_destroy": (_I, [_P]),
+    "picoattn_p2p_set_timeout": (_I, [_P, C.c_double]),
     "picoattn_decode_splitkv_p2p": (_I, [_CFG, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                          _P, _Z, _P, _P]),
     "picoattn_prefill": (_I, [_CFG, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P]),

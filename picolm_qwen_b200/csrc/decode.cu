@@ -200,14 +200,14 @@ __device__ __forceinline__ void ld_word(const uint64_t* p, float& v, uint32_t& s
     seq = b;
 }
 
-// Waits (bounded) until, for every rank r < n, the words lse_src(r) and
-// o_src(r) carry sequence number seq; their values go to lr[r], o[r].  Each
-// pass loads every missing word at once, so the ranks' words arrive in
-// parallel rather than one round trip after another.  A wait that gives up
-// leaves NaN (and PICOATTN_DEV_TIMEOUT set).
+// Waits (bounded by timeout_ns) until, for every rank r < n, the words
+// lse_src(r) and o_src(r) carry sequence number seq; their values go to lr[r],
+// o[r].  Each pass loads every missing word at once, so the ranks' words
+// arrive in parallel rather than one round trip after another.  A wait that
+// gives up leaves NaN (and PICOATTN_DEV_TIMEOUT set).
 template <class Src>
 __device__ __forceinline__ void wait_words(int n, Src src, int col, uint32_t seq, float (&lr)[8], float (&o)[8],
-                                           unsigned int* status) {
+                                           unsigned int* status, unsigned long long timeout_ns) {
     uint32_t done = 0u;
     const uint32_t all = (1u << n) - 1u;
     uint64_t t0 = 0;
@@ -231,7 +231,7 @@ __device__ __forceinline__ void wait_words(int n, Src src, int col, uint32_t seq
             const uint64_t now = global_timer_ns();
             if (it == 0u) t0 = now;
             else if ((*reinterpret_cast<volatile unsigned int*>(status) & PICOATTN_DEV_TIMEOUT) ||
-                     now - t0 > 2000000000ull) {
+                     now - t0 > timeout_ns) {
                 atomicOr(status, PICOATTN_DEV_TIMEOUT);
 #pragma unroll
                 for (int r = 0; r < 8; r++)
@@ -301,7 +301,7 @@ __device__ __forceinline__ void exchange_slice(const DecodeArgs& a, int b, int h
         const uint64_t* base = reinterpret_cast<const uint64_t*>(x.peers[x.rank] + x.slots);
         auto src = [&](int r) { return base + (((size_t)par * x.n_ranks + r) * rows + idx) * kXchgWords; };
         float lr[8], o[8];  // n_ranks <= 8
-        wait_words(x.n_ranks, src, col, seq, lr, o, a.status);
+        wait_words(x.n_ranks, src, col, seq, lr, o, a.status, x.timeout_ns);
         x.out[((size_t)b * a.hq + h) * HD + z * kXchgCols + col] = combine_ranks(x.n_ranks, lr, o);
     }
 }
@@ -453,7 +453,7 @@ __device__ __forceinline__ float xchg_collect(const DecodeArgs& a, int h, int z,
     const uint64_t* base = reinterpret_cast<const uint64_t*>(x.peers[x.rank] + x.slots);
     auto src = [&](int r) { return base + (((size_t)par * x.n_ranks + r) * rows + idx) * kXchgWords; };
     float lr[8], o[8];  // n_ranks <= 8
-    wait_words(x.n_ranks, src, lane, seq, lr, o, a.status);
+    wait_words(x.n_ranks, src, lane, seq, lr, o, a.status, x.timeout_ns);
     return combine_ranks(x.n_ranks, lr, o);
 }
 

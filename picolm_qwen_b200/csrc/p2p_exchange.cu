@@ -46,6 +46,7 @@ struct P2PComm {
     uint8_t** peers_dev = nullptr;
     bool open = false;
     int device = 0;
+    unsigned long long timeout_ns = 2000000000ull;  // the exchange wait's bound
 };
 
 P2PComm* as_comm(void* c) { return static_cast<P2PComm*>(c); }
@@ -111,6 +112,13 @@ int32_t picoattn_p2p_open(void* comm, const void* ipc_handles) {
     return PICOATTN_OK;
 }
 
+int32_t picoattn_p2p_set_timeout(void* comm, double timeout_s) {
+    P2PComm* c = as_comm(comm);
+    if (!c || !(timeout_s > 0.0) || timeout_s > 60.0) return PICOATTN_EINVAL;
+    c->timeout_ns = (unsigned long long)(timeout_s * 1e9);
+    return PICOATTN_OK;
+}
+
 int32_t picoattn_p2p_destroy(void* comm) {
     P2PComm* c = as_comm(comm);
     if (!c) return PICOATTN_EINVAL;
@@ -142,6 +150,7 @@ int32_t picoattn_decode_splitkv_p2p(const picoattn_config_t* cfg, int32_t layer,
     x.rank = c->rank;
     x.n_ranks = c->lay.n_ranks;
     x.out = out;
+    x.timeout_ns = c->timeout_ns;
     float* shard = reinterpret_cast<float*>(c->local + c->lay.shard);
     return decode_shard_impl(cfg, layer, n_seqs, max_ctx, row_offset, local_rows, q, k, v, q_norm_w, k_norm_w,
                              rope_cos, rope_sin, k_cache, v_cache, pos, shard, workspace, workspace_bytes,

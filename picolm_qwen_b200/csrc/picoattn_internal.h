@@ -85,6 +85,7 @@ struct XchgArgs {
     size_t slots, counters;
     int rank, n_ranks;
     float* out;             // [n_seqs][hq][hd] the combined output
+    unsigned long long timeout_ns;  // bound on the wait for the other ranks' words
 };
 
 struct DecodeArgs {
