@@ -737,24 +737,20 @@ def run_longctx(args, dev, world, rank, local) -> dict:
         del graph
     roof = None
     if world == 1:
-        # the attention kernel alone: events around every ATTEND stage of one step
+        # the call's kernels (attention with the new row's append, and the merge
+        # of its pieces): events around each one-sequence call
         att = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
         for l in range(L):
-            for stg, evi in ((abi.STAGE_PREPARE, None), (abi.STAGE_ATTEND, att[l]), (abi.STAGE_COMBINE, None)):
-                if evi is not None:
-                    evi[0].record(stream)
-                r = lib.picoattn_decode_staged(cfgp, l, 1, S, q[l].data_ptr(), k[l].data_ptr(), v[l].data_ptr(),
-                                               None, None, *common, out[l].data_ptr(), ws.data_ptr(), ws_n, sh, stg)
-                if r != 0:
-                    raise abi.PicoAttnError(r, "picoattn_decode_staged")
-                if evi is not None:
-                    evi[1].record(stream)
+            att[l][0].record(stream)
+            layer(l, sh)
+            att[l][1].record(stream)
         torch.cuda.synchronize(dev)
         attn_ms = float(np.mean([a.elapsed_time(b) for a, b in att]))
         per_launch = 2 * S * kvd * 2
         peak, peak_kind = measured_peaks()
         ach = per_launch / (attn_ms / 1e3) / 1e9
-        roof = {"bound": "hbm", "kernel": "decode_attn_kernel<128>", "achieved": round(ach, 1), "peak": peak,
+        roof = {"bound": "hbm", "kernel": "decode_attn_kernel<128> + decode_merge_seq_kernel<128> (one call)",
+                "achieved": round(ach, 1), "peak": peak,
                 "peak_kind": peak_kind, "unit": "GB/s", "frac": round(ach / peak, 4),
                 "mean_launch_ms": round(attn_ms, 5), "algorithmic_bytes_per_launch": per_launch,
                 "traffic": profiled_traffic("long_context")}
@@ -850,17 +846,16 @@ def run_small(args, dev, spec) -> dict:
     torch.cuda.synchronize(dev)
     ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
     del graph
-    # the attention kernel alone: events around every ATTEND stage (staged calls), L2 flushed per step
+    # the call's kernels (attention, merge): events around every one-sequence
+    # call, L2 flushed per step
     att = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
            for _ in range(steps)]
     for i in range(steps):
         flush.zero_()
         for l in range(L):
-            call(l, abi.STAGE_PREPARE, sh)
             att[i][l][0].record(stream)
-            call(l, abi.STAGE_ATTEND, sh)
+            call(l, abi.STAGE_ALL, sh)
             att[i][l][1].record(stream)
-            call(l, abi.STAGE_COMBINE, sh)
     torch.cuda.synchronize(dev)
     attn_ms = float(np.mean([a.elapsed_time(b) for e in att for (a, b) in e]))
     if st.status() != 0:
@@ -876,7 +871,8 @@ def run_small(args, dev, spec) -> dict:
                        "rope": "interleaved" if spec["rope_mode"] == 1 else "neox", "bytes_per_step": step_b,
                        "l2": "512 MiB written between timed steps; each step timed alone",
                        "timing": f"CUDA graph of the {L} layer calls"},
-            "roofline": {"bound": "hbm (launch-latency dominated at this size)", "kernel": "decode_attn_kernel<64>",
+            "roofline": {"bound": "hbm (launch-latency dominated at this size)",
+                         "kernel": "decode_attn_kernel<64> + decode_merge_seq_kernel<64> (one call)",
                          "achieved": round(layer_b / (attn_ms / 1e3) / 1e9, 1), "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(layer_b / (attn_ms / 1e3) / 1e9 / peak, 4),

@@ -457,14 +457,12 @@ __device__ __forceinline__ float xchg_collect(const DecodeArgs& a, int h, int z,
     return combine_ranks(x.n_ranks, lr, o);
 }
 
-// Merge for one sequence.  Its attention kernel leaves plan.merge_blocks SMs
-// free (the grid is sized that way), so the blocks of this kernel, launched
-// while that kernel runs, land there, and the next call's attention CTAs take
-// the SMs the attention kernel frees without waiting for this merge.  Block i
-// takes heads i, i + gridDim.x, ...; a head's G*W pieces (acc rows, and their
-// (max, sum) pairs) are contiguous in the partial slots.  While the next
-// call's attention keeps the memory system busy an L2 read takes microseconds,
-// so the merge's time is set by the bytes it has in flight: each chunk of up
+// Merge for one sequence: one block per q head (plan.merge_blocks), launched
+// while the attention kernel runs (programmatic dependent launch); its blocks
+// take SMs as attention CTAs exit and wait for the attention kernel to
+// complete.  Block i takes heads i, i + gridDim.x, ...; a head's G*W pieces
+// (acc rows, and their (max, sum) pairs) are contiguous in the partial slots.
+// The merge's time is set by the round trips it makes: each chunk of up
 // to MergeSeqShape::CK pieces (a whole head for one piece per attention CTA)
 // arrives by one bulk copy (TMA: its cost is per copy, not per byte), and the
 // block keeps kMergeSeqRing chunks, its whole share for a 16K-row shard, in
@@ -1218,13 +1216,16 @@ bool make_decode_plan(const picoattn_config_t& cfg, int n_seqs, int max_ctx, Dec
     const int sms = device_sm_count();
     const int per_sm = p.smem_bytes <= 113 * 1024 ? 2 : 1;
     const long long work_rows = (long long)n_seqs * max_ctx;
-    // One sequence: some SMs stay free for the merge kernel, which then overlaps
-    // the next call's attention.  A short shard needs the merge done quickly
-    // (16 blocks); a long one gains more from attention bandwidth than it loses
-    // in merge time (measured on B200: 16 blocks best up to 32K rows, 8 at 64K,
-    // 4 at 128K).
-    p.merge_blocks = work_rows <= 40 * 1024 ? 16 : (work_rows <= 80 * 1024 ? 8 : 4);
-    const int attn_sms = n_seqs == 1 ? std::max(1, sms - p.merge_blocks) : sms;
+    // One sequence: the merge kernel takes one block per q head (up to one per
+    // SM).  Its blocks become resident as attention CTAs exit and start the
+    // moment the attention kernel completes, each with one head's pieces.  (The
+    // next call's attention reads its q only after this merge completes, so
+    // nothing is gained by reserving SMs for the merge to overlap it; measured
+    // on B200, a head per block on every SM beats 4-16 blocks on reserved SMs at
+    // every length: 128K rows 114 -> 93.5 us per layer, a 16K-row shard 25.2 ->
+    // 22.0, 4K rows 14.4 -> 13.2.)
+    p.merge_blocks = std::min(hq, sms);
+    const int attn_sms = sms;
     long long g = std::min<long long>((long long)attn_sms * per_sm, (work_rows + 63) / 64);
     p.grid_ctas = (int)std::max<long long>(1, g);
     p.max_grid = sms * 2;

@@ -5,6 +5,7 @@ Tolerance on the attention output, from the task's parity bar:
 The KV-cache row written at `pos` must equal the reference's fp16 bits exactly
 (integer work: cpp/quant.hpp:102-135 rounding of the same fp32 values).
 """
+import ctypes as C
 import glob
 import os
 
@@ -338,3 +339,42 @@ def test_single_sequence_bad_position_is_flagged(cuda):
     st.decode(0, q, k, v, torch.tensor([100], dtype=torch.int32, device="cuda"), out)
     torch.cuda.synchronize()
     assert st.status() == 0 and torch.isfinite(out).all()
+
+
+@pytest.mark.parametrize("n_ctx", [900, 24000])
+def test_single_sequence_staged_calls_vs_oracle(cuda, oracle, n_ctx):
+    """One sequence with its stages in separate calls (prep kernel, attention
+    kernel, merge kernel), against the oracle; and the one-call form (the
+    attention kernel appending the new row itself) on the same inputs."""
+    from picolm_qwen_b200 import abi
+    from picolm_qwen_b200.runtime import stream_handle
+    hq, hkv, hd = 40, 8, 128
+    kvd = hkv * hd
+    rng = np.random.default_rng(n_ctx)
+    cfg = abi.Config.make(1, hq, hkv, hd, n_ctx, 1e6)
+    st = make_state(cfg)
+    kc = np.zeros((n_ctx, kvd), np.uint16)
+    vc = np.zeros((n_ctx, kvd), np.uint16)
+    kc[:n_ctx - 1], vc[:n_ctx - 1] = random_cache_rows(oracle, rng, n_ctx - 1, kvd)
+    q = rng.standard_normal((1, hq * hd)).astype(np.float32)
+    k = rng.standard_normal((1, kvd)).astype(np.float32)
+    v = rng.standard_normal((1, kvd)).astype(np.float32)
+    cos_t, sin_t = oracle.rope_table(n_ctx, hd, 1e6)
+    pos = np.array([n_ctx - 1], np.int32)
+    ref = oracle.decode_batch(hq, hkv, hd, 0, q, k, v, None, None, cos_t, sin_t, [kc.copy()], [vc.copy()], pos,
+                              n_threads=8)[0]
+    L = abi.lib()
+    dq, dk, dv, dpos = dev(q), dev(k), dev(v), dev(pos)
+    for staged in (True, False):
+        st.k_cache[0, 0] = dev(kc.view(np.int16))
+        st.v_cache[0, 0] = dev(vc.view(np.int16))
+        out = torch.full((1, hq * hd), float("nan"), device="cuda")
+        args = (C.byref(cfg), 0, 1, n_ctx, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), None, None,
+                st.rope_cos.data_ptr(), st.rope_sin.data_ptr(), st.k_ptrs.data_ptr(), st.v_ptrs.data_ptr(),
+                dpos.data_ptr(), out.data_ptr(), st.workspace.data_ptr(), st.workspace.numel(), stream_handle())
+        stage_list = (abi.STAGE_PREPARE, abi.STAGE_ATTEND, abi.STAGE_COMBINE) if staged else (abi.STAGE_ALL,)
+        for stg in stage_list:
+            assert L.picoattn_decode_staged(*args, stg) == 0
+        torch.cuda.synchronize()
+        assert st.status() == 0
+        assert_close(out.cpu().numpy()[0], ref, f"{'staged' if staged else 'one call'} {n_ctx}")
