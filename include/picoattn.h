@@ -457,6 +457,69 @@ int32_t picoattn_decode_layer(const picoattn_config_t* cfg, int32_t layer, int32
                               const int32_t* pos, float* x, void* workspace, size_t workspace_bytes,
                               picoattn_stream_t stream);
 
+/* ---- The rest of the decode layer: norms, FFN, logits ------------------------
+ *
+ * With these the whole per-token forward of the C++ engine
+ * (Model::forward, cpp/model.hpp:288-458) runs on the device: per layer
+ * picoattn_decode_block (attention norm, picoattn_decode_layer, the FFN
+ * block), then picoattn_logits.  Only the embedding row (a table lookup,
+ * cpp/model.hpp:302-308) is the caller's.  Weights as for picoattn_matvec;
+ * norm weights fp32 [dim] (the reference dequantises them once at load,
+ * cpp/model.hpp:924-945).  The model-dimension norms add their squares in
+ * the GPU's order (the reference: four SSE lanes), so they agree to fp32
+ * rounding; eps is the reference's 1e-6. */
+
+/* out[v] = x[v] / sqrt(mean(x[v]^2) + 1e-6) * weight for v < n_vec, dim
+ * floats each (TensorOps::rmsnorm, cpp/tensor.hpp:146-176).  x, out 16-byte
+ * aligned; out may equal x. */
+int32_t picoattn_rmsnorm(const float* x, const float* weight, float* out, int32_t dim, int32_t n_vec,
+                         picoattn_stream_t stream);
+
+/* One layer's FFN weights as the model file holds them. */
+typedef struct {
+    const void* w_gate;  /* [n_ffn][dim] */
+    const void* w_up;    /* [n_ffn][dim] */
+    const void* w_down;  /* [dim][n_ffn] */
+    int32_t gate_type, up_type, down_type;  /* PICOATTN_WT_* */
+    const float* b_gate; /* fp32 [n_ffn] or NULL */
+    const float* b_down; /* fp32 [dim] or NULL (the reference multiplies up without a bias) */
+} picoattn_ffn_weights_t;
+
+size_t picoattn_ffn_workspace_size(int32_t dim, int32_t n_ffn, int32_t n_vec);
+
+/* The FFN block of one layer and its residual, in place on x [n_vec][dim]
+ * (cpp/model.hpp:429-452):
+ *   xb = rmsnorm(x, ffn_norm_w); h = silu(Wg.xb + bg) * (Wu.xb); x += Wd.h + bd
+ * gate and up go out as one launch; silu (1/(1+e^-x), times x) and the
+ * product in one kernel; the down projection adds into x. */
+int32_t picoattn_ffn(const picoattn_ffn_weights_t* weights, const float* ffn_norm_w, int32_t dim, int32_t n_ffn,
+                     int32_t n_vec, float* x, void* workspace, size_t workspace_bytes, picoattn_stream_t stream);
+
+size_t picoattn_logits_workspace_size(int32_t dim, int32_t n_vec);
+
+/* logits[v] = W_out . rmsnorm(x[v], output_norm_w) for v < n_vec, vocab each
+ * (cpp/model.hpp:454-457). */
+int32_t picoattn_logits(const float* x, const float* output_norm_w, const void* w_out, int32_t w_type, int32_t dim,
+                        int32_t vocab, int32_t n_vec, float* logits, void* workspace, size_t workspace_bytes,
+                        picoattn_stream_t stream);
+
+size_t picoattn_decode_block_workspace_size(const picoattn_config_t* cfg, int32_t dim, int32_t n_ffn,
+                                            int32_t n_seqs, int32_t max_ctx);
+
+/* One whole transformer layer of the decode step for n_seqs sequences, on
+ * the residual x [n_seqs][dim] in place (cpp/model.hpp:315-452):
+ *   xb = rmsnorm(x, attn_norm_w); picoattn_decode_layer(xb -> x); picoattn_ffn(x)
+ * Arguments as for those calls.  The workspace begins with a decode
+ * workspace: initialise it with picoattn_workspace_init;
+ * picoattn_workspace_status reads it. */
+int32_t picoattn_decode_block(const picoattn_config_t* cfg, int32_t layer, int32_t dim, int32_t n_ffn,
+                              int32_t n_seqs, int32_t max_ctx, const float* attn_norm_w,
+                              const picoattn_layer_weights_t* attn_weights, const float* ffn_norm_w,
+                              const picoattn_ffn_weights_t* ffn_weights, const float* q_norm_w,
+                              const float* k_norm_w, const float* rope_cos, const float* rope_sin,
+                              uint16_t* const* k_cache, uint16_t* const* v_cache, const int32_t* pos, float* x,
+                              void* workspace, size_t workspace_bytes, picoattn_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -410,9 +410,19 @@ class RefFullModel:
             L.pref_full_attn_bias.restype = C.POINTER(C.c_float)
             L.pref_full_attn_bias.argtypes = [C.c_void_p, C.c_int, C.c_int]
             L.pref_full_ffn.argtypes = [C.c_void_p, C.c_int, _f32p]
+            L.pref_full_model_norm.restype = C.POINTER(C.c_float)
+            L.pref_full_model_norm.argtypes = [C.c_void_p, C.c_int, C.c_int]
+            L.pref_full_ffn_weight.restype = C.c_void_p
+            L.pref_full_ffn_weight.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_int),
+                                               C.POINTER(C.c_size_t)]
+            L.pref_full_ffn_bias.restype = C.POINTER(C.c_float)
+            L.pref_full_ffn_bias.argtypes = [C.c_void_p, C.c_int, C.c_int]
+            L.pref_full_set_ffn_weights.restype = C.c_int
+            L.pref_full_set_ffn_weights.argtypes = [C.c_void_p, C.c_int, C.c_uint64]
             L._full_proto = True
         self.ref, self.L = ref, L
         self.nl, self.hq, self.hkv, self.hd, self.vocab, self.S = n_layers, hq, hkv, hd, vocab, max_seq
+        self.n_ffn = n_ffn
         self.dim, self.kvd = hq * hd, hkv * hd
         self.qk_norm = bool(qk_norm)
         self.h = L.pref_full_create(n_layers, hq, hkv, hd, n_ffn, vocab, max_seq, rope_base, rope_mode,
@@ -459,6 +469,25 @@ class RefFullModel:
         if not self.qk_norm:
             return None
         return np.ctypeslib.as_array(self.L.pref_full_norm_w(self.h, layer, which), shape=(self.hd,)).copy()
+
+    def model_norm(self, layer, which):
+        """fp32 [dim]: which 0 attention norm, 1 FFN norm of layer; 2 the output norm."""
+        return np.ctypeslib.as_array(self.L.pref_full_model_norm(self.h, layer, which), shape=(self.dim,)).copy()
+
+    def ffn_weight(self, layer, which):
+        """(bytes as uint8, GGUF type): which 0 gate, 1 up, 2 down of layer; 3 the output matrix."""
+        t, n = C.c_int(), C.c_size_t()
+        p = self.L.pref_full_ffn_weight(self.h, layer, which, C.byref(t), C.byref(n))
+        return np.ctypeslib.as_array((C.c_uint8 * n.value).from_address(p)).copy(), t.value
+
+    def ffn_bias(self, layer, which):
+        """fp32 bias the engine keeps: which 0 gate [n_ffn], 1 down [dim]."""
+        n = self.n_ffn if which == 0 else self.dim
+        return np.ctypeslib.as_array(self.L.pref_full_ffn_bias(self.h, layer, which), shape=(n,)).copy()
+
+    def set_ffn_weights(self, wtype: int, seed: int = 2) -> None:
+        """Every layer's gate/up/down and the output matrix as seeded random blocks of a GGUF type."""
+        assert self.L.pref_full_set_ffn_weights(self.h, int(wtype), seed) == 0
 
     def set_attn_weights(self, wtype: int, seed: int = 1) -> None:
         """Every layer's q/k/v/o weights as seeded random blocks of a GGUF type."""

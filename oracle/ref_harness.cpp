@@ -466,24 +466,48 @@ uint16_t* pref_full_vcache(void* hp) { return ((FullHarness*)hp)->model.state.va
 // of a GGUF type (1 F32 stays as created; 2 F16, 3 Q4_0, 9 Q8_0, 13 Q4_K,
 // 15 Q6_K), scaled so W.x keeps roughly unit variance; the engine then
 // dequantises them in its matmul as it would a model file's.  0 or -1.
-int pref_full_set_attn_weights(void* hp, int type, uint64_t seed) {
-    auto* h = (FullHarness*)hp;
-    int be = 0, bb = 0;
+static bool quant_block(int type, int* be, int* bb) {
     switch (type) {
-        case 2: be = 1; bb = 2; break;
-        case 3: be = 32; bb = 18; break;
-        case 9: be = 32; bb = 34; break;
-        case 13: be = 256; bb = 144; break;
-        case 15: be = 256; bb = 210; break;
-        default: return -1;
+        case 2: *be = 1; *bb = 2; return true;
+        case 3: *be = 32; *bb = 18; return true;
+        case 9: *be = 32; *bb = 34; return true;
+        case 13: *be = 256; *bb = 144; return true;
+        case 15: *be = 256; *bb = 210; return true;
+        default: return false;
     }
-    Rng r{seed};
+}
+
+// n_out rows of n_in weights as random blocks of a GGUF type, the scales chosen
+// so that W.x keeps roughly unit variance for unit-variance x
+static std::vector<uint8_t> random_blocks(Rng& r, int type, int be, int bb, int n_in, int n_out) {
     auto u01 = [&]() { return 0.5f * (r.next(1.0f) + 1.0f); };
     auto f16 = [&](float v, uint8_t* p) {
         const uint16_t b = fp32_to_fp16(v);
         p[0] = (uint8_t)(b & 0xFF);
         p[1] = (uint8_t)(b >> 8);
     };
+    const size_t nb = (size_t)n_out * (n_in / be);
+    std::vector<uint8_t> bytes(nb * bb);
+    const float a = 1.0f / std::sqrt((float)n_in);
+    for (size_t i = 0; i < nb; i++) {
+        uint8_t* p = bytes.data() + i * bb;
+        for (int j = 0; j < bb; j++) p[j] = (uint8_t)(r.next(1.0f) * 127.5f + 127.5f);
+        switch (type) {
+            case 2: f16((2.0f * u01() - 1.0f) * 1.7320508f * a, p); break;
+            case 3: f16(a / 4.6f * (0.5f + u01()), p); break;
+            case 9: f16(a / 74.0f * (0.5f + u01()), p); break;
+            case 13: f16(a / 140.0f * (0.5f + u01()), p); f16(a / 100.0f * u01(), p + 2); break;
+            case 15: f16(a / (74.0f * 18.0f) * (0.5f + u01()), p + 208); break;
+        }
+    }
+    return bytes;
+}
+
+int pref_full_set_attn_weights(void* hp, int type, uint64_t seed) {
+    auto* h = (FullHarness*)hp;
+    int be = 0, bb = 0;
+    if (!quant_block(type, &be, &bb)) return -1;
+    Rng r{seed};
     const int dims_in[4] = {h->dim, h->dim, h->dim, h->dim};
     const int dims_out[4] = {h->dim, h->kvd, h->kvd, h->dim};
     const char* const keys[4] = {layer::ATTN_Q, layer::ATTN_K, layer::ATTN_V, layer::ATTN_OUTPUT};
@@ -492,21 +516,7 @@ int pref_full_set_attn_weights(void* hp, int type, uint64_t seed) {
         for (int w = 0; w < 4; w++) {
             const int n_in = dims_in[w], n_out = dims_out[w];
             if (n_in % be) return -1;
-            const size_t nb = (size_t)n_out * (n_in / be);
-            std::vector<uint8_t> bytes(nb * bb);
-            const float a = 1.0f / std::sqrt((float)n_in);
-            for (size_t i = 0; i < nb; i++) {
-                uint8_t* p = bytes.data() + i * bb;
-                for (int j = 0; j < bb; j++) p[j] = (uint8_t)(r.next(1.0f) * 127.5f + 127.5f);
-                switch (type) {
-                    case 2: f16((2.0f * u01() - 1.0f) * 1.7320508f * a, p); break;
-                    case 3: f16(a / 4.6f * (0.5f + u01()), p); break;
-                    case 9: f16(a / 74.0f * (0.5f + u01()), p); break;
-                    case 13: f16(a / 140.0f * (0.5f + u01()), p); f16(a / 100.0f * u01(), p + 2); break;
-                    case 15: f16(a / (74.0f * 18.0f) * (0.5f + u01()), p + 208); break;
-                }
-            }
-            h->qstore.push_back(std::move(bytes));
+            h->qstore.push_back(random_blocks(r, type, be, bb, n_in, n_out));
             lw.set(keys[w], h->qstore.back().data(), (uint32_t)type);
         }
     }
@@ -542,6 +552,61 @@ const float* pref_full_attn_bias(void* hp, int l, int which) {
 
 // FFN block and residual of layer l on x, whose attention block is done
 void pref_full_ffn(void* hp, int l, float* x) { full_ffn((FullHarness*)hp, l, x); }
+
+// The per-layer norm weights the engine keeps (which 0: attention norm, 1: FFN
+// norm; 2: the output norm, layer ignored), fp32 [dim].
+const float* pref_full_model_norm(void* hp, int l, int which) {
+    auto& st = ((FullHarness*)hp)->model.state;
+    return which == 0 ? st.attn_norm_w[l].data() : (which == 1 ? st.ffn_norm_w[l].data() : st.output_norm_w.data());
+}
+
+// layer l's FFN weights as the engine holds them (which 0: gate, 1: up,
+// 2: down; 3: the output (logits) matrix, layer ignored), their GGUF type and
+// byte count; and the fp32 gate (0) and down (1) biases it keeps
+const void* pref_full_ffn_weight(void* hp, int l, int which, int* type, size_t* bytes) {
+    auto* h = (FullHarness*)hp;
+    Model& m = h->model;
+    if (which == 3) {
+        auto e = m.weights.get(output::OUTPUT);
+        *type = (int)e.type;
+        *bytes = gguf_type_row_size((GGUFType)e.type, h->dim) * (size_t)h->vocab;
+        return e.ptr;
+    }
+    const char* const keys[3] = {layer::FFN_GATE, layer::FFN_UP, layer::FFN_DOWN};
+    auto e = m.weights.get_layer(l).get(keys[which]);
+    const int n_in = which == 2 ? h->n_ffn : h->dim, n_out = which == 2 ? h->dim : h->n_ffn;
+    *type = (int)e.type;
+    *bytes = gguf_type_row_size((GGUFType)e.type, n_in) * (size_t)n_out;
+    return e.ptr;
+}
+const float* pref_full_ffn_bias(void* hp, int l, int which) {
+    auto& st = ((FullHarness*)hp)->model.state;
+    return which == 0 ? st.ffn_gate_bias[l].data() : st.ffn_down_bias[l].data();
+}
+
+// Replaces every layer's gate/up/down weights and the output matrix with
+// seeded random blocks of a GGUF type (as pref_full_set_attn_weights does for
+// the attention projections).  0 or -1.
+int pref_full_set_ffn_weights(void* hp, int type, uint64_t seed) {
+    auto* h = (FullHarness*)hp;
+    int be = 0, bb = 0;
+    if (!quant_block(type, &be, &bb)) return -1;
+    Rng r{seed};
+    for (int l = 0; l < h->L; l++) {
+        LayerWeights& lw = h->model.weights.get_layer(l);
+        const char* const keys[3] = {layer::FFN_GATE, layer::FFN_UP, layer::FFN_DOWN};
+        for (int w = 0; w < 3; w++) {
+            const int n_in = w == 2 ? h->n_ffn : h->dim, n_out = w == 2 ? h->dim : h->n_ffn;
+            if (n_in % be) return -1;
+            h->qstore.push_back(random_blocks(r, type, be, bb, n_in, n_out));
+            lw.set(keys[w], h->qstore.back().data(), (uint32_t)type);
+        }
+    }
+    if (h->dim % be) return -1;
+    h->qstore.push_back(random_blocks(r, type, be, bb, h->dim, h->vocab));
+    h->model.weights.set(output::OUTPUT, h->qstore.back().data(), (uint32_t)type);
+    return 0;
+}
 
 // Projections with the reference's own code: one row dequantised
 // (dequantize_row, cpp/quant.hpp:283-295) and matmul_bias per vector

@@ -95,6 +95,15 @@ class LayerWeights(C.Structure):
     ]
 
 
+class FfnWeights(C.Structure):
+    """picoattn_ffn_weights_t: device pointers and PICOATTN_WT_* types."""
+    _fields_ = [
+        ("w_gate", C.c_void_p), ("w_up", C.c_void_p), ("w_down", C.c_void_p),
+        ("gate_type", C.c_int32), ("up_type", C.c_int32), ("down_type", C.c_int32),
+        ("b_gate", C.c_void_p), ("b_down", C.c_void_p),
+    ]
+
+
 _P = C.c_void_p
 _I = C.c_int32
 _Z = C.c_size_t
@@ -149,6 +158,14 @@ PROTOTYPES = {
     "picoattn_decode_layer_workspace_size": (_Z, [_CFG, _I, _I, _I]),
     "picoattn_decode_layer": (_I, [_CFG, _I, _I, _I, _I, _P, C.POINTER(LayerWeights), _P, _P, _P, _P, _P, _P, _P,
                                    _P, _P, _Z, _P]),
+    "picoattn_rmsnorm": (_I, [_P, _P, _P, _I, _I, _P]),
+    "picoattn_ffn_workspace_size": (_Z, [_I, _I, _I]),
+    "picoattn_ffn": (_I, [C.POINTER(FfnWeights), _P, _I, _I, _I, _P, _P, _Z, _P]),
+    "picoattn_logits_workspace_size": (_Z, [_I, _I]),
+    "picoattn_logits": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P, _Z, _P]),
+    "picoattn_decode_block_workspace_size": (_Z, [_CFG, _I, _I, _I, _I]),
+    "picoattn_decode_block": (_I, [_CFG, _I, _I, _I, _I, _I, _P, C.POINTER(LayerWeights), _P, C.POINTER(FfnWeights),
+                                   _P, _P, _P, _P, _P, _P, _P, _P, _P, _Z, _P]),
 }
 
 _lib = None

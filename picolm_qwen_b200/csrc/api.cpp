@@ -386,4 +386,126 @@ int32_t picoattn_decode_layer(const picoattn_config_t* cfg, int32_t layer, int32
     return cuda_status(launch_matvec(o, s));
 }
 
+size_t picoattn_ffn_workspace_size(int32_t dim, int32_t n_ffn, int32_t n_vec) {
+    if (dim <= 0 || n_ffn <= 0 || n_vec <= 0) return 0;
+    // xb [n_vec][dim], gate and up [n_vec][n_ffn], fp32
+    return align_up((size_t)n_vec * dim * 4, 256) + 2 * align_up((size_t)n_vec * n_ffn * 4, 256);
+}
+
+int32_t picoattn_rmsnorm(const float* x, const float* weight, float* out, int32_t dim, int32_t n_vec,
+                         picoattn_stream_t stream) {
+    if (!x || !weight || !out || dim <= 0 || n_vec <= 0) return PICOATTN_EINVAL;
+    if (!aligned16(x) || !aligned16(out) || !aligned16(weight)) return PICOATTN_EINVAL;
+    const int32_t st = device_ok();
+    if (st != PICOATTN_OK) return st;
+    return cuda_status(launch_rmsnorm(x, weight, out, dim, n_vec, (cudaStream_t)stream));
+}
+
+int32_t picoattn_ffn(const picoattn_ffn_weights_t* w, const float* ffn_norm_w, int32_t dim, int32_t n_ffn,
+                     int32_t n_vec, float* x, void* workspace, size_t workspace_bytes, picoattn_stream_t stream) {
+    if (!w || !ffn_norm_w || !x || !workspace || dim <= 0 || n_ffn <= 0 || n_vec <= 0) return PICOATTN_EINVAL;
+    if (!aligned16(x) || !aligned16(workspace) || !aligned16(ffn_norm_w)) return PICOATTN_EINVAL;
+    for (int32_t t : {w->gate_type, w->up_type, w->down_type})
+        if (weight_block_elems(t) == 0) return PICOATTN_EUNSUPPORTED;
+    if (workspace_bytes < picoattn_ffn_workspace_size(dim, n_ffn, n_vec)) return PICOATTN_ENOSPACE;
+    uint8_t* base = static_cast<uint8_t*>(workspace);
+    float* xb = reinterpret_cast<float*>(base);
+    float* gate = reinterpret_cast<float*>(base + align_up((size_t)n_vec * dim * 4, 256));
+    float* up = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(gate) + align_up((size_t)n_vec * n_ffn * 4, 256));
+    MatvecArgs gu{};
+    if (!matvec_part(w->gate_type, w->w_gate, w->b_gate, dim, n_ffn, gate, (size_t)n_ffn, &gu.part[0]) ||
+        !matvec_part(w->up_type, w->w_up, nullptr, dim, n_ffn, up, (size_t)n_ffn, &gu.part[1]))
+        return PICOATTN_EINVAL;
+    MatvecArgs dn{};
+    if (!matvec_part(w->down_type, w->w_down, w->b_down, n_ffn, dim, x, (size_t)dim, &dn.part[0]))
+        return PICOATTN_EINVAL;
+    int32_t st = device_ok();
+    if (st != PICOATTN_OK) return st;
+    const cudaStream_t s = (cudaStream_t)stream;
+    st = cuda_status(launch_rmsnorm(x, ffn_norm_w, xb, dim, n_vec, s));
+    if (st != PICOATTN_OK) return st;
+    gu.n_parts = 2;
+    gu.n_in = dim;
+    gu.n_vec = n_vec;
+    gu.rows_total = 2 * n_ffn;
+    gu.x = xb;
+    st = cuda_status(launch_matvec(gu, s));
+    if (st != PICOATTN_OK) return st;
+    st = cuda_status(launch_silu_mul(gate, up, (size_t)n_vec * n_ffn, s));
+    if (st != PICOATTN_OK) return st;
+    dn.n_parts = 1;
+    dn.n_in = n_ffn;
+    dn.n_vec = n_vec;
+    dn.rows_total = dim;
+    dn.accumulate = 1;
+    dn.x = gate;
+    return cuda_status(launch_matvec(dn, s));
+}
+
+size_t picoattn_logits_workspace_size(int32_t dim, int32_t n_vec) {
+    if (dim <= 0 || n_vec <= 0) return 0;
+    return align_up((size_t)n_vec * dim * 4, 256);
+}
+
+int32_t picoattn_logits(const float* x, const float* output_norm_w, const void* w_out, int32_t w_type, int32_t dim,
+                        int32_t vocab, int32_t n_vec, float* logits, void* workspace, size_t workspace_bytes,
+                        picoattn_stream_t stream) {
+    if (!x || !output_norm_w || !w_out || !logits || !workspace || dim <= 0 || vocab <= 0 || n_vec <= 0)
+        return PICOATTN_EINVAL;
+    if (!aligned16(x) || !aligned16(logits) || !aligned16(workspace) || !aligned16(output_norm_w))
+        return PICOATTN_EINVAL;
+    if (weight_block_elems(w_type) == 0) return PICOATTN_EUNSUPPORTED;
+    if (workspace_bytes < picoattn_logits_workspace_size(dim, n_vec)) return PICOATTN_ENOSPACE;
+    float* xb = static_cast<float*>(workspace);
+    MatvecArgs a{};
+    if (!matvec_part(w_type, w_out, nullptr, dim, vocab, logits, (size_t)vocab, &a.part[0])) return PICOATTN_EINVAL;
+    int32_t st = device_ok();
+    if (st != PICOATTN_OK) return st;
+    const cudaStream_t s = (cudaStream_t)stream;
+    st = cuda_status(launch_rmsnorm(x, output_norm_w, xb, dim, n_vec, s));
+    if (st != PICOATTN_OK) return st;
+    a.n_parts = 1;
+    a.n_in = dim;
+    a.n_vec = n_vec;
+    a.rows_total = vocab;
+    a.x = xb;
+    return cuda_status(launch_matvec(a, s));
+}
+
+// Workspace of picoattn_decode_block: the decode-layer workspace first (its
+// status header at offset 0), then the normalised hidden state xb, then the
+// FFN's workspace.
+size_t picoattn_decode_block_workspace_size(const picoattn_config_t* cfg, int32_t dim, int32_t n_ffn,
+                                            int32_t n_seqs, int32_t max_ctx) {
+    const size_t l = picoattn_decode_layer_workspace_size(cfg, dim, n_seqs, max_ctx);
+    const size_t f = picoattn_ffn_workspace_size(dim, n_ffn, n_seqs);
+    if (l == 0 || f == 0) return 0;
+    return align_up(l, 256) + align_up((size_t)n_seqs * dim * 4, 256) + f;
+}
+
+int32_t picoattn_decode_block(const picoattn_config_t* cfg, int32_t layer, int32_t dim, int32_t n_ffn,
+                              int32_t n_seqs, int32_t max_ctx, const float* attn_norm_w,
+                              const picoattn_layer_weights_t* attn_weights, const float* ffn_norm_w,
+                              const picoattn_ffn_weights_t* ffn_weights, const float* q_norm_w,
+                              const float* k_norm_w, const float* rope_cos, const float* rope_sin,
+                              uint16_t* const* k_cache, uint16_t* const* v_cache, const int32_t* pos, float* x,
+                              void* workspace, size_t workspace_bytes, picoattn_stream_t stream) {
+    if (!attn_norm_w || !x || !workspace || dim <= 0 || n_seqs <= 0 || n_ffn <= 0) return PICOATTN_EINVAL;
+    if (!aligned16(attn_norm_w) || !aligned16(x) || !aligned16(workspace)) return PICOATTN_EINVAL;
+    const size_t l = picoattn_decode_layer_workspace_size(cfg, dim, n_seqs, max_ctx);
+    if (l == 0) return picoattn_config_check(cfg) != PICOATTN_OK ? picoattn_config_check(cfg) : PICOATTN_EINVAL;
+    const size_t total = picoattn_decode_block_workspace_size(cfg, dim, n_ffn, n_seqs, max_ctx);
+    if (workspace_bytes < total) return PICOATTN_ENOSPACE;
+    uint8_t* base = static_cast<uint8_t*>(workspace);
+    float* xb = reinterpret_cast<float*>(base + align_up(l, 256));
+    uint8_t* ffn_ws = base + align_up(l, 256) + align_up((size_t)n_seqs * dim * 4, 256);
+    int32_t st = picoattn_rmsnorm(x, attn_norm_w, xb, dim, n_seqs, stream);
+    if (st != PICOATTN_OK) return st;
+    st = picoattn_decode_layer(cfg, layer, dim, n_seqs, max_ctx, xb, attn_weights, q_norm_w, k_norm_w, rope_cos,
+                               rope_sin, k_cache, v_cache, pos, x, workspace, l, stream);
+    if (st != PICOATTN_OK) return st;
+    return picoattn_ffn(ffn_weights, ffn_norm_w, dim, n_ffn, n_seqs, x, ffn_ws,
+                        picoattn_ffn_workspace_size(dim, n_ffn, n_seqs), stream);
+}
+
 }  // extern "C"

@@ -153,6 +153,11 @@ bool matvec_part(int type, const void* w, const float* bias, int n_in, int n_out
                  MatvecPart* p);
 cudaError_t launch_matvec(const MatvecArgs& a, cudaStream_t stream);
 
+// The rest of a decode layer (layer_ops.cu): model-dimension RMSNorm of n_vec
+// vectors, and the FFN gate gate = silu(gate) * up over n elements.
+cudaError_t launch_rmsnorm(const float* x, const float* w, float* out, int dim, int n_vec, cudaStream_t stream);
+cudaError_t launch_silu_mul(float* gate, const float* up, size_t n, cudaStream_t stream);
+
 struct PrefillArgs {
     int hq, hkv, g, hd, kvd, max_seq, layer, n_tok, start, n_qtiles;
     int rope_mode, in_dtype;

@@ -72,7 +72,7 @@ __device__ __forceinline__ uint32_t h2_ref16(uint32_t w) {
 // keep all 32 lanes busy.  Lane u then folds vector u's chains as
 // (c0+c2)+(c1+c3) and computes its scale, as in vec_rmsnorm.
 template <int HD>
-__global__ void __launch_bounds__(256) prefill_prep_kernel(PrefillArgs a) {
+__device__ __forceinline__ void prefill_prep(const PrefillArgs& a) {
     constexpr int V = HD / 32;  // elements per lane
     constexpr int U = 8;        // vectors per warp
     constexpr int CH = HD / 4;  // terms per chain
@@ -193,6 +193,18 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(PrefillArgs a) {
             }
         }
     }
+}
+
+// Launched with programmatic stream serialisation after the previous layer's
+// attention kernel: it waits for that kernel (which still reads the q operand
+// and may still write the output) before it reads or writes anything, and lets
+// the attention kernel after it launch only once its own stores are done, so
+// that kernel's early CTAs do not take SMs the rest of this grid needs.
+template <int HD>
+__global__ void __launch_bounds__(256) prefill_prep_kernel(PrefillArgs a) {
+    pdl_wait();
+    prefill_prep<HD>(a);
+    pdl_trigger();
 }
 
 // ---------------------------------------------------------------------------
@@ -1114,11 +1126,17 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         fence_mbar_init();
     }
     constexpr int W_TMA = 4 * kPairParts, W_MMA = W_TMA + 1, W_EPI = W_TMA + 2;
+    // Programmatic dependent launch: the next kernel (the next layer's prep,
+    // which waits for this one to complete) may launch now; this kernel set
+    // itself up while the prep kernel before it finished, and waits for it
+    // before its first load of q or the cache and its first store.
+    pdl_trigger();
     if (warp == W_MMA) tmem_alloc_pair(tmem_slot, 512);
     tc_fence_before();
     cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated in both
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_wait();
 
     // item r-th of this cluster: serpentine over the longest-first order
     auto item_of = [&](int r) {
@@ -1457,7 +1475,17 @@ cudaError_t launch_prefill_hd(const PrefillArgs& a, cudaStream_t stream, unsigne
     if (stages & PICOATTN_STAGE_PREPARE) {
         // one warp per (token, kind, group of 8 heads), 8 warps per block
         const long warps = (long)a.n_tok * ((a.hq + 7) / 8 + 2 * ((a.hkv + 7) / 8));
-        prefill_prep_kernel<HD><<<(unsigned)((warps + 7) / 8), 256, 0, stream>>>(a);
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.gridDim = dim3((unsigned)((warps + 7) / 8), 1, 1);
+        cfg.blockDim = dim3(256, 1, 1);
+        cfg.stream = stream;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, prefill_prep_kernel<HD>, a);
+        if (e != cudaSuccess) return e;
     }
     if (stages & PICOATTN_STAGE_ATTEND) {
         const PrefillSetup& st = prefill_setup<HD>();
@@ -1478,15 +1506,17 @@ cudaError_t launch_prefill_hd(const PrefillArgs& a, cudaStream_t stream, unsigne
                 return cudaErrorInvalidValue;
             const int clusters = n_pair_items < st.pair_clusters ? n_pair_items : st.pair_clusters;
             cudaLaunchConfig_t cfg = {};
-            cudaLaunchAttribute attr[1];
+            cudaLaunchAttribute attr[2];
             attr[0].id = cudaLaunchAttributeClusterDimension;
             attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
+            attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[1].val.programmaticStreamSerializationAllowed = 1;
             cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
             cfg.blockDim = dim3(kPairThreads, 1, 1);
             cfg.dynamicSmemBytes = PairSmem::kDynBytes;
             cfg.stream = stream;
             cfg.attrs = attr;
-            cfg.numAttrs = 1;
+            cfg.numAttrs = 2;
             cudaError_t e = cudaLaunchKernelEx(&cfg, prefill_attn_pair_kernel, mq, mk, mv, mo, a);
             if (e != cudaSuccess) return e;
             return cudaGetLastError();

@@ -51,6 +51,57 @@ class LayerProj:
             abi.ptr(bq), abi.ptr(bk), abi.ptr(bv), abi.ptr(bo))
 
 
+class FfnProj:
+    """One layer's FFN weights on the device (uint8 GGUF blocks) and fp32 biases."""
+
+    def __init__(self, w_gate, w_up, w_down, types, b_gate=None, b_down=None):
+        self.tensors = (w_gate, w_up, w_down, b_gate, b_down)  # kept alive with the struct
+        self.struct = abi.FfnWeights(w_gate.data_ptr(), w_up.data_ptr(), w_down.data_ptr(), *types,
+                                     abi.ptr(b_gate), abi.ptr(b_down))
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor, stream: torch.cuda.Stream | None = None):
+    """out = rmsnorm(x) * weight per row of x [n_vec, dim] (TensorOps::rmsnorm, cpp/tensor.hpp:146-176)."""
+    dim = weight.numel()
+    abi.check(abi.lib().picoattn_rmsnorm(x.data_ptr(), weight.data_ptr(), out.data_ptr(), dim, x.numel() // dim,
+                                         stream_handle(stream)), "picoattn_rmsnorm")
+
+
+class Scratch:
+    """A grow-only device byte buffer for the calls that take a workspace."""
+
+    def __init__(self, device):
+        self.device = torch.device(device)
+        self.buf = None
+
+    def get(self, n: int) -> torch.Tensor:
+        if self.buf is None or self.buf.numel() < n:
+            self.buf = torch.zeros(max(n, 256), dtype=torch.uint8, device=self.device)
+        return self.buf
+
+
+def ffn(proj: "FfnProj", ffn_norm_w: torch.Tensor, n_ffn: int, x: torch.Tensor, scratch: "Scratch",
+        stream: torch.cuda.Stream | None = None) -> None:
+    """The FFN block and its residual in place on x [n_vec, dim] (cpp/model.hpp:429-452)."""
+    dim = ffn_norm_w.numel()
+    n_vec = x.numel() // dim
+    n = abi.lib().picoattn_ffn_workspace_size(dim, n_ffn, n_vec)
+    ws = scratch.get(n)
+    abi.check(abi.lib().picoattn_ffn(C.byref(proj.struct), ffn_norm_w.data_ptr(), dim, n_ffn, n_vec, x.data_ptr(),
+                                     ws.data_ptr(), ws.numel(), stream_handle(stream)), "picoattn_ffn")
+
+
+def logits(x: torch.Tensor, output_norm_w: torch.Tensor, w_out: torch.Tensor, w_type: int, vocab: int,
+           out: torch.Tensor, scratch: "Scratch", stream: torch.cuda.Stream | None = None) -> None:
+    """out [n_vec, vocab] = W_out . rmsnorm(x) (cpp/model.hpp:454-457)."""
+    dim = output_norm_w.numel()
+    n_vec = x.numel() // dim
+    ws = scratch.get(abi.lib().picoattn_logits_workspace_size(dim, n_vec))
+    abi.check(abi.lib().picoattn_logits(x.data_ptr(), output_norm_w.data_ptr(), w_out.data_ptr(), w_type, dim, vocab,
+                                        n_vec, out.data_ptr(), ws.data_ptr(), ws.numel(), stream_handle(stream)),
+              "picoattn_logits")
+
+
 class AttnState:
     """KV caches of n_seqs sequences in the reference layout plus RoPE tables.
 
@@ -115,6 +166,34 @@ class AttnState:
             self.k_ptrs.data_ptr(), self.v_ptrs.data_ptr(), pos.data_ptr(), x.data_ptr(),
             self.layer_ws.data_ptr(), self.layer_ws.numel(), stream_handle(stream))
         abi.check(st, "picoattn_decode_layer")
+
+    def decode_block(self, layer: int, dim: int, n_ffn: int, x: torch.Tensor, attn_norm_w: torch.Tensor,
+                     proj: LayerProj, ffn_norm_w: torch.Tensor, ffn_proj: FfnProj, pos: torch.Tensor,
+                     q_norm_w: torch.Tensor | None = None, k_norm_w: torch.Tensor | None = None,
+                     stream: torch.cuda.Stream | None = None) -> None:
+        """One whole layer of the decode step on the residual x [B, dim] in place
+        (cpp/model.hpp:315-452): attention norm, the attention block, the FFN block."""
+        B = x.shape[0]
+        key = (dim, n_ffn, B)
+        if getattr(self, "block_ws", None) is None or self.block_ws_key != key:
+            n = abi.lib().picoattn_decode_block_workspace_size(C.byref(self.cfg), dim, n_ffn, B, self.max_ctx)
+            if n == 0:
+                raise abi.PicoAttnError(abi.PICOATTN_EUNSUPPORTED, "decode_block_workspace_size")
+            self.block_ws = torch.zeros(n, dtype=torch.uint8, device=self.device)
+            self.block_ws_key = key
+            abi.check(abi.lib().picoattn_workspace_init(self.block_ws.data_ptr(), n, stream_handle(stream)),
+                      "ws init")
+        st = abi.lib().picoattn_decode_block(
+            C.byref(self.cfg), layer, dim, n_ffn, B, self.max_ctx, attn_norm_w.data_ptr(), C.byref(proj.struct),
+            ffn_norm_w.data_ptr(), C.byref(ffn_proj.struct), abi.ptr(q_norm_w), abi.ptr(k_norm_w),
+            self.rope_cos.data_ptr(), self.rope_sin.data_ptr(), self.k_ptrs.data_ptr(), self.v_ptrs.data_ptr(),
+            pos.data_ptr(), x.data_ptr(), self.block_ws.data_ptr(), self.block_ws.numel(), stream_handle(stream))
+        abi.check(st, "picoattn_decode_block")
+
+    def block_status(self) -> int:
+        v = C.c_uint32(0)
+        abi.check(abi.lib().picoattn_workspace_status(self.block_ws.data_ptr(), stream_handle(), C.byref(v)))
+        return v.value
 
     def decode_one(self, layer: int, pos: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                    out: torch.Tensor, q_norm_w: torch.Tensor | None = None, k_norm_w: torch.Tensor | None = None,

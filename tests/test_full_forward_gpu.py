@@ -150,3 +150,112 @@ def test_full_forward_decode_layer_quantized_weights(cuda, wtype):
     scale = np.abs(want).max()
     err = np.abs(got - want).max()
     assert err <= 2e-2 * scale, f"max logit error {err:.3g} of scale {scale:.3g}"
+
+
+def _device_model(m, L, dev):
+    """Every layer's weights of a RefFullModel on the device, as the engine holds them."""
+    from picolm_qwen_b200.runtime import FfnProj, LayerProj
+    layers = []
+    for l in range(L):
+        aw = [m.attn_weight(l, i) for i in range(4)]
+        proj = LayerProj(*(dev(w) for w, _ in aw), [t for _, t in aw], *(dev(m.attn_bias(l, i)) for i in range(4)))
+        fw = [m.ffn_weight(l, i) for i in range(3)]
+        fproj = FfnProj(*(dev(w) for w, _ in fw), [t for _, t in fw], dev(m.ffn_bias(l, 0)), dev(m.ffn_bias(l, 1)))
+        layers.append((dev(m.model_norm(l, 0)), proj, dev(m.model_norm(l, 1)), fproj))
+    out_w, out_t = m.ffn_weight(0, 3)
+    return layers, dev(m.model_norm(0, 2)), dev(out_w), out_t
+
+
+@pytest.mark.parametrize("attn_t,ffn_t", [(13, 13), (9, 15)], ids=["Q4_K-Q4_K", "Q8_0-Q6_K"])
+def test_full_forward_whole_decode_step_on_device(cuda, attn_t, ffn_t):
+    """Every decode step wholly on the device: per layer one picoattn_decode_block
+    (attention norm, projections, QK-norm, RoPE, cache append, attention,
+    output projection, FFN norm, gate/up, SwiGLU, down projection, both
+    residuals), then picoattn_logits (final norm, output matrix); only the
+    embedding row comes from the host.  Quantised attention, FFN and output
+    weights.  The reference runs the unmodified Model::forward on the same
+    model; the next-token argmax must be identical at every step and the logits
+    agree within 2e-2 of their scale."""
+    from picolm_qwen_b200 import abi
+    from picolm_qwen_b200.runtime import AttnState, Scratch, logits
+    if not __import__("os").path.exists(pyoracle.REF_SO):
+        pytest.skip("oracle/_ref not built")
+    ref = pyoracle.RefHarness()
+    hq, hkv, hd, seed = 4, 2, 128, 31
+    L, S, vocab, n_gen, n_ffn = 3, 64, 211, 32, 512
+    kw = dict(n_layers=L, hq=hq, hkv=hkv, hd=hd, n_ffn=n_ffn, vocab=vocab, max_seq=S, rope_base=1e6,
+              rope_mode=0, qk_norm=1, seed=seed)
+    m_ref, m = pyoracle.RefFullModel(ref, **kw), pyoracle.RefFullModel(ref, **kw)
+    for mm in (m_ref, m):
+        mm.set_attn_weights(attn_t, 8)
+        mm.set_ffn_weights(ffn_t, 9)
+    dim = hq * hd
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    cfg = abi.Config.make(L, hq, hkv, hd, S, 1e6, abi.ROPE_NEOX)
+    st = AttnState(cfg, n_seqs=1, max_ctx=S)
+    norms = [(dev(m.norm_w(l, 0)), dev(m.norm_w(l, 1))) for l in range(L)]
+    layers, out_norm, out_w, out_t = _device_model(m, L, dev)
+    scratch = Scratch("cuda")
+    lg = torch.empty((1, vocab), device="cuda")
+    got, want = [], []
+    tok = 7
+    for pos in range(n_gen):
+        want.append(m_ref.forward(tok, pos))
+        x = dev(m.embed(tok)[None])
+        pos_t = torch.tensor([pos], dtype=torch.int32, device="cuda")
+        for l in range(L):
+            an, proj, fn, fproj = layers[l]
+            st.decode_block(l, dim, n_ffn, x, an, proj, fn, fproj, pos_t, *norms[l])
+        logits(x, out_norm, out_w, out_t, vocab, lg, scratch)
+        got.append(lg.cpu().numpy()[0])
+        tok = int(np.argmax(want[-1]))
+    torch.cuda.synchronize()
+    assert st.block_status() == 0
+    got, want = np.stack(got), np.stack(want)
+    same = (np.argmax(got, 1) == np.argmax(want, 1))
+    assert same.all(), f"argmax differs at steps {np.nonzero(~same)[0].tolist()}"
+    scale = np.abs(want).max()
+    err = np.abs(got - want).max()
+    assert err <= 2e-2 * scale, f"max logit error {err:.3g} of scale {scale:.3g}"
+
+
+@pytest.mark.parametrize("ffn_t", [1, 13, 15], ids=["F32", "Q4_K", "Q6_K"])
+def test_rmsnorm_ffn_logits_vs_reference(cuda, ffn_t):
+    """picoattn_rmsnorm, picoattn_ffn and picoattn_logits on their own against
+    the reference's TensorOps::rmsnorm, FFN block (cpp/model.hpp:429-452) and
+    logits (cpp/model.hpp:454-457) on the same model weights and inputs.  The
+    weights are dequantised bit-identically and the sums run in another order,
+    so the outputs agree to fp32 rounding: |gpu - ref| <= 1e-4 (1 + |ref|)."""
+    from picolm_qwen_b200.runtime import Scratch, ffn, logits, rmsnorm
+    if not __import__("os").path.exists(pyoracle.REF_SO):
+        pytest.skip("oracle/_ref not built")
+    ref = pyoracle.RefHarness()
+    hq, hkv, hd, n_ffn, vocab = 8, 2, 128, 1536, 1000
+    m = pyoracle.RefFullModel(ref, n_layers=1, hq=hq, hkv=hkv, hd=hd, n_ffn=n_ffn, vocab=vocab, max_seq=8,
+                              rope_base=1e6, rope_mode=0, qk_norm=0, seed=3)
+    if ffn_t != 1:
+        m.set_ffn_weights(ffn_t, 4)
+    dim = hq * hd
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    rng = np.random.default_rng(ffn_t)
+    xs = rng.standard_normal((3, dim)).astype(np.float32)
+    layers, out_norm, out_w, out_t = _device_model(m, 1, dev)
+    an, _, fn, fproj = layers[0]
+    scratch = Scratch("cuda")
+    # rmsnorm
+    out = torch.empty((3, dim), device="cuda")
+    rmsnorm(dev(xs), an, out)
+    want = np.stack([m.attn_norm(0, x) for x in xs])
+    assert np.allclose(out.cpu().numpy(), want, rtol=1e-5, atol=1e-6)
+    # FFN block with its residual, three vectors at once
+    x = dev(xs)
+    ffn(fproj, fn, n_ffn, x, scratch)
+    want = np.stack([m.ffn(0, xv) for xv in xs])
+    got = x.cpu().numpy()
+    assert np.all(np.abs(got - want) <= 1e-4 * (1 + np.abs(want))), f"ffn max err {np.abs(got - want).max():.3g}"
+    # logits
+    lg = torch.empty((3, vocab), device="cuda")
+    logits(dev(xs), out_norm, out_w, out_t, vocab, lg, scratch)
+    want = np.stack([m.logits(xv) for xv in xs])
+    got = lg.cpu().numpy()
+    assert np.all(np.abs(got - want) <= 1e-4 * (1 + np.abs(want))), f"logits max err {np.abs(got - want).max():.3g}"
