@@ -425,6 +425,10 @@ def run_ours(args) -> None:
     if world == 1 and not args.no_layer:
         torch.cuda.empty_cache()
         layer_line = run_layer(args, dev)
+    step_line = None
+    if world == 1 and not args.no_step:
+        torch.cuda.empty_cache()
+        step_line = run_token_step(args, dev)
     small_lines = []
     if world == 1 and not args.no_small:
         for spec in SMALL:
@@ -481,6 +485,8 @@ def run_ours(args) -> None:
             line["long_context"] = longctx_line
         if layer_line is not None:
             line["decode_layer"] = layer_line
+        if step_line is not None:
+            line["token_step"] = step_line
         for sl in small_lines:
             line["small_cfg%d" % sl["config"]["baseline_config"]] = sl
         if world == 1 and not args.no_cpu:
@@ -1019,10 +1025,152 @@ def run_layer(args, dev) -> dict:
                        "cached_rows": S - 1, "weights": "q,k,o Q4_K; v Q6_K (seeded random blocks)",
                        "bytes_per_step": total, "weight_bytes": wbytes, "kv_bytes": kv_bytes},
             "frac_of_hbm": round(gbs / peak, 4),
-            "roofline": {"bound": "hbm", "kernel": "matvec1_kernel<4> (Q4_K, 3584 x 3584, one vector)",
+            "roofline": {"bound": "hbm", "kernel": "matvecq_direct_kernel (Q4_K, 3584 x 3584, one vector)",
                          "achieved": round(mv_bytes / (mv_us / 1e6) / 1e9, 1), "peak": peak, "peak_kind": peak_kind,
                          "unit": "GB/s", "frac": round(mv_bytes / (mv_us / 1e6) / 1e9 / peak, 4),
                          "us_per_launch": round(mv_us, 2), "weight_bytes_per_launch": mv_bytes}}
+
+
+STEP = dict(name="qwen2.5-7b-token-step-q4km", n_layers=28, n_heads=28, n_kv_heads=4, head_dim=128, dim=3584,
+            n_ffn=18944, vocab=152064, rope_base=1e6, ctx=4096, seed=0,
+            attn_types=(13, 13, 15, 13), ffn_types=(13, 13, 15), out_type=15)
+
+
+def random_blocks_dev(wtype: int, n_in: int, n_out: int, g, dev):
+    """n_out rows of n_in weights of a GGUF block type as random bytes on the
+    device, every block's fp16 scales set small and positive (Q4_K: d, dmin at
+    bytes 0-3; Q6_K: d at bytes 208-209) so activations stay finite."""
+    import torch
+    from picolm_qwen_b200 import abi
+    nb = abi.lib().picoattn_weight_bytes(wtype, n_in, n_out)
+    w = torch.randint(0, 256, (nb,), generator=g, device=dev, dtype=torch.uint8)
+    bsz = 144 if wtype == 13 else 210
+    v = w.view(-1, bsz)
+    at = 0 if wtype == 13 else 208
+    v[:, at:at + 2] = torch.tensor([0x00, 0x10], dtype=torch.uint8, device=dev)  # fp16 0x1000 ~ 2.4e-4
+    if wtype == 13:
+        v[:, 2:4] = torch.tensor([0x00, 0x08], dtype=torch.uint8, device=dev)
+    return w, nb
+
+
+def run_token_step(args, dev) -> dict:
+    """A whole decode step of a Qwen2.5-7B-shaped model on the device, one
+    sequence at position ctx - 1: per layer one picoattn_decode_block
+    (attention norm, q/k/v projections, QK-norm-free attention over 4096 rows,
+    output projection, FFN norm, gate/up, SwiGLU, down projection, residuals),
+    then picoattn_logits over the 152064-row output matrix; Q4_K_M-style
+    weights (attention q, k, o and FFN gate, up Q4_K; v, down and the output
+    matrix Q6_K; seeded random blocks, each layer its own), 4.7 GB per token;
+    the step replayed as one CUDA graph (the embedding row is the input)."""
+    import torch
+    from picolm_qwen_b200 import abi
+    from picolm_qwen_b200.runtime import AttnState, FfnProj, LayerProj, Scratch, logits
+    p = STEP
+    L, hq, hkv, hd, dim, S = p["n_layers"], p["n_heads"], p["n_kv_heads"], p["head_dim"], p["dim"], p["ctx"]
+    n_ffn, vocab = p["n_ffn"], p["vocab"]
+    qd, kvd = hq * hd, hkv * hd
+    cfg = abi.Config.make(L, hq, hkv, hd, S, p["rope_base"], abi.ROPE_NEOX)
+    st = AttnState(cfg, n_seqs=1, max_ctx=S)
+    g = torch.Generator(device=dev).manual_seed(p["seed"])
+    for c in (st.k_cache, st.v_cache):
+        c.copy_((torch.randn(c.shape, generator=g, device=dev) * 0.5).half().view(torch.int16))
+    layers, wbytes = [], 0
+    for _ in range(L):
+        aw = []
+        for t, (n_in, n_out) in zip(p["attn_types"], ((dim, qd), (dim, kvd), (dim, kvd), (qd, dim))):
+            w, nb = random_blocks_dev(t, n_in, n_out, g, dev)
+            aw.append(w)
+            wbytes += nb
+        fw = []
+        for t, (n_in, n_out) in zip(p["ffn_types"], ((dim, n_ffn), (dim, n_ffn), (n_ffn, dim))):
+            w, nb = random_blocks_dev(t, n_in, n_out, g, dev)
+            fw.append(w)
+            wbytes += nb
+        an = 1 + 0.1 * torch.randn(dim, generator=g, device=dev)
+        fn = 1 + 0.1 * torch.randn(dim, generator=g, device=dev)
+        layers.append((an, LayerProj(*aw, p["attn_types"]), fn, FfnProj(*fw, p["ffn_types"])))
+    w_out, nb = random_blocks_dev(p["out_type"], dim, vocab, g, dev)
+    wbytes += nb
+    out_norm = 1 + 0.1 * torch.randn(dim, generator=g, device=dev)
+    x0 = torch.randn(1, dim, generator=g, device=dev)
+    x = torch.empty_like(x0)
+    lg = torch.empty((1, vocab), device=dev)
+    pos = torch.tensor([S - 1], dtype=torch.int32, device=dev)
+    scratch = Scratch(dev)
+    s = torch.cuda.Stream(dev)
+
+    def step(stream):
+        x.copy_(x0)
+        for l in range(L):
+            an, proj, fn, fproj = layers[l]
+            st.decode_block(l, dim, n_ffn, x, an, proj, fn, fproj, pos, stream=stream)
+        logits(x, out_norm, w_out, p["out_type"], vocab, lg, scratch, stream=stream)
+
+    with torch.cuda.stream(s):
+        step(s)
+        torch.cuda.synchronize(dev)
+        if st.block_status() != 0:
+            raise RuntimeError("token step flagged bad input")
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            step(s)
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    if not torch.isfinite(lg).all():
+        raise RuntimeError("token step logits not finite")
+    steps = max(5, args.steps // 4)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    del graph
+    kv_bytes = L * 2 * S * kvd * 2
+    total = wbytes + kv_bytes
+    peak, peak_kind = measured_peaks()
+    gbs = total / (ms / 1e3) / 1e9
+    line = {"metric": "decode tokens/s (one sequence, whole model on the device)", "value": round(1e3 / ms, 2),
+            "unit": "tok/s", "ms_per_token": round(ms, 4), "steps": steps,
+            "config": {"workload": p["name"], "layers": L, "heads_q_kv_dim": [hq, hkv, hd], "dim": dim,
+                       "n_ffn": n_ffn, "vocab": vocab, "cached_rows": S - 1,
+                       "weights": "attention q,k,o + FFN gate,up Q4_K; v, down, output Q6_K (seeded random blocks)",
+                       "bytes_per_token": total, "weight_bytes": wbytes, "kv_bytes": kv_bytes,
+                       "l2": "4.7 GB per token, larger than L2, no flush",
+                       "timing": "CUDA graph of 28 picoattn_decode_block calls + picoattn_logits"},
+            "achieved_gbs": round(gbs, 1), "frac_of_hbm": round(gbs / peak, 4), "peak": peak, "peak_kind": peak_kind}
+    del st, layers, w_out
+    if not args.no_cpu:
+        try:
+            line["cpu_baseline"] = cpu_token_step()
+        except Exception as e:  # the CPU leg never hides a GPU number
+            line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+    return line
+
+
+def cpu_token_step() -> dict:
+    """The reference's unmodified Model::forward on a one-layer model of the same
+    shape (Q4_K weights, vocab 1024) on one thread (the engine's default): one
+    layer's time x 28 layers, the 152064-row output matrix left out."""
+    from oracle import pyoracle
+    p = STEP
+    ref = pyoracle.RefHarness()
+    m = pyoracle.RefFullModel(ref, n_layers=1, hq=p["n_heads"], hkv=p["n_kv_heads"], hd=p["head_dim"],
+                              n_ffn=p["n_ffn"], vocab=1024, max_seq=64, rope_base=p["rope_base"], rope_mode=0,
+                              qk_norm=0, seed=1)
+    m.set_attn_weights(13, 3)
+    m.set_ffn_weights(13, 4)
+    m.forward(5, 0)  # first touch of every weight page
+    t0 = time.perf_counter()
+    m.forward(9, 1)
+    per_layer = time.perf_counter() - t0
+    tok_s = 1.0 / (per_layer * p["n_layers"])
+    m.close()
+    return {"value": round(tok_s, 4), "unit": "tok/s", "cores": 1, "kind": "reference",
+            "sample": f"Model::forward of a one-layer model of this shape (Q4_K weights, vocab 1024) on one thread: "
+                      f"{per_layer * 1e3:.1f} ms per layer, x {p['n_layers']} layers; output matrix left out"}
 
 
 def main() -> None:
@@ -1036,6 +1184,8 @@ def main() -> None:
     ap.add_argument("--no-longctx", action="store_true", help="skip the long-context (Qwen2.5-32B, 128K) leg")
     ap.add_argument("--no-layer", action="store_true",
                     help="skip the decode-layer leg (projections + attention, Qwen2.5-7B, Q4_K_M weights)")
+    ap.add_argument("--no-step", action="store_true",
+                    help="skip the whole-model token step leg (Qwen2.5-7B shape, Q4_K_M-style weights)")
     ap.add_argument("--no-small", action="store_true",
                     help="skip the small single-sequence legs (TinyLlama p=511, Qwen2.5-0.5B 4096)")
     ap.add_argument("--seqs", type=int, default=WORKLOAD["n_seqs"],
