@@ -55,7 +55,8 @@ typedef struct CUstream_st* picoattn_stream_t;
 #define PICOATTN_EDEVICE      -8  /* current device is not sm_100 */
 #define PICOATTN_EDEVSTATUS   -9  /* a kernel flagged bad input (see workspace status) */
 #define PICOATTN_EIO         -10  /* a file could not be opened, read or written */
-#define PICOATTN_EFORMAT     -11  /* not a KVCP file, or its shape does not match the config */
+#define PICOATTN_EFORMAT     -11  /* not a KVCP/GGUF file, or its shape does not match the config */
+#define PICOATTN_ENOENT      -12  /* no such tensor in the model file */
 
 /* Device-side sticky status bits (picoattn_workspace_status). */
 #define PICOATTN_DEV_BAD_POS      0x1u  /* pos[b] < 0, >= max_seq_len or >= max_ctx */
@@ -519,6 +520,52 @@ int32_t picoattn_decode_block(const picoattn_config_t* cfg, int32_t layer, int32
                               const float* k_norm_w, const float* rope_cos, const float* rope_sin,
                               uint16_t* const* k_cache, uint16_t* const* v_cache, const int32_t* pos, float* x,
                               void* workspace, size_t workspace_bytes, picoattn_stream_t stream);
+
+/* ---- GGUF model files to the device -------------------------------------------
+ *
+ * The C++ engine's loader (Model::parse_gguf, cpp/model.hpp:705-902) on the
+ * host: the file is mapped read-only and parsed with the engine's rules (the
+ * metadata keys it reads, by substring, cpp/gguf_metadata.hpp:241-275; its
+ * defaults and its context cap: max_seq_len_override when smaller than the
+ * file's context, else at most 2048; tensor types shifted by one into the
+ * engine's numbering = PICOATTN_WT_*; tensors under the engine's keys:
+ * layer -1 for token_embd, output_norm and output (output = token_embd when
+ * the file has none), else blk.<layer>.<key> with ".weight" removed).
+ * picoattn_gguf_upload copies every tensor into one caller-allocated device
+ * arena (256-byte aligned) and adds fp32 copies of the norms and biases (the
+ * arrays the engine dequantises at load, cpp/model.hpp:924-1000), so that
+ * picoattn_gguf_arena_tensor hands picoattn_decode_block and picoattn_logits
+ * their weights.  Not on the token path: open maps the file, upload copies
+ * it and synchronises the stream. */
+typedef struct picoattn_gguf picoattn_gguf_t;
+
+/* The model shape as the engine reads it from the file. */
+typedef struct {
+    int32_t n_embd, n_ffn, n_heads, n_kv_heads, n_layers, vocab_size, max_seq_len, head_dim;
+    float rope_freq_base;
+    int32_t alignment;  /* general.alignment, 0 when absent (32 used) */
+} picoattn_gguf_config_t;
+
+/* PICOATTN_EIO (cannot open or map), PICOATTN_EFORMAT (not a GGUF v2/v3 file
+ * the engine can read), else PICOATTN_OK and *out. */
+int32_t picoattn_gguf_open(const char* path, int32_t max_seq_len_override, picoattn_gguf_t** out);
+int32_t picoattn_gguf_close(picoattn_gguf_t* model);
+int32_t picoattn_gguf_get_config(const picoattn_gguf_t* model, picoattn_gguf_config_t* cfg);
+/* Type (PICOATTN_WT_*), byte count and file offset of a tensor by the engine's
+ * key (layer -1: token_embd, output_norm, output); PICOATTN_ENOENT if absent. */
+int32_t picoattn_gguf_find(const picoattn_gguf_t* model, int32_t layer, const char* key, int32_t* type,
+                           size_t* bytes, size_t* file_offset);
+/* Device bytes the arena needs. */
+size_t picoattn_gguf_arena_bytes(const picoattn_gguf_t* model);
+/* Copies the model into `arena` (device, 256-byte aligned) and synchronises
+ * `stream`; norms and biases must be F32 or F16 (else PICOATTN_EUNSUPPORTED). */
+int32_t picoattn_gguf_upload(const picoattn_gguf_t* model, void* arena, size_t arena_bytes,
+                             picoattn_stream_t stream);
+/* A tensor's device address in the arena and its type: the file's bytes, or
+ * for norms and biases (keys attn_norm, ffn_norm, output_norm, attn_q_norm,
+ * attn_k_norm, *_b) their fp32 copy (type PICOATTN_WT_F32). */
+int32_t picoattn_gguf_arena_tensor(const picoattn_gguf_t* model, const void* arena, int32_t layer, const char* key,
+                                   const void** dev_ptr, int32_t* type);
 
 #ifdef __cplusplus
 }

@@ -373,6 +373,61 @@ class RefModel:
             pass
 
 
+class RefGguf:
+    """A GGUF file loaded by the engine's own Model::load (test only)."""
+
+    def __init__(self, ref: RefHarness, path: str, max_seq_override: int = 0, rope_mode: int = 0):
+        L = ref.L
+        if not hasattr(L, "_gguf_proto"):
+            L.pref_gguf_load.restype = C.c_void_p
+            L.pref_gguf_load.argtypes = [C.c_char_p, C.c_int, C.c_int]
+            L.pref_gguf_free.argtypes = [C.c_void_p]
+            L.pref_gguf_config.argtypes = [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_float)]
+            L.pref_gguf_tensor.restype = C.c_longlong
+            L.pref_gguf_tensor.argtypes = [C.c_void_p, C.c_int, C.c_char_p, C.POINTER(C.c_int)]
+            L.pref_gguf_forward.restype = C.c_int
+            L.pref_gguf_forward.argtypes = [C.c_void_p, C.c_int, C.c_int, _f32p]
+            L._gguf_proto = True
+        self.L = L
+        self.h = L.pref_gguf_load(path.encode(), max_seq_override, rope_mode)
+
+    @property
+    def loaded(self) -> bool:
+        return bool(self.h)
+
+    def config(self) -> dict:
+        ints = (C.c_int * 9)()
+        rb = C.c_float()
+        self.L.pref_gguf_config(self.h, ints, C.byref(rb))
+        names = ("n_embd", "n_ffn", "n_heads", "n_kv_heads", "n_layers", "vocab_size", "max_seq_len", "head_dim",
+                 "alignment")
+        d = dict(zip(names, list(ints)))
+        d["rope_freq_base"] = rb.value
+        return d
+
+    def tensor(self, layer: int, key: str):
+        """(file offset, engine type) or None."""
+        t = C.c_int()
+        off = self.L.pref_gguf_tensor(self.h, layer, key.encode(), C.byref(t))
+        return None if off < 0 else (off, t.value)
+
+    def forward(self, token: int, pos: int, vocab: int) -> np.ndarray:
+        out = np.empty(vocab, np.float32)
+        assert self.L.pref_gguf_forward(self.h, token, pos, out) == 0
+        return out
+
+    def close(self):
+        if self.h:
+            self.L.pref_gguf_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class RefFullModel:
     """Multi-layer reference Model with seeded random F32 weights (test only).
 

@@ -608,6 +608,52 @@ int pref_full_set_ffn_weights(void* hp, int type, uint64_t seed) {
     return 0;
 }
 
+// ---------------------------------------------------------------------------
+// GGUF files through the engine's own loader (Model::load, cpp/model.hpp:207-224)
+// ---------------------------------------------------------------------------
+
+// The model loaded from `path` (mapping, parse_gguf, allocate_run_state) with
+// the RoPE of the file name's choice made explicit, or null.
+void* pref_gguf_load(const char* path, int max_seq_override, int rope_mode) {
+    auto* m = new Model();
+    if (m->load(path, max_seq_override) != 0) {
+        delete m;
+        return nullptr;
+    }
+    m->rope_fn = rope_for(rope_mode);
+    return m;
+}
+void pref_gguf_free(void* mp) { delete (Model*)mp; }
+
+// ints: n_embd, n_ffn, n_heads, n_kv_heads, n_layers, vocab_size, max_seq_len,
+// head_dim, alignment (0 if absent); *rope_base
+void pref_gguf_config(void* mp, int* ints, float* rope_base) {
+    auto& ci = ((Model*)mp)->config.ints();
+    const char* const keys[9] = {cfg::N_EMBD, cfg::N_FFN, cfg::N_HEADS, cfg::N_KV_HEADS, cfg::N_LAYERS,
+                                 cfg::VOCAB_SIZE, cfg::MAX_SEQ_LEN, cfg::HEAD_DIM, cfg::ALIGNMENT};
+    for (int i = 0; i < 9; i++) ints[i] = getInt(ci, keys[i]);
+    *rope_base = getFloat(((Model*)mp)->config.floats(), cfg::ROPE_FREQ_BASE);
+}
+
+// The tensor the engine holds under (layer, key) (layer -1: the output
+// tensors): its byte offset in the mapped file and its type; -1 if absent.
+long long pref_gguf_tensor(void* mp, int layer, const char* key, int* type) {
+    Model* m = (Model*)mp;
+    metadata::WeightEntry e = layer < 0 ? m->weights.get(key) : m->weights.get_layer(layer).get(key);
+    if (!e) return -1;
+    *type = (int)e.type;
+    return (long long)((const uint8_t*)e.ptr - (const uint8_t*)m->mmap_addr);
+}
+
+// Model::forward of the loaded model: logits [vocab]
+int pref_gguf_forward(void* mp, int token, int pos, float* logits) {
+    Model* m = (Model*)mp;
+    const int vocab = getInt(m->config.ints(), cfg::VOCAB_SIZE);
+    if (token < 0 || token >= vocab || pos < 0 || pos >= getInt(m->config.ints(), cfg::MAX_SEQ_LEN)) return -1;
+    std::memcpy(logits, m->forward(token, pos), sizeof(float) * (size_t)vocab);
+    return 0;
+}
+
 // Projections with the reference's own code: one row dequantised
 // (dequantize_row, cpp/quant.hpp:283-295) and matmul_bias per vector
 // (cpp/tensor.hpp:110-143; the bias as the F32 array the engine keeps).

@@ -26,6 +26,7 @@ PICOATTN_EDEVICE = -8
 PICOATTN_EDEVSTATUS = -9
 PICOATTN_EIO = -10
 PICOATTN_EFORMAT = -11
+PICOATTN_ENOENT = -12
 
 KVCP_MAGIC = 0x4B564350
 
@@ -95,6 +96,13 @@ class LayerWeights(C.Structure):
     ]
 
 
+class GgufConfig(C.Structure):
+    """picoattn_gguf_config_t."""
+    _fields_ = [(n, C.c_int32) for n in ("n_embd", "n_ffn", "n_heads", "n_kv_heads", "n_layers", "vocab_size",
+                                          "max_seq_len", "head_dim")] + [("rope_freq_base", C.c_float),
+                                                                         ("alignment", C.c_int32)]
+
+
 class FfnWeights(C.Structure):
     """picoattn_ffn_weights_t: device pointers and PICOATTN_WT_* types."""
     _fields_ = [
@@ -159,6 +167,14 @@ PROTOTYPES = {
     "picoattn_decode_layer": (_I, [_CFG, _I, _I, _I, _I, _P, C.POINTER(LayerWeights), _P, _P, _P, _P, _P, _P, _P,
                                    _P, _P, _Z, _P]),
     "picoattn_rmsnorm": (_I, [_P, _P, _P, _I, _I, _P]),
+    "picoattn_gguf_open": (_I, [C.c_char_p, _I, C.POINTER(C.c_void_p)]),
+    "picoattn_gguf_close": (_I, [_P]),
+    "picoattn_gguf_get_config": (_I, [_P, C.POINTER(GgufConfig)]),
+    "picoattn_gguf_find": (_I, [_P, _I, C.c_char_p, C.POINTER(C.c_int32), C.POINTER(C.c_size_t),
+                                C.POINTER(C.c_size_t)]),
+    "picoattn_gguf_arena_bytes": (_Z, [_P]),
+    "picoattn_gguf_upload": (_I, [_P, _P, _Z, _P]),
+    "picoattn_gguf_arena_tensor": (_I, [_P, _P, _I, C.c_char_p, C.POINTER(C.c_void_p), C.POINTER(C.c_int32)]),
     "picoattn_ffn_workspace_size": (_Z, [_I, _I, _I]),
     "picoattn_ffn": (_I, [C.POINTER(FfnWeights), _P, _I, _I, _I, _P, _P, _Z, _P]),
     "picoattn_logits_workspace_size": (_Z, [_I, _I]),

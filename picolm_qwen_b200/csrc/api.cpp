@@ -137,7 +137,8 @@ const char* picoattn_strerror(int32_t s) {
         case PICOATTN_EDEVICE: return "device is not sm_100";
         case PICOATTN_EDEVSTATUS: return "a kernel flagged bad input";
         case PICOATTN_EIO: return "file could not be opened, read or written";
-        case PICOATTN_EFORMAT: return "not a KVCP file of this shape";
+        case PICOATTN_EFORMAT: return "not a KVCP or GGUF file of this shape";
+        case PICOATTN_ENOENT: return "no such tensor in the model file";
         default: return "unknown status";
     }
 }

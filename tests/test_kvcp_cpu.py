@@ -74,4 +74,4 @@ def test_library_kvcp_size_and_host_validation(tmp_path):
     other = tmp_path / "other.kvcp"
     other.write_bytes(np.array([MAGIC, 1, 4, 128], "<u4").tobytes())  # 4 layers, the config has 3
     assert lib.picoattn_kvcp_load(C.byref(cfg), str(other).encode(), 16, 16, C.byref(n), None) == abi.PICOATTN_EFORMAT
-    assert lib.picoattn_strerror(abi.PICOATTN_EFORMAT) == b"not a KVCP file of this shape"
+    assert lib.picoattn_strerror(abi.PICOATTN_EFORMAT) == b"not a KVCP or GGUF file of this shape"
