@@ -868,6 +868,9 @@ cudaError_t launch_matvec(const MatvecArgs& a, cudaStream_t stream) {
         return cudaSuccess;
     });
     if (se != cudaSuccess) return se;
+    // one vector of Q4_K / Q6_K weights: the tensor-core kernel
+    const cudaError_t me = launch_matvec_mma(a, stream);
+    if (me != cudaErrorNotSupported) return me;
     bool f32 = false;  // F32 chunks need the 4 KB slots
     for (int p = 0; p < a.n_parts; p++) f32 = f32 || a.part[p].type == PICOATTN_WT_F32;
     if (f32) {

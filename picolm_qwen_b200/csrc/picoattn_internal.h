@@ -152,6 +152,9 @@ int weight_block_bytes(int type);
 bool matvec_part(int type, const void* w, const float* bias, int n_in, int n_out, float* out, size_t out_stride,
                  MatvecPart* p);
 cudaError_t launch_matvec(const MatvecArgs& a, cudaStream_t stream);
+// One vector of Q4_K / Q6_K matrices on the integer tensor cores (matvec_mma.cu);
+// cudaErrorNotSupported when the launch does not fit it.
+cudaError_t launch_matvec_mma(const MatvecArgs& a, cudaStream_t stream);
 
 // The rest of a decode layer (layer_ops.cu): model-dimension RMSNorm of n_vec
 // vectors, and the FFN gate gate = silu(gate) * up over n elements.

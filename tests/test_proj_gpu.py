@@ -73,6 +73,83 @@ def test_matvec_vs_reference(cuda, oracle, ref, wtype, n_in, n_out, n_vec):
     assert (err <= bound + 1e-6 * np.abs(res0)).all()
 
 
+TC_TYPES = (13, 15)  # Q4_K, Q6_K: the integer tensor-core kernel
+
+
+@pytest.mark.parametrize("wtype", TC_TYPES, ids=["Q4_K", "Q6_K"])
+@pytest.mark.parametrize("n_in,n_out", [(768, 33), (256, 16), (512, 19000), (18944, 48), (2816, 1000)])
+def test_matvec_tensor_core_shapes(cuda, oracle, ref, wtype, n_in, n_out):
+    """Odd super-block counts (Q6_K rows then start 2 bytes off a word), ragged
+    last tiles, many tiles per block and the longest rows, against the
+    reference; and a rerun gives the same bits."""
+    from picolm_qwen_b200.runtime import matvec
+    rng = np.random.default_rng(n_in * 31 + n_out + wtype)
+    w = wg.make(wtype, n_in, n_out, rng)
+    x = rng.standard_normal((1, n_in)).astype(np.float32)
+    bias = rng.standard_normal(n_out).astype(np.float32)
+    exp = ref.matvec(w, wtype, bias, n_in, n_out, x)
+    wd, xd, bd = dev(w), dev(x), dev(bias)
+    out = torch.full((1, n_out), float("nan"), device="cuda")
+    matvec(wd, wtype, n_in, n_out, xd, out, bd)
+    again = torch.full((1, n_out), float("nan"), device="cuda")
+    matvec(wd, wtype, n_in, n_out, xd, again, bd)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    bound = 3e-5 * magnitude(oracle, w, wtype, n_in, n_out, x, bias)
+    err = np.abs(got.astype(np.float64) - exp)
+    assert (err <= bound).all(), f"max err {err.max():.3g}, bound there {bound.flat[err.argmax()]:.3g}"
+    assert np.array_equal(got.view(np.uint32), again.cpu().numpy().view(np.uint32))
+
+
+@pytest.mark.parametrize("wtype", TC_TYPES, ids=["Q4_K", "Q6_K"])
+@pytest.mark.parametrize("case", ["outliers", "zero-block", "tiny-block", "all-tiny", "all-huge", "mixed-scales"])
+def test_matvec_tensor_core_value_ranges(cuda, oracle, ref, wtype, case):
+    """x is carried as integers scaled per 256-element super-block: elements far
+    below their block's largest, blocks of zeros, blocks near the bottom and
+    top of the fp32 range."""
+    from picolm_qwen_b200.runtime import matvec
+    n_in, n_out = 1280, 64
+    rng = np.random.default_rng(sum(map(ord, case)) + wtype)
+    w = wg.make(wtype, n_in, n_out, rng)
+    x = rng.standard_normal((1, n_in)).astype(np.float32)
+    if case == "outliers":
+        x[0, [3, 300, 700]] = [4e4, -2.5e4, 1e5]
+    elif case == "zero-block":
+        x[0, 256:512] = 0
+    elif case == "tiny-block":
+        x[0, 512:768] *= 1e-33
+    elif case == "all-tiny":
+        x *= 1e-35
+    elif case == "all-huge":
+        x *= 1e25
+    else:  # every super-block its own scale
+        x *= (10.0 ** rng.integers(-6, 7, n_in // 256)).repeat(256).astype(np.float32)
+    exp = ref.matvec(w, wtype, None, n_in, n_out, x)
+    out = torch.full((1, n_out), float("nan"), device="cuda")
+    matvec(dev(w), wtype, n_in, n_out, dev(x), out, None)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().astype(np.float64)
+    bound = 3e-5 * magnitude(oracle, w, wtype, n_in, n_out, x, None)
+    err = np.abs(got - exp)
+    assert np.isfinite(got).all() and (err <= bound).all(), f"max err {err.max():.3g}"
+
+
+@pytest.mark.parametrize("wtype", TC_TYPES, ids=["Q4_K", "Q6_K"])
+def test_matvec_tensor_core_nan_input(cuda, oracle, ref, wtype):
+    """A NaN in x makes every row NaN, as in the reference's fp32 loop."""
+    from picolm_qwen_b200.runtime import matvec
+    n_in, n_out = 512, 32
+    rng = np.random.default_rng(3)
+    w = wg.make(wtype, n_in, n_out, rng)
+    x = rng.standard_normal((1, n_in)).astype(np.float32)
+    x[0, 400] = np.nan
+    out = torch.zeros((1, n_out), device="cuda")
+    matvec(dev(w), wtype, n_in, n_out, dev(x), out, None)
+    torch.cuda.synchronize()
+    assert np.isnan(out.cpu().numpy()).all()
+    assert np.isnan(ref.matvec(w, wtype, None, n_in, n_out, x)).all()
+
+
 SHAPES = {
     # name: (hq, hkv, hd, dim, rope_mode, qk_norm, types q/k/v/o, biases)
     "qwen2.5-7b-q4km": (28, 4, 128, 3584, 0, False, (13, 13, 15, 13), True),
