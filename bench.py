@@ -1025,7 +1025,7 @@ def run_layer(args, dev) -> dict:
                        "cached_rows": S - 1, "weights": "q,k,o Q4_K; v Q6_K (seeded random blocks)",
                        "bytes_per_step": total, "weight_bytes": wbytes, "kv_bytes": kv_bytes},
             "frac_of_hbm": round(gbs / peak, 4),
-            "roofline": {"bound": "hbm", "kernel": "matvecq_direct_kernel (Q4_K, 3584 x 3584, one vector)",
+            "roofline": {"bound": "hbm", "kernel": "matvec_mma_kernel<0> (Q4_K, 3584 x 3584, one vector)",
                          "achieved": round(mv_bytes / (mv_us / 1e6) / 1e9, 1), "peak": peak, "peak_kind": peak_kind,
                          "unit": "GB/s", "frac": round(mv_bytes / (mv_us / 1e6) / 1e9 / peak, 4),
                          "us_per_launch": round(mv_us, 2), "weight_bytes_per_launch": mv_bytes}}
@@ -1132,6 +1132,38 @@ def run_token_step(args, dev) -> dict:
     total = wbytes + kv_bytes
     peak, peak_kind = measured_peaks()
     gbs = total / (ms / 1e3) / 1e9
+    # the projections alone (picoattn_matvec, one vector; each graph streams
+    # every layer's own matrix, or the output matrix, so every launch reads HBM)
+    lib = abi.lib()
+    xin = {n: torch.randn(1, n, generator=g, device=dev) for n in (dim, n_ffn)}
+    yout = torch.empty(1, max(vocab, n_ffn), device=dev)
+    projs = {"attn_o_q4k": [(layers[l][1].tensors[3], p["attn_types"][3], qd, dim) for l in range(L)],
+             "ffn_gate_q4k": [(layers[l][3].tensors[0], p["ffn_types"][0], dim, n_ffn) for l in range(L)],
+             "ffn_down_q6k": [(layers[l][3].tensors[2], p["ffn_types"][2], n_ffn, dim) for l in range(L)],
+             "output_q6k": [(w_out, p["out_type"], dim, vocab)] * 4}
+    kernels = {}
+    for name, calls in projs.items():
+        pg = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(pg, stream=s):
+                for w, t, n_in, n_out in calls:
+                    lib.picoattn_matvec(w.data_ptr(), t, None, n_in, n_out, 1, xin[n_in].data_ptr(),
+                                        yout.data_ptr(), 0, s.cuda_stream)
+        for _ in range(3):
+            pg.replay()
+        torch.cuda.synchronize(dev)
+        e0.record()  # the graph replays on the current stream
+        for _ in range(steps):
+            pg.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        us = e0.elapsed_time(e1) / steps / len(calls) * 1e3
+        nb = lib.picoattn_weight_bytes(calls[0][1], calls[0][2], calls[0][3])
+        kernels[name] = {"us_per_launch": round(us, 2), "weight_bytes": nb,
+                         "gbs": round(nb / (us / 1e6) / 1e9, 1), "frac": round(nb / (us / 1e6) / 1e9 / peak, 4),
+                         "launches_per_token": L if name != "output_q6k" else 1}
+        del pg
+    down = kernels["ffn_down_q6k"]
     line = {"metric": "decode tokens/s (one sequence, whole model on the device)", "value": round(1e3 / ms, 2),
             "unit": "tok/s", "ms_per_token": round(ms, 4), "steps": steps,
             "config": {"workload": p["name"], "layers": L, "heads_q_kv_dim": [hq, hkv, hd], "dim": dim,
@@ -1140,7 +1172,12 @@ def run_token_step(args, dev) -> dict:
                        "bytes_per_token": total, "weight_bytes": wbytes, "kv_bytes": kv_bytes,
                        "l2": "4.7 GB per token, larger than L2, no flush",
                        "timing": "CUDA graph of 28 picoattn_decode_block calls + picoattn_logits"},
-            "achieved_gbs": round(gbs, 1), "frac_of_hbm": round(gbs / peak, 4), "peak": peak, "peak_kind": peak_kind}
+            "achieved_gbs": round(gbs, 1), "frac_of_hbm": round(gbs / peak, 4), "peak": peak, "peak_kind": peak_kind,
+            "projections": kernels,
+            "roofline": {"bound": "hbm", "kernel": "matvec_mma_kernel<1> (Q6_K FFN down, 18944 -> 3584, one vector)",
+                         "achieved": down["gbs"], "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": down["frac"], "us_per_launch": down["us_per_launch"],
+                         "weight_bytes_per_launch": down["weight_bytes"]}}
     del st, layers, w_out
     if not args.no_cpu:
         try:

@@ -335,12 +335,17 @@ size_t picoattn_decode_layer_workspace_size(const picoattn_config_t* cfg, int32_
     return layer_ws(*cfg, n_seqs, max_ctx, &l) ? l.total : 0;
 }
 
-int32_t picoattn_decode_layer(const picoattn_config_t* cfg, int32_t layer, int32_t dim, int32_t n_seqs,
-                              int32_t max_ctx, const float* xb, const picoattn_layer_weights_t* wt,
-                              const float* q_norm_w, const float* k_norm_w, const float* rope_cos,
-                              const float* rope_sin, uint16_t* const* k_cache, uint16_t* const* v_cache,
-                              const int32_t* pos, float* x, void* workspace, size_t workspace_bytes,
-                              picoattn_stream_t stream) {
+}  // extern "C"
+
+namespace {
+
+// picoattn_decode_layer; qkv_after_own: the launch before it is this
+// library's own (its weights may be read before that kernel finishes)
+int32_t decode_layer_impl(const picoattn_config_t* cfg, int32_t layer, int32_t dim, int32_t n_seqs, int32_t max_ctx,
+                          const float* xb, const picoattn_layer_weights_t* wt, const float* q_norm_w,
+                          const float* k_norm_w, const float* rope_cos, const float* rope_sin,
+                          uint16_t* const* k_cache, uint16_t* const* v_cache, const int32_t* pos, float* x,
+                          void* workspace, size_t workspace_bytes, picoattn_stream_t stream, bool qkv_after_own) {
     int32_t st = picoattn_config_check(cfg);
     if (st != PICOATTN_OK) return st;
     if (!wt || !xb || !x || !k_cache || !v_cache || !pos || !workspace || dim <= 0 || n_seqs <= 0)
@@ -373,6 +378,7 @@ int32_t picoattn_decode_layer(const picoattn_config_t* cfg, int32_t layer, int32
     qkv.n_vec = n_seqs;
     qkv.rows_total = qd + 2 * kvd;
     qkv.x = xb;
+    qkv.weights_ready = qkv_after_own ? 1 : 0;
     st = cuda_status(launch_matvec(qkv, s));
     if (st != PICOATTN_OK) return st;
     st = decode_common(cfg, layer, n_seqs, max_ctx, q, k, v, q_norm_w, k_norm_w, rope_cos, rope_sin, k_cache,
@@ -384,7 +390,22 @@ int32_t picoattn_decode_layer(const picoattn_config_t* cfg, int32_t layer, int32
     o.rows_total = dim;
     o.accumulate = 1;
     o.x = attn;
+    o.weights_ready = 1;  // after the decode kernels
     return cuda_status(launch_matvec(o, s));
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t picoattn_decode_layer(const picoattn_config_t* cfg, int32_t layer, int32_t dim, int32_t n_seqs,
+                              int32_t max_ctx, const float* xb, const picoattn_layer_weights_t* wt,
+                              const float* q_norm_w, const float* k_norm_w, const float* rope_cos,
+                              const float* rope_sin, uint16_t* const* k_cache, uint16_t* const* v_cache,
+                              const int32_t* pos, float* x, void* workspace, size_t workspace_bytes,
+                              picoattn_stream_t stream) {
+    return decode_layer_impl(cfg, layer, dim, n_seqs, max_ctx, xb, wt, q_norm_w, k_norm_w, rope_cos, rope_sin,
+                             k_cache, v_cache, pos, x, workspace, workspace_bytes, stream, false);
 }
 
 size_t picoattn_ffn_workspace_size(int32_t dim, int32_t n_ffn, int32_t n_vec) {
@@ -430,6 +451,7 @@ int32_t picoattn_ffn(const picoattn_ffn_weights_t* w, const float* ffn_norm_w, i
     gu.n_vec = n_vec;
     gu.rows_total = 2 * n_ffn;
     gu.x = xb;
+    gu.weights_ready = 1;  // after the norm kernel
     st = cuda_status(launch_matvec(gu, s));
     if (st != PICOATTN_OK) return st;
     st = cuda_status(launch_silu_mul(gate, up, (size_t)n_vec * n_ffn, s));
@@ -440,6 +462,7 @@ int32_t picoattn_ffn(const picoattn_ffn_weights_t* w, const float* ffn_norm_w, i
     dn.rows_total = dim;
     dn.accumulate = 1;
     dn.x = gate;
+    dn.weights_ready = 1;
     return cuda_status(launch_matvec(dn, s));
 }
 
@@ -470,6 +493,7 @@ int32_t picoattn_logits(const float* x, const float* output_norm_w, const void* 
     a.n_vec = n_vec;
     a.rows_total = vocab;
     a.x = xb;
+    a.weights_ready = 1;
     return cuda_status(launch_matvec(a, s));
 }
 
@@ -502,8 +526,8 @@ int32_t picoattn_decode_block(const picoattn_config_t* cfg, int32_t layer, int32
     uint8_t* ffn_ws = base + align_up(l, 256) + align_up((size_t)n_seqs * dim * 4, 256);
     int32_t st = picoattn_rmsnorm(x, attn_norm_w, xb, dim, n_seqs, stream);
     if (st != PICOATTN_OK) return st;
-    st = picoattn_decode_layer(cfg, layer, dim, n_seqs, max_ctx, xb, attn_weights, q_norm_w, k_norm_w, rope_cos,
-                               rope_sin, k_cache, v_cache, pos, x, workspace, l, stream);
+    st = decode_layer_impl(cfg, layer, dim, n_seqs, max_ctx, xb, attn_weights, q_norm_w, k_norm_w, rope_cos,
+                           rope_sin, k_cache, v_cache, pos, x, workspace, l, stream, true);
     if (st != PICOATTN_OK) return st;
     return picoattn_ffn(ffn_weights, ffn_norm_w, dim, n_ffn, n_seqs, x, ffn_ws,
                         picoattn_ffn_workspace_size(dim, n_ffn, n_seqs), stream);

@@ -304,9 +304,11 @@ template <int kMode>
 __global__ void __launch_bounds__(kMmMaxSlices * 32) matvec_mma_kernel(MmArgs p) {
     constexpr int kRaw = kMode == 0 ? kRawQ4K : kRawQ6K;
     extern __shared__ __align__(16) uint8_t mm_smem[];
-    pdl_trigger();
-    pdl_wait();
     const MatvecArgs& a = p.a;
+    pdl_trigger();
+    // the weights may be read before the kernels ahead of this one finish only
+    // when none of them writes them (weights_ready); x always after
+    if (!a.weights_ready) pdl_wait();
     const int nsb = p.nsb, S = p.slices, T = p.tiles_per_block;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     // shared memory: B fragments of every super-block [nsb][8][32], digit
@@ -316,67 +318,71 @@ __global__ void __launch_bounds__(kMmMaxSlices * 32) matvec_mma_kernel(MmArgs p)
     float* partial = reinterpret_cast<float*>(bf_all + (size_t)nsb * 256 + (size_t)S * 256);
     float* xsum = partial + (size_t)T * S * 16;
     float* pw = xsum + 8 * nsb;
-    const int b0 = warp * nsb / S, b1 = (warp + 1) * nsb / S;
-    if (warp < S) prep_x(a.x, b0, b1, bf_all + (size_t)b0 * 256, pw, xsum, dig, lane);
-    __syncwarp();
-    const uint32_t bmask = g < 4 ? 0xFFFFFFFFu : 0u;  // B column g: low half (k < 16) or high half
+    const int b0 = warp * nsb / S, b1 = (warp + 1) * nsb / S, ns = b1 - b0;
     const int tile0 = blockIdx.x * T;
     const int n_my = min(T, p.n_tiles - tile0);
-    const int ns = b1 - b0;
-    if (warp < S && ns > 0) {
-        // rows g and g + 8 of a tile (clamped to its matrix) and their type
-        auto tile_info = [&](int tl, const uint8_t*& r0, const uint8_t*& r1, int& type) {
-            const int tile = tile0 + tl;
-            int pi = 0;
-            while (pi + 1 < a.n_parts && tile >= p.tile_start[pi + 1]) pi++;
-            const MatvecPart& P = a.part[pi];
-            const int row = (tile - p.tile_start[pi]) * 16 + g;
-            const int ra = min(row, P.n_out - 1), rb = min(row + 8, P.n_out - 1);
-            r0 = P.w + (size_t)ra * P.row_bytes;
-            r1 = P.w + (size_t)rb * P.row_bytes;
-            type = P.type;
-        };
-        auto load = [&](const uint8_t* r0, const uint8_t* r1, int type, int b, uint32_t (&w0)[kRaw],
-                        uint32_t (&w1)[kRaw]) {
-            if (kMode == 0 || (kMode == 2 && type == PICOATTN_WT_Q4_K)) {
-                load_q4k<kRaw>(r0 + (size_t)b * 144, t, w0);
-                load_q4k<kRaw>(r1 + (size_t)b * 144, t, w1);
-            } else if constexpr (kMode != 0) {
-                load_q6k<kRaw>(r0 + (size_t)b * 210, t, w0);
-                load_q6k<kRaw>(r1 + (size_t)b * 210, t, w1);
-            }
-        };
-        // the warp's (tile, super-block) steps: a step's words are loaded and
-        // used at once; the many warps of an SM (small register footprint) keep
-        // the loads in flight
-        const int steps = n_my * ns;
-        float acc0 = 0.f, acc1 = 0.f;
-        const uint8_t *r0, *r1;
-        int ty;
+    const int steps = n_my * ns;
+    // rows g and g + 8 of a tile (clamped to its matrix) and their type
+    auto tile_info = [&](int tl, const uint8_t*& r0, const uint8_t*& r1, int& type) {
+        const int tile = tile0 + tl;
+        int pi = 0;
+        while (pi + 1 < a.n_parts && tile >= p.tile_start[pi + 1]) pi++;
+        const MatvecPart& P = a.part[pi];
+        const int row = (tile - p.tile_start[pi]) * 16 + g;
+        const int ra = min(row, P.n_out - 1), rb = min(row + 8, P.n_out - 1);
+        r0 = P.w + (size_t)ra * P.row_bytes;
+        r1 = P.w + (size_t)rb * P.row_bytes;
+        type = P.type;
+    };
+    auto load = [&](const uint8_t* r0, const uint8_t* r1, int type, int b, uint32_t (&w0)[kRaw],
+                    uint32_t (&w1)[kRaw]) {
+        if (kMode == 0 || (kMode == 2 && type == PICOATTN_WT_Q4_K)) {
+            load_q4k<kRaw>(r0 + (size_t)b * 144, t, w0);
+            load_q4k<kRaw>(r1 + (size_t)b * 144, t, w1);
+        } else if constexpr (kMode != 0) {
+            load_q6k<kRaw>(r0 + (size_t)b * 210, t, w0);
+            load_q6k<kRaw>(r1 + (size_t)b * 210, t, w1);
+        }
+    };
+    // the warp's (tile, super-block) steps: a step's words are loaded and used
+    // at once, the many warps of an SM (small register footprint) keeping the
+    // loads in flight; the first step's words are requested before x is
+    // prepared
+    const uint8_t *r0 = nullptr, *r1 = nullptr;
+    int ty = 0;
+    uint32_t w0[kRaw], w1[kRaw];
+    if (steps > 0) {
         tile_info(0, r0, r1, ty);
-        int ctl = 0;
-        for (int st = 0; st < steps; st++) {
-            const int tl = st / ns, bi = st - tl * ns, b = b0 + bi;
+        load(r0, r1, ty, b0, w0, w1);
+    }
+    if (a.weights_ready) pdl_wait();
+    if (ns > 0) prep_x(a.x, b0, b1, bf_all + (size_t)b0 * 256, pw, xsum, dig, lane);
+    __syncwarp();
+    const uint32_t bmask = g < 4 ? 0xFFFFFFFFu : 0u;  // B column g: low half (k < 16) or high half
+    float acc0 = 0.f, acc1 = 0.f;
+    int ctl = 0;
+    for (int st = 0; st < steps; st++) {
+        const int tl = st / ns, bi = st - tl * ns, b = b0 + bi;
+        if (st > 0) {
             if (tl != ctl) tile_info(tl, r0, r1, ty), ctl = tl;
-            uint32_t w0[kRaw], w1[kRaw];
             load(r0, r1, ty, b, w0, w1);
-            const float r = pw[b] * ((t & 1) ? 65536.f : 1.f);
-            const uint32_t* bf = bf_all + (size_t)b * 256;
-            if (kMode == 0 || (kMode == 2 && ty == PICOATTN_WT_Q4_K))
-                sb_q4k<kRaw>(w0, w1, bf, bmask, r, xsum + 8 * b, t, lane, acc0, acc1);
-            else if constexpr (kMode != 0)
-                sb_q6k<kRaw>(w0, w1, bf, bmask, r, t, lane, acc0, acc1);
-            if (bi == ns - 1) {
-                acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-                acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
-                acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-                acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
-                if (t == 0) {
-                    partial[((size_t)tl * S + warp) * 16 + g] = acc0;
-                    partial[((size_t)tl * S + warp) * 16 + g + 8] = acc1;
-                }
-                acc0 = acc1 = 0.f;
+        }
+        const float r = pw[b] * ((t & 1) ? 65536.f : 1.f);
+        const uint32_t* bf = bf_all + (size_t)b * 256;
+        if (kMode == 0 || (kMode == 2 && ty == PICOATTN_WT_Q4_K))
+            sb_q4k<kRaw>(w0, w1, bf, bmask, r, xsum + 8 * b, t, lane, acc0, acc1);
+        else if constexpr (kMode != 0)
+            sb_q6k<kRaw>(w0, w1, bf, bmask, r, t, lane, acc0, acc1);
+        if (bi == ns - 1) {  // the tile's slice is done: the quad's four parts of each row
+            acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+            acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+            acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+            acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+            if (t == 0) {
+                partial[((size_t)tl * S + warp) * 16 + g] = acc0;
+                partial[((size_t)tl * S + warp) * 16 + g + 8] = acc1;
             }
+            acc0 = acc1 = 0.f;
         }
     }
     __syncthreads();
@@ -389,10 +395,7 @@ __global__ void __launch_bounds__(kMmMaxSlices * 32) matvec_mma_kernel(MmArgs p)
         const int row = (tile - p.tile_start[pi]) * 16 + rr;
         if (row >= P.n_out) continue;
         float y = 0.f;
-        for (int w = 0; w < S; w++) {
-            const int nsw = (w + 1) * nsb / S - w * nsb / S;
-            if (nsw > 0) y += partial[((size_t)tl * S + w) * 16 + rr];
-        }
+        for (int w = 0; w < S; w++) y += partial[((size_t)tl * S + w) * 16 + rr];
         if (P.bias) y = __fadd_rn(y, P.bias[row]);
         float* op = P.out + row;
         *op = a.accumulate ? __fadd_rn(*op, y) : y;

@@ -146,6 +146,10 @@ struct MatvecArgs {
     MatvecPart part[3];
     int n_parts, n_in, n_vec, rows_total, accumulate;
     const float* x;  // [n_vec][n_in], 16-byte aligned
+    // 1: no kernel ahead of this launch in the stream writes the weight
+    // matrices (a launch that follows one of this library's own kernels), so
+    // the tensor-core kernel may read them before the programmatic-launch wait
+    int weights_ready;
 };
 int weight_block_elems(int type);  // weights per block of a PICOATTN_WT_* type (0: unsupported)
 int weight_block_bytes(int type);
