@@ -1210,6 +1210,25 @@ def cpu_token_step() -> dict:
                       f"{per_layer * 1e3:.1f} ms per layer, x {p['n_layers']} layers; output matrix left out"}
 
 
+def profile_matvec(wtype: int, n_in: int, n_out: int) -> None:
+    """Three picoattn_matvec launches of one shape, each on its own copy of the
+    matrix (the copies together larger than L2), then exit."""
+    import torch
+    from picolm_qwen_b200 import abi
+    lib = abi.lib()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    nb = lib.picoattn_weight_bytes(wtype, n_in, n_out)
+    copies = max(3, -(-300_000_000 // max(nb, 1)))
+    ws = [random_blocks_dev(wtype, n_in, n_out, g, "cuda")[0] for _ in range(copies)]
+    x = torch.randn(1, n_in, generator=g, device="cuda")
+    out = torch.empty(1, n_out, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    for i in range(3):
+        abi.check(lib.picoattn_matvec(ws[i].data_ptr(), wtype, None, n_in, n_out, 1, x.data_ptr(), out.data_ptr(),
+                                      0, s), "picoattn_matvec")
+    torch.cuda.synchronize()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1225,9 +1244,15 @@ def main() -> None:
                     help="skip the whole-model token step leg (Qwen2.5-7B shape, Q4_K_M-style weights)")
     ap.add_argument("--no-small", action="store_true",
                     help="skip the small single-sequence legs (TinyLlama p=511, Qwen2.5-0.5B 4096)")
+    ap.add_argument("--profile-matvec", type=int, nargs=3, metavar=("TYPE", "N_IN", "N_OUT"),
+                    help="only launch picoattn_matvec three times on seeded random blocks of that shape (over "
+                         "weight copies larger than L2 together) and exit: the case the projection ncu captures use")
     ap.add_argument("--seqs", type=int, default=WORKLOAD["n_seqs"],
                     help="sequences per GPU (default 64 = the benchmark; smaller only for profiling)")
     args = ap.parse_args()
+    if args.profile_matvec:
+        profile_matvec(*args.profile_matvec)
+        return
     WORKLOAD["n_seqs"] = args.seqs
     if args.warmup < 3:
         args.warmup = 3

@@ -39,6 +39,9 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "device_common.cuh"
 #include "picoattn_internal.h"
@@ -247,9 +250,16 @@ __device__ __forceinline__ void sb_q6k(const uint32_t (&w0)[kRaw], const uint32_
 __device__ __forceinline__ void prep_x(const float* x, int b0, int b1, uint32_t* bf, float* pw, float* xsum,
                                        uint32_t* dig, int lane) {
     const int g = lane >> 2, t = lane & 3;
+    // the slice's x lands in its B-fragment area first (1 KB per super-block
+    // either way), every piece in flight at once
+    for (int i = lane; i < (b1 - b0) * 64; i += 32) cp_async16(bf + 4 * i, x + 256 * b0 + 4 * i);
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncwarp();
     for (int b = b0; b < b1; b++) {
-        const float4 v0 = __ldg(reinterpret_cast<const float4*>(x + 256 * b + 8 * lane));
-        const float4 v1 = __ldg(reinterpret_cast<const float4*>(x + 256 * b + 8 * lane + 4));
+        const float* xb = reinterpret_cast<const float*>(bf + (b - b0) * 256);
+        const float4 v0 = *reinterpret_cast<const float4*>(xb + 8 * lane);
+        const float4 v1 = *reinterpret_cast<const float4*>(xb + 8 * lane + 4);
         const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
         uint32_t mx = 0;
 #pragma unroll
@@ -299,9 +309,10 @@ __device__ __forceinline__ void prep_x(const float* x, int b0, int b1, uint32_t*
     }
 }
 
-// kMode: 0 every matrix Q4_K, 1 every matrix Q6_K, 2 both (chosen per tile)
+// kMode: 0 every matrix Q4_K, 1 every matrix Q6_K, 2 both (chosen per tile).
+// The single-format kernels fit 64 registers, so two 16-warp blocks share an SM.
 template <int kMode>
-__global__ void __launch_bounds__(kMmMaxSlices * 32) matvec_mma_kernel(MmArgs p) {
+__global__ void __launch_bounds__(kMmMaxSlices * 32, kMode == 2 ? 1 : 2) matvec_mma_kernel(MmArgs p) {
     constexpr int kRaw = kMode == 0 ? kRawQ4K : kRawQ6K;
     extern __shared__ __align__(16) uint8_t mm_smem[];
     const MatvecArgs& a = p.a;
@@ -425,24 +436,10 @@ cudaError_t launch_matvec_mma(const MatvecArgs& a, cudaStream_t stream) {
     }
     p.tile_start[a.n_parts] = tiles;
     p.n_tiles = tiles;
-    // slices (warps per row tile): with few tiles, up to 16 so that every SM
-    // holds enough warps whose loads are all in flight at once; with many,
-    // 4..8 (a block's x preparation is shared by more tiles).  Among those the
-    // most whose longest slice is within 15 % of the mean (warps of a block
-    // finish together), else the most even.
-    const int sms = device_sm_count();
-    const int s_hi = std::min(p.nsb, tiles <= 4 * sms ? kMmMaxSlices : 8);
-    const int s_lo = std::min(s_hi, tiles <= 4 * sms ? 8 : 4);
-    p.slices = s_hi;
-    double best = 1e9;
-    for (int sl = s_hi; sl >= s_lo; sl--) {
-        const double waste = (double)((p.nsb + sl - 1) / sl) * sl / p.nsb;
-        if (waste <= 1.15) {
-            p.slices = sl;
-            break;
-        }
-        if (waste < best - 1e-9) best = waste, p.slices = sl;
-    }
+    int n4 = 0;
+    for (int i = 0; i < a.n_parts; i++) n4 += a.part[i].type == PICOATTN_WT_Q4_K;
+    const void* kern = n4 == a.n_parts ? (const void*)matvec_mma_kernel<0>
+                                       : (n4 == 0 ? (const void*)matvec_mma_kernel<1> : (const void*)matvec_mma_kernel<2>);
     static PerDeviceOnce setup;
     const cudaError_t se = setup.run([] {
         for (auto k : {matvec_mma_kernel<0>, matvec_mma_kernel<1>, matvec_mma_kernel<2>}) {
@@ -452,22 +449,59 @@ cudaError_t launch_matvec_mma(const MatvecArgs& a, cudaStream_t stream) {
         return cudaSuccess;
     });
     if (se != cudaSuccess) return se;
-    int n4 = 0;
-    for (int i = 0; i < a.n_parts; i++) n4 += a.part[i].type == PICOATTN_WT_Q4_K;
-    const void* kern = n4 == a.n_parts ? (const void*)matvec_mma_kernel<0>
-                                       : (n4 == 0 ? (const void*)matvec_mma_kernel<1> : (const void*)matvec_mma_kernel<2>);
-    auto smem_for = [&](int tpb) {
-        return (size_t)p.nsb * 256 * 4 + (size_t)p.nsb * 4 + (size_t)p.nsb * 32 + (size_t)tpb * p.slices * 64 +
-               (size_t)p.slices * 1024;
+    auto smem_for = [&](int sl, int tpb) {
+        return (size_t)p.nsb * 256 * 4 + (size_t)sl * 1024 + (size_t)tpb * sl * 64 + (size_t)p.nsb * 32 +
+               (size_t)p.nsb * 4;
     };
-    if (smem_for(1) > 220 * 1024) return cudaErrorNotSupported;
-    // one wave: as many blocks as fit on the SMs at once, the tiles dealt evenly
-    int per_sm = 0;
-    cudaError_t oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 32 * p.slices, smem_for(kMmMaxTiles));
-    if (oe != cudaSuccess) return oe;
-    const long long slots = (long long)std::max(1, per_sm) * sms;
-    p.tiles_per_block = (int)std::max(1LL, std::min<long long>(kMmMaxTiles, (tiles + slots - 1) / slots));
-    const size_t smem = smem_for(p.tiles_per_block);
+    // the launch shape: S warps per row tile (each a contiguous slice of the
+    // super-blocks; at most 15 % longer than the mean slice, or the most even),
+    // T tiles per block, one wave of the blocks that fit.  Among the slice
+    // counts, the one with the fewest steps per warp (T x slice length),
+    // counting SMs left idle as lost time; the larger on ties.
+    const int sms = device_sm_count();
+    int dev = 0;
+    cudaError_t de = cudaGetDevice(&dev);
+    if (de != cudaSuccess) return de;
+    const int mode = n4 == a.n_parts ? 0 : (n4 == 0 ? 1 : 2);
+    const long long key = (((long long)dev * 4 + mode) * 4096 + p.nsb) * (1LL << 24) + tiles;
+    static std::mutex shape_mu;
+    static std::map<long long, std::pair<int, int>> shapes;  // key -> (slices, tiles per block)
+    {
+        std::lock_guard<std::mutex> lk(shape_mu);
+        const auto it = shapes.find(key);
+        if (it != shapes.end()) {
+            p.slices = it->second.first;
+            p.tiles_per_block = it->second.second;
+        }
+    }
+    double best_cost = 1e30;
+    int best_s = p.slices, best_t = p.tiles_per_block;
+    for (int sl = best_s ? 0 : std::min(p.nsb, kMmMaxSlices); sl >= 1; sl--) {
+        const int len = (p.nsb + sl - 1) / sl;
+        if ((double)len * sl / p.nsb > 1.15 && sl != 1 && sl != std::min(p.nsb, kMmMaxSlices)) continue;
+        int per_sm = 0;
+        cudaError_t oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 32 * sl, smem_for(sl, 1));
+        if (oe != cudaSuccess) return oe;
+        if (per_sm < 1) continue;
+        const long long slots = (long long)per_sm * sms;
+        int tpb = (int)std::min<long long>(kMmMaxTiles, (tiles + slots - 1) / slots);
+        // the slice sums of T tiles must fit beside the rest
+        while (tpb > 1 && smem_for(sl, tpb) > 220 * 1024) tpb--;
+        const long long blocks = (tiles + tpb - 1) / tpb;
+        const long long waves = (blocks + slots - 1) / slots;
+        const double busy = std::min(1.0, (double)blocks / sms);
+        const double cost = (double)tpb * len * waves / busy;
+        if (cost < best_cost - 1e-9) best_cost = cost, best_s = sl, best_t = tpb;
+        if (sl <= 4 && best_s) break;
+    }
+    if (best_s == 0 || smem_for(best_s, best_t) > 220 * 1024) return cudaErrorNotSupported;
+    p.slices = best_s;
+    p.tiles_per_block = best_t;
+    {
+        std::lock_guard<std::mutex> lk(shape_mu);
+        shapes[key] = {best_s, best_t};
+    }
+    const size_t smem = smem_for(best_s, best_t);
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)((tiles + p.tiles_per_block - 1) / p.tiles_per_block));
     cfg.blockDim = dim3((unsigned)(32 * p.slices));
