@@ -1229,6 +1229,44 @@ def profile_matvec(wtype: int, n_in: int, n_out: int) -> None:
     torch.cuda.synchronize()
 
 
+def profile_longctx(rows: int) -> None:
+    """The long-context leg's call (all stages, one sequence at position
+    rows - 1) on layers 0, 1, 2 of a 3-layer cache of `rows` rows, then exit."""
+    import torch
+    from picolm_qwen_b200 import abi
+    from picolm_qwen_b200.runtime import stream_handle
+    p = LONGCTX
+    hq, hkv, hd = p["n_heads"], p["n_kv_heads"], p["head_dim"]
+    kvd, qd, L = hkv * hd, hq * hd, 3
+    cfg = abi.Config.make(L, hq, hkv, hd, rows, p["rope_base"], abi.ROPE_NEOX)
+    lib = abi.lib()
+    cfgp = C.byref(cfg)
+    g = torch.Generator(device="cuda").manual_seed(3000)
+    kc = (torch.randn((L, rows, kvd), generator=g, device="cuda") * 0.5).half().view(torch.int16)
+    vc = (torch.randn((L, rows, kvd), generator=g, device="cuda") * 0.5).half().view(torch.int16)
+    q = torch.randn((L, qd), generator=g, device="cuda")
+    k = torch.randn((L, kvd), generator=g, device="cuda")
+    v = torch.randn((L, kvd), generator=g, device="cuda")
+    out = torch.empty((L, qd), device="cuda")
+    cos = np.empty(rows * hd // 2, np.float32)
+    sin = np.empty_like(cos)
+    assert lib.picoattn_rope_table(cfgp, cos.ctypes.data, sin.ctypes.data) == 0
+    d_cos, d_sin = torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda()
+    kp = torch.tensor([kc.data_ptr()], dtype=torch.int64, device="cuda")
+    vp = torch.tensor([vc.data_ptr()], dtype=torch.int64, device="cuda")
+    pos = torch.tensor([rows - 1], dtype=torch.int32, device="cuda")
+    ws_n = lib.picoattn_decode_workspace_size(cfgp, 1, rows)
+    ws = torch.zeros(ws_n, dtype=torch.uint8, device="cuda")
+    sh = stream_handle()
+    assert lib.picoattn_workspace_init(ws.data_ptr(), ws_n, sh) == 0
+    for l in range(L):
+        abi.check(lib.picoattn_decode_staged(cfgp, l, 1, rows, q[l].data_ptr(), k[l].data_ptr(), v[l].data_ptr(),
+                                             None, None, d_cos.data_ptr(), d_sin.data_ptr(), kp.data_ptr(),
+                                             vp.data_ptr(), pos.data_ptr(), out[l].data_ptr(), ws.data_ptr(), ws_n,
+                                             sh, abi.STAGE_ALL), "picoattn_decode_staged")
+    torch.cuda.synchronize()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1247,11 +1285,17 @@ def main() -> None:
     ap.add_argument("--profile-matvec", type=int, nargs=3, metavar=("TYPE", "N_IN", "N_OUT"),
                     help="only launch picoattn_matvec three times on seeded random blocks of that shape (over "
                          "weight copies larger than L2 together) and exit: the case the projection ncu captures use")
+    ap.add_argument("--profile-longctx", type=int, metavar="ROWS",
+                    help="only run the long-context call (Qwen2.5-32B heads, one sequence) on three layers of ROWS "
+                         "cached rows each and exit: the case the long-context ncu capture uses")
     ap.add_argument("--seqs", type=int, default=WORKLOAD["n_seqs"],
                     help="sequences per GPU (default 64 = the benchmark; smaller only for profiling)")
     args = ap.parse_args()
     if args.profile_matvec:
         profile_matvec(*args.profile_matvec)
+        return
+    if args.profile_longctx:
+        profile_longctx(args.profile_longctx)
         return
     WORKLOAD["n_seqs"] = args.seqs
     if args.warmup < 3:
