@@ -816,8 +816,16 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
     // The merge kernel may launch now: it waits for this grid to complete.
     pdl_trigger();
     const uint32_t row_bytes = (uint32_t)a.kvd * 2u;
-    const uint32_t stride = row_bytes + 16u;  // padded rows: ldmatrix is conflict-free
-    const uint32_t tile_bytes = (uint32_t)T * stride;
+    // A tile of T rows is 8 groups of Gr = T/8 consecutive rows, each group
+    // padded by 16 bytes; an ldmatrix 8x8 matrix takes one row from each group
+    // (rows Gr*q + u, q = 0..7), whose 16-byte pieces then fall in 8 different
+    // bank quads (row_bytes is a multiple of 128), so it is conflict-free.
+    // Key order within a tile: 16-key group rg holds u = 2rg (keys 0-7 of the
+    // MMA) and u = 2rg + 1 (keys 8-15), q = the key's position in each half.
+    const int Gr = T / 8;
+    const uint32_t gstride = (uint32_t)Gr * row_bytes + 16u;
+    const uint32_t stride = row_bytes + 16u;             // the tile's space: T padded rows
+    const uint32_t tile_bytes = (uint32_t)T * stride;  // >= 8 * gstride
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + a.stages;
     long long* s_prefix = reinterpret_cast<long long*>(smem + 48);
@@ -944,13 +952,30 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
                 if (lane == 0) mbar_arrive_expect_tx(&full[s], 2u * (uint32_t)T * row_bytes);
                 __syncwarp();
                 uint8_t* kdst = tiles + (size_t)s * 2u * tile_bytes;
-                // Rows past the end of the segment repeat its last row: finite data
-                // whose scores are masked, so no stale shared memory is ever used.
-                for (int i = lane; i < 2 * T; i += 32) {
-                    const int kv = i >= T, r = kv ? i - T : i;
-                    const int src_row = row0 + min(r, valid - 1);
-                    const uint16_t* src = (kv ? vslab : kslab) + (size_t)src_row * a.kvd;
-                    bulk_g2s(kdst + kv * tile_bytes + (uint32_t)r * stride, src, row_bytes, &full[s]);
+                // The tile's rows in 8 groups of Gr = T/8 consecutive rows, one bulk
+                // copy per group (a copy's cost is per copy, not per byte).  A group
+                // may reach past the segment into rows that are final and finite
+                // (other slices' rows; their scores are masked) but never to a row
+                // that is unwritten or still being written: the sequence's new row
+                // only after this CTA waited for it (rows_ok).  Such a group, and
+                // rows past the segment end, go row by row, rows past the end
+                // repeating its last row: finite data, masked, so no stale shared
+                // memory is ever used.
+                const int rows_ok = (dep_done || has_new) ? seq_rows : seq_rows - 1;
+                for (int i = lane; i < 16; i += 32) {
+                    const int kv = i >> 3, q = i & 7;
+                    const uint16_t* base = kv ? vslab : kslab;
+                    uint8_t* dst = kdst + kv * tile_bytes + (uint32_t)q * gstride;
+                    const int g0 = row0 + Gr * q;
+                    if (g0 + Gr <= rows_ok) {
+                        bulk_g2s(dst, base + (size_t)g0 * a.kvd, (uint32_t)Gr * row_bytes, &full[s]);
+                    } else {
+                        for (int u = 0; u < Gr; u++) {
+                            const int src_row = row0 + min(Gr * q + u, valid - 1);
+                            bulk_g2s(dst + (uint32_t)u * row_bytes, base + (size_t)src_row * a.kvd, row_bytes,
+                                     &full[s]);
+                        }
+                    }
                 }
             }
         });
@@ -961,8 +986,13 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
     const int kvh = warp / W, wi = warp % W;
     const int gid = lane >> 2, tig = lane & 3;
     const int G_q = a.g;
-    const uint32_t k_lane = (uint32_t)((lane & 7) + ((lane >> 4) << 3)) * stride + (uint32_t)(((lane >> 3) & 1) * 16);
-    const uint32_t v_lane = (uint32_t)((lane & 7) + (((lane >> 3) & 1) << 3)) * stride + (uint32_t)((lane >> 4) * 16);
+    // ldmatrix row addresses (matrix lane >> 3, row lane & 7 = group q): K
+    // matrices (keys 0-7 | dims 0-7, keys 0-7 | dims 8-15, keys 8-15 | ...),
+    // V transposed (keys 0-7 | dims 0-7, keys 8-15 | dims 0-7, ...)
+    const uint32_t k_lane = (uint32_t)(lane & 7) * gstride + (uint32_t)(lane >> 4) * row_bytes +
+                            (uint32_t)(((lane >> 3) & 1) * 16);
+    const uint32_t v_lane = (uint32_t)(lane & 7) * gstride + (uint32_t)((lane >> 3) & 1) * row_bytes +
+                            (uint32_t)((lane >> 4) * 16);
     const uint32_t head_off = (uint32_t)kvh * HD * 2u;
     const uint32_t tiles_u32 = smem_u32(tiles);
     float* sq = qstage + warp * 4 * HD;
@@ -998,8 +1028,8 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
             const int valid = min(T, r1 - row0);
             const uint32_t kbase = tiles_u32 + (uint32_t)s * 2u * tile_bytes + head_off;
             const uint32_t vbase = kbase + tile_bytes;
-            for (int rg = wi; rg * 16 < valid; rg += W) {
-                const uint32_t goff = (uint32_t)(rg * 16) * stride;
+            for (int rg = wi; rg * 16 < T && 2 * rg < valid; rg += W) {
+                const uint32_t goff = (uint32_t)(2 * rg) * row_bytes;
                 float sc[2][4];
 #pragma unroll
                 for (int j = 0; j < 2; j++) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
@@ -1010,13 +1040,13 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
                     mma_16816(sc[0], qa[kk], bk[0], bk[1]);
                     mma_16816(sc[1], qa[kk], bk[2], bk[3]);
                 }
-                const int nvalid = valid - rg * 16;
-                if (nvalid < 16) {
+                // key (S column 2tig + (e & 1) of half j) = row Gr * column + 2rg + j
+                if (Gr * 7 + 2 * rg + 1 >= valid) {
 #pragma unroll
                     for (int j = 0; j < 2; j++)
 #pragma unroll
                         for (int e = 0; e < 4; e++)
-                            if (8 * j + 2 * tig + (e & 1) >= nvalid) sc[j][e] = -INFINITY;
+                            if (Gr * (2 * tig + (e & 1)) + 2 * rg + j >= valid) sc[j][e] = -INFINITY;
                 }
                 float mx0 = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
                 float mx1 = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
