@@ -102,17 +102,30 @@ __device__ __forceinline__ uint32_t q6_signed(uint32_t q) {
 
 // The words of one super-block of one row that a lane needs.
 //   Q4_K: w[0..3] the block's 16-byte head (d, dmin, 12 scale bytes);
-//         w[4+m] the code bytes of mma m (qs bytes 32(m/2) + 16(m%2) + 4t..+3)
+//         w[4+m] the code bytes of mma m (qs bytes 32(m/2) + 16(m%2) + 4t..+3, or
+//         32(m/2) + 8t + 4(m%2)..+3 in launches of Q4_K only)
 //   Q6_K: w[3(2c+h)+0..2] = ql[64c+16h+4t], ql[64c+32+16h+4t], qh[32c+16h+4t];
 //         w[12..15] the 16 scale bytes; w[16] d (low half)
 constexpr int kRawQ4K = 12, kRawQ6K = 17;
 
-template <int kRaw>
+// kPairs (launches of Q4_K only): lane t takes bytes 8t..8t+7 of each 32-byte
+// group (mma 2jg + h uses bytes 8t + 4h..+3), one 8-byte load per group, so an
+// instruction's 8 rows x 32 bytes are whole sectors.  Otherwise the layout
+// Q6_K shares: bytes 16h + 4t..+3 of the group.
+template <bool kPairs, int kRaw>
 __device__ __forceinline__ void load_q4k(const uint8_t* blk, int t, uint32_t (&w)[kRaw]) {
     const uint4 h = __ldg(reinterpret_cast<const uint4*>(blk));
     w[0] = h.x, w[1] = h.y, w[2] = h.z, w[3] = h.w;
+    if constexpr (kPairs) {
 #pragma unroll
-    for (int m = 0; m < 8; m++) w[4 + m] = ldg32(blk + 16 + 32 * (m >> 1) + 16 * (m & 1) + 4 * t);
+        for (int jg = 0; jg < 4; jg++) {
+            const uint2 v = __ldg(reinterpret_cast<const uint2*>(blk + 16 + 32 * jg + 8 * t));
+            w[4 + 2 * jg] = v.x, w[5 + 2 * jg] = v.y;
+        }
+    } else {
+#pragma unroll
+        for (int m = 0; m < 8; m++) w[4 + m] = ldg32(blk + 16 + 32 * (m >> 1) + 16 * (m & 1) + 4 * t);
+    }
 }
 
 template <bool kMis, int kRaw>
@@ -247,6 +260,7 @@ __device__ __forceinline__ void sb_q6k(const uint32_t (&w0)[kRaw], const uint32_
 // super-block), scales (pw: 2^(E_b-29), a power of two down to 2^-149; 0 for
 // blocks whose largest magnitude is below 2^-120, NaN for non-finite x) and
 // group sums (xsum, 8 per super-block).  dig: 256 words of scratch.
+template <bool kPairs>
 __device__ __forceinline__ void prep_x(const float* x, int b0, int b1, uint32_t* bf, float* pw, float* xsum,
                                        uint32_t* dig, int lane) {
     const int g = lane >> 2, t = lane & 3;
@@ -295,12 +309,14 @@ __device__ __forceinline__ void prep_x(const float* x, int b0, int b1, uint32_t*
         *reinterpret_cast<uint4*>(dig + 8 * lane) = make_uint4(dw[0], dw[1], dw[2], dw[3]);
         *reinterpret_cast<uint4*>(dig + 8 * lane + 4) = make_uint4(dw[4], dw[5], dw[6], dw[7]);
         __syncwarp();
-        // lane (g, t), mma m: digit g%4 of x at 64(m/2) + 16(m%2) + 32(g/4) + 4t + 0..3
+        // lane (g, t), mma m: digit g%4 of x at 64(m/2) + 32(g/4) + 16(m%2) + 4t + 0..3
+        // (kPairs: 64(m/2) + 32(g/4) + 8t + 4(m%2) + 0..3), the weights lane t
+        // of the A fragment holds for k = 4t..4t+3 (g < 4) or 16 + 4t.. (g >= 4)
         const uint32_t j = (uint32_t)(g & 3);
         const uint32_t sel = j | ((4u + j) << 4);
 #pragma unroll
         for (int m = 0; m < 8; m++) {
-            const int p = 64 * (m >> 1) + 16 * (m & 1) + 32 * (g >> 2) + 4 * t;
+            const int p = 64 * (m >> 1) + 32 * (g >> 2) + (kPairs ? 8 * t + 4 * (m & 1) : 16 * (m & 1) + 4 * t);
             const uint4 q = *reinterpret_cast<const uint4*>(dig + p);
             const uint32_t lo = __byte_perm(q.x, q.y, sel), hi = __byte_perm(q.z, q.w, sel);
             bf[(b - b0) * 256 + m * 32 + lane] = __byte_perm(lo, hi, 0x5410);
@@ -348,8 +364,8 @@ __global__ void __launch_bounds__(kMmMaxSlices * 32, kMode == 2 ? 1 : 2) matvec_
     auto load = [&](const uint8_t* r0, const uint8_t* r1, int type, int b, uint32_t (&w0)[kRaw],
                     uint32_t (&w1)[kRaw]) {
         if (kMode == 0 || (kMode == 2 && type == PICOATTN_WT_Q4_K)) {
-            load_q4k<kRaw>(r0 + (size_t)b * 144, t, w0);
-            load_q4k<kRaw>(r1 + (size_t)b * 144, t, w1);
+            load_q4k<kMode == 0, kRaw>(r0 + (size_t)b * 144, t, w0);
+            load_q4k<kMode == 0, kRaw>(r1 + (size_t)b * 144, t, w1);
         } else if constexpr (kMode != 0) {
             load_q6k<kRaw>(r0 + (size_t)b * 210, t, w0);
             load_q6k<kRaw>(r1 + (size_t)b * 210, t, w1);
@@ -367,7 +383,7 @@ __global__ void __launch_bounds__(kMmMaxSlices * 32, kMode == 2 ? 1 : 2) matvec_
         load(r0, r1, ty, b0, w0, w1);
     }
     if (a.weights_ready) pdl_wait();
-    if (ns > 0) prep_x(a.x, b0, b1, bf_all + (size_t)b0 * 256, pw, xsum, dig, lane);
+    if (ns > 0) prep_x<kMode == 0>(a.x, b0, b1, bf_all + (size_t)b0 * 256, pw, xsum, dig, lane);
     __syncwarp();
     const uint32_t bmask = g < 4 ? 0xFFFFFFFFu : 0u;  // B column g: low half (k < 16) or high half
     float acc0 = 0.f, acc1 = 0.f;
