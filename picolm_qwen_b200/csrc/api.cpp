@@ -339,13 +339,31 @@ size_t picoattn_decode_layer_workspace_size(const picoattn_config_t* cfg, int32_
 
 namespace {
 
-// picoattn_decode_layer; qkv_after_own: the launch before it is this
-// library's own (its weights may be read before that kernel finishes)
+// A launch of the tensor-core mat-vec with x formed on the fly (fused norm or
+// SwiGLU, MatvecArgs.x_norm_w / x_up); when that kernel does not take the
+// launch, the separate kernel first (`unfused`), then the plain mat-vec.
+template <class Unfused>
+cudaError_t matvec_fused(MatvecArgs a, cudaStream_t s, Unfused&& unfused) {
+    const cudaError_t e = launch_matvec_mma(a, s);
+    if (e != cudaErrorNotSupported) return e;
+    const float* x = nullptr;
+    const cudaError_t u = unfused(&x);
+    if (u != cudaSuccess) return u;
+    a.x = x;
+    a.x_norm_w = a.x_up = nullptr;
+    return launch_matvec(a, s);
+}
+
+// picoattn_decode_layer.  qkv_after_own: the launch before it is this
+// library's own (its weights may be read before that kernel finishes).
+// attn_norm_w: xb is the raw residual, normalised inside the projection
+// launch (or by a norm kernel into xb_scratch when that cannot be).
 int32_t decode_layer_impl(const picoattn_config_t* cfg, int32_t layer, int32_t dim, int32_t n_seqs, int32_t max_ctx,
                           const float* xb, const picoattn_layer_weights_t* wt, const float* q_norm_w,
                           const float* k_norm_w, const float* rope_cos, const float* rope_sin,
                           uint16_t* const* k_cache, uint16_t* const* v_cache, const int32_t* pos, float* x,
-                          void* workspace, size_t workspace_bytes, picoattn_stream_t stream, bool qkv_after_own) {
+                          void* workspace, size_t workspace_bytes, picoattn_stream_t stream, bool qkv_after_own,
+                          const float* attn_norm_w = nullptr, float* xb_scratch = nullptr) {
     int32_t st = picoattn_config_check(cfg);
     if (st != PICOATTN_OK) return st;
     if (!wt || !xb || !x || !k_cache || !v_cache || !pos || !workspace || dim <= 0 || n_seqs <= 0)
@@ -379,7 +397,15 @@ int32_t decode_layer_impl(const picoattn_config_t* cfg, int32_t layer, int32_t d
     qkv.rows_total = qd + 2 * kvd;
     qkv.x = xb;
     qkv.weights_ready = qkv_after_own ? 1 : 0;
-    st = cuda_status(launch_matvec(qkv, s));
+    if (attn_norm_w) {
+        qkv.x_norm_w = attn_norm_w;
+        st = cuda_status(matvec_fused(qkv, s, [&](const float** xo) {
+            *xo = xb_scratch;
+            return launch_rmsnorm(xb, attn_norm_w, xb_scratch, dim, n_seqs, s);
+        }));
+    } else {
+        st = cuda_status(launch_matvec(qkv, s));
+    }
     if (st != PICOATTN_OK) return st;
     st = decode_common(cfg, layer, n_seqs, max_ctx, q, k, v, q_norm_w, k_norm_w, rope_cos, rope_sin, k_cache,
                        v_cache, nullptr, nullptr, pos, 0, attn, workspace, l.q, s, PICOATTN_STAGE_ALL);
@@ -423,8 +449,13 @@ int32_t picoattn_rmsnorm(const float* x, const float* weight, float* out, int32_
     return cuda_status(launch_rmsnorm(x, weight, out, dim, n_vec, (cudaStream_t)stream));
 }
 
-int32_t picoattn_ffn(const picoattn_ffn_weights_t* w, const float* ffn_norm_w, int32_t dim, int32_t n_ffn,
-                     int32_t n_vec, float* x, void* workspace, size_t workspace_bytes, picoattn_stream_t stream) {
+}  // extern "C"
+
+namespace {
+
+// picoattn_ffn; after_own: the launch before it is this library's own
+int32_t ffn_impl(const picoattn_ffn_weights_t* w, const float* ffn_norm_w, int32_t dim, int32_t n_ffn, int32_t n_vec,
+                 float* x, void* workspace, size_t workspace_bytes, picoattn_stream_t stream, bool after_own) {
     if (!w || !ffn_norm_w || !x || !workspace || dim <= 0 || n_ffn <= 0 || n_vec <= 0) return PICOATTN_EINVAL;
     if (!aligned16(x) || !aligned16(workspace) || !aligned16(ffn_norm_w)) return PICOATTN_EINVAL;
     for (int32_t t : {w->gate_type, w->up_type, w->down_type})
@@ -444,26 +475,41 @@ int32_t picoattn_ffn(const picoattn_ffn_weights_t* w, const float* ffn_norm_w, i
     int32_t st = device_ok();
     if (st != PICOATTN_OK) return st;
     const cudaStream_t s = (cudaStream_t)stream;
-    st = cuda_status(launch_rmsnorm(x, ffn_norm_w, xb, dim, n_vec, s));
-    if (st != PICOATTN_OK) return st;
+    // norm, gate and up in one launch when the tensor-core kernel takes it
     gu.n_parts = 2;
     gu.n_in = dim;
     gu.n_vec = n_vec;
     gu.rows_total = 2 * n_ffn;
-    gu.x = xb;
-    gu.weights_ready = 1;  // after the norm kernel
-    st = cuda_status(launch_matvec(gu, s));
+    gu.x = x;
+    gu.x_norm_w = ffn_norm_w;
+    gu.weights_ready = after_own ? 1 : 0;
+    st = cuda_status(matvec_fused(gu, s, [&](const float** xo) {
+        *xo = xb;
+        return launch_rmsnorm(x, ffn_norm_w, xb, dim, n_vec, s);
+    }));
     if (st != PICOATTN_OK) return st;
-    st = cuda_status(launch_silu_mul(gate, up, (size_t)n_vec * n_ffn, s));
-    if (st != PICOATTN_OK) return st;
+    // SwiGLU and the down projection in one launch likewise
     dn.n_parts = 1;
     dn.n_in = n_ffn;
     dn.n_vec = n_vec;
     dn.rows_total = dim;
     dn.accumulate = 1;
     dn.x = gate;
-    dn.weights_ready = 1;
-    return cuda_status(launch_matvec(dn, s));
+    dn.x_up = up;
+    dn.weights_ready = 1;  // after the gate/up launch
+    return cuda_status(matvec_fused(dn, s, [&](const float** xo) {
+        *xo = gate;
+        return launch_silu_mul(gate, up, (size_t)n_vec * n_ffn, s);
+    }));
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t picoattn_ffn(const picoattn_ffn_weights_t* w, const float* ffn_norm_w, int32_t dim, int32_t n_ffn,
+                     int32_t n_vec, float* x, void* workspace, size_t workspace_bytes, picoattn_stream_t stream) {
+    return ffn_impl(w, ffn_norm_w, dim, n_ffn, n_vec, x, workspace, workspace_bytes, stream, false);
 }
 
 size_t picoattn_logits_workspace_size(int32_t dim, int32_t n_vec) {
@@ -486,15 +532,16 @@ int32_t picoattn_logits(const float* x, const float* output_norm_w, const void* 
     int32_t st = device_ok();
     if (st != PICOATTN_OK) return st;
     const cudaStream_t s = (cudaStream_t)stream;
-    st = cuda_status(launch_rmsnorm(x, output_norm_w, xb, dim, n_vec, s));
-    if (st != PICOATTN_OK) return st;
     a.n_parts = 1;
     a.n_in = dim;
     a.n_vec = n_vec;
     a.rows_total = vocab;
-    a.x = xb;
-    a.weights_ready = 1;
-    return cuda_status(launch_matvec(a, s));
+    a.x = x;
+    a.x_norm_w = output_norm_w;  // the final norm inside the launch when it can be
+    return cuda_status(matvec_fused(a, s, [&](const float** xo) {
+        *xo = xb;
+        return launch_rmsnorm(x, output_norm_w, xb, dim, n_vec, s);
+    }));
 }
 
 // Workspace of picoattn_decode_block: the decode-layer workspace first (its
@@ -524,13 +571,13 @@ int32_t picoattn_decode_block(const picoattn_config_t* cfg, int32_t layer, int32
     uint8_t* base = static_cast<uint8_t*>(workspace);
     float* xb = reinterpret_cast<float*>(base + align_up(l, 256));
     uint8_t* ffn_ws = base + align_up(l, 256) + align_up((size_t)n_seqs * dim * 4, 256);
-    int32_t st = picoattn_rmsnorm(x, attn_norm_w, xb, dim, n_seqs, stream);
+    // the attention norm inside the q/k/v launch (into xb only when that
+    // launch cannot take it), then the FFN after this call's own kernels
+    int32_t st = decode_layer_impl(cfg, layer, dim, n_seqs, max_ctx, x, attn_weights, q_norm_w, k_norm_w, rope_cos,
+                                   rope_sin, k_cache, v_cache, pos, x, workspace, l, stream, false, attn_norm_w, xb);
     if (st != PICOATTN_OK) return st;
-    st = decode_layer_impl(cfg, layer, dim, n_seqs, max_ctx, xb, attn_weights, q_norm_w, k_norm_w, rope_cos,
-                           rope_sin, k_cache, v_cache, pos, x, workspace, l, stream, true);
-    if (st != PICOATTN_OK) return st;
-    return picoattn_ffn(ffn_weights, ffn_norm_w, dim, n_ffn, n_seqs, x, ffn_ws,
-                        picoattn_ffn_workspace_size(dim, n_ffn, n_seqs), stream);
+    return ffn_impl(ffn_weights, ffn_norm_w, dim, n_ffn, n_seqs, x, ffn_ws,
+                    picoattn_ffn_workspace_size(dim, n_ffn, n_seqs), stream, true);
 }
 
 }  // extern "C"

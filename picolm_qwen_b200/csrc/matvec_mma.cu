@@ -262,7 +262,7 @@ __device__ __forceinline__ void sb_q6k(const uint32_t (&w0)[kRaw], const uint32_
 // group sums (xsum, 8 per super-block).  dig: 256 words of scratch.
 template <bool kPairs>
 __device__ __forceinline__ void prep_x(const float* x, int b0, int b1, uint32_t* bf, float* pw, float* xsum,
-                                       uint32_t* dig, int lane) {
+                                       uint32_t* dig, int lane, const float* norm_w, float norm_s, const float* up) {
     const int g = lane >> 2, t = lane & 3;
     // the slice's x lands in its B-fragment area first (1 KB per super-block
     // either way), every piece in flight at once
@@ -274,7 +274,23 @@ __device__ __forceinline__ void prep_x(const float* x, int b0, int b1, uint32_t*
         const float* xb = reinterpret_cast<const float*>(bf + (b - b0) * 256);
         const float4 v0 = *reinterpret_cast<const float4*>(xb + 8 * lane);
         const float4 v1 = *reinterpret_cast<const float4*>(xb + 8 * lane + 4);
-        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        if (norm_w) {  // (x * s) * w, the norm's two roundings
+            const float4 w0 = __ldg(reinterpret_cast<const float4*>(norm_w + 256 * b + 8 * lane));
+            const float4 w1 = __ldg(reinterpret_cast<const float4*>(norm_w + 256 * b + 8 * lane + 4));
+            const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int i = 0; i < 8; i++) v[i] = __fmul_rn(__fmul_rn(v[i], norm_s), w[i]);
+        } else if (up) {  // silu(g) * up: the reciprocal of 1 + e^-g, times g, times up
+            const float4 u0 = __ldg(reinterpret_cast<const float4*>(up + 256 * b + 8 * lane));
+            const float4 u1 = __ldg(reinterpret_cast<const float4*>(up + 256 * b + 8 * lane + 4));
+            const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v[i])));
+                v[i] = __fmul_rn(__fmul_rn(v[i], sig), u[i]);
+            }
+        }
         uint32_t mx = 0;
 #pragma unroll
         for (int i = 0; i < 8; i++) mx = max(mx, __float_as_uint(v[i]) & 0x7FFFFFFFu);
@@ -345,6 +361,7 @@ __global__ void __launch_bounds__(kMmMaxSlices * 32, kMode == 2 ? 1 : 2) matvec_
     float* partial = reinterpret_cast<float*>(bf_all + (size_t)nsb * 256 + (size_t)S * 256);
     float* xsum = partial + (size_t)T * S * 16;
     float* pw = xsum + 8 * nsb;
+    float* red = pw + nsb;  // [S] per-warp sums of squares (fused norm)
     const int b0 = warp * nsb / S, b1 = (warp + 1) * nsb / S, ns = b1 - b0;
     const int tile0 = blockIdx.x * T;
     const int n_my = min(T, p.n_tiles - tile0);
@@ -383,7 +400,25 @@ __global__ void __launch_bounds__(kMmMaxSlices * 32, kMode == 2 ? 1 : 2) matvec_
         load(r0, r1, ty, b0, w0, w1);
     }
     if (a.weights_ready) pdl_wait();
-    if (ns > 0) prep_x<kMode == 0>(a.x, b0, b1, bf_all + (size_t)b0 * 256, pw, xsum, dig, lane);
+    float norm_s = 1.f;
+    if (a.x_norm_w) {
+        // the norm's scale 1 / sqrt(mean(x^2) + 1e-6) over the whole vector, by
+        // every block alike (the same order of additions in each)
+        float ss = 0.f;
+        for (int i = threadIdx.x; i < a.n_in / 4; i += blockDim.x) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(a.x) + i);
+            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        float tot = 0.f;
+        for (int i = 0; i < S; i++) tot += red[i];
+        norm_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)a.n_in), 1e-6f)));
+    }
+    if (ns > 0)
+        prep_x<kMode == 0>(a.x, b0, b1, bf_all + (size_t)b0 * 256, pw, xsum, dig, lane, a.x_norm_w, norm_s, a.x_up);
     __syncwarp();
     const uint32_t bmask = g < 4 ? 0xFFFFFFFFu : 0u;  // B column g: low half (k < 16) or high half
     float acc0 = 0.f, acc1 = 0.f;
@@ -437,6 +472,8 @@ __global__ void __launch_bounds__(kMmMaxSlices * 32, kMode == 2 ? 1 : 2) matvec_
 cudaError_t launch_matvec_mma(const MatvecArgs& a, cudaStream_t stream) {
     if (a.n_vec != 1 || a.n_in % 256 != 0 || a.n_parts < 1 || a.n_parts > 3) return cudaErrorNotSupported;
     if ((reinterpret_cast<uintptr_t>(a.x) & 15u) != 0) return cudaErrorNotSupported;
+    if ((reinterpret_cast<uintptr_t>(a.x_norm_w) | reinterpret_cast<uintptr_t>(a.x_up)) & 15u)
+        return cudaErrorNotSupported;
     MmArgs p{};
     p.a = a;
     p.nsb = a.n_in / 256;
@@ -467,7 +504,7 @@ cudaError_t launch_matvec_mma(const MatvecArgs& a, cudaStream_t stream) {
     if (se != cudaSuccess) return se;
     auto smem_for = [&](int sl, int tpb) {
         return (size_t)p.nsb * 256 * 4 + (size_t)sl * 1024 + (size_t)tpb * sl * 64 + (size_t)p.nsb * 32 +
-               (size_t)p.nsb * 4;
+               (size_t)p.nsb * 4 + (size_t)kMmMaxSlices * 4;
     };
     // the launch shape: S warps per row tile (each a contiguous slice of the
     // super-blocks; at most 15 % longer than the mean slice, or the most even),

@@ -150,6 +150,12 @@ struct MatvecArgs {
     // matrices (a launch that follows one of this library's own kernels), so
     // the tensor-core kernel may read them before the programmatic-launch wait
     int weights_ready;
+    // The tensor-core kernel only (launch_matvec_mma): x is formed on the fly
+    // from the caller's vector.  x_norm_w: x = rmsnorm(x) with these weights
+    // (the model-dimension norm, as launch_rmsnorm computes it); x_up: x =
+    // silu(x) * x_up (the FFN gate).  Null: x as given.
+    const float* x_norm_w;
+    const float* x_up;
 };
 int weight_block_elems(int type);  // weights per block of a PICOATTN_WT_* type (0: unsupported)
 int weight_block_bytes(int type);
