@@ -260,7 +260,8 @@ __device__ __forceinline__ void sb_q6k(const uint32_t (&w0)[kRaw], const uint32_
 // super-block), scales (pw: 2^(E_b-29), a power of two down to 2^-149; 0 for
 // blocks whose largest magnitude is below 2^-120, NaN for non-finite x) and
 // group sums (xsum, 8 per super-block).  dig: 256 words of scratch.
-template <bool kPairs>
+// kFuse: 0 x as given, 1 x = (x * norm_s) * norm_w, 2 x = silu(x) * up
+template <bool kPairs, int kFuse>
 __device__ __forceinline__ void prep_x(const float* x, int b0, int b1, uint32_t* bf, float* pw, float* xsum,
                                        uint32_t* dig, int lane, const float* norm_w, float norm_s, const float* up) {
     const int g = lane >> 2, t = lane & 3;
@@ -275,13 +276,13 @@ __device__ __forceinline__ void prep_x(const float* x, int b0, int b1, uint32_t*
         const float4 v0 = *reinterpret_cast<const float4*>(xb + 8 * lane);
         const float4 v1 = *reinterpret_cast<const float4*>(xb + 8 * lane + 4);
         float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        if (norm_w) {  // (x * s) * w, the norm's two roundings
+        if constexpr (kFuse == 1) {  // (x * s) * w, the norm's two roundings
             const float4 w0 = __ldg(reinterpret_cast<const float4*>(norm_w + 256 * b + 8 * lane));
             const float4 w1 = __ldg(reinterpret_cast<const float4*>(norm_w + 256 * b + 8 * lane + 4));
             const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
             for (int i = 0; i < 8; i++) v[i] = __fmul_rn(__fmul_rn(v[i], norm_s), w[i]);
-        } else if (up) {  // silu(g) * up: the reciprocal of 1 + e^-g, times g, times up
+        } else if constexpr (kFuse == 2) {  // silu(g) * up: the reciprocal of 1 + e^-g, times g, times up
             const float4 u0 = __ldg(reinterpret_cast<const float4*>(up + 256 * b + 8 * lane));
             const float4 u1 = __ldg(reinterpret_cast<const float4*>(up + 256 * b + 8 * lane + 4));
             const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
@@ -342,8 +343,9 @@ __device__ __forceinline__ void prep_x(const float* x, int b0, int b1, uint32_t*
 }
 
 // kMode: 0 every matrix Q4_K, 1 every matrix Q6_K, 2 both (chosen per tile).
+// kFuse: x as given (0), normalised on the fly (1: x_norm_w), silu(x) * x_up (2).
 // The single-format kernels fit 64 registers, so two 16-warp blocks share an SM.
-template <int kMode>
+template <int kMode, int kFuse>
 __global__ void __launch_bounds__(kMmMaxSlices * 32, kMode == 2 ? 1 : 2) matvec_mma_kernel(MmArgs p) {
     constexpr int kRaw = kMode == 0 ? kRawQ4K : kRawQ6K;
     extern __shared__ __align__(16) uint8_t mm_smem[];
@@ -401,7 +403,7 @@ __global__ void __launch_bounds__(kMmMaxSlices * 32, kMode == 2 ? 1 : 2) matvec_
     }
     if (a.weights_ready) pdl_wait();
     float norm_s = 1.f;
-    if (a.x_norm_w) {
+    if constexpr (kFuse == 1) {
         // the norm's scale 1 / sqrt(mean(x^2) + 1e-6) over the whole vector, by
         // every block alike (the same order of additions in each)
         float ss = 0.f;
@@ -418,7 +420,8 @@ __global__ void __launch_bounds__(kMmMaxSlices * 32, kMode == 2 ? 1 : 2) matvec_
         norm_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)a.n_in), 1e-6f)));
     }
     if (ns > 0)
-        prep_x<kMode == 0>(a.x, b0, b1, bf_all + (size_t)b0 * 256, pw, xsum, dig, lane, a.x_norm_w, norm_s, a.x_up);
+        prep_x<kMode == 0, kFuse>(a.x, b0, b1, bf_all + (size_t)b0 * 256, pw, xsum, dig, lane, a.x_norm_w, norm_s,
+                                  a.x_up);
     __syncwarp();
     const uint32_t bmask = g < 4 ? 0xFFFFFFFFu : 0u;  // B column g: low half (k < 16) or high half
     float acc0 = 0.f, acc1 = 0.f;
@@ -491,14 +494,22 @@ cudaError_t launch_matvec_mma(const MatvecArgs& a, cudaStream_t stream) {
     p.n_tiles = tiles;
     int n4 = 0;
     for (int i = 0; i < a.n_parts; i++) n4 += a.part[i].type == PICOATTN_WT_Q4_K;
-    const void* kern = n4 == a.n_parts ? (const void*)matvec_mma_kernel<0>
-                                       : (n4 == 0 ? (const void*)matvec_mma_kernel<1> : (const void*)matvec_mma_kernel<2>);
+    using Kern = void (*)(MmArgs);
+    static const Kern kernels[3][3] = {
+        {matvec_mma_kernel<0, 0>, matvec_mma_kernel<0, 1>, matvec_mma_kernel<0, 2>},
+        {matvec_mma_kernel<1, 0>, matvec_mma_kernel<1, 1>, matvec_mma_kernel<1, 2>},
+        {matvec_mma_kernel<2, 0>, matvec_mma_kernel<2, 1>, matvec_mma_kernel<2, 2>}};
+    const int mode = n4 == a.n_parts ? 0 : (n4 == 0 ? 1 : 2);
+    const int fuse = a.x_norm_w ? 1 : (a.x_up ? 2 : 0);
+    const Kern kfn = kernels[mode][fuse];
+    const void* kern = (const void*)kfn;
     static PerDeviceOnce setup;
     const cudaError_t se = setup.run([] {
-        for (auto k : {matvec_mma_kernel<0>, matvec_mma_kernel<1>, matvec_mma_kernel<2>}) {
-            const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-            if (e != cudaSuccess) return e;
-        }
+        for (const auto& row : kernels)
+            for (Kern k : row) {
+                const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+                if (e != cudaSuccess) return e;
+            }
         return cudaSuccess;
     });
     if (se != cudaSuccess) return se;
@@ -515,8 +526,7 @@ cudaError_t launch_matvec_mma(const MatvecArgs& a, cudaStream_t stream) {
     int dev = 0;
     cudaError_t de = cudaGetDevice(&dev);
     if (de != cudaSuccess) return de;
-    const int mode = n4 == a.n_parts ? 0 : (n4 == 0 ? 1 : 2);
-    const long long key = (((long long)dev * 4 + mode) * 4096 + p.nsb) * (1LL << 24) + tiles;
+    const long long key = ((((long long)dev * 4 + mode) * 4 + fuse) * 4096 + p.nsb) * (1LL << 24) + tiles;
     static std::mutex shape_mu;
     static std::map<long long, std::pair<int, int>> shapes;  // key -> (slices, tiles per block)
     {
@@ -565,9 +575,7 @@ cudaError_t launch_matvec_mma(const MatvecArgs& a, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (n4 == a.n_parts) return cudaLaunchKernelEx(&cfg, matvec_mma_kernel<0>, p);
-    if (n4 == 0) return cudaLaunchKernelEx(&cfg, matvec_mma_kernel<1>, p);
-    return cudaLaunchKernelEx(&cfg, matvec_mma_kernel<2>, p);
+    return cudaLaunchKernelEx(&cfg, kfn, p);
 }
 
 }  // namespace picoattn
