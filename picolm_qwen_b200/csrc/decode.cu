@@ -420,6 +420,170 @@ __device__ __forceinline__ void merge_slice(const DecodeArgs& a, int G, int b, i
     }
 }
 
+// Merge for one sequence: one block per q head (plan.merge_blocks), launched
+// while the attention kernel runs (programmatic dependent launch); its blocks
+// take SMs as attention CTAs exit and wait for the attention kernel to
+// complete.  Block i takes heads i, i + gridDim.x, ...; a head's G*W pieces
+// (acc rows, and their (max, sum) pairs) are contiguous in the partial slots.
+// The merge's time is set by the round trips it makes: each chunk of up
+// to MergeSeqShape::CK pieces (a whole head for one piece per attention CTA)
+// arrives by one bulk copy (TMA: its cost is per copy, not per byte), and the
+// block keeps kMergeSeqRing chunks, its whole share for a 16K-row shard, in
+// flight.  Per chunk warp 0 folds the (max, sum) pairs into the running
+// log2-sum-exp and writes each piece's weight to shared memory; then thread
+// (column, group) adds the weighted acc rows of every NG-th piece (four
+// independent sums, no branch), and the groups are added when the head is
+// done.  Calls with a peer exchange take the column-slice merge instead.
+constexpr int kMergeSeqThreads = 512;
+constexpr int kMergeSeqRing = 3;
+constexpr int kMergeSeqMaxUnits = 512;  // (head, 32-column slice) units of one block: hq <= 128
+
+template <int HD>
+struct MergeSeqShape {
+    static constexpr int CK = HD == 128 ? 144 : 280;  // pieces per chunk slot (72 / 70 KB of acc rows)
+    static constexpr int NG = kMergeSeqThreads / HD;
+    static constexpr int off_bar = 0;
+    static constexpr int off_seq = 32;
+    static constexpr int off_w = off_seq + kMergeSeqMaxUnits * 4;  // [CK] weights, then keep, L, M
+    static constexpr int off_ml = (off_w + (CK + 32) * 4 + 15) / 16 * 16;
+    static constexpr int off_buf = (off_ml + kMergeSeqRing * (CK + 2) * 8 + 127) / 128 * 128;
+    static constexpr int off_red = off_buf + kMergeSeqRing * CK * HD * 4;
+    static constexpr int bytes = off_red + 2 * NG * HD * 4;  // group sums, double-buffered by head
+    static_assert(bytes <= 227 * 1024, "one block per SM");
+};
+
+template <int HD>
+__global__ void __launch_bounds__(kMergeSeqThreads, 1) decode_merge_seq_kernel(DecodeArgs a, int G) {
+    pdl_trigger();
+    pdl_wait();
+    using Sh = MergeSeqShape<HD>;
+    constexpr int NG = Sh::NG, CK = Sh::CK, NR = kMergeSeqRing;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Sh::off_bar);
+    float* w_s = reinterpret_cast<float*>(smem + Sh::off_w);
+    float2* ml_s = reinterpret_cast<float2*>(smem + Sh::off_ml);
+    float* buf = reinterpret_cast<float*>(smem + Sh::off_buf);
+    float* red = reinterpret_cast<float*>(smem + Sh::off_red);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int col = tid % HD, grp = tid / HD;
+    const int pos = seq_pos(a, 0);
+    const bool ok = pos_ok(a, pos);
+    const long long R = ok ? local_len(a, pos) : 0;
+    const int W = a.warps_per_head, lw = __ffs(W) - 1;  // W is 1, 2, 4 or 8
+    const bool empty = !ok || R == 0;  // a rejected position: NaN; no rows in this shard: an empty partial
+    if (!empty && G == 1 && W == 1) return;  // written directly by the attention kernel
+    const int n_heads = (int)blockIdx.x < a.hq ? (a.hq - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int n_pieces = G * W;
+    const int n_chunks = (n_pieces + CK - 1) / CK;
+    const int cpc = ((n_pieces + n_chunks - 1) / n_chunks + 1) & ~1;  // pieces per chunk: even, <= CK
+    const int n_steps = empty ? 0 : n_heads * n_chunks;
+    auto head_of = [&](int hi) { return (int)blockIdx.x + hi * (int)gridDim.x; };
+    // a finished head: threads tid < HD hold column tid (warp z = slice z)
+    auto finish = [&](int hi, float res, float lse) {
+        const int h = head_of(hi);
+        {
+            const size_t row_stride = a.shard_out ? (size_t)(HD + 2) : (size_t)HD;
+            float* dst = (a.shard_out ? a.shard_out : a.out) + (size_t)h * row_stride;
+            dst[tid] = res;
+            if (a.shard_out && tid == 0) dst[HD] = lse;
+        }
+    };
+    // step -> (head hi, chunk c) in ring slot step % NR, by thread 0: two bulk
+    // copies (acc rows; the (max, sum) pairs rounded up to an even count, a
+    // 16-byte multiple: the slot after a head's last piece exists, n_slots > G*W,
+    // and chunk starts are even, n_slots even)
+    auto issue = [&](int step) {
+        const int hi = step / n_chunks, c = step % n_chunks, sl = step % NR;
+        const int k0 = c * cpc, cnt = min(cpc, n_pieces - k0);
+        const size_t first = (size_t)head_of(hi) * a.n_slots + k0;
+        const uint32_t ob = (uint32_t)cnt * HD * 4u, mb = (uint32_t)((cnt + 1) & ~1) * 8u;
+        mbar_arrive_expect_tx(&full[sl], ob + mb);
+        bulk_g2s(buf + (size_t)sl * CK * HD, a.part_o + first * HD, ob, &full[sl]);
+        bulk_g2s(ml_s + sl * (CK + 2), a.part_ml + first * 2, mb, &full[sl]);
+    };
+    if (tid == 0) {
+        for (int sl = 0; sl < NR; sl++) mbar_init(&full[sl], 1);
+        fence_mbar_init();
+        for (int j = 0; j < NR && j < n_steps; j++) issue(j);
+    }
+    __syncthreads();
+    if (empty && tid < HD)
+        for (int hi = 0; hi < n_heads; hi++)
+            finish(hi, ok ? 0.f : __int_as_float(0x7fc00000), ok ? -INFINITY : __int_as_float(0x7fc00000));
+    float M = -INFINITY, L = 0.f;  // running log2-sum-exp of the head (warp 0)
+    float acc = 0.f;               // this thread's group sum of column col
+    bool live = true;              // the waits have not timed out
+    for (int step = 0; step < n_steps; step++) {
+        const int hi = step / n_chunks, c = step % n_chunks, sl = step % NR;
+        const int k0 = c * cpc, cnt = min(cpc, n_pieces - k0);
+        if (live) live = mbar_wait(&full[sl], (uint32_t)((step / NR) & 1), a.status);
+        const float2* mls = ml_s + sl * (CK + 2);
+        const float* bs = buf + (size_t)sl * CK * HD;
+        if (warp == 0) {
+            // pieces of CTAs with empty slices (R < G) hold stale slots: weight 0
+            float cm = -INFINITY;
+            for (int j = lane; j < cnt; j += 32) {
+                const int i = (k0 + j) >> lw;
+                if (R >= G || slice_start(i, R, G) < slice_start(i + 1, R, G)) cm = fmaxf(cm, mls[j].x);
+            }
+            for (int o = 16; o; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
+            const float Mn = fmaxf(M, cm);
+            const float keep = Mn == -INFINITY ? 1.f : ex2(M - Mn);  // 0 while M = -inf
+            float ls = 0.f;
+            for (int j = lane; j < cnt; j += 32) {
+                const int i = (k0 + j) >> lw;
+                const bool v = Mn != -INFINITY && (R >= G || slice_start(i, R, G) < slice_start(i + 1, R, G));
+                const float wj = v ? ex2(mls[j].x - Mn) : 0.f;
+                w_s[j] = wj;
+                if (v) ls += wj * mls[j].y;
+            }
+            for (int o = 16; o; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+            L = L * keep + ls;
+            M = Mn;
+            if (lane == 0) w_s[CK] = keep, w_s[CK + 1] = L, w_s[CK + 2] = M;
+        }
+        __syncthreads();  // weights of this chunk
+        // read now: warp 0 rewrites them in the next step, after the barrier below
+        const float keep = w_s[CK], Lh = w_s[CK + 1], Mh = w_s[CK + 2];
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        int j = grp;
+        for (; j + 3 * NG < cnt; j += 4 * NG) {
+            const float w0 = w_s[j], w1 = w_s[j + NG], w2 = w_s[j + 2 * NG], w3 = w_s[j + 3 * NG];
+            const float v0 = bs[j * HD + col], v1 = bs[(j + NG) * HD + col];
+            const float v2 = bs[(j + 2 * NG) * HD + col], v3 = bs[(j + 3 * NG) * HD + col];
+            s0 += w0 != 0.f ? w0 * v0 : 0.f;  // weight 0: a stale slot may hold anything
+            s1 += w1 != 0.f ? w1 * v1 : 0.f;
+            s2 += w2 != 0.f ? w2 * v2 : 0.f;
+            s3 += w3 != 0.f ? w3 * v3 : 0.f;
+        }
+        for (; j < cnt; j += NG) {
+            const float w0 = w_s[j];
+            s0 += w0 != 0.f ? w0 * bs[j * HD + col] : 0.f;
+        }
+        acc = acc * keep + ((s0 + s1) + (s2 + s3));
+        const bool last = c == n_chunks - 1;
+        float* rh = red + (hi & 1) * NG * HD;
+        if (last) rh[grp * HD + col] = acc;
+        __syncthreads();  // slot sl and the weights are read; group sums complete
+        // the slot is free: the chunk NR steps ahead goes into it
+        if (tid == 0 && step + NR < n_steps) issue(step + NR);
+        if (last) {
+            // the head is done: its group sums, in the half of red for its parity
+            // (the next head's sums may be written while the column threads still
+            // read these; the head after that writes here only after they passed
+            // another barrier)
+            if (tid < HD) {
+                float o = 0.f;
+#pragma unroll
+                for (int g2 = 0; g2 < NG; g2++) o += rh[g2 * HD + tid];
+                finish(hi, o / Lh, Mh + __log2f(Lh));
+            }
+            acc = 0.f;
+            M = -INFINITY, L = 0.f;
+        }
+    }
+}
+
 // RPT: acc rows per thread held in registers, enough for one long sequence's
 // pieces (one per attention CTA) with 32- or 64-column slices; the whole-row
 // variant serves many short sequences of a few pieces each and keeps two.
@@ -953,6 +1117,9 @@ cudaError_t launch_decode_hd(const DecodeArgs& a_in, const DecodePlan& plan, cud
             e = cudaFuncSetAttribute(decode_merge_kernel<HD, 64>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(decode_merge_kernel<HD, 32>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(decode_merge_seq_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     MergeSeqShape<HD>::bytes);
         return e;
     });
     if (se != cudaSuccess) return se;
@@ -968,13 +1135,18 @@ cudaError_t launch_decode_hd(const DecodeArgs& a_in, const DecodePlan& plan, cud
     if (e == cudaSuccess && (stages & PICOATTN_STAGE_ATTEND))
         e = launch_pdl(decode_attn_kernel<HD>, dim3((unsigned)plan.grid_ctas), dim3((plan.compute_warps + 1) * 32),
                        (size_t)plan.smem_bytes, stream, a);
-    if (e == cudaSuccess && (stages & PICOATTN_STAGE_COMBINE)) {
+    // One sequence: one block per q head fed by bulk copies, except with a
+    // peer exchange, where the column-slice kernel below posts and combines
+    // 32-column slices (measured on B200: the 8-GPU split-KV step at 16K rows
+    // per rank 21,805 -> 22,956 GB/s with it, while a whole-model token step
+    // on one GPU runs 341 tok/s with the per-head merge against 320).
+    if (e == cudaSuccess && (stages & PICOATTN_STAGE_COMBINE) && a.n_seqs == 1 && a.x.peers == nullptr) {
+        e = launch_pdl(decode_merge_seq_kernel<HD>, dim3((unsigned)plan.merge_blocks), dim3(kMergeSeqThreads),
+                       (size_t)MergeSeqShape<HD>::bytes, stream, a, plan.grid_ctas);
+    } else if (e == cudaSuccess && (stages & PICOATTN_STAGE_COMBINE)) {
         // column slices: the narrowest of 32 or 64 columns that keeps the grid
         // within one block per SM (a block beside each attention CTA of the next
-        // call), else one block per (head, sequence).  One sequence takes the
-        // same kernel: measured on B200 against a one-block-per-head merge fed
-        // by bulk copies, 4K rows 11.9 -> 11.1 us per layer, 128K 87.6 -> 86.6,
-        // and the 8-GPU split-KV step (16K rows per rank) 21,805 -> 22,956 GB/s.
+        // call), else one block per (head, sequence)
         const long units = (long)a.hq * a.n_seqs;
         const int sms = plan.max_grid / 2;
         const dim3 blk(256);
@@ -1029,11 +1201,15 @@ bool make_decode_plan(const picoattn_config_t& cfg, int n_seqs, int max_ctx, Dec
     const int sms = device_sm_count();
     const int per_sm = p.smem_bytes <= 113 * 1024 ? 2 : 1;
     const long long work_rows = (long long)n_seqs * max_ctx;
-    // The attention grid takes every SM.  (The next call's attention reads its
-    // q only after this call's merge completes, so nothing is gained by
-    // reserving SMs for the merge to overlap it; measured on B200 with one
-    // sequence, 128K rows 114 -> 93.5 us per layer, a 16K-row shard 25.2 ->
-    // 22.0, 4K rows 14.4 -> 13.2 against 4-16 reserved SMs.)
+    // One sequence: the merge kernel takes one block per q head (up to one per
+    // SM).  Its blocks become resident as attention CTAs exit and start the
+    // moment the attention kernel completes, each with one head's pieces.  (The
+    // next call's attention reads its q only after this merge completes, so
+    // nothing is gained by reserving SMs for the merge to overlap it; measured
+    // on B200, a head per block on every SM beats 4-16 blocks on reserved SMs at
+    // every length: 128K rows 114 -> 93.5 us per layer, a 16K-row shard 25.2 ->
+    // 22.0, 4K rows 14.4 -> 13.2.)
+    p.merge_blocks = std::min(hq, sms);
     const int attn_sms = sms;
     long long g = std::min<long long>((long long)attn_sms * per_sm, (work_rows + 63) / 64);
     p.grid_ctas = (int)std::max<long long>(1, g);

@@ -62,6 +62,7 @@ struct DecodePlan {
     int tile_rows;        // rows per pipeline stage (multiple of 16*warps_per_head)
     int stages;           // pipeline depth
     int grid_ctas;        // persistent CTAs of the attention kernel
+    int merge_blocks;     // one sequence: blocks of the merge kernel (one per q head, at most one per SM)
     int max_grid;         // upper bound on grid_ctas (sizes the partial slots)
     int n_slots;          // partial slots per head: (max_grid + n_seqs) * warps_per_head, rounded up to even
     int smem_bytes;       // dynamic shared memory per CTA
