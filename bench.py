@@ -755,7 +755,7 @@ def run_longctx(args, dev, world, rank, local) -> dict:
         per_launch = 2 * S * kvd * 2
         peak, peak_kind = measured_peaks()
         ach = per_launch / (attn_ms / 1e3) / 1e9
-        roof = {"bound": "hbm", "kernel": "decode_attn_kernel<128> + decode_merge_kernel<128, 64> (one call)",
+        roof = {"bound": "hbm", "kernel": "decode_attn_kernel<128> + decode_merge_seq_kernel<128> (one call)",
                 "achieved": round(ach, 1), "peak": peak,
                 "peak_kind": peak_kind, "unit": "GB/s", "frac": round(ach / peak, 4),
                 "mean_launch_ms": round(attn_ms, 5), "algorithmic_bytes_per_launch": per_launch,
@@ -878,7 +878,7 @@ def run_small(args, dev, spec) -> dict:
                        "l2": "512 MiB written between timed steps; each step timed alone",
                        "timing": f"CUDA graph of the {L} layer calls"},
             "roofline": {"bound": "hbm (launch-latency dominated at this size)",
-                         "kernel": "decode_attn_kernel<64> + decode_merge_kernel<64, 32> (one call)",
+                         "kernel": "decode_attn_kernel<64> + decode_merge_seq_kernel<64> (one call)",
                          "achieved": round(layer_b / (attn_ms / 1e3) / 1e9, 1), "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(layer_b / (attn_ms / 1e3) / 1e9 / peak, 4),
