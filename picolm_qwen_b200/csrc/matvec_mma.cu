@@ -399,6 +399,20 @@ __global__ void __launch_bounds__(kMmMaxSlices * 32, kMode == 2 ? 1 : 2) matvec_
     uint32_t w0[kRaw], w1[kRaw];
     if (steps > 0) {
         tile_info(0, r0, r1, ty);
+        if (a.weights_ready && t == 0) {
+            // the first tile's rows of this warp's slice into L2 while the kernel
+            // before still runs: one bulk prefetch per row (rows g and g + 8),
+            // between 16-byte boundaries inside the row's slice
+            const size_t bb = ty == PICOATTN_WT_Q4_K ? 144 : 210;
+            for (int k = 0; k < 2; k++) {
+                const uint8_t* rp = k ? r1 : r0;
+                const uintptr_t s0 = (reinterpret_cast<uintptr_t>(rp + b0 * bb) + 15) & ~(uintptr_t)15;
+                const uintptr_t s1 = reinterpret_cast<uintptr_t>(rp + b1 * bb) & ~(uintptr_t)15;
+                if (s1 > s0)
+                    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(s0), "r"((uint32_t)(s1 - s0))
+                                 : "memory");
+            }
+        }
         load(r0, r1, ty, b0, w0, w1);
     }
     if (a.weights_ready) pdl_wait();
