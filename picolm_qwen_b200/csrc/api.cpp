@@ -436,8 +436,10 @@ int32_t picoattn_decode_layer(const picoattn_config_t* cfg, int32_t layer, int32
 
 size_t picoattn_ffn_workspace_size(int32_t dim, int32_t n_ffn, int32_t n_vec) {
     if (dim <= 0 || n_ffn <= 0 || n_vec <= 0) return 0;
-    // xb [n_vec][dim], gate and up [n_vec][n_ffn], fp32
-    return align_up((size_t)n_vec * dim * 4, 256) + 2 * align_up((size_t)n_vec * n_ffn * 4, 256);
+    // xb [n_vec][dim], gate and up [n_vec][n_ffn], fp32; then the down
+    // projection's x fragments (one vector, n_ffn a multiple of 256)
+    return align_up((size_t)n_vec * dim * 4, 256) + 2 * align_up((size_t)n_vec * n_ffn * 4, 256) +
+           align_up(xfrag_bytes(n_ffn), 256);
 }
 
 int32_t picoattn_rmsnorm(const float* x, const float* weight, float* out, int32_t dim, int32_t n_vec,
@@ -488,15 +490,31 @@ int32_t ffn_impl(const picoattn_ffn_weights_t* w, const float* ffn_norm_w, int32
         return launch_rmsnorm(x, ffn_norm_w, xb, dim, n_vec, s);
     }));
     if (st != PICOATTN_OK) return st;
-    // SwiGLU and the down projection in one launch likewise
+    // SwiGLU and the down projection: x's fragments made once by a small
+    // kernel (each down block would otherwise prepare the whole n_ffn-long x),
+    // else SwiGLU inside the down launch, else the separate kernels
     dn.n_parts = 1;
     dn.n_in = n_ffn;
     dn.n_vec = n_vec;
     dn.rows_total = dim;
     dn.accumulate = 1;
     dn.x = gate;
-    dn.x_up = up;
     dn.weights_ready = 1;  // after the gate/up launch
+    uint32_t* xfrag = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(up) +
+                                                  align_up((size_t)n_vec * n_ffn * 4, 256));
+    if (n_vec == 1 && xfrag_bytes(n_ffn) > 0) {
+        const bool pairs = w->down_type == PICOATTN_WT_Q4_K;
+        MatvecArgs pre = dn;
+        pre.xfrag = xfrag;
+        pre.xfrag_pairs = pairs ? 1 : 0;
+        const cudaError_t e = launch_xfrag(gate, up, n_ffn, pairs, xfrag, s);
+        if (e != cudaErrorNotSupported) {
+            if (e != cudaSuccess) return cuda_status(e);
+            const cudaError_t m = launch_matvec_mma(pre, s);
+            if (m != cudaErrorNotSupported) return cuda_status(m);
+        }
+    }
+    dn.x_up = up;
     return cuda_status(matvec_fused(dn, s, [&](const float** xo) {
         *xo = gate;
         return launch_silu_mul(gate, up, (size_t)n_vec * n_ffn, s);

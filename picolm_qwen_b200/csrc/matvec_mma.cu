@@ -343,7 +343,8 @@ __device__ __forceinline__ void prep_x(const float* x, int b0, int b1, uint32_t*
 }
 
 // kMode: 0 every matrix Q4_K, 1 every matrix Q6_K, 2 both (chosen per tile).
-// kFuse: x as given (0), normalised on the fly (1: x_norm_w), silu(x) * x_up (2).
+// kFuse: x as given (0), normalised on the fly (1: x_norm_w), silu(x) * x_up (2),
+// fragments made beforehand by launch_xfrag (3: xfrag).
 // The single-format kernels fit 64 registers, so two 16-warp blocks share an SM.
 template <int kMode, int kFuse>
 __global__ void __launch_bounds__(kMmMaxSlices * 32, kMode == 2 ? 1 : 2) matvec_mma_kernel(MmArgs p) {
@@ -433,9 +434,21 @@ __global__ void __launch_bounds__(kMmMaxSlices * 32, kMode == 2 ? 1 : 2) matvec_
         for (int i = 0; i < S; i++) tot += red[i];
         norm_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)a.n_in), 1e-6f)));
     }
-    if (ns > 0)
+    if constexpr (kFuse == 3) {
+        // x's fragments, scales and group sums made once by launch_xfrag
+        // (a.xfrag: [nsb][256] words, then [nsb] scales, then [nsb][8] sums)
+        const uint32_t* xf = a.xfrag;
+        const float* xpw = reinterpret_cast<const float*>(xf + (size_t)nsb * 256);
+        const float* xxs = xpw + nsb;
+        for (int i = lane; i < ns * 64; i += 32) cp_async16(bf_all + (size_t)b0 * 256 + 4 * i, xf + (size_t)b0 * 256 + 4 * i);
+        cp_async_commit();
+        for (int i = lane; i < ns; i += 32) pw[b0 + i] = xpw[b0 + i];
+        for (int i = lane; i < 8 * ns; i += 32) xsum[8 * b0 + i] = xxs[8 * b0 + i];
+        cp_async_wait<0>();
+    } else if (ns > 0) {
         prep_x<kMode == 0, kFuse>(a.x, b0, b1, bf_all + (size_t)b0 * 256, pw, xsum, dig, lane, a.x_norm_w, norm_s,
                                   a.x_up);
+    }
     __syncwarp();
     const uint32_t bmask = g < 4 ? 0xFFFFFFFFu : 0u;  // B column g: low half (k < 16) or high half
     float acc0 = 0.f, acc1 = 0.f;
@@ -481,7 +494,50 @@ __global__ void __launch_bounds__(kMmMaxSlices * 32, kMode == 2 ? 1 : 2) matvec_
     }
 }
 
+// x's fragments, scales and group sums once for a whole launch, one warp per
+// 256-element block (the x preparation of matvec_mma_kernel, written to global
+// memory: [nsb][256] words, [nsb] scales, [nsb][8] group sums).  kFuse 2:
+// x = silu(x) * up.
+template <bool kPairs, int kFuse>
+__global__ void __launch_bounds__(256) xfrag_kernel(const float* x, const float* up, int nsb, uint32_t* out) {
+    __shared__ __align__(16) uint32_t sm[8][512];  // per warp: fragments, digit scratch
+    pdl_trigger();
+    pdl_wait();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = blockIdx.x * 8 + warp;
+    if (b >= nsb) return;
+    float* pw = reinterpret_cast<float*>(out + (size_t)nsb * 256);
+    float* xs = pw + nsb;
+    prep_x<kPairs, kFuse>(x, b, b + 1, sm[warp], pw, xs, sm[warp] + 256, lane, nullptr, 1.f, up);
+    __syncwarp();
+    for (int i = lane; i < 64; i += 32)
+        reinterpret_cast<uint4*>(out + (size_t)b * 256)[i] = reinterpret_cast<const uint4*>(sm[warp])[i];
+}
+
 }  // namespace
+
+size_t xfrag_bytes(int n_in) { return n_in % 256 ? 0 : (size_t)(n_in / 256) * (1024 + 4 + 32); }
+
+cudaError_t launch_xfrag(const float* x, const float* up, int n_in, bool pairs, uint32_t* out, cudaStream_t stream) {
+    if (n_in % 256 != 0 || ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(up) |
+                             reinterpret_cast<uintptr_t>(out)) & 15u))
+        return cudaErrorNotSupported;
+    const int nsb = n_in / 256;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)((nsb + 7) / 8));
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (up)
+        return pairs ? cudaLaunchKernelEx(&cfg, xfrag_kernel<true, 2>, x, up, nsb, out)
+                     : cudaLaunchKernelEx(&cfg, xfrag_kernel<false, 2>, x, up, nsb, out);
+    return pairs ? cudaLaunchKernelEx(&cfg, xfrag_kernel<true, 0>, x, up, nsb, out)
+                 : cudaLaunchKernelEx(&cfg, xfrag_kernel<false, 0>, x, up, nsb, out);
+}
 
 // One vector of Q4_K / Q6_K matrices: returns cudaErrorNotSupported when the
 // launch does not fit this kernel (other formats, several vectors, rows of
@@ -489,8 +545,15 @@ __global__ void __launch_bounds__(kMmMaxSlices * 32, kMode == 2 ? 1 : 2) matvec_
 cudaError_t launch_matvec_mma(const MatvecArgs& a, cudaStream_t stream) {
     if (a.n_vec != 1 || a.n_in % 256 != 0 || a.n_parts < 1 || a.n_parts > 3) return cudaErrorNotSupported;
     if ((reinterpret_cast<uintptr_t>(a.x) & 15u) != 0) return cudaErrorNotSupported;
-    if ((reinterpret_cast<uintptr_t>(a.x_norm_w) | reinterpret_cast<uintptr_t>(a.x_up)) & 15u)
+    if ((reinterpret_cast<uintptr_t>(a.x_norm_w) | reinterpret_cast<uintptr_t>(a.x_up) |
+         reinterpret_cast<uintptr_t>(a.xfrag)) & 15u)
         return cudaErrorNotSupported;
+    // fragments made for another position map (launch_xfrag's pairs flag)
+    if (a.xfrag) {
+        int q4 = 0;
+        for (int i = 0; i < a.n_parts; i++) q4 += a.part[i].type == PICOATTN_WT_Q4_K;
+        if ((q4 == a.n_parts) != (a.xfrag_pairs != 0)) return cudaErrorNotSupported;
+    }
     MmArgs p{};
     p.a = a;
     p.nsb = a.n_in / 256;
@@ -509,12 +572,12 @@ cudaError_t launch_matvec_mma(const MatvecArgs& a, cudaStream_t stream) {
     int n4 = 0;
     for (int i = 0; i < a.n_parts; i++) n4 += a.part[i].type == PICOATTN_WT_Q4_K;
     using Kern = void (*)(MmArgs);
-    static const Kern kernels[3][3] = {
-        {matvec_mma_kernel<0, 0>, matvec_mma_kernel<0, 1>, matvec_mma_kernel<0, 2>},
-        {matvec_mma_kernel<1, 0>, matvec_mma_kernel<1, 1>, matvec_mma_kernel<1, 2>},
-        {matvec_mma_kernel<2, 0>, matvec_mma_kernel<2, 1>, matvec_mma_kernel<2, 2>}};
+    static const Kern kernels[3][4] = {
+        {matvec_mma_kernel<0, 0>, matvec_mma_kernel<0, 1>, matvec_mma_kernel<0, 2>, matvec_mma_kernel<0, 3>},
+        {matvec_mma_kernel<1, 0>, matvec_mma_kernel<1, 1>, matvec_mma_kernel<1, 2>, matvec_mma_kernel<1, 3>},
+        {matvec_mma_kernel<2, 0>, matvec_mma_kernel<2, 1>, matvec_mma_kernel<2, 2>, matvec_mma_kernel<2, 3>}};
     const int mode = n4 == a.n_parts ? 0 : (n4 == 0 ? 1 : 2);
-    const int fuse = a.x_norm_w ? 1 : (a.x_up ? 2 : 0);
+    const int fuse = a.xfrag ? 3 : (a.x_norm_w ? 1 : (a.x_up ? 2 : 0));
     const Kern kfn = kernels[mode][fuse];
     const void* kern = (const void*)kfn;
     static PerDeviceOnce setup;

@@ -156,6 +156,10 @@ struct MatvecArgs {
     // silu(x) * x_up (the FFN gate).  Null: x as given.
     const float* x_norm_w;
     const float* x_up;
+    // x's fragments made beforehand by launch_xfrag (x then unused), for the
+    // position map of launches of Q4_K only (xfrag_pairs = 1) or the other one
+    const uint32_t* xfrag;
+    int xfrag_pairs;
 };
 int weight_block_elems(int type);  // weights per block of a PICOATTN_WT_* type (0: unsupported)
 int weight_block_bytes(int type);
@@ -165,6 +169,11 @@ cudaError_t launch_matvec(const MatvecArgs& a, cudaStream_t stream);
 // One vector of Q4_K / Q6_K matrices on the integer tensor cores (matvec_mma.cu);
 // cudaErrorNotSupported when the launch does not fit it.
 cudaError_t launch_matvec_mma(const MatvecArgs& a, cudaStream_t stream);
+// x's integer-digit fragments for the tensor-core mat-vec, made once (x =
+// silu(x) * up when up is given): xfrag_bytes(n_in) bytes at out (0: n_in not
+// a multiple of 256).  pairs: for launches of Q4_K matrices only.
+size_t xfrag_bytes(int n_in);
+cudaError_t launch_xfrag(const float* x, const float* up, int n_in, bool pairs, uint32_t* out, cudaStream_t stream);
 
 // The rest of a decode layer (layer_ops.cu): model-dimension RMSNorm of n_vec
 // vectors, and the FFN gate gate = silu(gate) * up over n elements.
