@@ -259,3 +259,16 @@ def test_rmsnorm_ffn_logits_vs_reference(cuda, ffn_t):
     want = np.stack([m.logits(xv) for xv in xs])
     got = lg.cpu().numpy()
     assert np.all(np.abs(got - want) <= 1e-4 * (1 + np.abs(want))), f"logits max err {np.abs(got - want).max():.3g}"
+    # one vector: for Q4_K/Q6_K weights the norm runs inside the gate/up launch,
+    # the SwiGLU inside the fragment kernel of the down launch, and the final
+    # norm inside the logits launch
+    want_f = m.ffn(0, xs[1])
+    x1 = dev(xs[1:2])
+    ffn(fproj, fn, n_ffn, x1, scratch)
+    got = x1.cpu().numpy()[0]
+    assert np.all(np.abs(got - want_f) <= 1e-4 * (1 + np.abs(want_f))), f"ffn (one vector) max err {np.abs(got - want_f).max():.3g}"
+    lg1 = torch.empty((1, vocab), device="cuda")
+    logits(dev(xs[2:3]), out_norm, out_w, out_t, vocab, lg1, scratch)
+    want_l = m.logits(xs[2])
+    got = lg1.cpu().numpy()[0]
+    assert np.all(np.abs(got - want_l) <= 1e-4 * (1 + np.abs(want_l))), f"logits (one vector) max err {np.abs(got - want_l).max():.3g}"
