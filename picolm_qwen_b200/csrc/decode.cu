@@ -455,7 +455,6 @@ struct MergeSeqShape {
 template <int HD>
 __global__ void __launch_bounds__(kMergeSeqThreads, 1) decode_merge_seq_kernel(DecodeArgs a, int G) {
     pdl_trigger();
-    pdl_wait();
     using Sh = MergeSeqShape<HD>;
     constexpr int NG = Sh::NG, CK = Sh::CK, NR = kMergeSeqRing;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -471,7 +470,10 @@ __global__ void __launch_bounds__(kMergeSeqThreads, 1) decode_merge_seq_kernel(D
     const long long R = ok ? local_len(a, pos) : 0;
     const int W = a.warps_per_head, lw = __ffs(W) - 1;  // W is 1, 2, 4 or 8
     const bool empty = !ok || R == 0;  // a rejected position: NaN; no rows in this shard: an empty partial
-    if (!empty && G == 1 && W == 1) return;  // written directly by the attention kernel
+    if (!empty && G == 1 && W == 1) {  // written directly by the attention kernel
+        pdl_wait();
+        return;
+    }
     const int n_heads = (int)blockIdx.x < a.hq ? (a.hq - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
     const int n_pieces = G * W;
     const int n_chunks = (n_pieces + CK - 1) / CK;
@@ -501,11 +503,17 @@ __global__ void __launch_bounds__(kMergeSeqThreads, 1) decode_merge_seq_kernel(D
         bulk_g2s(buf + (size_t)sl * CK * HD, a.part_o + first * HD, ob, &full[sl]);
         bulk_g2s(ml_s + sl * (CK + 2), a.part_ml + first * 2, mb, &full[sl]);
     };
+    // The position (read above: no kernel of this library writes it, and a
+    // caller's kernel that does completes before this one starts) and the
+    // barriers are set up before waiting for the attention kernel, whose
+    // partials are read only after the wait.
     if (tid == 0) {
         for (int sl = 0; sl < NR; sl++) mbar_init(&full[sl], 1);
         fence_mbar_init();
-        for (int j = 0; j < NR && j < n_steps; j++) issue(j);
     }
+    pdl_wait();
+    if (tid == 0)
+        for (int j = 0; j < NR && j < n_steps; j++) issue(j);
     __syncthreads();
     if (empty && tid < HD)
         for (int hi = 0; hi < n_heads; hi++)
@@ -639,22 +647,31 @@ __device__ __forceinline__ void for_each_segment(const DecodeArgs& a, const long
 // by log2(e)/sqrt(hd) so scores come out in log2 units (the reference divides by
 // sqrtf(hd) and uses expf), rounded to fp16.  Four heads at a time pass through
 // the warp's staging area sq (4*HD floats) into the lanes that hold their rows.
+// The RoPE row of the position and the q-norm weights (QRot::load) are
+// constants of the model, so a caller may load them before waiting for the
+// kernel that writes q.
 template <int HD>
-__device__ __forceinline__ void q_fragments(const DecodeArgs& a, int b, int pos, int kvh, float* sq, int lane,
-                                            uint32_t (&qa)[HD / 16][4]) {
+struct QRot {
+    RopeLane<HD> rl;
+    float w[HD / 32];  // the q-norm weights of this lane's elements, shared by every head
+    __device__ __forceinline__ void load(const DecodeArgs& a, int pos, int lane) {
+        rope_lane_load<HD>(rl, a.rope_cos + (size_t)pos * (HD / 2), a.rope_sin + (size_t)pos * (HD / 2), a.rope_mode,
+                           lane);
+        if (a.qn_w) {
+#pragma unroll
+            for (int j = 0; j < HD / 32; j++) w[j] = a.qn_w[(HD / 32) * lane + j];
+        }
+    }
+};
+
+template <int HD>
+__device__ __forceinline__ void q_fragments(const DecodeArgs& a, int b, const QRot<HD>& qr, int kvh, float* sq,
+                                            int lane, uint32_t (&qa)[HD / 16][4]) {
     constexpr int V = HD / 32;
     const int G_q = a.g, gid = lane >> 2, tig = lane & 3;
     const float qscale = 1.4426950408889634f / sqrtf((float)HD);
 #pragma unroll
     for (int kk = 0; kk < HD / 16; kk++) qa[kk][0] = qa[kk][1] = qa[kk][2] = qa[kk][3] = 0u;
-    RopeLane<HD> rl;
-    rope_lane_load<HD>(rl, a.rope_cos + (size_t)pos * (HD / 2), a.rope_sin + (size_t)pos * (HD / 2), a.rope_mode,
-                       lane);
-    float w[V];  // the q-norm weights of this lane's elements, shared by every head
-    if (a.qn_w) {
-#pragma unroll
-        for (int j = 0; j < V; j++) w[j] = a.qn_w[V * lane + j];
-    }
     const float* qb = a.q + ((size_t)b * a.hq + (size_t)kvh * G_q) * HD;
     // four heads at a time; the next four heads' loads are issued before this
     // group's arithmetic, so their latency overlaps it
@@ -678,11 +695,11 @@ __device__ __forceinline__ void q_fragments(const DecodeArgs& a, int b, int pos,
             live[u] = u0 + u < G_q;
         }
         if (u0 + 4 < G_q) load4(u0 + 4);
-        if (a.qn_w) vec_rmsnorm4<HD>(x, w, live, a.eps, sq, lane);
+        if (a.qn_w) vec_rmsnorm4<HD>(x, qr.w, live, a.eps, sq, lane);
 #pragma unroll
         for (int u = 0; u < 4; u++) {
             if (live[u]) {
-                vec_rope<HD>(x[u], rl, a.rope_mode, lane);
+                vec_rope<HD>(x[u], qr.rl, a.rope_mode, lane);
                 vec_store_f32<HD>(x[u], sq + u * HD, lane);
             }
         }
@@ -847,15 +864,22 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
         named_bar_arrive(kSetupBar, blockDim.x);
     } else {
         if (a.fused_append) {  // one sequence: q from the caller's buffer, rotated here
-            // q, k and v may come from the kernel before this one (a projection
-            // that let this kernel launch early): wait for it before reading them
-            pdl_wait();
+            // The position, its RoPE row and the q-norm weights are read at once
+            // (no kernel of this library writes them, and a kernel of the caller's
+            // that does has completed before this one starts: it makes no early
+            // launch); q, k and v may come from the kernel before this one (a
+            // projection that let this kernel launch early), so they are read only
+            // after waiting for it.
             int p = 0;
             if (lane == 0) p = seq_pos(a, 0);
             p = __shfl_sync(0xffffffffu, p, 0);
             // a rejected position leaves no rows (the CTA exits below) and must not
             // index the RoPE table
-            if (pos_ok(a, p)) q_fragments<HD>(a, 0, p, warp / W, qstage + warp * 4 * HD, lane, qa);
+            const bool p_ok = pos_ok(a, p);
+            QRot<HD> qr;
+            if (p_ok) qr.load(a, p, lane);
+            pdl_wait();
+            if (p_ok) q_fragments<HD>(a, 0, qr, warp / W, qstage + warp * 4 * HD, lane, qa);
         }
         named_bar_sync(kSetupBar, blockDim.x);
     }
@@ -925,6 +949,23 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
                             bulk_g2s(dst + (uint32_t)u * row_bytes, base + (size_t)src_row * a.kvd, row_bytes,
                                      &full[s]);
                         }
+                    }
+                }
+                if (a.n_seqs == 1 && t == a.stages - 1) {
+                    // One sequence: with the ring's first tiles requested, the rows
+                    // after them (final rows only, up to ~40 MB over the grid) are
+                    // requested into L2 at once, so the cache keeps streaming while
+                    // the kernels before this one (the previous layer's merge and
+                    // exchange) finish and the compute warps wait for q; the ring
+                    // then reads them from L2.  A hint: nothing waits for it.
+                    const int ahead = (int)((40u << 20) / gridDim.x / (2u * row_bytes));
+                    const int p0 = row0 + T, p1 = min(min(r1, rows_ok), p0 + ahead);
+                    if (p1 > p0) {
+                        const int per = (p1 - p0 + 15) / 16;
+                        const int c0 = p0 + (lane & 15) * per, c1 = min(p1, c0 + per);
+                        if (c1 > c0)
+                            bulk_prefetch_l2((lane >> 4 ? vslab : kslab) + (size_t)c0 * a.kvd,
+                                             (uint32_t)(c1 - c0) * row_bytes);
                     }
                 }
             }

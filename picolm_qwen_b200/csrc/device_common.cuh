@@ -153,6 +153,12 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// Bulk prefetch of `bytes` of global memory into L2 (TMA engine, no completion
+// to wait for: a hint).  src 16-byte aligned; bytes a multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Per-thread asynchronous copies global -> shared through the load path (not
 // the TMA engine): 16 bytes (L2 only) or 8 bytes, grouped per thread by
 // commit_group; wait_group<N> returns when at most N of this thread's groups
