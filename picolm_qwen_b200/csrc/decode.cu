@@ -722,6 +722,98 @@ __device__ __forceinline__ void q_fragments(const DecodeArgs& a, int b, const QR
     }
 }
 
+// The same A operand for a layer without q-norm, straight from the caller's q
+// rows.  Lane (gid, tig) holds columns 16kk + 2tig + {0, 1, 8, 9} of heads gid
+// and gid + 8, and both columns of every RoPE pair it needs are its own: the
+// two columns of a float2 (interleaved), or columns c and c + HD/2, which is
+// step kk + HD/32 (NeoX).  So each lane loads its values with float2 loads and
+// rotates them in registers, with vec_rope's operations and roundings, then
+// scales and rounds them as q_fragments does: the same fragments, without the
+// staging through shared memory.  QRope holds the lane's RoPE factors, which
+// depend on the position only (loaded before waiting for the kernel that
+// writes q).
+template <int HD>
+struct QRope {
+    float c[HD / 8], s[HD / 8];
+    __device__ __forceinline__ void load(const DecodeArgs& a, int pos, int lane) {
+        const int tig = lane & 3;
+        const float* cr = a.rope_cos + (size_t)pos * (HD / 2);
+        const float* sr = a.rope_sin + (size_t)pos * (HD / 2);
+        if (a.rope_mode == PICOATTN_ROPE_NEOX) {  // factor 4kk + 2h + e: column 16kk + 2tig + 8h + e < HD/2
+#pragma unroll
+            for (int kk = 0; kk < HD / 32; kk++)
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const int col = 16 * kk + 2 * tig + 8 * h;
+                    const float2 cc = *reinterpret_cast<const float2*>(cr + col);
+                    const float2 ss = *reinterpret_cast<const float2*>(sr + col);
+                    c[4 * kk + 2 * h] = cc.x, c[4 * kk + 2 * h + 1] = cc.y;
+                    s[4 * kk + 2 * h] = ss.x, s[4 * kk + 2 * h + 1] = ss.y;
+                }
+        } else {  // factor 2kk + h: the pair of columns 16kk + 2tig + 8h, +1
+#pragma unroll
+            for (int kk = 0; kk < HD / 16; kk++)
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const int i = 8 * kk + tig + 4 * h;
+                    c[2 * kk + h] = cr[i];
+                    s[2 * kk + h] = sr[i];
+                }
+        }
+    }
+};
+
+template <int HD>
+__device__ __forceinline__ void q_fragments_direct(const DecodeArgs& a, int b, const QRope<HD>& r, int kvh, int lane,
+                                                   uint32_t (&qa)[HD / 16][4]) {
+    constexpr int K = HD / 16, H = HD / 32;
+    const int G_q = a.g, gid = lane >> 2, tig = lane & 3;
+    const float qscale = 1.4426950408889634f / sqrtf((float)HD);
+#pragma unroll
+    for (int kk = 0; kk < K; kk++) qa[kk][0] = qa[kk][1] = qa[kk][2] = qa[kk][3] = 0u;
+    const float* qb = a.q + ((size_t)b * a.hq + (size_t)kvh * G_q) * HD + 2 * tig;
+#pragma unroll
+    for (int half = 0; half < 2; half++) {
+        const int row = gid + 8 * half;
+        if (row >= G_q) continue;
+        float2 x[K][2];
+#pragma unroll
+        for (int kk = 0; kk < K; kk++)
+#pragma unroll
+            for (int h = 0; h < 2; h++)
+                x[kk][h] = *reinterpret_cast<const float2*>(qb + (size_t)row * HD + 16 * kk + 8 * h);
+        float2 y[K][2];
+        if (a.rope_mode == PICOATTN_ROPE_NEOX) {
+#pragma unroll
+            for (int kk = 0; kk < H; kk++)
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const int f = 4 * kk + 2 * h;
+                    const float2 lo = x[kk][h], hi = x[kk + H][h];
+                    y[kk][h].x = __fsub_rn(__fmul_rn(lo.x, r.c[f]), __fmul_rn(hi.x, r.s[f]));
+                    y[kk][h].y = __fsub_rn(__fmul_rn(lo.y, r.c[f + 1]), __fmul_rn(hi.y, r.s[f + 1]));
+                    y[kk + H][h].x = __fadd_rn(__fmul_rn(lo.x, r.s[f]), __fmul_rn(hi.x, r.c[f]));
+                    y[kk + H][h].y = __fadd_rn(__fmul_rn(lo.y, r.s[f + 1]), __fmul_rn(hi.y, r.c[f + 1]));
+                }
+        } else {
+#pragma unroll
+            for (int kk = 0; kk < K; kk++)
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const int f = 2 * kk + h;
+                    const float x0 = x[kk][h].x, x1 = x[kk][h].y;
+                    y[kk][h].x = __fsub_rn(__fmul_rn(x0, r.c[f]), __fmul_rn(x1, r.s[f]));
+                    y[kk][h].y = __fadd_rn(__fmul_rn(x0, r.s[f]), __fmul_rn(x1, r.c[f]));
+                }
+        }
+#pragma unroll
+        for (int kk = 0; kk < K; kk++) {
+            qa[kk][half] = pack_half2(y[kk][0].x * qscale, y[kk][0].y * qscale);
+            qa[kk][2 + half] = pack_half2(y[kk][1].x * qscale, y[kk][1].y * qscale);
+        }
+    }
+}
+
 // The same A operand from the q rows the prep kernel rotated (workspace q_rot).
 template <int HD>
 __device__ __forceinline__ void q_from_rot(const DecodeArgs& a, int b, int kvh, int lane, uint32_t (&qa)[HD / 16][4]) {
@@ -876,10 +968,17 @@ __global__ void __launch_bounds__(288, 1) decode_attn_kernel(DecodeArgs a) {
             // a rejected position leaves no rows (the CTA exits below) and must not
             // index the RoPE table
             const bool p_ok = pos_ok(a, p);
-            QRot<HD> qr;
-            if (p_ok) qr.load(a, p, lane);
-            pdl_wait();
-            if (p_ok) q_fragments<HD>(a, 0, qr, warp / W, qstage + warp * 4 * HD, lane, qa);
+            if (a.qn_w == nullptr) {
+                QRope<HD> qr;
+                if (p_ok) qr.load(a, p, lane);
+                pdl_wait();
+                if (p_ok) q_fragments_direct<HD>(a, 0, qr, warp / W, lane, qa);
+            } else {
+                QRot<HD> qr;
+                if (p_ok) qr.load(a, p, lane);
+                pdl_wait();
+                if (p_ok) q_fragments<HD>(a, 0, qr, warp / W, qstage + warp * 4 * HD, lane, qa);
+            }
         }
         named_bar_sync(kSetupBar, blockDim.x);
     }
