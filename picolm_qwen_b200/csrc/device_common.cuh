@@ -38,6 +38,22 @@ __device__ __forceinline__ uint16_t f32_to_f16_ref(float f) {
     return (uint16_t)(sgn | (word >> 13));
 }
 
+// Two values through f32_to_f16_ref, packed (first in the low half).  Magnitudes
+// in [2^-14, 2^16) -- fp32 exponent fields 113..142, the reference's normal
+// branch -- take the straight-line form of that branch: the word minus the
+// exponent rebias plus half an ulp, shifted (a carry out of 2^16 - 16 still
+// gives inf, as there); anything else goes through the full function.
+__device__ __forceinline__ uint32_t f32x2_to_f16_ref(float a, float b) {
+    const uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
+    const uint32_t ma = ua & 0x7FFFFFFFu, mb = ub & 0x7FFFFFFFu;
+    if (ma - 0x38800000u < 0x0F000000u && mb - 0x38800000u < 0x0F000000u) {
+        const uint32_t ha = ((ma - 0x37FFF000u) >> 13) | ((ua >> 16) & 0x8000u);
+        const uint32_t hb = ((mb - 0x37FFF000u) >> 13) | ((ub >> 16) & 0x8000u);
+        return ha | (hb << 16);
+    }
+    return (uint32_t)f32_to_f16_ref(a) | ((uint32_t)f32_to_f16_ref(b) << 16);
+}
+
 // ---------------------------------------------------------------------------
 // PTX wrappers
 // ---------------------------------------------------------------------------

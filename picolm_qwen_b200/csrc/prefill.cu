@@ -22,6 +22,7 @@
 //                  rescaled only when a row maximum grows by more than 8
 //                  (p <= 2^8 stays exact in fp16), which keeps the O round trip
 //                  off the common path.
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <mutex>
@@ -62,135 +63,270 @@ __device__ __forceinline__ uint32_t h2_ref16(uint32_t w) {
     return r;
 }
 
-// One warp = up to 8 head vectors of ONE kind (q, k or v) of one token, so the
-// three paths never run predicated inside each other; lane l owns elements
-// [V*l, V*l+V) of each vector.
+// A unit = up to 8 head vectors of ONE kind (q, k or v) of one token, so the
+// three paths never run predicated inside each other.  Each lane holds V =
+// HD/32 elements of each vector, both members of its RoPE pairs (prep_idx), so
+// RoPE needs no exchange between lanes.
+//
+// The grid is one wave of blocks that stays resident (8 warps each); warp w of
+// W takes units w, w+W, w+2W, ...  Each warp stages its units' inputs in a ring
+// of kPrepStages shared-memory slots by cp.async (16 bytes per lane, L2 only),
+// so the next units' loads are in flight while it works on the current one:
+// the kernel streams at the memory's rate instead of waiting once per unit.
+// A slot holds the unit's 8 rows, each HD * element bytes plus 16 bytes of
+// padding (the padding puts the rows of the 8 vectors on different banks).
+//
 // RMSNorm: the reference accumulates the squares of elements i = c, c+4, c+8, ...
-// into lane c = i % 4 in index order (cpp/tensor.hpp:146-176).  The squares are
-// written to shared memory transposed, chain c of vector u as one contiguous
-// row, and lane 4u+c runs that chain with 128-bit loads: 8 vectors x 4 chains
-// keep all 32 lanes busy.  Lane u then folds vector u's chains as
-// (c0+c2)+(c1+c3) and computes its scale, as in vec_rmsnorm.
-template <int HD>
-__device__ __forceinline__ void prefill_prep(const PrefillArgs& a) {
-    constexpr int V = HD / 32;  // elements per lane
-    constexpr int U = 8;        // vectors per warp
-    constexpr int CH = HD / 4;  // terms per chain
-    constexpr int RS = CH + 4;  // chain row stride (floats): 16-byte rows, conflict-free 128-bit reads
-    __shared__ __align__(16) float sq_all[8][U * 4 * RS];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (blockIdx.x == 0 && threadIdx.x == 0) *a.work_counter = 0;  // attention work queue
-    const int qg = (a.hq + U - 1) / U, kg = (a.hkv + U - 1) / U;
-    const int wpt = qg + 2 * kg;  // warps per token
-    const int gw = blockIdx.x * 8 + warp;
-    const int tok = gw / wpt;
-    if (tok >= a.n_tok) return;
-    const int r = gw - tok * wpt;
-    const int kind = r < qg ? 0 : (r < qg + kg ? 1 : 2);
-    const int h0 = (kind == 0 ? r : (kind == 1 ? r - qg : r - qg - kg)) * U;
-    const int nheads = kind == 0 ? a.hq : a.hkv;
-    const int nh = min(U, nheads - h0);
-    const int pos = a.start + tok;
-    const size_t crow = ((size_t)a.layer * a.max_seq + pos) * a.kvd;
+// into lane c = i % 4 in index order (cpp/tensor.hpp:146-176).  Lane 4u+c runs
+// chain c of vector u straight from the staged row (elements c + 4m, m in
+// order), all 32 lanes busy for 8 vectors; lane u then folds vector u's chains
+// as (c0+c2)+(c1+c3) and computes its scale, as in vec_rmsnorm.
+constexpr int kPrepUnit = 8;    // head vectors per unit
+constexpr int kPrepStages = 2;  // staged units per warp
+constexpr int kPrepWarps = 8;   // warps per block
 
-    if (kind == 2) {  // v: stored as the reference's fp16 of the input
-        uint16_t* dst = a.v_cache + crow + (size_t)h0 * HD;
-        if (a.in_dtype == PICOATTN_DTYPE_F16) {
-            const __half* src = reinterpret_cast<const __half*>(a.v) + ((size_t)tok * a.hkv + h0) * HD;
+__host__ __device__ constexpr int prep_row_bytes(int hd, int esize) { return hd * esize + 16; }
+__host__ __device__ constexpr int prep_slot_bytes(int hd, int esize) {
+    return kPrepUnit * prep_row_bytes(hd, esize);
+}
+__host__ __device__ constexpr int prep_smem_bytes(int hd, int esize) {
+    return kPrepWarps * kPrepStages * prep_slot_bytes(hd, esize);
+}
+
+// Units are numbered kind-major: every token's q groups first (token-major),
+// then every token's k groups, then the v groups, so the warps of an SM mostly
+// run the same one of the three code paths at a time.
+struct PrepUnit {
+    int tok, kind, h0, nh;
+};
+
+__device__ __forceinline__ PrepUnit prep_unit(const PrefillArgs& a, int unit, int qg, int kg) {
+    PrepUnit p;
+    const int nq = a.n_tok * qg, nk = a.n_tok * kg;
+    int g;
+    if (unit < nq) {
+        p.kind = 0, p.tok = unit / qg, g = unit - p.tok * qg;
+    } else if (unit < nq + nk) {
+        unit -= nq;
+        p.kind = 1, p.tok = unit / kg, g = unit - p.tok * kg;
+    } else {
+        unit -= nq + nk;
+        p.kind = 2, p.tok = unit / kg, g = unit - p.tok * kg;
+    }
+    p.h0 = g * kPrepUnit;
+    p.nh = min(kPrepUnit, (p.kind == 0 ? a.hq : a.hkv) - p.h0);
+    return p;
+}
+
+// This lane's share of the copy of one unit's rows into `slot`: 16-byte pieces,
+// lane-strided, then one commit (an empty group when the unit does not exist,
+// so every lane has committed the same number of groups).
+template <int HD, int ES>
+__device__ __forceinline__ void prep_stage(const PrefillArgs& a, int unit, int n_units, int qg, int kg,
+                                           uint8_t* slot, int lane) {
+    if (unit < n_units) {
+        const PrepUnit p = prep_unit(a, unit, qg, kg);
+        const void* base = p.kind == 0 ? a.q : (p.kind == 1 ? a.k : a.v);
+        const int nheads = p.kind == 0 ? a.hq : a.hkv;
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(base) + ((size_t)p.tok * nheads + p.h0) * HD * ES;
+        constexpr int PR = HD * ES / 16;  // 16-byte pieces per row (a power of two, 8..32)
 #pragma unroll
-            for (int u = 0; u < U; u++) {
-                if (u < nh) {
-                    if constexpr (V == 4) {
-                        uint2 w = *reinterpret_cast<const uint2*>(src + u * HD + V * lane);
-                        w.x = h2_ref16(w.x), w.y = h2_ref16(w.y);
-                        *reinterpret_cast<uint2*>(dst + u * HD + V * lane) = w;
-                    } else {
-                        const uint32_t w = *reinterpret_cast<const uint32_t*>(src + u * HD + V * lane);
-                        *reinterpret_cast<uint32_t*>(dst + u * HD + V * lane) = h2_ref16(w);
-                    }
+        for (int it = 0; it < kPrepUnit * PR / 32; it++) {
+            const int i = lane + 32 * it, u = i / PR, pc = i % PR;
+            if (u < p.nh) cp_async16(slot + u * prep_row_bytes(HD, ES) + 16 * pc, src + (size_t)u * HD * ES + 16 * pc);
+        }
+    }
+    cp_async_commit();
+}
+
+// Element e of a staged row as fp32 (fp16 rows widened exactly); elements e, e+1.
+template <int ES>
+__device__ __forceinline__ float prep_elem(const uint8_t* row, int e) {
+    if constexpr (ES == 2) return __half2float(reinterpret_cast<const __half*>(row)[e]);
+    else return reinterpret_cast<const float*>(row)[e];
+}
+template <int ES>
+__device__ __forceinline__ float2 prep_elem2(const uint8_t* row, int e) {
+    if constexpr (ES == 2) return __half22float2(*reinterpret_cast<const __half2*>(row + 2 * e));
+    else return *reinterpret_cast<const float2*>(row + 4 * e);
+}
+
+// The elements of a head vector lane l holds, x[0..V-1], chosen so that both
+// of its RoPE pairs stay inside the lane:
+//   HD 128: 2l, 2l+1, 64+2l, 65+2l  (NeoX pairs (2l, 64+2l), (2l+1, 65+2l);
+//           interleaved pairs (2l, 2l+1), (64+2l, 65+2l))
+//   HD 64:  NeoX l, 32+l; interleaved 2l, 2l+1 (one pair)
+template <int HD>
+__device__ __forceinline__ int prep_idx(int lane, int j, bool neox) {
+    if constexpr (HD == 128) return (j < 2 ? 2 * lane : 64 + 2 * lane) + (j & 1);
+    else return neox ? lane + 32 * j : 2 * lane + j;
+}
+
+template <int HD, int ES>
+__device__ __forceinline__ void prep_load(float (&x)[HD / 32], const uint8_t* row, int lane, bool neox) {
+    if constexpr (HD == 128) {
+        const float2 a = prep_elem2<ES>(row, 2 * lane), b = prep_elem2<ES>(row, 64 + 2 * lane);
+        x[0] = a.x, x[1] = a.y, x[2] = b.x, x[3] = b.y;
+    } else if (neox) {
+        x[0] = prep_elem<ES>(row, lane), x[1] = prep_elem<ES>(row, 32 + lane);
+    } else {
+        const float2 a = prep_elem2<ES>(row, 2 * lane);
+        x[0] = a.x, x[1] = a.y;
+    }
+}
+
+// 16-bit results h[j] of x[j] to dst at this lane's element positions
+template <int HD>
+__device__ __forceinline__ void prep_store16(uint16_t* dst, const uint32_t (&hp)[HD / 64], int lane, bool neox) {
+    if constexpr (HD == 128) {
+        *reinterpret_cast<uint32_t*>(dst + 2 * lane) = hp[0];
+        *reinterpret_cast<uint32_t*>(dst + 64 + 2 * lane) = hp[1];
+    } else if (neox) {
+        dst[lane] = (uint16_t)(hp[0] & 0xFFFFu);
+        dst[32 + lane] = (uint16_t)(hp[0] >> 16);
+    } else {
+        *reinterpret_cast<uint32_t*>(dst + 2 * lane) = hp[0];
+    }
+}
+
+// RoPE of one pair (products and sums rounded separately, as vec_rope):
+// (x0, x1) -> (x0*c - x1*s, x0*s + x1*c).  Scalar intrinsics: a packed
+// multiply followed by a packed subtract may be contracted into one fused
+// multiply-add, which rounds differently from the reference.
+__device__ __forceinline__ void prep_rot(float& x0, float& x1, float c, float s) {
+    const float a = x0, b = x1;
+    x0 = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+    x1 = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+}
+
+// RoPE of this lane's pairs.
+template <int HD>
+__device__ __forceinline__ void prep_rope(float (&x)[HD / 32], const float* crow, const float* srow, int lane,
+                                          bool neox) {
+    if constexpr (HD == 128) {
+        if (neox) {  // table rows 2l, 2l+1; pairs (x0, x2), (x1, x3)
+            const float2 c = *reinterpret_cast<const float2*>(crow + 2 * lane);
+            const float2 s = *reinterpret_cast<const float2*>(srow + 2 * lane);
+            prep_rot(x[0], x[2], c.x, s.x);
+            prep_rot(x[1], x[3], c.y, s.y);
+        } else {     // table rows l, 32+l; pairs (x0, x1), (x2, x3)
+            prep_rot(x[0], x[1], crow[lane], srow[lane]);
+            prep_rot(x[2], x[3], crow[32 + lane], srow[32 + lane]);
+        }
+    } else {
+        prep_rot(x[0], x[1], crow[lane], srow[lane]);
+    }
+}
+
+// fp16 input bits -> the reference's fp16 rounding of their fp32 value (the
+// identity except on NaN, h2_ref16): a half is NaN when its magnitude plus
+// 0x3FF carries into bit 15, so one add tests both halves of a word.
+__device__ __forceinline__ uint32_t h2_ref16_fast(uint32_t w) {
+    return (((w & 0x7FFF7FFFu) + 0x03FF03FFu) & 0x80008000u) ? h2_ref16(w) : w;
+}
+
+// One unit whose rows are staged in `slot`.  Every row of the slot is read and
+// processed whether or not the unit has that head (rows past nh hold stale
+// data, and their results are never stored), so the arithmetic runs without
+// per-head branches.
+template <int HD, int ES>
+__device__ __forceinline__ void prep_unit_run(const PrefillArgs& a, const PrepUnit& p, const uint8_t* slot, int lane) {
+    constexpr int V = HD / 32;
+    constexpr int U = kPrepUnit;
+    constexpr int RB = prep_row_bytes(HD, ES);
+    const int nh = p.nh;
+    const int pos = a.start + p.tok;
+    const size_t crow = ((size_t)a.layer * a.max_seq + pos) * a.kvd;
+    const bool neox = a.rope_mode == PICOATTN_ROPE_NEOX;
+
+    if (p.kind == 2) {  // v: stored as the reference's fp16 of the input
+        uint16_t* dst = a.v_cache + crow + (size_t)p.h0 * HD;
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            if constexpr (ES == 2) {  // the bits themselves, NaN payloads aside
+                if constexpr (V == 4) {
+                    uint2 w = *reinterpret_cast<const uint2*>(slot + u * RB + 8 * lane);
+                    w.x = h2_ref16_fast(w.x), w.y = h2_ref16_fast(w.y);
+                    if (u < nh) *reinterpret_cast<uint2*>(dst + u * HD + V * lane) = w;
+                } else {
+                    const uint32_t w = h2_ref16_fast(*reinterpret_cast<const uint32_t*>(slot + u * RB + 4 * lane));
+                    if (u < nh) *reinterpret_cast<uint32_t*>(dst + u * HD + V * lane) = w;
                 }
+            } else {
+                float x[V];
+                prep_load<HD, ES>(x, slot + u * RB, lane, neox);
+                uint32_t hp[V / 2];
+#pragma unroll
+                for (int j = 0; j < V / 2; j++) hp[j] = f32x2_to_f16_ref(x[2 * j], x[2 * j + 1]);
+                if (u < nh) prep_store16<HD>(dst + u * HD, hp, lane, neox);
             }
-        } else {
-            Vec<HD> x[U];
-#pragma unroll
-            for (int u = 0; u < U; u++)
-                if (u < nh) vec_load<HD>(x[u], a.v, ((size_t)tok * a.hkv + h0 + u) * HD, a.in_dtype, lane);
-#pragma unroll
-            for (int u = 0; u < U; u++)
-                if (u < nh) vec_store_ref16<HD>(x[u], dst + u * HD, lane);
         }
         return;
     }
 
-    const void* src = kind == 0 ? a.q : a.k;
-    Vec<HD> x[U];
+    float x[U][V];
 #pragma unroll
-    for (int u = 0; u < U; u++)
-        if (u < nh) vec_load<HD>(x[u], src, ((size_t)tok * nheads + h0 + u) * HD, a.in_dtype, lane);
-    RopeLane<HD> rl;
-    rope_lane_load<HD>(rl, a.rope_cos + (size_t)pos * (HD / 2), a.rope_sin + (size_t)pos * (HD / 2), a.rope_mode,
-                       lane);
+    for (int u = 0; u < U; u++) prep_load<HD, ES>(x[u], slot + u * RB, lane, neox);
     if (a.qn_w) {
-        const float* wsrc = kind == 0 ? a.qn_w : a.kn_w;
+        const float* wsrc = p.kind == 0 ? a.qn_w : a.kn_w;
         float w[V];
 #pragma unroll
-        for (int j = 0; j < V; j++) w[j] = wsrc[V * lane + j];
-        float* sq = sq_all[warp];
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            if (u < nh) {
-#pragma unroll
-                for (int j = 0; j < V; j++) {
-                    const int i = V * lane + j;
-                    sq[(u * 4 + (i & 3)) * RS + (i >> 2)] = __fmul_rn(x[u].x[j], x[u].x[j]);
-                }
-            }
-        }
-        __syncwarp();
+        for (int j = 0; j < V; j++) w[j] = wsrc[prep_idx<HD>(lane, j, neox)];
+        // chain c = lane & 3 of vector lane >> 2: elements c, c+4, ..., in order
+        constexpr int CH = HD / 4;
         float part = 0.f;
-        if ((lane >> 2) < nh) {
-            const float4* row = reinterpret_cast<const float4*>(sq + lane * RS);  // (u*4 + c) == lane
+        const uint8_t* row = slot + (lane >> 2) * RB;
+        const int c = lane & 3;
 #pragma unroll
-            for (int k4 = 0; k4 < CH / 4; k4++) {
-                const float4 t = row[k4];
-                part = __fadd_rn(part, t.x);
-                part = __fadd_rn(part, t.y);
-                part = __fadd_rn(part, t.z);
-                part = __fadd_rn(part, t.w);
-            }
+        for (int m = 0; m < CH; m++) {
+            const float e = prep_elem<ES>(row, c + 4 * m);
+            part = __fadd_rn(part, __fmul_rn(e, e));
         }
         const int s4 = (lane & 7) * 4;
         const float c0 = __shfl_sync(0xffffffffu, part, s4 + 0), c1 = __shfl_sync(0xffffffffu, part, s4 + 1);
         const float c2 = __shfl_sync(0xffffffffu, part, s4 + 2), c3 = __shfl_sync(0xffffffffu, part, s4 + 3);
         const float ss = __fadd_rn(__fadd_rn(c0, c2), __fadd_rn(c1, c3));
-        const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)HD), a.eps)));
+        // ss / HD: HD is a power of two, so the product with 1/HD is the same
+        // correctly rounded quotient
+        const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / (float)HD), a.eps)));
+        // (x * scale) * w, two roundings, as vec_rmsnorm
 #pragma unroll
         for (int u = 0; u < U; u++) {
             const float su = __shfl_sync(0xffffffffu, scale, u);
-            if (u < nh) {
+            const uint64_t s2 = f2_pack(su, su);
 #pragma unroll
-                for (int j = 0; j < V; j++) x[u].x[j] = __fmul_rn(__fmul_rn(x[u].x[j], su), w[j]);
-            }
+            for (int j = 0; j < V; j += 2)
+                f2_unpack(f2_mul(f2_mul(f2_pack(x[u][j], x[u][j + 1]), s2), f2_pack(w[j], w[j + 1])), x[u][j],
+                          x[u][j + 1]);
         }
     }
-    if (kind == 0) {
+    const float* rc = a.rope_cos + (size_t)pos * (HD / 2);
+    const float* rs = a.rope_sin + (size_t)pos * (HD / 2);
+    if (p.kind == 0) {
         const float qscale = 1.4426950408889634f / sqrtf((float)HD);
-        __half* dst = a.q16 + ((size_t)tok * a.hq + h0) * HD;
+        const uint64_t qs2 = f2_pack(qscale, qscale);
+        uint16_t* dst = reinterpret_cast<uint16_t*>(a.q16 + ((size_t)p.tok * a.hq + p.h0) * HD);
 #pragma unroll
         for (int u = 0; u < U; u++) {
-            if (u < nh) {
-                vec_rope<HD>(x[u], rl, a.rope_mode, lane);
-                vec_store_h16_scaled<HD>(x[u], dst + u * HD, qscale, lane);
+            prep_rope<HD>(x[u], rc, rs, lane, neox);
+            uint32_t hp[V / 2];
+#pragma unroll
+            for (int j = 0; j < V / 2; j++) {
+                float lo, hi;
+                f2_unpack(f2_mul(f2_pack(x[u][2 * j], x[u][2 * j + 1]), qs2), lo, hi);
+                hp[j] = pack_half2(lo, hi);
             }
+            if (u < nh) prep_store16<HD>(dst + u * HD, hp, lane, neox);
         }
     } else {
-        uint16_t* dst = a.k_cache + crow + (size_t)h0 * HD;
+        uint16_t* dst = a.k_cache + crow + (size_t)p.h0 * HD;
 #pragma unroll
         for (int u = 0; u < U; u++) {
-            if (u < nh) {
-                vec_rope<HD>(x[u], rl, a.rope_mode, lane);
-                vec_store_ref16<HD>(x[u], dst + u * HD, lane);
-            }
+            prep_rope<HD>(x[u], rc, rs, lane, neox);
+            uint32_t hp[V / 2];
+#pragma unroll
+            for (int j = 0; j < V / 2; j++) hp[j] = f32x2_to_f16_ref(x[u][2 * j], x[u][2 * j + 1]);
+            if (u < nh) prep_store16<HD>(dst + u * HD, hp, lane, neox);
         }
     }
 }
@@ -200,10 +336,29 @@ __device__ __forceinline__ void prefill_prep(const PrefillArgs& a) {
 // and may still write the output) before it reads or writes anything, and lets
 // the attention kernel after it launch only once its own stores are done, so
 // that kernel's early CTAs do not take SMs the rest of this grid needs.
-template <int HD>
-__global__ void __launch_bounds__(256) prefill_prep_kernel(PrefillArgs a) {
+template <int HD, int ES>
+__global__ void __launch_bounds__(kPrepWarps * 32) prefill_prep_kernel(PrefillArgs a) {
+    extern __shared__ __align__(16) uint8_t prep_smem[];
     pdl_wait();
-    prefill_prep<HD>(a);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (blockIdx.x == 0 && threadIdx.x == 0) *a.work_counter = 0;  // attention work queue
+    const int qg = (a.hq + kPrepUnit - 1) / kPrepUnit, kg = (a.hkv + kPrepUnit - 1) / kPrepUnit;
+    const int n_units = a.n_tok * (qg + 2 * kg);
+    const int W = gridDim.x * kPrepWarps;
+    const int first = blockIdx.x * kPrepWarps + warp;
+    uint8_t* ring = prep_smem + (size_t)warp * kPrepStages * prep_slot_bytes(HD, ES);
+#pragma unroll
+    for (int s = 0; s < kPrepStages; s++)
+        prep_stage<HD, ES>(a, first + s * W, n_units, qg, kg, ring + s * prep_slot_bytes(HD, ES), lane);
+    for (int k = 0, unit = first; unit < n_units; k++, unit += W) {
+        uint8_t* slot = ring + (k % kPrepStages) * prep_slot_bytes(HD, ES);
+        cp_async_wait<kPrepStages - 1>();  // this lane's pieces of the unit have landed
+        __syncwarp();                      // and every other lane's
+        prep_unit_run<HD, ES>(a, prep_unit(a, unit, qg, kg), slot, lane);
+        __syncwarp();  // every lane has read the slot before it is refilled
+        prep_stage<HD, ES>(a, unit + kPrepStages * W, n_units, qg, kg, slot, lane);
+    }
+    cp_async_wait<0>();
     pdl_trigger();
 }
 
@@ -1412,16 +1567,34 @@ bool make_out_map(CUtensorMap* m, float* base, uint64_t inner, uint64_t rows) {
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// One-time, per-device setup of the attention kernels for one head_dim: their
-// shared-memory limits, and whether the CTA-pair and head-pair kernels can be
-// resident (the CTA pair needs kPairThreads threads x 80 registers and 2-CTA clusters).
+// One-time, per-device setup of the prefill kernels for one head_dim: their
+// shared-memory limits, the prep kernel's resident blocks per SM (its grid is
+// one wave), and whether the CTA-pair and head-pair kernels can be resident
+// (the CTA pair needs kPairThreads threads x 80 registers and 2-CTA clusters).
 struct PrefillSetup {
     bool done = false;
     cudaError_t err = cudaSuccess;
     int pair_clusters = 0;  // resident CTA-pair clusters, 0 if none
     bool pair_ok = false;   // head-pair kernel resident
     int sms = 148;
+    int prep_blocks[2] = {1, 1};  // prep blocks per SM: fp16 inputs, fp32 inputs
 };
+
+// The prep kernel for one input element size: the largest shared-memory
+// carveout (the attention kernel after it needs it too, so the SM need not
+// change its split between the two) and its resident blocks per SM.
+template <int HD, int ES>
+cudaError_t prep_setup(int& blocks) {
+    cudaError_t e = cudaFuncSetAttribute(prefill_prep_kernel<HD, ES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         prep_smem_bytes(HD, ES));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(prefill_prep_kernel<HD, ES>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e == cudaSuccess)
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, prefill_prep_kernel<HD, ES>, kPrepWarps * 32,
+                                                          prep_smem_bytes(HD, ES));
+    if (e == cudaSuccess && blocks < 1) e = cudaErrorInvalidConfiguration;
+    return e;
+}
 
 template <int HD>
 const PrefillSetup& prefill_setup() {
@@ -1434,6 +1607,10 @@ const PrefillSetup& prefill_setup() {
     if (st.done) return st;
     st.done = true;
     cudaDeviceGetAttribute(&st.sms, cudaDevAttrMultiProcessorCount, dev);
+    st.err = prep_setup<HD, 2>(st.prep_blocks[0]);
+    if (st.err != cudaSuccess) return st;
+    st.err = prep_setup<HD, 4>(st.prep_blocks[1]);
+    if (st.err != cudaSuccess) return st;
     st.err = cudaFuncSetAttribute(prefill_attn_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   AttnSmem<HD>::kDynBytes);
     if (st.err != cudaSuccess) return st;
@@ -1473,18 +1650,26 @@ int prefill_variant(const PrefillSetup& st, int g) {
 template <int HD>
 cudaError_t launch_prefill_hd(const PrefillArgs& a, cudaStream_t stream, unsigned stages) {
     if (stages & PICOATTN_STAGE_PREPARE) {
-        // one warp per (token, kind, group of 8 heads), 8 warps per block
-        const long warps = (long)a.n_tok * ((a.hq + 7) / 8 + 2 * ((a.hkv + 7) / 8));
+        // units of (token, kind, group of 8 heads); one wave of 8-warp blocks,
+        // fewer when there are fewer units than warps
+        const PrefillSetup& st = prefill_setup<HD>();
+        if (st.err != cudaSuccess) return st.err;
+        const bool f16 = a.in_dtype == PICOATTN_DTYPE_F16;
+        const long units = (long)a.n_tok * ((a.hq + kPrepUnit - 1) / kPrepUnit + 2 * ((a.hkv + kPrepUnit - 1) / kPrepUnit));
+        const long wave = (long)st.prep_blocks[f16 ? 0 : 1] * st.sms;
+        const long blocks = std::min((units + kPrepWarps - 1) / kPrepWarps, wave);
         cudaLaunchConfig_t cfg = {};
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.gridDim = dim3((unsigned)((warps + 7) / 8), 1, 1);
-        cfg.blockDim = dim3(256, 1, 1);
+        cfg.gridDim = dim3((unsigned)blocks, 1, 1);
+        cfg.blockDim = dim3(kPrepWarps * 32, 1, 1);
+        cfg.dynamicSmemBytes = f16 ? prep_smem_bytes(HD, 2) : prep_smem_bytes(HD, 4);
         cfg.stream = stream;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        const cudaError_t e = cudaLaunchKernelEx(&cfg, prefill_prep_kernel<HD>, a);
+        const cudaError_t e = f16 ? cudaLaunchKernelEx(&cfg, prefill_prep_kernel<HD, 2>, a)
+                                  : cudaLaunchKernelEx(&cfg, prefill_prep_kernel<HD, 4>, a);
         if (e != cudaSuccess) return e;
     }
     if (stages & PICOATTN_STAGE_ATTEND) {
