@@ -280,7 +280,11 @@ __device__ __forceinline__ void prep_unit_run(const PrefillArgs& a, const PrepUn
 #pragma unroll
         for (int m = 0; m < CH; m++) {
             const float e = prep_elem<ES>(row, c + 4 * m);
-            part = __fadd_rn(part, __fmul_rn(e, e));
+            // the square of a widened fp16 value is exact in fp32 (at most 22
+            // significant bits, no underflow), so one fused multiply-add rounds
+            // exactly as the reference's rounded square plus rounded sum
+            if constexpr (ES == 2) part = __fmaf_rn(e, e, part);
+            else part = __fadd_rn(part, __fmul_rn(e, e));
         }
         const int s4 = (lane & 7) * 4;
         const float c0 = __shfl_sync(0xffffffffu, part, s4 + 0), c1 = __shfl_sync(0xffffffffu, part, s4 + 1);
