@@ -584,6 +584,24 @@ def run_prefill(args, dev, world, rank, local) -> dict:
     torch.cuda.synchronize(dev)
     ms = t0.elapsed_time(t1)
     del graph
+    # the prep kernel alone, as a graph of its 36 launches: the step time per
+    # layer less this is the attention kernel's share of the step (there its
+    # launch and set-up run under the prep kernel before it)
+    pgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(pgraph):
+        gh = torch.cuda.current_stream(dev).cuda_stream
+        for l in range(L):
+            layer_call(l, abi.STAGE_PREPARE, stream_h=gh)
+    pgraph.replay()
+    torch.cuda.synchronize(dev)
+    t0.record(stream)
+    for i in range(steps):
+        pgraph.replay()
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    prep_graph_ms = t0.elapsed_time(t1)
+    del pgraph
+    step_ms_local = ms
     # the attention kernel alone: event pairs around every ATTEND launch
     evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
            for _ in range(steps)]
@@ -607,6 +625,7 @@ def run_prefill(args, dev, world, rank, local) -> dict:
         pass
     peak = float(peaks.get("bf16_tflops", 1590.0))
     achieved = flops_layer / (attn_ms / 1e3) / 1e12
+    in_step_us = (step_ms_local - prep_graph_ms) / steps / L * 1e3
     variant = lib.picoattn_prefill_kernel(cfgp)
     kernel = {abi.PREFILL_CTA_PAIR: "prefill_attn_pair_kernel (2-SM CTA pair, tcgen05 cta_group::2)",
               abi.PREFILL_HEAD_PAIR: "prefill_attn2_kernel<128> (head pair, 1 SM)",
@@ -624,7 +643,13 @@ def run_prefill(args, dev, world, rank, local) -> dict:
                          "peak": peak, "peak_kind": "measured" if peaks else "fallback", "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4), "mean_launch_ms": round(attn_ms, 5),
                          "algorithmic_flops_per_launch": flops_layer},
-            "prep_ms_per_layer": round(ms / steps / L - attn_ms, 5)}
+            "prep_ms_per_layer": round(ms / steps / L - attn_ms, 5),
+            "in_step": {"method": "graph step time per layer less the prep kernel's time per layer in a graph of "
+                                  "its launches alone (this rank)",
+                        "prep_us_per_layer": round(prep_graph_ms / steps / L * 1e3, 2),
+                        "attention_us_per_layer": round(in_step_us, 2),
+                        "attention_tflops": round(flops_layer / (in_step_us / 1e6) / 1e12, 1),
+                        "frac": round(flops_layer / (in_step_us / 1e6) / 1e12 / peak, 4)}}
 
 
 LONGCTX = dict(name="qwen2.5-32b-128k-decode", n_layers=64, n_heads=40, n_kv_heads=8, head_dim=128,
