@@ -113,6 +113,9 @@ def run_case(oracle, hq, hkv, hd, n_tok, start, mode=0, norm=True, f16=True, see
     dict(hq=4, hkv=4, hd=64, n_tok=1, start=0),                      # a one-token prompt
     dict(hq=4, hkv=4, hd=128, n_tok=1, start=300),                   # one token after a long cache
     dict(hq=16, hkv=4, hd=128, n_tok=333, start=1000, norm=False),   # long cached prefix
+    dict(hq=8, hkv=2, hd=128, n_tok=150, start=40, mode=1),          # interleaved RoPE at head_dim 128, QK-norm
+    dict(hq=8, hkv=4, hd=64, n_tok=70, start=3, mode=1, f16=False),  # fp32 inputs, interleaved, head_dim 64
+    dict(hq=12, hkv=4, hd=64, n_tok=33, start=0, f16=False),        # fp32 inputs, NeoX + QK-norm, head_dim 64, G = 3
 ])
 def test_prefill_vs_oracle(cuda, oracle, case):
     st, got, ref, kc, vc = run_case(oracle, **case)
