@@ -744,11 +744,9 @@ struct QRope {
             for (int kk = 0; kk < HD / 32; kk++)
 #pragma unroll
                 for (int h = 0; h < 2; h++) {
-                    const int col = 16 * kk + 2 * tig + 8 * h;
-                    const float2 cc = *reinterpret_cast<const float2*>(cr + col);
-                    const float2 ss = *reinterpret_cast<const float2*>(sr + col);
-                    c[4 * kk + 2 * h] = cc.x, c[4 * kk + 2 * h + 1] = cc.y;
-                    s[4 * kk + 2 * h] = ss.x, s[4 * kk + 2 * h + 1] = ss.y;
+                    const int col = 16 * kk + 2 * tig + 8 * h;  // 4-byte loads: the tables need only 4-byte alignment
+                    c[4 * kk + 2 * h] = cr[col], c[4 * kk + 2 * h + 1] = cr[col + 1];
+                    s[4 * kk + 2 * h] = sr[col], s[4 * kk + 2 * h + 1] = sr[col + 1];
                 }
         } else {  // factor 2kk + h: the pair of columns 16kk + 2tig + 8h, +1
 #pragma unroll

@@ -204,11 +204,10 @@ template <int HD>
 __device__ __forceinline__ void prep_rope(float (&x)[HD / 32], const float* crow, const float* srow, int lane,
                                           bool neox) {
     if constexpr (HD == 128) {
-        if (neox) {  // table rows 2l, 2l+1; pairs (x0, x2), (x1, x3)
-            const float2 c = *reinterpret_cast<const float2*>(crow + 2 * lane);
-            const float2 s = *reinterpret_cast<const float2*>(srow + 2 * lane);
-            prep_rot(x[0], x[2], c.x, s.x);
-            prep_rot(x[1], x[3], c.y, s.y);
+        if (neox) {  // table rows 2l, 2l+1; pairs (x0, x2), (x1, x3) (4-byte loads: the
+                     // caller's table need only be 4-byte aligned)
+            prep_rot(x[0], x[2], crow[2 * lane], srow[2 * lane]);
+            prep_rot(x[1], x[3], crow[2 * lane + 1], srow[2 * lane + 1]);
         } else {     // table rows l, 32+l; pairs (x0, x1), (x2, x3)
             prep_rot(x[0], x[1], crow[lane], srow[lane]);
             prep_rot(x[2], x[3], crow[32 + lane], srow[32 + lane]);
