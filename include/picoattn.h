@@ -136,7 +136,8 @@ size_t picoattn_decode_workspace_size(const picoattn_config_t* cfg, int32_t n_se
  *   k, v     [n_seqs][n_kv_heads*head_dim] fp32 (state.xb2 before each store)
  *   q_norm_w, k_norm_w  [head_dim] fp32 per-layer QK-RMSNorm weights, or both
  *            NULL when the layer has none (cpp/model.hpp:326-349)
- *   rope_cos, rope_sin  [max_seq_len][head_dim/2] fp32 (picoattn_rope_table)
+ *   rope_cos, rope_sin  [max_seq_len][head_dim/2] fp32 (picoattn_rope_table);
+ *            any 4-byte aligned address
  *   k_cache, v_cache    device array of n_seqs device pointers; entry b is
  *            sequence b's cache base, uint16 [n_layers][max_seq_len][kv_dim],
  *            16-byte aligned
